@@ -1,0 +1,321 @@
+#!/usr/bin/env python
+"""MoE-layer throughput of libflashmoe on B200 (BASELINE.json metric:
+"MoE-layer tokens/s at 1/2/4/8 B200; % of HBM (decode) / tensor (prefill) roof").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+A step is one fm_moe_block call (router, top-k, sort, grouped 4-bit SwiGLU experts,
+combine, gated shared expert) over one batch of the workload's tokens.  Default
+workload: BASELINE configs[1], the Qwen1.5-MoE-A2.7B-shaped layer on a 4096-token
+prefill batch (synthetic seeded inputs and weights, MLX packed 4-bit layout).
+
+value  = tokens of all ranks / max-over-ranks device time per step (inputs resident)
+e2e    = the same through the public API with the step's x copied from pinned host
+         memory and y read back to pinned host memory inside the timed region
+N > 1  = independent replicas (each rank runs its own batch on its own weights copy)
+--impl reference: the CPU restatement of the reference's MLX path (the reference
+needs MLX + Metal, which this box cannot run) timed on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from flashmlx_b200 import synthetic as S  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+DEFAULT_CONFIG = "qwen15_prefill"
+CPU_SAMPLE_TOKENS = 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(S.CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(3, a.warmup)
+    return a
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in FALLBACK_PEAKS if k in d}, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def rank_info():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU
+def cpu_oracle_throughput(shape, layer_np, x_np, min_seconds=10.0):
+    """Tokens/s of the CPU restatement on a bounded sample (all host threads)."""
+    from oracle import oracle as O
+    O.build()
+    L = O.Layer(shape, layer_np)
+    n = min(CPU_SAMPLE_TOKENS, x_np.shape[0])
+    sample = x_np[:n]
+    done, t0 = 0, time.perf_counter()
+    while True:
+        L.moe_block(sample)
+        done += n
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, {"cores": O.NTHREADS, "kind": "port",
+                       "sample": f"first {n} tokens of the {shape.name} batch (seed 0), "
+                                 f"repeated {done // n}x over {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU port of the reference path; rank 0 only."""
+    if rank != 0:
+        return
+    shape = S.CONFIGS[args.config]
+    layer_np = S.make_layer(shape, args.seed)
+    x_np = S.make_x(shape, args.seed)
+    from oracle import oracle as O
+    O.build()
+    L = O.Layer(shape, layer_np)
+    n = min(CPU_SAMPLE_TOKENS, x_np.shape[0])
+    for _ in range(args.warmup):
+        L.moe_block(x_np[:n])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        L.moe_block(x_np[:n])
+    dt = (time.perf_counter() - t0) / args.steps
+    v = n / dt
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+u4",
+        "data": "synthetic", "config": {"workload": shape.name, "tokens_per_step": n},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": O.NTHREADS, "kind": "port",
+                         "sample": f"first {n} tokens of the {shape.name} batch per step"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference path needs MLX + Apple Metal (not installable here); CPU restatement "
+                "of its MLX semantics (oracle/oracle.cpp) timed instead",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU
+def kernel_work(shape, T, counts):
+    """Algorithmic FLOPs and bytes per launch of each kernel of one fm_moe_block call."""
+    H, I, E, k, Is = shape.hidden, shape.inter, shape.num_experts, shape.top_k, shape.shared_inter
+    P = T * k
+    wb = S.layer_weight_bytes(shape)
+    per_w = wb["per_weight"]
+    active = int((counts > 0).sum())
+    f_gu = 2.0 * P * H * I * 2 + 2.0 * T * H * Is * 2
+    f_dn = 2.0 * P * I * H + 2.0 * T * Is * H
+    b_gu = active * 2 * H * I * per_w + 2 * H * Is * per_w + T * H * 2 + P * I * 2 + T * Is * 2
+    b_dn = active * H * I * per_w + H * Is * per_w + P * I * 2 + T * Is * 2 + T * H * 4 * (2 if Is else 1)
+    f_rt = 2.0 * T * H * (E + (1 if Is else 0))
+    b_rt = E * H * 2 + T * H * 2 * 2 + T * H * 4 * (2 if Is else 1)
+    return {
+        "qgemm_tc_gateup": (f_gu, b_gu), "qgemv_gateup": (f_gu, b_gu),
+        "qgemm_tc_down": (f_dn, b_dn), "qgemv_down": (f_dn, b_dn),
+        "route": (f_rt, b_rt), "finalize": (0.0, T * H * (4 + 4 + 2) if Is else T * H * 6),
+    }, active
+
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
+    from flashmlx_b200 import ops
+
+    shape = S.CONFIGS[args.config]
+    T = shape.tokens
+    layer_np = S.make_layer(shape, args.seed)
+    x_np = S.make_x(shape, args.seed + rank)  # each replica gets its own batch
+    W = ops.MoEWeightsT.from_numpy(layer_np, dev)
+    block = ops.MoEBlock(shape, W)
+    block.reserve(T)
+    h = ops.default_handle(local_rank)
+    x = ops.bf16_from_numpy(x_np, dev)
+    y = torch.empty_like(x)
+    # routing of this batch (for the algorithmic byte count of the decode path)
+    _, routing = block(x, return_routing=True)
+    h.sync()
+    counts = np.diff(routing["expert_offsets"].cpu().numpy())
+    for _ in range(args.warmup):
+        block(x, out=y)
+    h.sync()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    h.profile(True)
+    h.profile_report(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        block(x, out=y)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h.sync()
+    dev_ms = e0.elapsed_time(e1) / args.steps
+    prof = h.profile_report(reset=True)
+    h.profile(False)
+
+    # end-to-end through the public API: pinned host x -> device -> block -> pinned host y
+    x_pin = torch.from_numpy(x_np.view(np.int16)).view(torch.bfloat16).pin_memory()
+    y_pin = torch.empty_like(x_pin).pin_memory()
+    x_e2e = torch.empty_like(x)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        x_e2e.copy_(x_pin, non_blocking=True)
+        block(x_e2e, out=y)
+        y_pin.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+
+    if world > 1:
+        t = torch.tensor([dev_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, e2e_ms = t.tolist()
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        work, active = kernel_work(shape, T, counts)
+        # dominant kernel by device time
+        name, (launches, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+        avg_ms = tot_ms / max(1, launches)
+        flops, nbytes = work.get(name, (0.0, 0.0))
+        tensor_bound = name.startswith("qgemm_tc")
+        if tensor_bound:
+            achieved = flops / (avg_ms * 1e-3) / 1e12
+            peak = peaks["bf16_tflops"]
+            roof = {"bound": "tensor", "unit": "TFLOP/s"}
+        else:
+            achieved = nbytes / (avg_ms * 1e-3) / 1e9
+            peak = peaks["hbm_gbs"]
+            roof = {"bound": "hbm", "unit": "GB/s"}
+        traffic = None
+        tfile = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tfile):
+            with open(tfile) as f:
+                traffic = json.load(f).get(shape.name, {}).get(name)
+        roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "traffic": traffic,
+                     "kernel": name, "kernel_ms": avg_ms, "peak_source": peak_src,
+                     "algorithmic": flops if tensor_bound else nbytes})
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, info = cpu_oracle_throughput(shape, layer_np, x_np)
+            cpu = {"value": v, "unit": "tokens/s", **info}
+        ours_launches = sum(n for kname, (n, _) in prof.items())
+        line = {
+            "metric": "moe_layer_tokens_per_s", "value": world * T / (dev_ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+u4",
+            "data": "synthetic",
+            "config": {"workload": shape.name, "tokens_per_rank": T, "hidden": shape.hidden,
+                       "inter": shape.inter, "experts": shape.num_experts, "top_k": shape.top_k,
+                       "shared_inter": shape.shared_inter, "active_experts": active,
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "weights exceed L2 (no flush between steps)"},
+            "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
+            "gpu_launches": ours_launches,
+            "kernels": {kname: {"launches": n, "avg_ms": ms / max(1, n)} for kname, (n, ms) in prof.items()},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank, world, local_rank = rank_info()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,623 @@
+// api.cu -- host implementation of the libflashmoe C ABI (include/flashmoe.h).
+//
+// Mirrors the reference's operator boundary: fm_quantized_matmul / fm_gather_qmm take
+// MLX's argument lists (model.cpp:478-479, 703-721), fm_moe_block takes the layer
+// config and stacked weights of LlamaModel::moe_block (model.cpp:750-807, model.h:40-72).
+// Every call is stream-ordered; no call allocates once fm_reserve() has sized the
+// workspace for the largest batch.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "flashmoe.h"
+#include "fm_internal.cuh"
+
+namespace fm {
+__global__ void route_kernel(const RouteArgs a);
+__global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
+                                uint16_t* y);
+cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
+cudaError_t qgemv_blocks_per_sm(int* n);
+namespace tc {
+cudaError_t init();
+cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
+}  // namespace tc
+}  // namespace fm
+
+struct fm_handle {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::string last_error;
+  int num_sms = 0;
+  int route_blocks_per_sm = 0;
+  int gemv_blocks_per_sm = 0;
+  int path = FM_PATH_AUTO;
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
+  // kernel timing (fm_profile_enable)
+  bool profile = false;
+  struct Pending {
+    const char* name;
+    cudaEvent_t a, b;
+  };
+  std::vector<Pending> pending;
+  std::vector<cudaEvent_t> event_pool;
+  struct Total {
+    const char* name;  // static string literal
+    int64_t launches;
+    double ms;
+  };
+  std::map<std::string, Total> totals;
+  const char* open_name = nullptr;
+  cudaEvent_t open_ev = nullptr;
+};
+
+namespace {
+
+using fm::GemmArgs;
+using fm::RouteArgs;
+using fm::TileTable;
+
+constexpr size_t kCtrlBytes = 256;  // error word + grid-sync counters, persistent
+
+int set_err(fm_handle* h, int status, const std::string& msg) {
+  if (h) h->last_error = msg;
+  return status;
+}
+
+int cuda_err(fm_handle* h, cudaError_t e, const char* what) {
+  return set_err(h, FM_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Per-call workspace carve-up.
+struct Plan {
+  size_t total = 0;
+  size_t partial, x_perm, topk_ids, topk_score, gate_sig, row_src, chunk_counts, pair_rank, totals, offsets,
+      sorted_token, sorted_score, sorted_flat, tab_a, tab_b, a_sorted, a_shared, y_acc, ysh;
+  size_t add(size_t bytes) {
+    const size_t off = total;
+    total = align_up(total + bytes, 256);
+    return off;
+  }
+};
+
+Plan make_plan(int64_t T, int64_t x_rows, int H, int E, int k, int epad, int ksplit, int64_t a_cols,
+               int64_t ash_cols, bool shared, bool moe) {
+  Plan p;
+  p.total = kCtrlBytes;
+  const int64_t P = T * k;
+  const int64_t nchunks = (T + fm::kRouteChunk - 1) / fm::kRouteChunk;
+  p.partial = p.add(moe ? sizeof(float) * ksplit * T * epad : 0);
+  p.x_perm = p.add(sizeof(uint16_t) * x_rows * H);
+  p.topk_ids = p.add(sizeof(int32_t) * P);
+  p.topk_score = p.add(sizeof(float) * P);
+  p.gate_sig = p.add(sizeof(float) * T);
+  p.row_src = p.add(sizeof(int32_t) * T);
+  p.chunk_counts = p.add(sizeof(int32_t) * nchunks * E);
+  p.pair_rank = p.add(sizeof(int32_t) * P);
+  p.totals = p.add(sizeof(int32_t) * E);
+  p.offsets = p.add(sizeof(int32_t) * (E + 1));
+  p.sorted_token = p.add(sizeof(int32_t) * P);
+  p.sorted_score = p.add(sizeof(float) * P);
+  p.sorted_flat = p.add(sizeof(int32_t) * P);
+  p.tab_a = p.add(sizeof(TileTable));
+  p.tab_b = p.add(moe ? sizeof(TileTable) : 0);
+  p.a_sorted = p.add(moe ? sizeof(uint16_t) * P * a_cols : 0);
+  p.a_shared = p.add(moe && shared ? sizeof(uint16_t) * T * ash_cols : 0);
+  p.y_acc = p.add(moe ? sizeof(float) * T * H : 0);
+  p.ysh = p.add(moe && shared ? sizeof(float) * T * H : 0);
+  return p;
+}
+
+int ensure_ws(fm_handle* h, size_t bytes) {
+  if (bytes <= h->ws_bytes) return FM_OK;
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaStreamSynchronize");
+  if (h->ws) cudaFree(h->ws);
+  h->ws = nullptr;
+  h->ws_bytes = 0;
+  const size_t want = align_up(bytes + bytes / 8, 1 << 20);
+  e = cudaMalloc(&h->ws, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(h, FM_ENOMEM, std::string("workspace allocation failed: ") + cudaGetErrorString(e));
+  }
+  h->ws_bytes = want;
+  e = cudaMemsetAsync(h->ws, 0, kCtrlBytes, h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
+  return FM_OK;
+}
+
+cudaEvent_t take_event(fm_handle* h) {
+  if (!h->event_pool.empty()) {
+    cudaEvent_t e = h->event_pool.back();
+    h->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+// brackets the next kernel launch with events when profiling is on
+void prof_begin(fm_handle* h, const char* name) {
+  if (!h->profile) return;
+  h->open_name = name;
+  h->open_ev = take_event(h);
+  cudaEventRecord(h->open_ev, h->stream);
+}
+
+void prof_end(fm_handle* h) {
+  if (!h->profile || !h->open_ev) return;
+  cudaEvent_t b = take_event(h);
+  cudaEventRecord(b, h->stream);
+  h->pending.push_back({h->open_name, h->open_ev, b});
+  h->open_ev = nullptr;
+}
+
+uint32_t* err_word(fm_handle* h) { return reinterpret_cast<uint32_t*>(h->ws); }
+fm::GridSync* grid_sync(fm_handle* h) { return reinterpret_cast<fm::GridSync*>(h->ws + 64); }
+
+template <class T>
+T* at(fm_handle* h, size_t off) {
+  return reinterpret_cast<T*>(h->ws + off);
+}
+
+bool quant_ok(int K, int gs, int bits) {
+  return bits == 4 && (gs == 32 || gs == 64 || gs == 128) && K > 0 && K % gs == 0;
+}
+
+int launch_route(fm_handle* h, RouteArgs& ra, int64_t items) {
+  const int max_blocks = h->route_blocks_per_sm * h->num_sms;
+  const int64_t nchunks = (ra.T + fm::kRouteChunk - 1) / fm::kRouteChunk;
+  int64_t want = std::max<int64_t>((items + 7) / 8, nchunks);
+  want = std::max<int64_t>(want, std::min<int64_t>(ra.E, h->num_sms));
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks)));
+  void* args[] = {&ra};
+  prof_begin(h, ra.do_router ? "route" : "route_given");
+  cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&fm::route_kernel), dim3(grid),
+                                              dim3(fm::kRouteThreads), args, 0, h->stream);
+  prof_end(h);
+  if (e != cudaSuccess) return cuda_err(h, e, "route_kernel launch");
+  return FM_OK;
+}
+
+template <int MODE>
+int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05) {
+  static const char* names[2][3] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain"},
+                                    {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain"}};
+  prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
+  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->num_sms, h->stream, ga)
+                                : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
+  prof_end(h);
+  if (e != cudaSuccess) return cuda_err(h, e, tcgen05 ? "qgemm_tc launch" : "qgemv launch");
+  return FM_OK;
+}
+
+int router_ksplit(const fm_handle* h, int64_t T, int H) {
+  const int64_t ntt = (T + 15) / 16;
+  const int64_t target = static_cast<int64_t>(h->num_sms) * 16;
+  int ks = static_cast<int>(std::min<int64_t>(16, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
+  ks = std::min(ks, std::max(1, H / 128));
+  return ks;
+}
+
+bool use_tc(const fm_handle* h, int64_t pairs, int E) {
+  if (h->path == FM_PATH_GEMV) return false;
+  if (h->path == FM_PATH_TCGEN05) return true;
+  return pairs >= 24LL * E;  // ~24+ activation rows per matrix on average
+}
+
+int check_moe(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w) {
+  if (!c || !w) return set_err(h, FM_EINVAL, "null config or weights");
+  if (c->hidden <= 0 || c->inter <= 0 || c->num_experts <= 0 || c->top_k <= 0 || c->top_k > c->num_experts)
+    return set_err(h, FM_EINVAL, "bad MoE dimensions");
+  if (c->num_experts > fm::kMaxExperts || c->top_k > 16)
+    return set_err(h, FM_EUNSUPPORTED, "num_experts > 512 or top_k > 16");
+  if (!quant_ok(c->hidden, c->group_size, c->bits) || !quant_ok(c->inter, c->group_size, c->bits))
+    return set_err(h, FM_EUNSUPPORTED, "only 4-bit affine with group size 32/64/128 is implemented");
+  if (c->hidden % 128 || c->inter % 128)
+    return set_err(h, FM_EUNSUPPORTED, "hidden and moe_intermediate_size must be multiples of 128");
+  if ((c->hidden / c->group_size) % 2 || (c->inter / c->group_size) % 2)
+    return set_err(h, FM_EUNSUPPORTED, "K / group_size must be even");
+  if (c->router_quantized || c->shared_gate_quantized)
+    return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
+  if (c->shared_inter < 0) return set_err(h, FM_EINVAL, "negative shared_inter");
+  if (c->shared_inter > 0) {
+    if (c->shared_inter % 128 || (c->shared_inter / c->group_size) % 2)
+      return set_err(h, FM_EUNSUPPORTED, "shared_expert_intermediate_size must be a multiple of 128");
+    if (!w->shared_gate.w || !w->shared_up.w || !w->shared_down.w || !w->shared_gate.scales ||
+        !w->shared_up.scales || !w->shared_down.scales || !w->shared_expert_gate_w)
+      return set_err(h, FM_EINVAL, "shared expert weights missing");
+  }
+  if (!w->router_w || !w->gate.w || !w->up.w || !w->down.w || !w->gate.scales || !w->up.scales ||
+      !w->down.scales)
+    return set_err(h, FM_EINVAL, "expert weights missing");
+  return FM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fm_status_string(int s) {
+  switch (s) {
+    case FM_OK: return "ok";
+    case FM_EINVAL: return "invalid argument";
+    case FM_EUNSUPPORTED: return "unsupported";
+    case FM_ECUDA: return "cuda error";
+    case FM_ENCCL: return "transport error";
+    case FM_ETIMEOUT: return "device wait timed out";
+    case FM_EDEVICE: return "device-side check failed";
+    case FM_ENOMEM: return "out of device memory";
+    default: return "unknown status";
+  }
+}
+
+int fm_create(fm_handle** out, int device, void* stream) {
+  if (!out) return FM_EINVAL;
+  *out = nullptr;
+  fm_handle* h = new (std::nothrow) fm_handle();
+  if (!h) return FM_ENOMEM;
+  h->device = device;
+  h->stream = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSetDevice(device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&h->num_sms, cudaDevAttrMultiProcessorCount, device);
+  int cc_major = 0, cc_minor = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e == cudaSuccess && !(cc_major == 10 && cc_minor == 0)) {
+    delete h;
+    return FM_EUNSUPPORTED;  // built for sm_100a only
+  }
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
+  if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&h->gemv_blocks_per_sm);
+  if (e == cudaSuccess) e = fm::tc::init();
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    delete h;
+    return FM_ECUDA;
+  }
+  h->gemv_blocks_per_sm = std::min(h->gemv_blocks_per_sm, 8);
+  const int rc = ensure_ws(h, kCtrlBytes);
+  if (rc != FM_OK) {
+    delete h;
+    return rc;
+  }
+  *out = h;
+  return FM_OK;
+}
+
+int fm_destroy(fm_handle* h) {
+  if (!h) return FM_EINVAL;
+  cudaStreamSynchronize(h->stream);
+  for (auto& p : h->pending) {
+    cudaEventDestroy(p.a);
+    cudaEventDestroy(p.b);
+  }
+  for (auto e : h->event_pool) cudaEventDestroy(e);
+  if (h->ws) cudaFree(h->ws);
+  delete h;
+  return FM_OK;
+}
+
+int fm_set_stream(fm_handle* h, void* stream) {
+  if (!h) return FM_EINVAL;
+  h->stream = static_cast<cudaStream_t>(stream);
+  return FM_OK;
+}
+
+const char* fm_last_error(const fm_handle* h) { return h ? h->last_error.c_str() : "null handle"; }
+
+int fm_set_path(fm_handle* h, int path) {
+  if (!h) return FM_EINVAL;
+  if (path != FM_PATH_AUTO && path != FM_PATH_GEMV && path != FM_PATH_TCGEN05)
+    return set_err(h, FM_EINVAL, "unknown path");
+  h->path = path;
+  return FM_OK;
+}
+
+size_t fm_workspace_bytes(const fm_handle* h) { return h ? h->ws_bytes : 0; }
+
+int fm_profile_enable(fm_handle* h, int on) {
+  if (!h) return FM_EINVAL;
+  h->profile = on != 0;
+  return FM_OK;
+}
+
+int fm_profile_report(fm_handle* h, fm_kernel_time* out, int capacity, int* count, int reset) {
+  if (!h || (capacity > 0 && !out)) return FM_EINVAL;
+  for (auto& p : h->pending) {
+    float ms = 0.f;
+    cudaError_t e = cudaEventSynchronize(p.b);
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, p.a, p.b);
+    if (e != cudaSuccess) return cuda_err(h, e, "kernel timing event");
+    auto it = h->totals.find(p.name);
+    if (it == h->totals.end()) it = h->totals.emplace(p.name, fm_handle::Total{p.name, 0, 0.0}).first;
+    it->second.launches += 1;
+    it->second.ms += ms;
+    h->event_pool.push_back(p.a);
+    h->event_pool.push_back(p.b);
+  }
+  h->pending.clear();
+  int n = 0;
+  for (auto& kv : h->totals) {
+    if (n < capacity) {
+      out[n].name = kv.second.name;
+      out[n].launches = kv.second.launches;
+      out[n].total_ms = kv.second.ms;
+    }
+    ++n;
+  }
+  if (count) *count = n;
+  if (reset) h->totals.clear();
+  return FM_OK;
+}
+
+int fm_sync_status(fm_handle* h) {
+  if (!h) return FM_EINVAL;
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaStreamSynchronize");
+  uint32_t word = 0;
+  e = cudaMemcpy(&word, h->ws, sizeof(word), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaMemcpy(error word)");
+  if (word == 0) return FM_OK;
+  cudaMemset(h->ws, 0, kCtrlBytes);  // clear the error word and the grid-sync counters
+  if (word & fm::DEVERR_TIMEOUT) return set_err(h, FM_ETIMEOUT, "a bounded device-side wait ran out");
+  if (word & fm::DEVERR_BOUNDS) return set_err(h, FM_EDEVICE, "an index failed its device-side bounds check");
+  return set_err(h, FM_EDEVICE, "device-side check failed");
+}
+
+int fm_reserve(fm_handle* h, const fm_moe_config* c, int64_t max_tokens) {
+  if (!h || !c || max_tokens < 0) return FM_EINVAL;
+  const int epad = (c->num_experts + 1 + 7) / 8 * 8;
+  const int ksplit = router_ksplit(h, max_tokens, c->hidden);
+  Plan p = make_plan(max_tokens, max_tokens, c->hidden, c->num_experts, c->top_k, epad, 16, c->inter,
+                     c->shared_inter, c->shared_inter > 0, true);
+  (void)ksplit;
+  return ensure_ws(h, p.total);
+}
+
+int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
+                 uint16_t* y, const fm_moe_outputs* outs) {
+  if (!h) return FM_EINVAL;
+  int rc = check_moe(h, c, w);
+  if (rc) return rc;
+  if (T < 0 || (T > 0 && (!x || !y))) return set_err(h, FM_EINVAL, "bad x / y / T");
+  if (T == 0) return FM_OK;
+  if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
+  const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k;
+  const bool shared = c->shared_inter > 0;
+  const int epad = (E + 1 + 7) / 8 * 8;
+  const int ksplit = router_ksplit(h, T, H);
+  const int64_t P = T * k;
+  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true);
+  rc = ensure_ws(h, p.total);
+  if (rc) return rc;
+  const bool tcp = use_tc(h, P, E);
+
+  RouteArgs ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.x = x;
+  ra.router_w = static_cast<const uint16_t*>(w->router_w);
+  ra.shared_gate_w = shared ? static_cast<const uint16_t*>(w->shared_expert_gate_w) : nullptr;
+  ra.router_bias = w->router_bias;
+  ra.T = T;
+  ra.H = H;
+  ra.E = E;
+  ra.k = k;
+  ra.norm_topk = c->norm_topk_prob;
+  ra.do_router = 1;
+  ra.ksplit = ksplit;
+  ra.epad = epad;
+  ra.partial = at<float>(h, p.partial);
+  ra.x_perm = at<uint16_t>(h, p.x_perm);
+  ra.x_rows = T;
+  ra.zero0 = at<float>(h, p.y_acc);
+  ra.zero0_n = T * H;
+  ra.zero1 = shared ? at<float>(h, p.ysh) : nullptr;
+  ra.zero1_n = shared ? T * H : 0;
+  ra.topk_ids = at<int32_t>(h, p.topk_ids);
+  ra.topk_score = at<float>(h, p.topk_score);
+  ra.gate_sig = at<float>(h, p.gate_sig);
+  ra.row_src = at<int32_t>(h, p.row_src);
+  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
+  ra.pair_rank = at<int32_t>(h, p.pair_rank);
+  ra.totals = at<int32_t>(h, p.totals);
+  ra.offsets = at<int32_t>(h, p.offsets);
+  ra.sorted_token = at<int32_t>(h, p.sorted_token);
+  ra.sorted_score = at<float>(h, p.sorted_score);
+  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.tab_a = at<TileTable>(h, p.tab_a);
+  ra.tab_b = at<TileTable>(h, p.tab_b);
+  ra.a_rows_per_block = 64;
+  ra.a_n = I;
+  ra.a_n_shared = c->shared_inter;
+  ra.b_n = H;
+  ra.chunk_max = tcp ? 256 : 32;
+  ra.chunk_align = tcp ? 16 : 8;
+  ra.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, I));
+  ra.has_shared = shared ? 1 : 0;
+  if (outs) {
+    ra.out_topk_ids = outs->topk_ids;
+    ra.out_topk_scores = outs->topk_scores;
+    ra.out_sorted_token = outs->sorted_token;
+    ra.out_offsets = outs->expert_offsets;
+  }
+  ra.gsync = grid_sync(h);
+  ra.err = err_word(h);
+  const int64_t items = ((T + 15) / 16) * ksplit;
+  rc = launch_route(h, ra, items);
+  if (rc) return rc;
+
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  ga.gs = c->group_size;
+  ga.err = err_word(h);
+  ga.sorted_token = ra.sorted_token;
+  ga.sorted_score = ra.sorted_score;
+  ga.sorted_flat = ra.sorted_flat;
+  // gate / up
+  ga.K = H;
+  ga.K_shared = H;
+  ga.N = I;
+  ga.N_shared = c->shared_inter;
+  ga.w0 = w->gate.w; ga.s0 = w->gate.scales; ga.b0 = w->gate.biases;
+  ga.w1 = w->up.w; ga.s1 = w->up.scales; ga.b1 = w->up.biases;
+  if (shared) {
+    ga.sw0 = w->shared_gate.w; ga.ss0 = w->shared_gate.scales; ga.sb0 = w->shared_gate.biases;
+    ga.sw1 = w->shared_up.w; ga.ss1 = w->shared_up.scales; ga.sb1 = w->shared_up.biases;
+  }
+  ga.act = ra.x_perm;
+  ga.act_shared = ra.x_perm;
+  ga.act_ld = H;
+  ga.act_shared_ld = H;
+  ga.out = at<uint16_t>(h, p.a_sorted);
+  ga.out_ld = I;
+  ga.out_shared = shared ? at<uint16_t>(h, p.a_shared) : nullptr;
+  ga.out_shared_ld = c->shared_inter;
+  ga.tab = ra.tab_a;
+  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp);
+  if (rc) return rc;
+  // down (+ combine)
+  GemmArgs gd = ga;
+  gd.K = I;
+  gd.K_shared = c->shared_inter;
+  gd.N = H;
+  gd.N_shared = H;
+  gd.w0 = w->down.w; gd.s0 = w->down.scales; gd.b0 = w->down.biases;
+  gd.w1 = nullptr; gd.s1 = nullptr; gd.b1 = nullptr;
+  if (shared) {
+    gd.sw0 = w->shared_down.w; gd.ss0 = w->shared_down.scales; gd.sb0 = w->shared_down.biases;
+  }
+  gd.sw1 = nullptr; gd.ss1 = nullptr; gd.sb1 = nullptr;
+  gd.act = ga.out;
+  gd.act_ld = I;
+  gd.act_shared = ga.out_shared;
+  gd.act_shared_ld = c->shared_inter;
+  gd.out = nullptr;
+  gd.out_shared = nullptr;
+  gd.y_acc = at<float>(h, p.y_acc);
+  gd.ysh = shared ? at<float>(h, p.ysh) : nullptr;
+  gd.y_ld = H;
+  gd.tab = ra.tab_b;
+  rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp);
+  if (rc) return rc;
+  // finalize: combine rounding + gated shared expert
+  const int64_t n4 = T * H / 4;
+  const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+  prof_begin(h, "finalize");
+  fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
+  prof_end(h);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "finalize launch");
+  return FM_OK;
+}
+
+int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int K, const uint32_t* w,
+                  const uint16_t* scales, const uint16_t* biases, int E, int N, const uint32_t* lhs_indices,
+                  const uint32_t* rhs_indices, int64_t B, int transpose, int group_size, int bits,
+                  int sorted_indices, uint16_t* out) {
+  (void)sorted_indices;  // a hint in MLX; the expert-major order is rebuilt either way
+  if (!h) return FM_EINVAL;
+  if (!transpose) return set_err(h, FM_EUNSUPPORTED, "transpose=false is not implemented");
+  if (!quant_ok(K, group_size, bits)) return set_err(h, FM_EUNSUPPORTED, "only 4-bit affine, group 32/64/128");
+  if (x_batches <= 0 || M <= 0 || E <= 0 || N <= 0 || B < 0) return set_err(h, FM_EINVAL, "bad sizes");
+  if (E > fm::kMaxExperts) return set_err(h, FM_EUNSUPPORTED, "more than 512 experts");
+  if (!lhs_indices && B % x_batches != 0) return set_err(h, FM_EINVAL, "x batch does not broadcast against rhs");
+  if (B == 0) return FM_OK;
+  if (!x || !w || !scales || !out || (!rhs_indices && E != 1)) return set_err(h, FM_EINVAL, "null pointer");
+  if (K % 64 || N % 16) return set_err(h, FM_EUNSUPPORTED, "K must be a multiple of 64 and N of 16");
+  const int64_t rows = B * M;
+  if (rows > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
+  bool tcp = use_tc(h, rows, E);
+  if (K % 128) tcp = true;                       // GEMV needs 128-wide K chunks
+  if ((K / group_size) % 2) tcp = false;         // tcgen05 path loads scale pairs
+  if (K % 128 && (K / group_size) % 2) return set_err(h, FM_EUNSUPPORTED, "K / group_size must be even");
+  Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false);
+  int rc = ensure_ws(h, p.total);
+  if (rc) return rc;
+
+  RouteArgs ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.x = x;
+  ra.T = rows;
+  ra.H = K;
+  ra.E = E;
+  ra.k = 1;
+  ra.do_router = 0;
+  ra.ksplit = 1;
+  ra.epad = 8;
+  ra.given_ids = rhs_indices;
+  ra.given_lhs = lhs_indices;
+  ra.x_batches = x_batches;
+  ra.batches = B;
+  ra.M = M;
+  ra.x_perm = at<uint16_t>(h, p.x_perm);
+  ra.x_rows = x_batches * M;
+  ra.topk_ids = at<int32_t>(h, p.topk_ids);
+  ra.topk_score = at<float>(h, p.topk_score);
+  ra.gate_sig = at<float>(h, p.gate_sig);
+  ra.row_src = at<int32_t>(h, p.row_src);
+  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
+  ra.pair_rank = at<int32_t>(h, p.pair_rank);
+  ra.totals = at<int32_t>(h, p.totals);
+  ra.offsets = at<int32_t>(h, p.offsets);
+  ra.sorted_token = at<int32_t>(h, p.sorted_token);
+  ra.sorted_score = at<float>(h, p.sorted_score);
+  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.tab_a = at<TileTable>(h, p.tab_a);
+  ra.tab_b = nullptr;
+  ra.a_rows_per_block = 128;
+  ra.a_n = N;
+  ra.a_n_shared = 0;
+  ra.chunk_max = tcp ? 256 : 32;
+  ra.chunk_align = tcp ? 16 : 8;
+  ra.b_ksplit_shared = 1;
+  ra.gsync = grid_sync(h);
+  ra.err = err_word(h);
+  const int64_t items = (ra.x_rows * (K / 8) + 255) / 256 * 8;
+  rc = launch_route(h, ra, items);
+  if (rc) return rc;
+
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  ga.K = K;
+  ga.K_shared = K;
+  ga.N = N;
+  ga.N_shared = N;
+  ga.gs = group_size;
+  ga.w0 = w; ga.s0 = scales; ga.b0 = biases;
+  ga.act = ra.x_perm;
+  ga.act_ld = K;
+  ga.sorted_token = ra.sorted_token;
+  ga.sorted_score = ra.sorted_score;
+  ga.sorted_flat = ra.sorted_flat;
+  ga.out = out;
+  ga.out_ld = N;
+  ga.tab = ra.tab_a;
+  ga.err = err_word(h);
+  return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp);
+}
+
+int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w,
+                        const uint16_t* scales, const uint16_t* biases, int N, int transpose, int group_size,
+                        int bits, uint16_t* out) {
+  if (!h) return FM_EINVAL;
+  if (M < 0) return set_err(h, FM_EINVAL, "negative M");
+  if (M == 0) return FM_OK;
+  if (M > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
+  // one expert, one batch of M rows: gather_qmm with E = 1 and no indices
+  return fm_gather_qmm(h, x, 1, static_cast<int>(M), K, w, scales, biases, 1, N, nullptr, nullptr, 1, transpose,
+                       group_size, bits, 1, out);
+}
+
+}  // extern "C"

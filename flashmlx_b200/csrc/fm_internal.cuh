@@ -1,0 +1,163 @@
+// fm_internal.cuh -- data structures shared by the libflashmoe kernels and host code.
+#pragma once
+
+#include <stdint.h>
+
+#include "fm_common.cuh"
+
+namespace fm {
+
+constexpr int kMaxExperts = 512;
+constexpr int kMaxGroups = kMaxExperts + 1;  // routed experts + the shared expert
+
+// One weight matrix set (an expert, or the shared expert) and the activation rows it
+// multiplies, cut into output-row blocks x token chunks x K splits.  Written on the
+// device by the routing kernel (the row counts are only known there).
+struct TileGroup {
+  int32_t expert;      // expert id, -1 = shared expert
+  int32_t row_begin;   // first activation row in the expert-major pair order
+  int32_t rows;        // activation rows of this group
+  int32_t chunk_rows;  // rows per token chunk
+  int32_t chunks;      // token chunks
+  int32_t nblocks;     // output-row blocks
+  int32_t ksplit;      // K splits (GEMV path only; partial sums are added atomically)
+  int32_t tile_begin;  // first tile id of the group
+};
+
+struct TileTable {
+  int32_t num_groups;
+  int32_t num_tiles;
+  int32_t pad[6];
+  TileGroup g[kMaxGroups];
+};
+
+struct TileInfo {
+  int group;
+  int expert;  // -1 shared
+  int rb;      // output-row block
+  int ks;      // K split index
+  int ksplit;
+  int row0;    // first activation row of the chunk
+  int nrows;   // activation rows in the chunk
+};
+
+FM_DEV TileInfo decode_tile(const TileTable* tab, int tile) {
+  int lo = 0, hi = tab->num_groups - 1;
+  while (lo < hi) {  // largest group with tile_begin <= tile
+    const int mid = (lo + hi + 1) >> 1;
+    if (tab->g[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
+  }
+  const TileGroup G = tab->g[lo];
+  int local = tile - G.tile_begin;
+  TileInfo t;
+  t.group = lo;
+  t.expert = G.expert;
+  t.ksplit = G.ksplit;
+  t.ks = local % G.ksplit;
+  local /= G.ksplit;
+  const int ch = local % G.chunks;
+  t.rb = local / G.chunks;
+  t.row0 = G.row_begin + ch * G.chunk_rows;
+  t.nrows = min(G.chunk_rows, G.rows - ch * G.chunk_rows);
+  return t;
+}
+
+enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
+
+// Arguments of the expert-product kernels (GEMV and tcgen05 paths).
+struct GemmArgs {
+  int K;          // reduction length of routed matrices (H for gate/up, I for down)
+  int K_shared;   // reduction length of the shared matrices
+  int N;          // output rows of a routed matrix (I for gate/up, H for down)
+  int N_shared;   // output rows of a shared matrix
+  int gs;         // quantization group size
+  int pad0;
+  // routed matrices, stacked [E, N, K/8]; gate/up mode: 0 = gate, 1 = up
+  const uint32_t* w0; const uint16_t* s0; const uint16_t* b0;
+  const uint32_t* w1; const uint16_t* s1; const uint16_t* b1;
+  // shared-expert matrices [N_shared, K_shared/8]
+  const uint32_t* sw0; const uint16_t* ss0; const uint16_t* sb0;
+  const uint32_t* sw1; const uint16_t* ss1; const uint16_t* sb1;
+  // activation rows (B operand), stored with the within-8 pair permutation
+  const uint16_t* act;         // routed rows: x_perm (gate/up, plain) or a_sorted (down)
+  const uint16_t* act_shared;  // shared rows: x_perm (gate/up) or a_shared (down)
+  int64_t act_ld;
+  int64_t act_shared_ld;
+  // pair metadata in expert-major order
+  const int32_t* sorted_token;  // token (gate/up, down) or source x row (plain)
+  const float* sorted_score;
+  const int32_t* sorted_flat;   // original pair / output row index
+  // outputs
+  uint16_t* out;          // gate/up: a_sorted [P, N]; plain: out [rows, N]
+  uint16_t* out_shared;   // gate/up: a_shared [T, N_shared]
+  int64_t out_ld;
+  int64_t out_shared_ld;
+  float* y_acc;           // down: [T, H] fp32, sum_k bf16(d*score)
+  float* ysh;             // down: [T, H] fp32 shared-expert sums
+  int64_t y_ld;
+  const TileTable* tab;
+  uint32_t* err;
+};
+
+// Arguments of the routing kernel.
+struct RouteArgs {
+  // router mode inputs
+  const uint16_t* x;            // [rows, H] bf16
+  const uint16_t* router_w;     // [E, H] bf16
+  const uint16_t* shared_gate_w;  // [1, H] bf16 or NULL
+  const uint16_t* router_bias;  // [E] bf16 or NULL
+  int64_t T;                    // tokens (router mode) / rows (given mode)
+  int H;                        // row length of x
+  int E;
+  int k;
+  int norm_topk;
+  int do_router;                // 1: router + top-k; 0: experts given
+  int ksplit;                   // router K slices (phase 1)
+  int epad;                     // padded logit width (multiple of 8, >= E + has shared gate)
+  // given mode (gather_qmm / quantized_matmul)
+  const uint32_t* given_ids;    // expert of batch b (NULL: all expert 0)
+  const uint32_t* given_lhs;    // x batch of batch b (NULL: broadcast)
+  int64_t x_batches;
+  int64_t batches;              // B
+  int M;                        // rows per batch
+  // workspace
+  float* partial;               // [ksplit, T, epad]
+  uint16_t* x_perm;             // [x_rows, H]
+  int64_t x_rows;               // rows of x to permute
+  float* zero0; int64_t zero0_n;  // buffers cleared in phase 1 (fp32 counts)
+  float* zero1; int64_t zero1_n;
+  int32_t* topk_ids;            // [T, k]
+  float* topk_score;            // [T, k]
+  float* gate_sig;              // [T]
+  int32_t* row_src;             // [T] source x row (given mode)
+  int32_t* chunk_counts;        // [nchunks, E]
+  int32_t* pair_rank;           // [T, k]
+  int32_t* totals;              // [E]
+  int32_t* offsets;             // [E + 1]
+  int32_t* sorted_token;        // [T*k]
+  float* sorted_score;          // [T*k]
+  int32_t* sorted_flat;         // [T*k]
+  // tile tables
+  TileTable* tab_a;             // gate/up (or plain)
+  TileTable* tab_b;             // down (NULL in plain mode)
+  int a_rows_per_block;         // 64 gate/up, 128 plain
+  int a_n;                      // routed output rows of table a
+  int a_n_shared;               // shared output rows of table a (0 = no shared group)
+  int b_n;                      // output rows of table b (H)
+  int chunk_max;                // token rows per chunk cap (32 GEMV, 256 tcgen05)
+  int chunk_align;              // chunk size granularity (8 GEMV, 16 tcgen05)
+  int b_ksplit_shared;          // K splits of the shared down group (GEMV)
+  int has_shared;
+  // user-visible outputs (nullable)
+  int32_t* out_topk_ids;
+  uint16_t* out_topk_scores;
+  int32_t* out_sorted_token;
+  int32_t* out_offsets;
+  GridSync* gsync;
+  uint32_t* err;
+};
+
+constexpr int kRouteThreads = 256;  // 8 warps
+constexpr int kRouteChunk = 64;     // tokens per counting chunk
+
+}  // namespace fm

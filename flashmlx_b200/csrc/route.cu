@@ -1,0 +1,434 @@
+// route.cu -- router, top-k, token/expert sort and tile planning in one cooperative kernel.
+//
+// Replaces the MLX op chain of LlamaModel::moe_block / switch_mlp up to the first
+// gather_qmm (model.cpp:757-775 and 682-700):
+//   matmul(x, Wr^T) -> softmax(precise) -> argpartition top-k -> take_along_axis
+//   -> argsort(flat ids) (stable) -> take(x, order / k)
+// and, in "given" mode, the index bookkeeping of a bare gather_qmm / quantized_matmul.
+//
+// Phases (grid barriers between them, every wait bounded):
+//   1  router partial logits (mma.sync over 16-token x 8-expert tiles, K split across
+//      warps), the pair-permuted copy x_perm of x, zeroing of the fp32 accumulators
+//   2  per token: bf16 logits, softmax, top-k (ties -> lower id), renorm, shared gate;
+//      per 64-token chunk: expert bitmasks -> chunk counts and stable in-chunk ranks
+//   3  per expert: exclusive scan of the chunk counts (stable order across chunks)
+//   4  expert offsets, tile tables for the expert-product kernels, scatter of the
+//      pairs into expert-major order
+#include "fm_internal.cuh"
+
+namespace fm {
+
+namespace {
+
+// within-8 pair permutation of one 16-byte chunk: [e0..e7] -> [e0,e4,e1,e5,e2,e6,e3,e7]
+FM_DEV uint4 perm_chunk(uint4 v) {
+  uint4 o;
+  o.x = __byte_perm(v.x, v.z, 0x5410);
+  o.y = __byte_perm(v.x, v.z, 0x7632);
+  o.z = __byte_perm(v.y, v.w, 0x5410);
+  o.w = __byte_perm(v.y, v.w, 0x7632);
+  return o;
+}
+
+FM_DEV uint4 ldg_v4(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+FM_DEV float warp_sum_bfly(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+FM_DEV float warp_max(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  return v;
+}
+
+// exclusive scan of n ints in shared memory by the whole block; returns the total
+__device__ int block_exclusive_scan(int* a, int n, int* s_tmp /* >= 33 ints */) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int per = (n + nt - 1) / nt;
+  const int lo = min(n, tid * per), hi = min(n, lo + per);
+  int local = 0;
+  for (int i = lo; i < hi; ++i) local += a[i];
+  // inclusive warp scan
+  const int lane = tid & 31, warp = tid >> 5;
+  int v = local;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    int u = __shfl_up_sync(0xffffffffu, v, off);
+    if (lane >= off) v += u;
+  }
+  if (lane == 31) s_tmp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = nt >> 5;
+    int w = (lane < nw) ? s_tmp[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += u;
+    }
+    if (lane < nw) s_tmp[lane] = w;  // inclusive per warp
+    if (lane == nw - 1) s_tmp[32] = w;
+  }
+  __syncthreads();
+  int run = v - local + (warp > 0 ? s_tmp[warp - 1] : 0);
+  for (int i = lo; i < hi; ++i) {
+    const int x = a[i];
+    a[i] = run;
+    run += x;
+  }
+  const int total = s_tmp[32];
+  __syncthreads();
+  return total;
+}
+
+struct RouteSmem {
+  uint32_t mask[kMaxExperts][2];  // token bitmask of the current chunk, per expert
+  int offs[kMaxExperts + 1];
+  int cnt_a[kMaxGroups + 1];
+  int cnt_b[kMaxGroups + 1];
+  int tmp[40];
+  int flag;
+};
+
+// ------------------------------------------------------------------ phase 1
+__device__ void phase_router(const RouteArgs& a) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int gw = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
+  const int nw = gridDim.x * (kRouteThreads / 32);
+  const int64_t T = a.T;
+  const int H = a.H;
+  const int ntt = static_cast<int>((T + 15) / 16);
+  const int kblocks = H / 32;
+  const int items = ntt * a.ksplit;
+  const int ngroups = (a.epad + 63) / 64;
+  const int Etot = a.E + (a.shared_gate_w ? 1 : 0);
+  for (int item = gw; item < items; item += nw) {
+    const int tt = item / a.ksplit, ks = item % a.ksplit;
+    const int64_t t0 = static_cast<int64_t>(tt) * 16;
+    const int kb0 = kblocks * ks / a.ksplit, kb1 = kblocks * (ks + 1) / a.ksplit;
+    const int64_t ta = t0 + g, tb = t0 + g + 8;
+    const uint16_t* xa = (ta < T) ? a.x + ta * H : nullptr;
+    const uint16_t* xb = (tb < T) ? a.x + tb * H : nullptr;
+    for (int eg = 0; eg < ngroups; ++eg) {
+      float acc[8][4];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      const uint16_t* wr[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = eg * 64 + 8 * j + g;
+        wr[j] = (e < a.E) ? a.router_w + static_cast<int64_t>(e) * H : (e == a.E ? a.shared_gate_w : nullptr);
+      }
+      for (int kb = kb0; kb < kb1; ++kb) {
+        const int koff = kb * 32 + 8 * c;
+        const uint4 z = make_uint4(0, 0, 0, 0);
+        const uint4 va = xa ? ldg_v4(xa + koff) : z;
+        const uint4 vb = xb ? ldg_v4(xb + koff) : z;
+        if (eg == 0) {
+          if (xa) *reinterpret_cast<uint4*>(a.x_perm + ta * H + koff) = perm_chunk(va);
+          if (xb) *reinterpret_cast<uint4*>(a.x_perm + tb * H + koff) = perm_chunk(vb);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 w = wr[j] ? ldg_v4(wr[j] + koff) : z;
+          mma_bf16_16816(acc[j], va.x, vb.x, va.y, vb.y, w.x, w.y);
+          mma_bf16_16816(acc[j], va.z, vb.z, va.w, vb.w, w.z, w.w);
+        }
+      }
+      float* part = a.partial + static_cast<int64_t>(ks) * T * a.epad;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = eg * 64 + 8 * j + 2 * c;
+        if (e < a.epad) {
+          if (ta < T) *reinterpret_cast<float2*>(part + ta * a.epad + e) = make_float2(acc[j][0], acc[j][1]);
+          if (tb < T) *reinterpret_cast<float2*>(part + tb * a.epad + e) = make_float2(acc[j][2], acc[j][3]);
+        }
+      }
+    }
+  }
+  (void)Etot;
+}
+
+__device__ void phase_permute_x(const RouteArgs& a) {
+  const int64_t chunks_per_row = a.H / 8;
+  const int64_t n = a.x_rows * chunks_per_row;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = ldg_v4(a.x + i * 8);
+    *reinterpret_cast<uint4*>(a.x_perm + i * 8) = perm_chunk(v);
+  }
+}
+
+__device__ void phase_zero(float* p, int64_t n) {
+  if (!p) return;
+  const int64_t n4 = n / 4;
+  float4* p4 = reinterpret_cast<float4*>(p);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p4[i] = z;
+  for (int64_t i = n4 * 4 + static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    p[i] = 0.f;
+}
+
+// ------------------------------------------------------------------ phase 2
+__device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl) {
+  const int lane = threadIdx.x & 31;
+  const int E = a.E, k = a.k;
+  constexpr int PER = kMaxExperts / 32;
+  float p[PER];
+  // bf16 logits: fixed-order sum of the K-split partials, then the optional bias
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = -INFINITY;
+    if (e < E) {
+      float s = 0.f;
+      for (int ks = 0; ks < a.ksplit; ++ks) s += a.partial[(static_cast<int64_t>(ks) * a.T + t) * a.epad + e];
+      float l = rbf(s);
+      if (a.router_bias) l = rbf(l + bf2f(a.router_bias[e]));
+      p[i] = l;
+      mx = fmaxf(mx, l);
+    } else if (e == E && a.shared_gate_w) {
+      float s = 0.f;
+      for (int ks = 0; ks < a.ksplit; ++ks) s += a.partial[(static_cast<int64_t>(ks) * a.T + t) * a.epad + e];
+      a.gate_sig[t] = rbf(sigmoid_f(rbf(s)));
+    }
+  }
+  mx = warp_max(mx);
+  // softmax(precise): fp32 exp; sum = lane-strided partial sums then xor butterfly
+  float part = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E) {
+      p[i] = expf(p[i] - mx);
+      part += p[i];
+    }
+  }
+  const float sum = warp_sum_bfly(part);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = (e < E) ? rbf(p[i] / sum) : -INFINITY;
+  }
+  // top-k: k rounds of warp argmax, ties toward the lower expert id.  NaN scores (bad
+  // input) rank lowest, and every round still returns a distinct valid id.
+  float sel_p[16];
+  int sel_e[16];
+  uint32_t taken = 0u;
+  for (int j = 0; j < k; ++j) {
+    float bv = -INFINITY;
+    int be = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e >= E || ((taken >> i) & 1u)) continue;
+      const float v = isnan(p[i]) ? -INFINITY : p[i];
+      if (v > bv || be == 0x7fffffff) {  // ascending e per lane: strict > keeps the lower id
+        bv = v;
+        be = e;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
+      if (ov > bv || (ov == bv && oe < be)) {
+        bv = ov;
+        be = oe;
+      }
+    }
+    sel_p[j] = bv;
+    sel_e[j] = be;
+    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+  }
+  float denom = 1.f;
+  if (a.norm_topk) {
+    float s = 0.f;
+    for (int j = 0; j < k; ++j) s += sel_p[j];
+    denom = rbf(s);
+  }
+  if (lane < k) {
+    float sp = 0.f;
+    int se = 0;
+    for (int j = 0; j < k; ++j)
+      if (j == lane) { sp = sel_p[j]; se = sel_e[j]; }
+    const float sc = a.norm_topk ? rbf(sp / denom) : sp;
+    a.topk_ids[t * k + lane] = se;
+    a.topk_score[t * k + lane] = sc;
+    if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
+    if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
+    atomicOr(&sm.mask[se][tl >> 5], 1u << (tl & 31));
+  }
+}
+
+__device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) {
+  if ((threadIdx.x & 31) != 0) return;
+  const int64_t b = r / a.M, m = r % a.M;
+  uint32_t e = a.given_ids ? a.given_ids[b] : 0u;
+  int64_t xb = a.given_lhs ? static_cast<int64_t>(a.given_lhs[b]) : b * a.x_batches / a.batches;
+  if (e >= static_cast<uint32_t>(a.E) || xb < 0 || xb >= a.x_batches) {
+    report(a.err, DEVERR_BOUNDS);
+    a.topk_ids[r] = -1;
+    return;
+  }
+  a.topk_ids[r] = static_cast<int32_t>(e);
+  a.topk_score[r] = 1.f;
+  a.row_src[r] = static_cast<int32_t>(xb * a.M + m);
+  atomicOr(&sm.mask[e][tl >> 5], 1u << (tl & 31));
+}
+
+__device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
+  const int warp = threadIdx.x >> 5;
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  const int k = a.do_router ? a.k : 1;
+  for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e][0] = sm.mask[e][1] = 0u;
+    __syncthreads();
+    for (int i = 0; i < kRouteChunk / 8; ++i) {
+      const int tl = warp * (kRouteChunk / 8) + i;
+      const int64_t t = static_cast<int64_t>(ch) * kRouteChunk + tl;
+      if (t >= a.T) break;
+      if (a.do_router) route_token(a, t, sm, tl);
+      else given_row(a, t, sm, tl);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x)
+      a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] = __popc(sm.mask[e][0]) + __popc(sm.mask[e][1]);
+    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
+    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
+    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
+      const int tl = i / k;
+      const int e = a.topk_ids[(t0 + tl) * k + (i % k)];
+      if (e < 0) continue;
+      const uint32_t m0 = sm.mask[e][0], m1 = sm.mask[e][1];
+      int rank;
+      if (tl < 32) rank = __popc(m0 & ((1u << tl) - 1u));
+      else rank = __popc(m0) + __popc(m1 & ((1u << (tl - 32)) - 1u));
+      a.pair_rank[(t0 + tl) * k + (i % k)] = rank;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ phase 3
+__device__ void phase_column_scan(const RouteArgs& a, RouteSmem& sm) {
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  int* buf = sm.cnt_a;  // reuse as scratch (kMaxGroups+1 >= 513 ints per pass)
+  const int cap = kMaxGroups;
+  for (int e = blockIdx.x; e < a.E; e += gridDim.x) {
+    int carry = 0;
+    for (int c0 = 0; c0 < nchunks; c0 += cap) {
+      const int n = min(cap, nchunks - c0);
+      for (int i = threadIdx.x; i < n; i += blockDim.x)
+        buf[i] = a.chunk_counts[static_cast<int64_t>(c0 + i) * a.E + e];
+      __syncthreads();
+      const int tot = block_exclusive_scan(buf, n, sm.tmp);
+      for (int i = threadIdx.x; i < n; i += blockDim.x)
+        a.chunk_counts[static_cast<int64_t>(c0 + i) * a.E + e] = buf[i] + carry;
+      carry += tot;
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) a.totals[e] = carry;
+  }
+}
+
+// ------------------------------------------------------------------ phase 4
+__device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, int rows_per_block, int n_routed,
+                            int n_shared, int ksplit_shared, int* cnt) {
+  const int has_sh = (n_shared > 0) ? 1 : 0;
+  const int ng = a.E + has_sh;
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) {
+    TileGroup G;
+    const bool sh = has_sh && gi == 0;
+    const int e = sh ? -1 : gi - has_sh;
+    G.expert = e;
+    G.row_begin = sh ? 0 : sm.offs[e];
+    G.rows = sh ? static_cast<int>(a.T) : (sm.offs[e + 1] - sm.offs[e]);
+    const int n = sh ? n_shared : n_routed;
+    G.nblocks = (n + rows_per_block - 1) / rows_per_block;
+    G.ksplit = sh ? ksplit_shared : 1;
+    if (G.rows > 0) {
+      const int c0 = (G.rows + a.chunk_max - 1) / a.chunk_max;
+      int cr = (G.rows + c0 - 1) / c0;
+      cr = (cr + a.chunk_align - 1) / a.chunk_align * a.chunk_align;
+      G.chunk_rows = cr;
+      G.chunks = (G.rows + cr - 1) / cr;
+    } else {
+      G.chunk_rows = a.chunk_align;
+      G.chunks = 0;
+    }
+    tab->g[gi] = G;
+    cnt[gi] = G.nblocks * G.chunks * G.ksplit;
+  }
+  __syncthreads();
+  const int total = block_exclusive_scan(cnt, ng, sm.tmp);
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) tab->g[gi].tile_begin = cnt[gi];
+  if (threadIdx.x == 0) {
+    tab->num_groups = ng;
+    tab->num_tiles = total;
+  }
+}
+
+__device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.offs[e] = a.totals[e];
+  __syncthreads();
+  const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
+  if (threadIdx.x == 0) sm.offs[a.E] = P;
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
+      a.offsets[e] = sm.offs[e];
+      if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
+    }
+    plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
+    if (a.tab_b) plan_groups(a, sm, a.tab_b, 128, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
+  }
+  const int k = a.do_router ? a.k : 1;
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
+    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
+    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
+      const int64_t flat = t0 * k + i;
+      const int e = a.topk_ids[flat];
+      if (e < 0) continue;
+      const int pos = sm.offs[e] + a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] + a.pair_rank[flat];
+      const int64_t t = flat / k;
+      a.sorted_token[pos] = a.do_router ? static_cast<int32_t>(t) : a.row_src[t];
+      a.sorted_score[pos] = a.topk_score[flat];
+      a.sorted_flat[pos] = static_cast<int32_t>(flat);
+      if (a.out_sorted_token) a.out_sorted_token[pos] = static_cast<int32_t>(t);
+    }
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  const unsigned nb = gridDim.x;
+  // phase 1
+  if (a.do_router) phase_router(a);
+  else phase_permute_x(a);
+  phase_zero(a.zero0, a.zero0_n);
+  phase_zero(a.zero1, a.zero1_n);
+  if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  // phase 2
+  phase_topk_count(a, sm);
+  if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  // phase 3
+  phase_column_scan(a, sm);
+  if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  // phase 4
+  phase_scatter(a, sm);
+}
+
+}  // namespace fm

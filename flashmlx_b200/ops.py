@@ -1,0 +1,305 @@
+"""Python mirror of the reference's operator calls, running on libflashmoe.
+
+Same names, argument meaning and error behaviour as the MLX calls the reference makes
+(server/src/model.cpp):
+
+    quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4)
+        <- mx::quantized_matmul                                   model.cpp:476-480
+    gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices, transpose=True,
+               group_size=64, bits=4, sorted_indices=False)
+        <- mx::gather_qmm                                         model.cpp:703-721
+    MoEBlock(config, weights)(x)
+        <- LlamaModel::moe_block                                  model.cpp:750-807
+
+Tensors are torch CUDA tensors used only as device buffers: bf16 activations,
+uint32 (or int32) packed weights, bf16 scales / biases.  Work is queued on torch's
+current stream.  Unsupported arguments raise ValueError / NotImplementedError before
+any launch, like MLX's argument checks; device-side failures raise FlashMoEError at
+the next `synchronize()`.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._lib import FlashMoEError, MoEConfig, MoEOutputs, MoEWeights, QWeight
+
+__all__ = ["Handle", "default_handle", "quantized_matmul", "gather_qmm", "MoEConfig", "MoEWeightsT", "MoEBlock",
+           "FlashMoEError", "synchronize", "bf16_from_numpy", "u32_from_numpy", "bf16_to_numpy"]
+
+_tls = threading.local()
+
+
+class Handle:
+    """One libflashmoe handle (device workspace + stream binding)."""
+
+    def __init__(self, device: int | None = None):
+        self.lib = _lib.load()
+        if device is None:
+            device = torch.cuda.current_device()
+        self.device = device
+        h = C.c_void_p()
+        with torch.cuda.device(device):
+            st = self.lib.fm_create(C.byref(h), device, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if st != _lib.FM_OK:
+            raise FlashMoEError(st, "fm_create failed: " + self.lib.fm_status_string(st).decode())
+        self.h = h
+
+    def close(self):
+        if self.h:
+            self.lib.fm_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def check(self, st: int):
+        if st != _lib.FM_OK:
+            raise FlashMoEError(st, self.lib.fm_last_error(self.h).decode())
+
+    def bind_stream(self, stream: torch.cuda.Stream | None = None):
+        s = stream if stream is not None else torch.cuda.current_stream(self.device)
+        self.check(self.lib.fm_set_stream(self.h, C.c_void_p(s.cuda_stream)))
+
+    def set_path(self, path: int):
+        self.check(self.lib.fm_set_path(self.h, path))
+
+    def sync(self):
+        self.check(self.lib.fm_sync_status(self.h))
+
+    def workspace_bytes(self) -> int:
+        return int(self.lib.fm_workspace_bytes(self.h))
+
+    def profile(self, on: bool = True):
+        self.check(self.lib.fm_profile_enable(self.h, int(on)))
+
+    def profile_report(self, reset: bool = True) -> dict:
+        """{kernel name: (launches, total device ms)} since the last reset."""
+        buf = (_lib.KernelTime * 32)()
+        n = C.c_int(0)
+        self.check(self.lib.fm_profile_report(self.h, buf, 32, C.byref(n), int(reset)))
+        return {buf[i].name.decode(): (int(buf[i].launches), float(buf[i].total_ms)) for i in range(min(n.value, 32))}
+
+
+def default_handle(device: int | None = None) -> Handle:
+    if device is None:
+        device = torch.cuda.current_device()
+    hs = getattr(_tls, "handles", None)
+    if hs is None:
+        hs = _tls.handles = {}
+    if device not in hs:
+        hs[device] = Handle(device)
+    return hs[device]
+
+
+def synchronize(device: int | None = None):
+    default_handle(device).sync()
+
+
+def bf16_from_numpy(a, device="cuda") -> torch.Tensor:
+    """bf16 bit patterns (numpy uint16) -> torch bf16 tensor on `device`."""
+    import numpy as np
+    return torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).to(device).view(torch.bfloat16)
+
+
+def u32_from_numpy(a, device="cuda") -> torch.Tensor:
+    """packed uint32 words (numpy) -> torch int32 tensor with the same bits on `device`."""
+    import numpy as np
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint32).view(np.int32)).to(device)
+
+
+def bf16_to_numpy(t: torch.Tensor):
+    import numpy as np
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _need(t, name, dtypes, device):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch tensor")
+    if t.device.type != "cuda" or (device is not None and t.device != device):
+        raise ValueError(f"{name} must live on {device}")
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name} has dtype {t.dtype}, expected one of {dtypes}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+_U32 = (torch.uint32, torch.int32)
+
+
+def quantized_matmul(x, w, scales, biases=None, transpose=True, group_size=64, bits=4, handle=None):
+    """x [..., K] bf16 @ dequant(w)^T -> [..., N] bf16 (mx::quantized_matmul, transpose=True)."""
+    if not transpose:
+        raise NotImplementedError("transpose=False is not implemented")
+    _need(x, "x", (torch.bfloat16,), None)
+    dev = x.device
+    _need(w, "w", _U32, dev)
+    _need(scales, "scales", (torch.bfloat16,), dev)
+    if biases is not None:
+        _need(biases, "biases", (torch.bfloat16,), dev)
+    K = x.shape[-1]
+    if w.dim() != 2 or w.shape[1] * 32 // bits != K:
+        raise ValueError(f"w of shape {tuple(w.shape)} does not match K={K} at {bits} bits")
+    N = w.shape[0]
+    if scales.shape != (N, K // group_size) or (biases is not None and biases.shape != scales.shape):
+        raise ValueError("scales / biases shape mismatch")
+    M = x.numel() // K
+    out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_quantized_matmul(h.h, _ptr(x), M, K, _ptr(w), _ptr(scales), _ptr(biases), N, int(transpose),
+                                      group_size, bits, _ptr(out)))
+    return out
+
+
+def gather_qmm(x, w, scales, biases=None, lhs_indices=None, rhs_indices=None, transpose=True, group_size=64,
+               bits=4, sorted_indices=False, handle=None):
+    """mx::gather_qmm: out[i] = x[lhs(i)] @ dequant(w[rhs[i]])^T, shape batch(idx) + [M, N]."""
+    if not transpose:
+        raise NotImplementedError("transpose=False is not implemented")
+    _need(x, "x", (torch.bfloat16,), None)
+    dev = x.device
+    _need(w, "w", _U32, dev)
+    _need(scales, "scales", (torch.bfloat16,), dev)
+    if biases is not None:
+        _need(biases, "biases", (torch.bfloat16,), dev)
+    if x.dim() < 2 or w.dim() != 3:
+        raise ValueError("x must be [..., M, K] and w [E, N, K*bits/32]")
+    M, K = x.shape[-2], x.shape[-1]
+    E, N = w.shape[0], w.shape[1]
+    if w.shape[2] * 32 // bits != K:
+        raise ValueError("w does not match K")
+    if rhs_indices is None:
+        raise ValueError("rhs_indices is required")
+    _need(rhs_indices, "rhs_indices", _U32, dev)
+    x_batch = tuple(x.shape[:-2])
+    xb = 1
+    for d in x_batch:
+        xb *= d
+    if lhs_indices is not None:
+        _need(lhs_indices, "lhs_indices", _U32, dev)
+        if lhs_indices.shape != rhs_indices.shape:
+            raise ValueError("lhs_indices and rhs_indices must have the same shape")
+        out_batch = tuple(rhs_indices.shape)
+    else:
+        out_batch = tuple(torch.broadcast_shapes(x_batch, tuple(rhs_indices.shape)))
+        if tuple(rhs_indices.shape) != out_batch:
+            raise NotImplementedError("rhs_indices must carry the full broadcast batch shape")
+        # x batch index i*xb/B is exact for x batch shapes that broadcast as a prefix
+        B = rhs_indices.numel()
+        if B % xb:
+            raise NotImplementedError("x batch does not broadcast as a prefix of the index batch")
+    B = rhs_indices.numel()
+    out = torch.empty(*out_batch, M, N, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_gather_qmm(h.h, _ptr(x), xb, M, K, _ptr(w), _ptr(scales), _ptr(biases), E, N,
+                                _ptr(lhs_indices), _ptr(rhs_indices), B, int(transpose), group_size, bits,
+                                int(sorted_indices), _ptr(out)))
+    return out
+
+
+@dataclass
+class MoEWeightsT:
+    """Stacked MoE-layer weights as torch CUDA tensors (MoEWeights, model.h:56-72)."""
+    router_w: torch.Tensor
+    gate: tuple
+    up: tuple
+    down: tuple
+    shared_gate: tuple | None = None
+    shared_up: tuple | None = None
+    shared_down: tuple | None = None
+    shared_expert_gate_w: torch.Tensor | None = None
+    router_bias: torch.Tensor | None = None
+
+    @staticmethod
+    def from_numpy(d: dict, device) -> "MoEWeightsT":
+        def bf(a):
+            return bf16_from_numpy(a, device)
+
+        def q(t):
+            w, s, b = t
+            return (u32_from_numpy(w, device), bf(s), bf(b) if b is not None else None)
+
+        return MoEWeightsT(
+            router_w=bf(d["router_w"]), gate=q(d["gate"]), up=q(d["up"]), down=q(d["down"]),
+            shared_gate=q(d["shared_gate"]) if "shared_gate" in d else None,
+            shared_up=q(d["shared_up"]) if "shared_up" in d else None,
+            shared_down=q(d["shared_down"]) if "shared_down" in d else None,
+            shared_expert_gate_w=bf(d["shared_expert_gate_w"]) if "shared_expert_gate_w" in d else None,
+            router_bias=bf(d["router_bias"]) if "router_bias" in d else None)
+
+
+def _qw(t):
+    if t is None:
+        return QWeight(None, None, None)
+    w, s, b = t
+    return QWeight(w.data_ptr(), s.data_ptr(), b.data_ptr() if b is not None else None)
+
+
+class MoEBlock:
+    """LlamaModel::moe_block on libflashmoe.  cfg: synthetic.MoEShape-like object."""
+
+    def __init__(self, shape, weights: MoEWeightsT, handle: Handle | None = None):
+        self.shape = shape
+        self.weights = weights
+        self.handle = handle
+        c = MoEConfig()
+        c.hidden, c.inter, c.num_experts, c.top_k = shape.hidden, shape.inter, shape.num_experts, shape.top_k
+        c.group_size, c.bits = shape.group_size, shape.bits
+        c.norm_topk_prob = int(shape.norm_topk_prob)
+        c.shared_inter = shape.shared_inter
+        c.router_quantized = 0
+        c.shared_gate_quantized = 0
+        self.cfg = c
+        W = MoEWeights()
+        W.router_w = weights.router_w.data_ptr()
+        W.gate, W.up, W.down = _qw(weights.gate), _qw(weights.up), _qw(weights.down)
+        W.shared_gate, W.shared_up, W.shared_down = (_qw(weights.shared_gate), _qw(weights.shared_up),
+                                                     _qw(weights.shared_down))
+        if weights.shared_expert_gate_w is not None:
+            W.shared_expert_gate_w = weights.shared_expert_gate_w.data_ptr()
+        if weights.router_bias is not None:
+            W.router_bias = weights.router_bias.data_ptr()
+        self.W = W
+
+    def _h(self, device):
+        return self.handle or default_handle(device.index)
+
+    def reserve(self, max_tokens: int, device=None):
+        h = self._h(device or self.weights.router_w.device)
+        h.check(h.lib.fm_reserve(h.h, C.byref(self.cfg), max_tokens))
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False):
+        _need(x, "x", (torch.bfloat16,), self.weights.router_w.device)
+        if x.shape[-1] != self.shape.hidden:
+            raise ValueError("x last dim must equal hidden size")
+        T = x.numel() // self.shape.hidden
+        y = out if out is not None else torch.empty_like(x)
+        outs = MoEOutputs()
+        routing = None
+        if return_routing:
+            k, E = self.shape.top_k, self.shape.num_experts
+            routing = {
+                "topk_ids": torch.empty(T, k, dtype=torch.int32, device=x.device),
+                "topk_scores": torch.empty(T, k, dtype=torch.bfloat16, device=x.device),
+                "sorted_token": torch.empty(T * k, dtype=torch.int32, device=x.device),
+                "expert_offsets": torch.empty(E + 1, dtype=torch.int32, device=x.device),
+            }
+            for n, t in routing.items():
+                setattr(outs, n, t.data_ptr())
+        h = self._h(x.device)
+        h.bind_stream()
+        h.check(h.lib.fm_moe_block(h.h, C.byref(self.cfg), C.byref(self.W), _ptr(x), T, _ptr(y), C.byref(outs)))
+        return (y, routing) if return_routing else y

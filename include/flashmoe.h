@@ -1,0 +1,176 @@
+/*
+ * flashmoe.h -- C ABI of libflashmoe, the B200 (sm_100a) MoE-block library.
+ *
+ * libflashmoe replaces, for FlashMLX's mixture-of-experts layers, the MLX operators
+ * the reference's model forward calls (server/src/model.cpp):
+ *
+ *   fm_quantized_matmul  <- mx::quantized_matmul(x, w, scales, biases, transpose=true,
+ *                           group_size, bits)        model.cpp:476-480, 531-535, 741-747
+ *   fm_gather_qmm        <- mx::gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices,
+ *                           transpose=true, group_size, bits, "affine", sorted_indices)
+ *                                                    model.cpp:703-721
+ *   fm_moe_block         <- LlamaModel::moe_block (router, softmax, top-k, switch_mlp,
+ *                           weighted combine, sigmoid-gated shared expert)
+ *                                                    model.cpp:750-807 (+673-748)
+ *
+ * Conventions
+ *   - bf16 tensors are passed as uint16_t bit patterns; all pointers are device
+ *     pointers unless stated otherwise; every tensor is dense row-major.
+ *   - Quantized weights use MLX's affine layout: w [.., N, K*bits/32] uint32 with
+ *     element j of a row at bits bits*(j % (32/bits)) of word j/(32/bits) (low first),
+ *     scales / biases [.., N, K/group_size] bf16, w_hat = scale * q + bias.
+ *   - Calls are asynchronous on the handle's stream.  They return a status for the
+ *     argument checks and launch; faults detected on the device (bounded waits that
+ *     ran out, failed bounds checks) surface at the next fm_sync_status().
+ *   - No C++ exception crosses this boundary.  The library never calls exit/abort.
+ *   - One handle per host thread / stream.  A handle owns a device workspace that
+ *     grows on demand; fm_reserve() sizes it up front so hot calls never allocate.
+ */
+#ifndef FLASHMOE_H_
+#define FLASHMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FM_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define FM_API __attribute__((visibility("default")))
+#else
+#define FM_API
+#endif
+
+typedef enum fm_status {
+  FM_OK = 0,
+  FM_EINVAL = 1,        /* bad argument (null pointer, negative size, index range) */
+  FM_EUNSUPPORTED = 2,  /* valid for MLX but not implemented here (bits, group size, shape) */
+  FM_ECUDA = 3,         /* a CUDA runtime call failed; fm_last_error() has the text */
+  FM_ENCCL = 4,         /* expert-parallel transport failure */
+  FM_ETIMEOUT = 5,      /* a bounded device-side wait ran out */
+  FM_EDEVICE = 6,       /* a kernel reported a failed device-side check */
+  FM_ENOMEM = 7         /* workspace allocation failed */
+} fm_status;
+
+typedef struct fm_handle fm_handle;
+
+/* One affine-quantized matrix (possibly stacked over experts). */
+typedef struct fm_qweight {
+  const uint32_t* w;       /* [.., N, K*bits/32] */
+  const uint16_t* scales;  /* [.., N, K/group_size] bf16 */
+  const uint16_t* biases;  /* [.., N, K/group_size] bf16, NULL = zero */
+} fm_qweight;
+
+/* ModelConfig's MoE fields (server/include/flashmlx/model.h:40-45) plus the
+ * quantization parameters (model.h:35-36). */
+typedef struct fm_moe_config {
+  int hidden;                /* H (hidden_size) */
+  int inter;                 /* I (moe_intermediate_size) */
+  int num_experts;           /* E */
+  int top_k;                 /* k (num_experts_per_tok) */
+  int group_size;            /* quant_group_size (64) */
+  int bits;                  /* quant_bits (4) */
+  int norm_topk_prob;        /* renormalise the k scores to sum 1 */
+  int shared_inter;          /* shared_expert_intermediate_size, 0 = no shared expert */
+  int router_quantized;      /* router weight quantized (model.cpp:757-760) */
+  int shared_gate_quantized; /* shared_expert_gate quantized (model.cpp:792-797) */
+} fm_moe_config;
+
+/* MoEWeights (model.h:56-72): stacked expert weights of one layer. */
+typedef struct fm_moe_weights {
+  const void* router_w;       /* [E, H] bf16, or [E, H*bits/32] uint32 when quantized */
+  const uint16_t* router_s;   /* quantized router only */
+  const uint16_t* router_b;
+  fm_qweight gate;            /* [E, I, H] */
+  fm_qweight up;              /* [E, I, H] */
+  fm_qweight down;            /* [E, H, I] */
+  fm_qweight shared_gate;     /* [Is, H] */
+  fm_qweight shared_up;       /* [Is, H] */
+  fm_qweight shared_down;     /* [H, Is] */
+  const void* shared_expert_gate_w; /* [1, H] bf16 (or packed when quantized) */
+  const uint16_t* shared_expert_gate_s;
+  const uint16_t* shared_expert_gate_b;
+  const uint16_t* router_bias; /* [E] bf16 added to the logits, NULL in the reference
+                                  model; used by the benchmark to skew expert load */
+} fm_moe_weights;
+
+/* Optional outputs of fm_moe_block (each pointer may be NULL). */
+typedef struct fm_moe_outputs {
+  int32_t* topk_ids;       /* [T, k] expert ids, descending score, ties -> lower id */
+  uint16_t* topk_scores;   /* [T, k] bf16 routing weights (after optional renorm) */
+  int32_t* sorted_token;   /* [T*k] token of each pair in stable expert-major order */
+  int32_t* expert_offsets; /* [E+1] start of each expert's segment in that order */
+} fm_moe_outputs;
+
+/* Handle lifecycle -------------------------------------------------------- */
+
+/* Creates a handle on `device`, issuing work on `stream` (a cudaStream_t, NULL =
+ * legacy default stream).  Replaces no reference interface: MLX binds its device
+ * and stream implicitly (mx::default_device / default_stream). */
+FM_API int fm_create(fm_handle** out, int device, void* stream);
+FM_API int fm_destroy(fm_handle* h);
+FM_API int fm_set_stream(fm_handle* h, void* stream);
+FM_API const char* fm_last_error(const fm_handle* h);
+FM_API const char* fm_status_string(int status);
+
+/* Synchronizes the stream and folds device-side error bits into a status.
+ * The MLX analogue is the sync at mx::eval (scheduler.cpp:204). */
+FM_API int fm_sync_status(fm_handle* h);
+
+/* Pre-sizes the workspace for fm_moe_block calls of up to max_tokens tokens. */
+FM_API int fm_reserve(fm_handle* h, const fm_moe_config* cfg, int64_t max_tokens);
+FM_API size_t fm_workspace_bytes(const fm_handle* h);
+
+/* Path selection for the expert products.  FM_PATH_AUTO picks the small-batch
+ * dequant-GEMV for few tokens per expert and the tcgen05 grouped GEMM otherwise. */
+enum { FM_PATH_AUTO = 0, FM_PATH_GEMV = 1, FM_PATH_TCGEN05 = 2 };
+FM_API int fm_set_path(fm_handle* h, int path);
+
+/* Kernel timing ------------------------------------------------------------------
+ * With profiling on, every kernel the handle launches is bracketed by CUDA events on
+ * the handle's stream; fm_profile_report() synchronizes and returns, per kernel
+ * name, the launch count and the summed device time since the last reset.  The
+ * reference's analogue is the ad-hoc std::chrono graph-build timers of
+ * model.cpp:1163-1259 / scheduler.cpp:532-658. */
+typedef struct fm_kernel_time {
+  const char* name;     /* static string, e.g. "qgemm_tc_gateup" */
+  int64_t launches;
+  double total_ms;
+} fm_kernel_time;
+FM_API int fm_profile_enable(fm_handle* h, int on);
+FM_API int fm_profile_report(fm_handle* h, fm_kernel_time* out, int capacity, int* count, int reset);
+
+/* Operators ------------------------------------------------------------------ */
+
+/* out[M, N] = x[M, K] @ w_hat^T.  Replaces mx::quantized_matmul with transpose=true
+ * (model.cpp:478-479, 509-511, 531-535, 741-747, 759-760, 793-796).
+ * transpose=0 returns FM_EUNSUPPORTED (the reference never calls it). */
+FM_API int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w,
+                        const uint16_t* scales, const uint16_t* biases, int N, int transpose,
+                        int group_size, int bits, uint16_t* out);
+
+/* out[B, M, N]: out[i] = x[lhs(i)] @ w_hat[rhs_indices[i]]^T, x [x_batches, M, K],
+ * w [E, N, K*bits/32].  lhs_indices == NULL broadcasts x against rhs: lhs(i) =
+ * i * x_batches / B (x [T,1,1,K] against rhs [T,k] gives lhs(i) = i / k).
+ * sorted_indices is MLX's hint that rhs is ascending (model.cpp:703-721); results
+ * do not depend on it.  Replaces mx::gather_qmm (model.cpp:703-721). */
+FM_API int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int K, const uint32_t* w,
+                  const uint16_t* scales, const uint16_t* biases, int E, int N,
+                  const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t B, int transpose,
+                  int group_size, int bits, int sorted_indices, uint16_t* out);
+
+/* y[T, H] = moe_block(x[T, H]).  Replaces LlamaModel::moe_block (model.cpp:750-807):
+ * router logits (bf16), softmax (fp32 inside, bf16 out), top-k, optional renorm,
+ * gate/up/down expert products with silu(g)*u, bf16(d*score) summed over k, plus
+ * bf16(sigmoid(x.wg) * shared(x)) when the layer has a shared expert. */
+FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* x,
+                 int64_t T, uint16_t* y, const fm_moe_outputs* outs);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHMOE_H_ */

@@ -1,0 +1,57 @@
+"""Parity metrics shared by the tests.
+
+Outputs of the MoE block have magnitudes around 40 (bf16 ulp ~0.25 there), so the
+north-star tolerances are applied in relative form:
+
+  max_rel = max_i |a_i - b_i| / max(|b_i|, rms(b))      <= 1e-2
+  mae_rel = mean_i |a_i - b_i| / mean_i |b_i|           <= 1e-3 (raw MAE reported too)
+
+The rms floor keeps near-zero reference elements from dominating max_rel.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from flashmlx_b200.synthetic import bf16_to_f32
+
+MAX_REL = 1e-2
+MAE_REL = 1e-3
+
+
+def metrics(a_bits: np.ndarray, b_bits: np.ndarray) -> dict:
+    a = bf16_to_f32(np.asarray(a_bits)).astype(np.float64).ravel()
+    b = bf16_to_f32(np.asarray(b_bits)).astype(np.float64).ravel()
+    d = np.abs(a - b)
+    rms = float(np.sqrt(np.mean(b * b))) if b.size else 0.0
+    den = np.maximum(np.abs(b), rms if rms > 0 else 1.0)
+    mean_abs = float(np.mean(np.abs(b))) if b.size else 0.0
+    return {
+        "max_rel": float(np.max(d / den)) if b.size else 0.0,
+        "mae": float(np.mean(d)) if b.size else 0.0,
+        "mae_rel": float(np.mean(d) / mean_abs) if mean_abs > 0 else float(np.mean(d)),
+        "exact_frac": float(np.mean(np.asarray(a_bits).ravel() == np.asarray(b_bits).ravel())) if b.size else 1.0,
+        "rms": rms,
+        "n": int(b.size),
+        "nonfinite": int(np.count_nonzero(~np.isfinite(a))),
+    }
+
+
+def assert_close(a_bits, b_bits, what="", max_rel=MAX_REL, mae_rel=MAE_REL):
+    m = metrics(a_bits, b_bits)
+    assert m["nonfinite"] == 0, f"{what}: non-finite outputs {m}"
+    assert m["max_rel"] <= max_rel and m["mae_rel"] <= mae_rel, f"{what}: {m}"
+    return m
+
+
+def near_tie_tokens(probs_bits: np.ndarray, k: int, ulps: int = 2) -> np.ndarray:
+    """Tokens whose k-th and (k+1)-th largest bf16 probabilities are within `ulps` ulps
+    (probabilities are positive, so bf16 bit patterns order like the values)."""
+    p = np.asarray(probs_bits).astype(np.int64)
+    if p.shape[1] <= k:
+        return np.zeros(p.shape[0], bool)
+    s = -np.sort(-p, axis=1)
+    return (s[:, k - 1] - s[:, k]) <= ulps
+
+
+def same_sets(a_ids: np.ndarray, b_ids: np.ndarray) -> np.ndarray:
+    return np.all(np.sort(a_ids, axis=1) == np.sort(b_ids, axis=1), axis=1)

@@ -1,0 +1,72 @@
+"""Helpers for the GPU tests: numpy <-> torch device buffers, oracle comparisons."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from flashmlx_b200 import synthetic as S
+from oracle import oracle as O
+from tests._parity import assert_close, near_tie_tokens, same_sets
+
+
+def dev_bf16(a: np.ndarray, device="cuda") -> torch.Tensor:
+    from flashmlx_b200.ops import bf16_from_numpy
+    return bf16_from_numpy(a, device)
+
+
+def dev_u32(a: np.ndarray, device="cuda") -> torch.Tensor:
+    from flashmlx_b200.ops import u32_from_numpy
+    return u32_from_numpy(a, device)
+
+
+def host_bf16(t: torch.Tensor) -> np.ndarray:
+    from flashmlx_b200.ops import bf16_to_numpy
+    return bf16_to_numpy(t)
+
+
+class GpuLayer:
+    """A synthetic MoE layer resident on the GPU plus its oracle twin."""
+
+    def __init__(self, shape, seed, device="cuda"):
+        from flashmlx_b200 import ops
+        self.shape = shape
+        self.np = S.make_layer(shape, seed)
+        self.weights = ops.MoEWeightsT.from_numpy(self.np, device)
+        self.block = ops.MoEBlock(shape, self.weights)
+        self.oracle = O.Layer(shape, self.np)
+
+    def run(self, x_np: np.ndarray):
+        x = dev_bf16(x_np)
+        y, r = self.block(x, return_routing=True)
+        torch.cuda.synchronize()
+        from flashmlx_b200 import ops
+        ops.synchronize()
+        return host_bf16(y), {k: (host_bf16(v) if v.dtype == torch.bfloat16 else v.cpu().numpy())
+                              for k, v in r.items()}
+
+    def check(self, x_np: np.ndarray, what: str, sample: np.ndarray | None = None):
+        """Routing vs the oracle (sets, near-ties excluded), permutation vs the oracle's
+        stable sort of the same ids (exact), activations vs the oracle evaluated on the
+        device's routing (all tokens, or a sample of rows)."""
+        shape = self.shape
+        y, r = self.run(x_np)
+        k, E = shape.top_k, shape.num_experts
+        ids, sc, lg, pr = O.route(x_np, self.np["router_w"], k, norm_topk=shape.norm_topk_prob,
+                                  router_bias=self.np.get("router_bias"))
+        ties = near_tie_tokens(pr, k)
+        agree = same_sets(r["topk_ids"], ids)
+        bad = ~agree & ~ties
+        assert not bad.any(), f"{what}: {bad.sum()} tokens routed differently (near-ties excluded: {ties.sum()})"
+        # scores bit-exact where the id sets agree (ordered the same way: descending, low id first)
+        ok = agree & ~ties
+        np.testing.assert_array_equal(r["topk_ids"][ok], ids[ok])
+        np.testing.assert_array_equal(r["topk_scores"][ok], sc[ok])
+        # permutation: canonical stable expert-major order of the device's own ids
+        st, sf, off = O.sort_pairs(r["topk_ids"], E)
+        np.testing.assert_array_equal(r["expert_offsets"], off)
+        np.testing.assert_array_equal(r["sorted_token"], st)
+        rows = np.arange(x_np.shape[0]) if sample is None else sample
+        yo, _, _ = self.oracle.moe_block(x_np[rows], forced_ids=r["topk_ids"][rows],
+                                         forced_scores=r["topk_scores"][rows])
+        m = assert_close(y[rows], yo, what)
+        return m, int(ties.sum())

@@ -1,0 +1,164 @@
+"""GPU parity of fm_moe_block (the whole MoE layer) against the CPU oracle, through the
+C ABI: routing ids (sets, near-ties excluded) and scores bit-exact, the expert-major
+permutation bit-exact, activations within the north-star tolerances, on both
+expert-product paths and every BASELINE configuration's layer shape."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from flashmlx_b200 import synthetic as S
+from tests.gpu_util import GpuLayer, dev_bf16, host_bf16
+
+pytestmark = pytest.mark.gpu
+PATHS = {"auto": 0, "gemv": 1, "tcgen05": 2}
+
+
+@pytest.fixture(scope="module")
+def ops():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from flashmlx_b200 import ops as _ops
+    return _ops
+
+
+_layers = {}
+
+
+def layer(name, seed=0):
+    key = (name, seed)
+    if key not in _layers:
+        _layers.clear()  # keep one resident layer at a time
+        torch.cuda.empty_cache()
+        _layers[key] = GpuLayer(S.CONFIGS[name], seed)
+    return _layers[key]
+
+
+def with_path(ops, path):
+    h = ops.default_handle()
+    h.set_path(PATHS[path])
+    return h
+
+
+@pytest.mark.parametrize("path", ["gemv", "tcgen05"])
+@pytest.mark.parametrize("T", [1, 15, 16, 32, 200])
+def test_qwen15_block(ops, path, T):
+    L = layer("qwen15_decode")
+    h = with_path(ops, path)
+    try:
+        x = S.make_x(L.shape, 100 + T, tokens=T)
+        L.check(x, f"qwen15 {path} T={T}")
+    finally:
+        h.set_path(0)
+
+
+def test_qwen15_decode_config0(ops):
+    """BASELINE configs[0] exactly: 32 decode tokens, seed 0."""
+    L = layer("qwen15_decode")
+    x = S.make_x(L.shape, 0)
+    m, ties = L.check(x, "configs[0]")
+    print("configs[0]", m, "near-ties", ties)
+
+
+@pytest.mark.parametrize("path", ["gemv", "tcgen05"])
+@pytest.mark.parametrize("T", [64, 700])
+def test_qwen3_block(ops, path, T):
+    L = layer("qwen3_decode")
+    h = with_path(ops, path)
+    try:
+        x = S.make_x(L.shape, 200 + T, tokens=T)
+        L.check(x, f"qwen3 {path} T={T}")
+    finally:
+        h.set_path(0)
+
+
+@pytest.mark.parametrize("path", ["gemv", "tcgen05"])
+def test_mixtral_block(ops, path):
+    L = layer("mixtral_prefill")
+    h = with_path(ops, path)
+    try:
+        x = S.make_x(L.shape, 300, tokens=48)
+        L.check(x, f"mixtral {path}")
+    finally:
+        h.set_path(0)
+
+
+def test_qwen15_prefill_config1_full(ops):
+    """BASELINE configs[1] at full size (T=4096): routing for every token, the
+    permutation exactly, activations on a sample of rows (tokens are independent)."""
+    L = layer("qwen15_prefill")
+    x = S.make_x(L.shape, 0)
+    sample = np.random.default_rng(0).choice(x.shape[0], 96, replace=False)
+    m, ties = L.check(x, "configs[1]", sample=np.sort(sample))
+    print("configs[1]", m, "near-ties", ties)
+
+
+def test_qwen3_prefill_full_sample(ops):
+    L = layer("qwen3_prefill")
+    x = S.make_x(L.shape, 0)
+    sample = np.sort(np.random.default_rng(1).choice(x.shape[0], 48, replace=False))
+    L.check(x, "configs[3] prefill", sample=sample)
+
+
+def test_all_tokens_one_expert(ops):
+    """Heavy skew: a large router bias sends every token to the same expert."""
+    L = layer("qwen15_decode", seed=5)
+    bias = np.zeros(L.shape.num_experts, np.float32)
+    bias[7] = 30.0
+    L.np["router_bias"] = S.f32_to_bf16(bias)
+    from flashmlx_b200 import ops as _ops
+    from oracle import oracle as O
+    L.weights.router_bias = dev_bf16(L.np["router_bias"])
+    L.block = _ops.MoEBlock(L.shape, L.weights)
+    L.oracle = O.Layer(L.shape, L.np)
+    for path in ("gemv", "tcgen05"):
+        h = with_path(ops, path)
+        try:
+            x = S.make_x(L.shape, 9, tokens=300)
+            y, r = L.run(x)
+            assert (r["topk_ids"] == 7).any(axis=1).all()
+            L.check(x, f"one hot expert {path}")
+        finally:
+            h.set_path(0)
+    _layers.clear()
+
+
+def test_deterministic_repeat(ops):
+    L = layer("qwen15_decode")
+    x = S.make_x(L.shape, 77, tokens=256)
+    for path in ("gemv", "tcgen05"):
+        h = with_path(ops, path)
+        try:
+            y1, r1 = L.run(x)
+            y2, r2 = L.run(x)
+            np.testing.assert_array_equal(r1["topk_ids"], r2["topk_ids"])
+            np.testing.assert_array_equal(r1["sorted_token"], r2["sorted_token"])
+            assert np.mean(y1 == y2) > 0.999, f"{path}: run-to-run differences beyond fp32 atomic order"
+        finally:
+            h.set_path(0)
+
+
+def test_paths_agree(ops):
+    L = layer("qwen15_decode")
+    x = S.make_x(L.shape, 55, tokens=128)
+    outs = []
+    for path in ("gemv", "tcgen05"):
+        h = with_path(ops, path)
+        try:
+            outs.append(L.run(x))
+        finally:
+            h.set_path(0)
+    (ya, ra), (yb, rb) = outs
+    np.testing.assert_array_equal(ra["topk_ids"], rb["topk_ids"])
+    from tests._parity import assert_close
+    assert_close(ya, yb, "gemv vs tcgen05")
+
+
+def test_moe_block_argument_errors(ops):
+    L = layer("qwen15_decode")
+    with pytest.raises(ValueError):
+        L.block(torch.zeros(4, 100, dtype=torch.bfloat16, device="cuda"))
+    y = L.block(torch.zeros(0, L.shape.hidden, dtype=torch.bfloat16, device="cuda"))
+    assert y.shape[0] == 0
+    _ = host_bf16
