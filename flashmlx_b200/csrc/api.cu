@@ -225,13 +225,11 @@ int check_moe(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w) {
     return set_err(h, FM_EUNSUPPORTED, "only 4-bit affine with group size 32/64/128 is implemented");
   if (c->hidden % 128 || c->inter % 128)
     return set_err(h, FM_EUNSUPPORTED, "hidden and moe_intermediate_size must be multiples of 128");
-  if ((c->hidden / c->group_size) % 2 || (c->inter / c->group_size) % 2)
-    return set_err(h, FM_EUNSUPPORTED, "K / group_size must be even");
   if (c->router_quantized || c->shared_gate_quantized)
     return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
   if (c->shared_inter < 0) return set_err(h, FM_EINVAL, "negative shared_inter");
   if (c->shared_inter > 0) {
-    if (c->shared_inter % 128 || (c->shared_inter / c->group_size) % 2)
+    if (c->shared_inter % 128)
       return set_err(h, FM_EUNSUPPORTED, "shared_expert_intermediate_size must be a multiple of 128");
     if (!w->shared_gate.w || !w->shared_up.w || !w->shared_down.w || !w->shared_gate.scales ||
         !w->shared_up.scales || !w->shared_down.scales || !w->shared_expert_gate_w)
@@ -539,9 +537,7 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   const int64_t rows = B * M;
   if (rows > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
   bool tcp = use_tc(h, rows, E);
-  if (K % 128) tcp = true;                       // GEMV needs 128-wide K chunks
-  if ((K / group_size) % 2) tcp = false;         // tcgen05 path loads scale pairs
-  if (K % 128 && (K / group_size) % 2) return set_err(h, FM_EUNSUPPORTED, "K / group_size must be even");
+  if (K % 128) tcp = true;  // the GEMV path works in 128-wide K chunks
   Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false);
   int rc = ensure_ws(h, p.total);
   if (rc) return rc;

@@ -174,16 +174,26 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
         cp_async16(smem_u32(ring + t * 32), src);
         cp_async16(smem_u32(ring + t * 32 + 16), src + 4);
         const int g0 = (k.ks * 64) / a.gs;
-        const int gp = g0 & ~1;  // aligned group pair (gpr is even, host-checked)
-        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8)),
-                     "l"(S + r * gpr + gp)
-                     : "memory");
-        if (B)
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8 + 4)),
-                       "l"(B + r * gpr + gp)
+        if ((gpr & 1) == 0) {
+          // 4-byte aligned group pair holding this k-step's group(s)
+          const int gp = g0 & ~1;
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8)),
+                       "l"(S + r * gpr + gp)
                        : "memory");
-        else
-          *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8 + 4) = 0u;
+          if (B)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8 + 4)),
+                         "l"(B + r * gpr + gp)
+                         : "memory");
+          else
+            *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8 + 4) = 0u;
+        } else {
+          // odd group count per row (group size >= 64, one group per k-step): scalar
+          // loads, the value duplicated into both halves of the slot
+          const uint32_t sv = __ldg(S + r * gpr + g0);
+          const uint32_t bv = B ? __ldg(B + r * gpr + g0) : 0u;
+          *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8) = sv * 0x10001u;
+          *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8 + 4) = bv * 0x10001u;
+        }
       }
     };
     // prologue: NRING-1 k-steps in flight

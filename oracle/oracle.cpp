@@ -90,17 +90,24 @@ inline float dot(const float* a, const float* b, int K) {
   return (s0 + s2) + (s1 + s3);
 }
 
-// One row of an MLX affine-quantized matrix, dequantized exactly in fp32.
+// Weight rounding mode: 0 = exact fp32 dequantization (MLX's documented arithmetic),
+// 1 = dequantized weights rounded once to bf16, as a bf16 tensor-core path must
+// (MLX's Metal qmm likewise dequantizes into bf16 threadgroup tiles).
+int g_weight_rounding = 0;
+
+// One row of an MLX affine-quantized matrix, dequantized in fp32 (fma(s, q, b)).
 void dequant_row(const uint32_t* wrow, const uint16_t* srow, const uint16_t* brow, int K,
                  int gs, int bits, float* out) {
   const int pf = 32 / bits;
   const uint32_t mask = (bits == 32) ? 0xffffffffu : ((1u << bits) - 1u);
+  const bool round_w = g_weight_rounding == 1;
   for (int g = 0; g < K / gs; ++g) {
     const float s = bf2f(srow[g]);
     const float b = brow ? bf2f(brow[g]) : 0.0f;
     for (int j = g * gs; j < (g + 1) * gs; ++j) {
       uint32_t q = (wrow[j / pf] >> ((j % pf) * bits)) & mask;
-      out[j] = std::fma(s, static_cast<float>(q), b);
+      const float w = std::fma(s, static_cast<float>(q), b);
+      out[j] = round_w ? rbf(w) : w;
     }
   }
 }
@@ -176,6 +183,13 @@ struct orc_moe_weights {
 };
 
 int orc_version() { return 1; }
+
+// 0: exact dequantization (default); 1: dequantized weights rounded to bf16.
+int orc_set_weight_rounding(int mode) {
+  if (mode != 0 && mode != 1) return 1;
+  g_weight_rounding = mode;
+  return 0;
+}
 
 // mx::quantized_matmul(x, w, s, b, transpose=true, gs, bits), x [M, K] -> out [M, N]
 int orc_quantized_matmul(const uint16_t* x, int64_t M, int K, const uint32_t* w, const uint16_t* s,

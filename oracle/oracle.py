@@ -58,7 +58,9 @@ def lib():
         L.orc_route.argtypes = [p, i64, i, p, p, p, i, p, i, i, i, i, i, p, p, p, p, i]
         L.orc_sort_pairs.argtypes = [p, i64, i, i, p, p, p]
         L.orc_moe_block.argtypes = [C.POINTER(MoEConfig), C.POINTER(MoEWeights), p, i64, p, p, p, p, p, i]
-        for f in ("orc_quantized_matmul", "orc_gather_qmm", "orc_route", "orc_sort_pairs", "orc_moe_block"):
+        L.orc_set_weight_rounding.argtypes = [i]
+        for f in ("orc_quantized_matmul", "orc_gather_qmm", "orc_route", "orc_sort_pairs", "orc_moe_block",
+                  "orc_set_weight_rounding"):
             getattr(L, f).restype = C.c_int
         _lib = L
     return _lib
@@ -73,6 +75,24 @@ def _c(a, dt):
 
 
 NTHREADS = os.cpu_count() or 1
+
+EXACT, BF16_WEIGHTS = 0, 1
+
+
+class weight_rounding:
+    """Context manager: evaluate the oracle with exact (default) or bf16-rounded
+    dequantized weights."""
+
+    def __init__(self, mode: int):
+        self.mode = mode
+
+    def __enter__(self):
+        lib().orc_set_weight_rounding(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        lib().orc_set_weight_rounding(EXACT)
+        return False
 
 
 def quantized_matmul(x, w, s, b, group_size=64, bits=4, nthreads=None):

@@ -6,7 +6,20 @@ import torch
 
 from flashmlx_b200 import synthetic as S
 from oracle import oracle as O
-from tests._parity import assert_close, near_tie_tokens, same_sets
+from tests._parity import EXACT_FLOOR, TIGHT, assert_close, near_tie_tokens, same_sets
+
+
+def check_vs_oracle(y_bits, oracle_fn, what):
+    """Compare against the oracle with bf16-rounded dequantized weights (tight) and with
+    exact dequantization (documented floor).  Returns both metric dicts."""
+    with O.weight_rounding(O.BF16_WEIGHTS):
+        yt = oracle_fn()
+    yt = yt[0] if isinstance(yt, tuple) else yt
+    mt = assert_close(y_bits, yt, what + " [oracle, bf16 weights]", **TIGHT)
+    ye = oracle_fn()
+    ye = ye[0] if isinstance(ye, tuple) else ye
+    me = assert_close(y_bits, ye, what + " [oracle, exact weights]", **EXACT_FLOOR)
+    return mt, me
 
 
 def dev_bf16(a: np.ndarray, device="cuda") -> torch.Tensor:
@@ -66,7 +79,6 @@ class GpuLayer:
         np.testing.assert_array_equal(r["expert_offsets"], off)
         np.testing.assert_array_equal(r["sorted_token"], st)
         rows = np.arange(x_np.shape[0]) if sample is None else sample
-        yo, _, _ = self.oracle.moe_block(x_np[rows], forced_ids=r["topk_ids"][rows],
-                                         forced_scores=r["topk_scores"][rows])
-        m = assert_close(y[rows], yo, what)
+        m = check_vs_oracle(y[rows], lambda: self.oracle.moe_block(
+            x_np[rows], forced_ids=r["topk_ids"][rows], forced_scores=r["topk_scores"][rows]), what)
         return m, int(ties.sum())
