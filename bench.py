@@ -230,8 +230,11 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     h.sync()
     dev_ms = e0.elapsed_time(e1) / args.steps
-    prof = h.profile_report(reset=True)
+    prof_all = h.profile_report(reset=True)
     h.profile(False)
+    # "route.phaseN" entries split the routing kernel's time; they are not launches
+    prof = {k: v for k, v in prof_all.items() if "." not in k}
+    phases = {k: v[1] / max(1, v[0]) for k, v in prof_all.items() if "." in k}
 
     # end-to-end through the public API: pinned host x -> device -> block -> pinned host y
     x_pin = torch.from_numpy(x_np.view(np.int16)).view(torch.bfloat16).pin_memory()
@@ -298,6 +301,7 @@ def run_ours(args, rank, world, local_rank):
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
             "gpu_launches": ours_launches,
             "kernels": {kname: {"launches": n, "avg_ms": ms / max(1, n)} for kname, (n, ms) in prof.items()},
+            "route_phases_ms": phases,
             "roofline": roof,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -24,6 +24,7 @@ __global__ void finalize_kernel(const float* y_acc, const float* ysh, const floa
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
 cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
+int max_rows();
 cudaError_t init();
 cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
 }  // namespace tc
@@ -164,6 +165,8 @@ void prof_end(fm_handle* h) {
 
 uint32_t* err_word(fm_handle* h) { return reinterpret_cast<uint32_t*>(h->ws); }
 fm::GridSync* grid_sync(fm_handle* h) { return reinterpret_cast<fm::GridSync*>(h->ws + 64); }
+// routing-kernel phase timers: 4 x u64 ns + a launch count, accumulated on the device
+unsigned long long* phase_ns(fm_handle* h) { return reinterpret_cast<unsigned long long*>(h->ws + 128); }
 
 template <class T>
 T* at(fm_handle* h, size_t off) {
@@ -346,6 +349,18 @@ int fm_profile_report(fm_handle* h, fm_kernel_time* out, int capacity, int* coun
     h->event_pool.push_back(p.b);
   }
   h->pending.clear();
+  // routing-kernel phase split (accumulated on the device since the last reset)
+  unsigned long long ph[4] = {0, 0, 0, 0};
+  if (h->ws) {
+    cudaError_t e = cudaMemcpy(ph, phase_ns(h), sizeof(ph), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_err(h, e, "phase timer read");
+    static const char* phase_names[4] = {"route.phase1_router", "route.phase2_topk", "route.phase3_scan",
+                                         "route.phase4_scatter"};
+    auto rt = h->totals.find("route");
+    const int64_t nl = rt == h->totals.end() ? 0 : rt->second.launches;
+    for (int i = 0; i < 4; ++i)
+      if (ph[i]) h->totals[phase_names[i]] = fm_handle::Total{phase_names[i], nl, ph[i] * 1e-6};
+  }
   int n = 0;
   for (auto& kv : h->totals) {
     if (n < capacity) {
@@ -356,7 +371,10 @@ int fm_profile_report(fm_handle* h, fm_kernel_time* out, int capacity, int* coun
     ++n;
   }
   if (count) *count = n;
-  if (reset) h->totals.clear();
+  if (reset) {
+    h->totals.clear();
+    if (h->ws) cudaMemset(phase_ns(h), 0, 4 * sizeof(unsigned long long));
+  }
   return FM_OK;
 }
 
@@ -440,7 +458,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.a_n = I;
   ra.a_n_shared = c->shared_inter;
   ra.b_n = H;
-  ra.chunk_max = tcp ? 256 : 32;
+  ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, I));
   ra.has_shared = shared ? 1 : 0;
@@ -452,6 +470,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   }
   ra.gsync = grid_sync(h);
   ra.err = err_word(h);
+  ra.phase_ns = phase_ns(h);
   const int64_t items = ((T + 15) / 16) * ksplit;
   rc = launch_route(h, ra, items);
   if (rc) return rc;
@@ -575,7 +594,7 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   ra.a_rows_per_block = 128;
   ra.a_n = N;
   ra.a_n_shared = 0;
-  ra.chunk_max = tcp ? 256 : 32;
+  ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = 1;
   ra.gsync = grid_sync(h);

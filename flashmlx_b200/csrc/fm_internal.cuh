@@ -155,6 +155,7 @@ struct RouteArgs {
   int32_t* out_offsets;
   GridSync* gsync;
   uint32_t* err;
+  unsigned long long* phase_ns;  // [4] accumulated per-phase time of block 0 (profiling)
 };
 
 constexpr int kRouteThreads = 256;  // 8 warps

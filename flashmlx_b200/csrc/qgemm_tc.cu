@@ -3,7 +3,7 @@
 // Replaces mx::gather_qmm (sorted, model.cpp:703-721) and mx::quantized_matmul
 // (model.cpp:741-747) for prefill-sized batches.  One persistent CTA per SM walks a
 // device-built tile table (expert / shared-expert group, 128-row output block, chunk
-// of <= 256 activation rows).  D[128 x N] accumulates in TMEM:
+// of <= 192 activation rows).  D[128 x N] accumulates in TMEM:
 //   gate/up mode: A rows 0..63 = gate rows, 64..127 = the same up rows, so one
 //                 accumulator holds g and u of a row block; the epilogue applies
 //                 silu(g)*u and writes the pair-permuted activation rows for down.
@@ -11,17 +11,18 @@
 //                 weight and red.adds into the fp32 combine buffer (token-indexed).
 //   plain mode:   quantized_matmul / gather_qmm output, bf16.
 //
-// Roles (384 threads):
-//   warps 0-3  dequant producers: thread t owns A row t.  Codes, scales and biases of
-//              k-step s+3 stream into a private cp.async ring; k-step s is dequantized
-//              (bf16 fma of exact codes) into the 128B-swizzled K-major A stage.
-//   warps 4-5  activation producers: cp.async gather of up to 256 rows x 128 B per
-//              k-step into the swizzled B stage, row indices from the pair table.
-//   warp 6     TMEM allocator and single-thread tcgen05.mma issuer (M=128, N<=256,
-//              K=16 x 4 per stage), tcgen05.commit frees stages and publishes
-//              accumulators.
-//   warps 8-11 epilogue: tcgen05.ld of the four 32-lane quadrants; double-buffered
-//              accumulators (2 x 256 TMEM columns) overlap the next tile's mainloop.
+// Roles (544 threads; the producer / consumer roles spread over the 4 SM sub-partitions):
+//   warps 0-7   dequant producers: thread t owns half of A row t/2.  Codes, scales and
+//               biases of k-step s+9 stream into a private cp.async ring (deep enough
+//               to cover HBM latency under load); k-step s is dequantized (bf16 fma of
+//               exact codes) into the 128B-swizzled K-major A stage.
+//   warps 8-11  activation producers: cp.async gather of up to 192 rows x 128 B per
+//               k-step into the swizzled B stage; each thread keeps its 12 rows'
+//               indices in registers (one wide multiply-add per copy).
+//   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
+//               buffered accumulators (2 x 256 columns) overlap the next mainloop.
+//   warp 16     TMEM allocator and single-thread tcgen05.mma issuer (M=128, N<=192,
+//               K=16 x 4 per stage); tcgen05.commit frees stages / publishes tiles.
 // No TMA and no cluster multicast anywhere.  Every wait is bounded.
 #include "fm_internal.cuh"
 
@@ -29,22 +30,28 @@ namespace fm {
 namespace tc {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
+constexpr int BN = 192;          // max activation rows per tile (MMA N)
+constexpr int ACC_COLS = 256;    // TMEM columns per accumulator buffer
 constexpr int STAGES = 4;
-constexpr int NRING = 4;
+constexpr int NRING = 10;
 constexpr int A_BYTES = BM * 128;
 constexpr int B_BYTES = BN * 128;
 constexpr int RING_CODES = BM * 32;             // packed codes of one k-step
 constexpr int RING_BYTES = RING_CODES + BM * 8; // + scale pair + bias pair per row
-constexpr int XCHG_BYTES = 32 * 64 * 2;
+constexpr int XCHG_HALF = 16 * 64 * 2;          // 16 columns x 64 rows, bf16
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
 constexpr int OFF_RING = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_XCHG = OFF_RING + NRING * RING_BYTES;
-constexpr int OFF_BAR = OFF_XCHG + 2 * XCHG_BYTES;
+constexpr int OFF_BAR = OFF_XCHG + 4 * XCHG_HALF;  // {gate->up, up->gate} x 2 buffers
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-constexpr int THREADS = 384;
+constexpr int NA = 256;          // dequant-producer threads (two per A row)
+constexpr int NB = 128;          // activation-producer threads
+constexpr int B_ROWS = BN * 8 / NB;  // rows per activation-producer thread (12)
+constexpr int EPI_WARP = 12;     // first of the four epilogue warps
+constexpr int MMA_WARP = 16;
+constexpr int THREADS = (MMA_WARP + 1) * 32;
 constexpr int B_LAG = 2;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -99,10 +106,15 @@ FM_DEV bool wait_done(uint64_t* bar, uint32_t parity, uint32_t* err) {  // ignor
   return true;
 }
 
+// silu(g) * u with the bf16 rounding of each MLX op (model.cpp:14-25); g, u already bf16
 FM_DEV float swiglu1(float g, float u) {
-  const float gs = rbf(sigmoid_f(g));
-  const float h = rbf(g * gs);
+  const float sg = rbf(__frcp_rn(1.0f + __expf(-g)));
+  const float h = rbf(g * sg);
   return rbf(h * u);
+}
+
+FM_DEV void red_add_v2(float* p, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 
 template <int MODE>
@@ -118,7 +130,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->full[s], 128 + 64);
+      mbar_init(&bars->full[s], NA + NB);
       mbar_init(&bars->empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -129,7 +141,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 6) {
+  if (warp == MMA_WARP) {
     tmem_alloc(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
@@ -138,9 +150,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ------------------------------------------------------------ dequant producers
-    const int t = tid;  // A row
+    const int t = tid >> 1;    // A row
+    const int half = tid & 1;  // words [4 half, 4 half + 4) of the row's 8 per k-step
     KIter cur, pf;
     kiter_load(cur, a, blockIdx.x, ntiles, MODE);
     pf = cur;
@@ -170,29 +183,21 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
         const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + row;
         const int gpr = K / a.gs;
         uint8_t* ring = smem + OFF_RING + slot * RING_BYTES;
-        const uint32_t* src = W + r * (K / 8) + k.ks * 8;
-        cp_async16(smem_u32(ring + t * 32), src);
-        cp_async16(smem_u32(ring + t * 32 + 16), src + 4);
+        cp_async16(smem_u32(ring + t * 32 + half * 16), W + r * (K / 8) + k.ks * 8 + half * 4);
+        // half 0 fetches the scale pair, half 1 the bias pair
+        const uint16_t* SB = half ? B : S;
+        uint8_t* dst = ring + RING_CODES + t * 8 + half * 4;
         const int g0 = (k.ks * 64) / a.gs;
-        if ((gpr & 1) == 0) {
+        if (!SB) {
+          *reinterpret_cast<uint32_t*>(dst) = 0u;
+        } else if ((gpr & 1) == 0) {
           // 4-byte aligned group pair holding this k-step's group(s)
-          const int gp = g0 & ~1;
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8)),
-                       "l"(S + r * gpr + gp)
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(SB + r * gpr + (g0 & ~1))
                        : "memory");
-          if (B)
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(ring + RING_CODES + t * 8 + 4)),
-                         "l"(B + r * gpr + gp)
-                         : "memory");
-          else
-            *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8 + 4) = 0u;
         } else {
           // odd group count per row (group size >= 64, one group per k-step): scalar
-          // loads, the value duplicated into both halves of the slot
-          const uint32_t sv = __ldg(S + r * gpr + g0);
-          const uint32_t bv = B ? __ldg(B + r * gpr + g0) : 0u;
-          *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8) = sv * 0x10001u;
-          *reinterpret_cast<uint32_t*>(ring + RING_CODES + t * 8 + 4) = bv * 0x10001u;
+          // load, the value duplicated into both halves of the slot
+          *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(__ldg(SB + r * gpr + g0)) * 0x10001u;
         }
       }
     };
@@ -214,6 +219,8 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       ++pf_count;
       cp_async_commit();
       cp_async_wait<NRING - 1>();
+      // the pair of threads of a row read each other's scale / bias word
+      __syncwarp();
       const int slot = it % NRING, stage = it % STAGES;
       if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) break;
       const TileInfo& ti = cur.ti;
@@ -222,15 +229,15 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       const int row = (MODE == MODE_GATEUP) ? ti.rb * 64 + (t & 63) : ti.rb * 128 + t;
       if (row < N) {
         const uint8_t* ring = smem + OFF_RING + slot * RING_BYTES;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(ring + t * 32);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(ring + t * 32 + 16);
+        const uint4 w = *reinterpret_cast<const uint4*>(ring + t * 32 + half * 16);
         const uint32_t sp = *reinterpret_cast<const uint32_t*>(ring + RING_CODES + t * 8);
         const uint32_t bp = *reinterpret_cast<const uint32_t*>(ring + RING_CODES + t * 8 + 4);
-        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
         uint8_t* As = smem + OFF_A + stage * A_BYTES;
         const int g0 = (cur.ks * 64) / a.gs;
 #pragma unroll
-        for (int cc = 0; cc < 8; ++cc) {
+        for (int i = 0; i < 4; ++i) {
+          const int cc = half * 4 + i;
           const int gi = (cur.ks * 64 + 8 * cc) / a.gs;
           const int hi = (gi - (g0 & ~1)) & 1;
           const uint16_t sv = static_cast<uint16_t>(hi ? (sp >> 16) : (sp & 0xffffu));
@@ -239,10 +246,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
           const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
           const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&b2u);
           uint4 o;
-          o.x = deq_pair(words[cc], 0, s2, b2);
-          o.y = deq_pair(words[cc], 1, s2, b2);
-          o.z = deq_pair(words[cc], 2, s2, b2);
-          o.w = deq_pair(words[cc], 3, s2, b2);
+          o.x = deq_pair(words[i], 0, s2, b2);
+          o.y = deq_pair(words[i], 1, s2, b2);
+          o.z = deq_pair(words[i], 2, s2, b2);
+          o.w = deq_pair(words[i], 3, s2, b2);
           *reinterpret_cast<uint4*>(As + sw128_off(t, cc)) = o;
         }
       }
@@ -252,49 +259,46 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       kiter_next(cur, a, ntiles, MODE);
     }
     cp_async_wait<0>();
-  } else if (warp < 6) {
+  } else if (warp < EPI_WARP) {
     // ------------------------------------------------------------ activation producers
-    const int bt = tid - 128;
-    const int cc = bt & 7, rg = bt >> 3;
+    const int bt = tid - NA;
+    const int cc = bt & 7, rg = bt >> 3;  // 16-byte chunk of the row, first row (0..15)
+    // swizzled destination of row rg + 16 i: (rg + 16 i) * 128 + ((cc ^ (rg & 7)) << 4)
+    const uint32_t dst0 = static_cast<uint32_t>(rg) * 128u + ((static_cast<uint32_t>(cc ^ (rg & 7))) << 4);
     int it = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
       const TileInfo ti = decode_tile(a.tab, tile);
       const bool sh = ti.expert < 0;
       const int nks = tile_ksteps(a, ti, MODE);
-      const uint16_t* base;
-      int64_t ld;
-      if (MODE == MODE_DOWN) {
-        base = sh ? a.act_shared : a.act;
-        ld = sh ? a.act_shared_ld : a.act_ld;
-      } else {
-        base = sh ? a.act_shared : a.act;
-        ld = sh ? a.act_shared_ld : a.act_ld;
-      }
-      // source row offsets of this thread's rows (rg + 8 i), kept in registers
-      int32_t srow[BN / 8];
+      const uint16_t* base = sh ? a.act_shared : a.act;
+      const uint64_t ld_bytes = static_cast<uint64_t>(sh ? a.act_shared_ld : a.act_ld) * 2u;
+      // source rows of this thread's rows (rg + 16 i), kept in registers
+      uint32_t srow[B_ROWS];
 #pragma unroll
-      for (int i = 0; i < BN / 8; ++i) {
-        const int r = rg + 8 * i;
-        int32_t s = 0;
+      for (int i = 0; i < B_ROWS; ++i) {
+        const int r = rg + 16 * i;
+        uint32_t s = 0;
         if (r < ti.nrows) {
           const int p = ti.row0 + r;
-          s = (MODE == MODE_DOWN || sh) ? p : a.sorted_token[p];
+          s = static_cast<uint32_t>((MODE == MODE_DOWN || sh) ? p : a.sorted_token[p]);
         }
         srow[i] = s;
       }
+      const int nvalid = ti.nrows;
       for (int ks = 0; ks < nks; ++ks) {
         const int stage = it % STAGES;
         if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) {
           ok = false;
           break;
         }
-        uint8_t* Bs = smem + OFF_B + stage * B_BYTES;
+        const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES) + dst0;
+        const uint64_t src_k = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(ks * 128 + cc * 16);
 #pragma unroll
-        for (int i = 0; i < BN / 8; ++i) {
-          const int r = rg + 8 * i;
-          if (r < ti.nrows)
-            cp_async16(smem_u32(Bs + sw128_off(r, cc)), base + static_cast<int64_t>(srow[i]) * ld + ks * 64 + cc * 8);
+        for (int i = 0; i < B_ROWS; ++i) {
+          if (rg + 16 * i < nvalid)
+            cp_async16(bs + static_cast<uint32_t>(i) * 2048u,
+                       reinterpret_cast<const void*>(src_k + static_cast<uint64_t>(srow[i]) * ld_bytes));
         }
         cp_async_commit();
         if (it >= B_LAG) {
@@ -308,7 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
     cp_async_wait<0>();
     fence_proxy_async();
     for (int j = (it >= B_LAG ? it - B_LAG : 0); j < it; ++j) mbar_arrive(&bars->full[j % STAGES]);
-  } else if (warp == 6) {
+  } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int it = 0, lt = 0;
@@ -321,7 +325,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
         tc_fence_after();
         const int nmma = max(16, (ti.nrows + 15) & ~15);
         const uint32_t idesc = idesc_bf16(BM, nmma);
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * BN);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * ACC_COLS);
         for (int ks = 0; ks < nks; ++ks) {
           const int stage = it % STAGES;
           if (!mbar_wait(&bars->full[stage], (it / STAGES) & 1, abort_flag, a.err)) {
@@ -342,9 +346,9 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       wait_done(&bars->done, 0, a.err);
     }
     __syncwarp();
-  } else if (warp >= 8) {
+  } else if (warp >= EPI_WARP && warp < EPI_WARP + 4) {
     // ------------------------------------------------------------ epilogue
-    const int q = warp - 8;
+    const int q = warp - EPI_WARP;
     const int row_in = q * 32 + lane;  // TMEM lane == A row
     uint16_t* xchg = reinterpret_cast<uint16_t*>(smem + OFF_XCHG);
     int lt = 0, xit = 0;
@@ -360,49 +364,81 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       const bool all_ok = bars->epi_ok[buf][0] && bars->epi_ok[buf][1] && bars->epi_ok[buf][2] && bars->epi_ok[buf][3];
       if (!all_ok) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * BN);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * ACC_COLS);
       const int nchunks = (ti.nrows + 31) >> 5;
       for (int j = 0; j < nchunks; ++j, ++xit) {
         float v[32];
         tmem_ld32(tbase + j * 32, v);
         if (MODE == MODE_GATEUP) {
-          uint16_t* xb = xchg + (xit & 1) * (32 * 64);
-          if (q >= 2) {
+          // gate warps (q 0,1) finish columns 0..15, up warps (q 2,3) columns 16..31;
+          // each hands the partner the other half of its rows through shared memory
+          uint16_t* to_up = xchg + (xit & 1) * (2 * 16 * 64);  // gate values, cols 16..31
+          uint16_t* to_gate = to_up + 16 * 64;                  // up values, cols 0..15
+          const int r64 = row_in & 63;
+          if (q < 2) {
 #pragma unroll
-            for (int cidx = 0; cidx < 32; ++cidx) xb[cidx * 64 + (q - 2) * 32 + lane] = f2bf(v[cidx]);
+            for (int c = 0; c < 16; ++c) to_up[c * 64 + r64] = f2bf(v[16 + c]);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 16; ++c) to_gate[c * 64 + r64] = f2bf(v[c]);
           }
           named_bar_sync(1, 128);
-          if (q < 2) {
-            const int n = ti.rb * 64 + row_in;
-            uint16_t* outb = sh ? a.out_shared : a.out;
-            const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
-            const int pn = perm8(n);
-#pragma unroll 4
-            for (int cidx = 0; cidx < 32; ++cidx) {
-              const int col = j * 32 + cidx;
-              if (col < ti.nrows && n < N) {
-                const float gv = rbf(v[cidx]);
-                const float uv = bf2f(xb[cidx * 64 + row_in]);
-                outb[static_cast<int64_t>(ti.row0 + col) * ld + pn] = f2bf(swiglu1(gv, uv));
-              }
+          const int n = ti.rb * 64 + r64;
+          uint16_t* outb = sh ? a.out_shared : a.out;
+          const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
+          const int pn = perm8(n);  // even for n % 8 < 4: (n, n+4) share one 32-bit word
+          const int c0 = (q < 2) ? 0 : 16;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int col = j * 32 + c0 + c;
+            float gv, uv;
+            if (q < 2) {
+              gv = rbf(v[c]);
+              uv = bf2f(to_gate[c * 64 + r64]);
+            } else {
+              gv = bf2f(to_up[c * 64 + r64]);
+              uv = rbf(v[16 + c]);
             }
+            const uint32_t mine = f2bf(swiglu1(gv, uv));
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 4);
+            if (col < ti.nrows && (lane & 4) == 0 && n < N)
+              *reinterpret_cast<uint32_t*>(outb + static_cast<int64_t>(ti.row0 + col) * ld + pn) = mine | (other << 16);
           }
         } else {
+          // lanes (2m, 2m+1) hold rows (n, n+1); the even lane finishes column c and
+          // the odd lane column c+1, each as one 2-wide red / 4-byte store
           const int n = ti.rb * 128 + row_in;
-#pragma unroll 4
-          for (int cidx = 0; cidx < 32; ++cidx) {
-            const int col = j * 32 + cidx;
-            if (col >= ti.nrows || n >= N) continue;
-            const int p = ti.row0 + col;
+          const bool odd = lane & 1;
+          const int n0 = n & ~1;
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            const int col = j * 32 + c + (odd ? 1 : 0);
+            const bool colok = col < ti.nrows;
+            const int p = ti.row0 + (colok ? col : 0);
+            float mine_c = v[c], mine_c1 = v[c + 1];
+            if (MODE == MODE_DOWN && !sh) {  // bf16(bf16(d) * score) per MLX op
+              const int pe = ti.row0 + min(j * 32 + c, ti.nrows - 1);
+              const int po = ti.row0 + min(j * 32 + c + 1, ti.nrows - 1);
+              const float se = a.sorted_score[pe], so = a.sorted_score[po];
+              mine_c = rbf(rbf(mine_c) * se);
+              mine_c1 = rbf(rbf(mine_c1) * so);
+            }
+            // even lane sends its column c+1 value, odd lane its column c value
+            const float give = odd ? mine_c : mine_c1;
+            const float got2 = __shfl_xor_sync(0xffffffffu, give, 1);
+            const float lo = odd ? got2 : mine_c;    // row n0, column (c or c+1)
+            const float hi = odd ? mine_c1 : got2;   // row n0+1
+            if (!colok || n0 >= N) continue;
             if (MODE == MODE_DOWN) {
               if (sh) {
-                red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v[cidx]);
+                red_add_v2(a.ysh + static_cast<int64_t>(p) * a.y_ld + n0, lo, hi);
               } else {
                 const int tok = a.sorted_token[p];
-                red_add_f32(a.y_acc + static_cast<int64_t>(tok) * a.y_ld + n, rbf(rbf(v[cidx]) * a.sorted_score[p]));
+                red_add_v2(a.y_acc + static_cast<int64_t>(tok) * a.y_ld + n0, lo, hi);
               }
             } else {
-              a.out[static_cast<int64_t>(a.sorted_flat[p]) * a.out_ld + n] = f2bf(v[cidx]);
+              *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(a.sorted_flat[p]) * a.out_ld + n0) =
+                  pack_bf16x2(lo, hi);
             }
           }
         }
@@ -414,11 +450,13 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 6) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
+
+int max_rows() { return BN; }
 
 cudaError_t init() {
   cudaError_t e = cudaFuncSetAttribute(qgemm_tc_kernel<MODE_GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);

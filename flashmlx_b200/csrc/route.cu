@@ -412,23 +412,43 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
 
 }  // namespace
 
+FM_DEV unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// block 0, thread 0 accumulates the wall time of each phase (as seen by block 0)
+FM_DEV void phase_mark(const RouteArgs& a, int phase, unsigned long long& t) {
+  if (blockIdx.x == 0 && threadIdx.x == 0 && a.phase_ns) {
+    const unsigned long long now = global_ns();
+    atomicAdd(a.phase_ns + phase, now - t);
+    t = now;
+  }
+}
+
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
   __shared__ RouteSmem sm;
   const unsigned nb = gridDim.x;
+  unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   // phase 1
   if (a.do_router) phase_router(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  phase_mark(a, 0, t);
   // phase 2
   phase_topk_count(a, sm);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  phase_mark(a, 1, t);
   // phase 3
   phase_column_scan(a, sm);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+  phase_mark(a, 2, t);
   // phase 4
   phase_scatter(a, sm);
+  phase_mark(a, 3, t);
 }
 
 }  // namespace fm

@@ -70,10 +70,16 @@ class GpuLayer:
         agree = same_sets(r["topk_ids"], ids)
         bad = ~agree & ~ties
         assert not bad.any(), f"{what}: {bad.sum()} tokens routed differently (near-ties excluded: {ties.sum()})"
-        # scores bit-exact where the id sets agree (ordered the same way: descending, low id first)
+        # ids in the same order (descending score, ties to the lower id) where the sets agree;
+        # scores bit-exact except for the rare token whose fp32 router dot product (tensor-
+        # core order vs CPU order) rounds one bf16 logit differently: <= 0.1% of tokens,
+        # within 8 bf16 ulps (one logit ulp moves every renormalised top-8 score)
         ok = agree & ~ties
         np.testing.assert_array_equal(r["topk_ids"][ok], ids[ok])
-        np.testing.assert_array_equal(r["topk_scores"][ok], sc[ok])
+        ds = np.abs(r["topk_scores"][ok].astype(np.int64) - sc[ok].astype(np.int64))
+        off_tokens = np.count_nonzero(ds.max(axis=1) > 0) if ds.size else 0
+        assert off_tokens <= max(1, int(1e-3 * ok.sum())), f"{what}: {off_tokens} tokens with different scores"
+        assert ds.size == 0 or ds.max() <= 8, f"{what}: score differs by {ds.max()} ulps"
         # permutation: canonical stable expert-major order of the device's own ids
         st, sf, off = O.sort_pairs(r["topk_ids"], E)
         np.testing.assert_array_equal(r["expert_offsets"], off)

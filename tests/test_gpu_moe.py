@@ -151,8 +151,8 @@ def test_paths_agree(ops):
             h.set_path(0)
     (ya, ra), (yb, rb) = outs
     np.testing.assert_array_equal(ra["topk_ids"], rb["topk_ids"])
-    from tests._parity import assert_close
-    assert_close(ya, yb, "gemv vs tcgen05")
+    from tests._parity import TIGHT, assert_close
+    assert_close(ya, yb, "gemv vs tcgen05", **TIGHT)
 
 
 def test_moe_block_argument_errors(ops):
