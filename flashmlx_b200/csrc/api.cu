@@ -5,9 +5,12 @@
 // config and stacked weights of LlamaModel::moe_block (model.cpp:750-807, model.h:40-72).
 // Every call is stream-ordered; no call allocates once fm_reserve() has sized the
 // workspace for the largest batch.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -26,7 +29,7 @@ cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
 int max_rows();
 cudaError_t init();
-cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
+cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps);
 }  // namespace tc
 }  // namespace fm
 
@@ -192,12 +195,54 @@ int launch_route(fm_handle* h, RouteArgs& ra, int64_t items) {
   return FM_OK;
 }
 
+// ---------------------------------------------------------------- TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2D row-major tensor [outer, inner] with the 128-byte swizzle; a null base leaves the
+// descriptor zeroed (the kernel never touches it)
+bool encode_2d(CUtensorMap* m, bool u32, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+               uint32_t box_outer) {
+  std::memset(m, 0, sizeof(*m));
+  if (!base) return true;
+  auto fn = tensor_map_encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * (u32 ? 4u : 2u)};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t es[2] = {1, 1};
+  return fn(m, u32 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// codes of a [rows, K] 4-bit matrix: uint32 words, box {4 k-steps, box_rows rows}
+bool encode_codes(CUtensorMap* m, const uint32_t* w, int64_t rows, int K, uint32_t box_rows) {
+  return encode_2d(m, true, w, static_cast<uint64_t>(K / 8), static_cast<uint64_t>(rows), 32, box_rows);
+}
+
+// bf16 activation rows [rows, cols]: one-row boxes for gather4 or 64-row boxes
+bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols, bool gather) {
+  return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, gather ? 1 : 64);
+}
+
 template <int MODE>
-int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05) {
+int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps* maps = nullptr) {
   static const char* names[2][3] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain"},
                                     {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain"}};
+  if (tcgen05 && !maps) return set_err(h, FM_EINVAL, "tcgen05 launch without tensor maps");
   prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
-  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->num_sms, h->stream, ga)
+  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->num_sms, h->stream, ga, *maps)
                                 : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
   prof_end(h);
   if (e != cudaSuccess) return cuda_err(h, e, tcgen05 ? "qgemm_tc launch" : "qgemv launch");
@@ -502,7 +547,24 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ga.out_shared = shared ? at<uint16_t>(h, p.a_shared) : nullptr;
   ga.out_shared_ld = c->shared_inter;
   ga.tab = ra.tab_a;
-  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp);
+  fm::TcMaps maps_gu, maps_dn;
+  if (tcp) {
+    const int Is = c->shared_inter;
+    bool ok = encode_codes(&maps_gu.code[0], w->gate.w, static_cast<int64_t>(E) * I, H, 64) &&
+              encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E) * I, H, 64) &&
+              encode_codes(&maps_gu.code[2], shared ? w->shared_gate.w : nullptr, Is, H, 64) &&
+              encode_codes(&maps_gu.code[3], shared ? w->shared_up.w : nullptr, Is, H, 64) &&
+              encode_act(&maps_gu.act[0], ra.x_perm, T, H, true) &&
+              encode_act(&maps_gu.act[1], shared ? ra.x_perm : nullptr, T, H, false) &&
+              encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E) * H, I, 128) &&
+              encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
+              encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
+              encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
+              encode_act(&maps_dn.act[0], at<uint16_t>(h, p.a_sorted), P, I, false) &&
+              encode_act(&maps_dn.act[1], shared ? at<uint16_t>(h, p.a_shared) : nullptr, T, Is, false);
+    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+  }
+  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
   if (rc) return rc;
   // down (+ combine)
   GemmArgs gd = ga;
@@ -526,7 +588,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   gd.ysh = shared ? at<float>(h, p.ysh) : nullptr;
   gd.y_ld = H;
   gd.tab = ra.tab_b;
-  rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp);
+  rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
   if (rc) return rc;
   // finalize: combine rounding + gated shared expert
   const int64_t n4 = T * H / 4;
@@ -620,7 +682,16 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   ga.out_ld = N;
   ga.tab = ra.tab_a;
   ga.err = err_word(h);
-  return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp);
+  fm::TcMaps maps;
+  if (tcp) {
+    const bool ok = encode_codes(&maps.code[0], w, static_cast<int64_t>(E) * N, K, 128) &&
+                    encode_codes(&maps.code[1], nullptr, 0, K, 128) && encode_codes(&maps.code[2], nullptr, 0, K, 128) &&
+                    encode_codes(&maps.code[3], nullptr, 0, K, 128) &&
+                    encode_act(&maps.act[0], ra.x_perm, ra.x_rows, K, true) &&
+                    encode_act(&maps.act[1], nullptr, 0, K, false);
+    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+  }
+  return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps);
 }
 
 int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w,

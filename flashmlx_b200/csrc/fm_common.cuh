@@ -94,6 +94,30 @@ FM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint3
   }
 }
 
+FM_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// ---------------------------------------------------------------- TMA (no multicast)
+// 2D tiled load of the map's box at element coordinates (x inner, y outer) into this
+// CTA's shared memory, completing `bytes` of transaction count on *bar.
+FM_DEV void tma_load_2d(uint32_t dst, const void* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// four rows (y0..y3) of a one-row-high box, stacked in shared memory
+FM_DEV void tma_gather4(uint32_t dst, const void* map, int x, int y0, int y1, int y2, int y3, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5, %6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---------------------------------------------------------------- cp.async
 FM_DEV void cp_async16(uint32_t dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");

@@ -1,6 +1,7 @@
 // fm_internal.cuh -- data structures shared by the libflashmoe kernels and host code.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 #include "fm_common.cuh"
@@ -41,12 +42,7 @@ struct TileInfo {
   int nrows;   // activation rows in the chunk
 };
 
-FM_DEV TileInfo decode_tile(const TileTable* tab, int tile) {
-  int lo = 0, hi = tab->num_groups - 1;
-  while (lo < hi) {  // largest group with tile_begin <= tile
-    const int mid = (lo + hi + 1) >> 1;
-    if (tab->g[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
-  }
+FM_DEV TileInfo tile_of_group(const TileTable* tab, int lo, int tile) {
   const TileGroup G = tab->g[lo];
   int local = tile - G.tile_begin;
   TileInfo t;
@@ -60,6 +56,25 @@ FM_DEV TileInfo decode_tile(const TileTable* tab, int tile) {
   t.row0 = G.row_begin + ch * G.chunk_rows;
   t.nrows = min(G.chunk_rows, G.rows - ch * G.chunk_rows);
   return t;
+}
+
+FM_DEV TileInfo decode_tile(const TileTable* tab, int tile) {
+  int lo = 0, hi = tab->num_groups - 1;
+  while (lo < hi) {  // largest group with tile_begin <= tile
+    const int mid = (lo + hi + 1) >> 1;
+    if (tab->g[mid].tile_begin <= tile) lo = mid; else hi = mid - 1;
+  }
+  return tile_of_group(tab, lo, tile);
+}
+
+// same, searching a shared-memory copy of the groups' tile_begin values
+FM_DEV TileInfo decode_tile(const TileTable* tab, const int* tile_begin, int ngroups, int tile) {
+  int lo = 0, hi = ngroups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_begin[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  return tile_of_group(tab, lo, tile);
 }
 
 enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
@@ -97,6 +112,19 @@ struct GemmArgs {
   int64_t y_ld;
   const TileTable* tab;
   uint32_t* err;
+};
+
+// TMA descriptors of one tcgen05 expert-product launch (host-encoded per call).
+//   code[0..3]: packed 4-bit weight codes as uint32 [rows, K/8], 128B swizzle, box
+//               {32 words = 4 k-steps, 64 rows (gate/up) | 128 rows (down, plain)}:
+//               gate/up: routed gate, routed up, shared gate, shared up;
+//               down / plain: routed, (unused), shared, (unused)
+//   act[0]:     routed activation rows, bf16 [rows, K], 128B swizzle; box {64, 1} for
+//               gather4 (gate/up, plain) or {64, 64} (down, contiguous rows)
+//   act[1]:     shared-expert activation rows, box {64, 64}
+struct alignas(64) TcMaps {
+  CUtensorMap code[4];
+  CUtensorMap act[2];
 };
 
 // Arguments of the routing kernel.

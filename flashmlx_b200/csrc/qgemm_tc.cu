@@ -11,19 +11,26 @@
 //                 weight and red.adds into the fp32 combine buffer (token-indexed).
 //   plain mode:   quantized_matmul / gather_qmm output, bf16.
 //
-// Roles (544 threads; the producer / consumer roles spread over the 4 SM sub-partitions):
-//   warps 0-7   dequant producers: thread t owns half of A row t/2.  Codes, scales and
-//               biases of k-step s+9 stream into a private cp.async ring (deep enough
-//               to cover HBM latency under load); k-step s is dequantized (bf16 fma of
-//               exact codes) into the 128B-swizzled K-major A stage.
-//   warps 8-11  activation producers: cp.async gather of up to 192 rows x 128 B per
-//               k-step into the swizzled B stage; each thread keeps its 12 rows'
-//               indices in registers (one wide multiply-add per copy).
+// Data movement: the packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows)
+// per load, 128B-swizzled, into a 3-deep ring.  Contiguous activation rows (down
+// projection, shared expert) arrive by TMA in 64-row boxes straight into the UMMA B
+// stage; token-gathered rows are copied with cp.async (the TMA unit's per-instruction
+// cost makes 4-row gather4 boxes too slow at 36-48 instructions per k-step).
+//
+// Roles (512 threads):
+//   warps 0-7   dequant producers: thread t owns half of A row t/2.  Per k-step: one
+//               16-byte code read, bf16 fma of the exact codes with the group's scale
+//               and bias (prefetched in registers a super-step ahead), four 16-byte
+//               stores into the 128B-swizzled K-major A stage.
+//   warp 8      code loader (one lane issues the TMA of each super-step).
+//   warps 9-10  activation loaders: cp.async gather of token rows (24 per thread, row
+//               indices in registers) or TMA of contiguous 64-row boxes.
+//   warp 11     TMEM allocator and single-thread tcgen05.mma issuer (M=128, N<=192,
+//               K=16 x 4 per stage); tcgen05.commit frees stages / publishes tiles.
 //   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
 //               buffered accumulators (2 x 256 columns) overlap the next mainloop.
-//   warp 16     TMEM allocator and single-thread tcgen05.mma issuer (M=128, N<=192,
-//               K=16 x 4 per stage); tcgen05.commit frees stages / publishes tiles.
-// No TMA and no cluster multicast anywhere.  Every wait is bounded.
+// No cluster multicast anywhere; every TMA source is this GPU's own memory.  Every
+// wait is bounded.
 #include "fm_internal.cuh"
 
 namespace fm {
@@ -33,31 +40,38 @@ constexpr int BM = 128;
 constexpr int BN = 192;          // max activation rows per tile (MMA N)
 constexpr int ACC_COLS = 256;    // TMEM columns per accumulator buffer
 constexpr int STAGES = 4;
-constexpr int NRING = 10;
+constexpr int NC = 3;            // code ring depth (super-steps of 4 k-steps)
+constexpr int KS_PER_SS = 4;
 constexpr int A_BYTES = BM * 128;
 constexpr int B_BYTES = BN * 128;
-constexpr int RING_CODES = BM * 32;             // packed codes of one k-step
-constexpr int RING_BYTES = RING_CODES + BM * 8; // + scale pair + bias pair per row
-constexpr int XCHG_HALF = 16 * 64 * 2;          // 16 columns x 64 rows, bf16
+constexpr int C_BYTES = BM * 128;  // 128 rows x 32 words
+constexpr int XCHG_HALF = 16 * 64 * 2;
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr int OFF_RING = OFF_B + STAGES * B_BYTES;
-constexpr int OFF_XCHG = OFF_RING + NRING * RING_BYTES;
-constexpr int OFF_BAR = OFF_XCHG + 4 * XCHG_HALF;  // {gate->up, up->gate} x 2 buffers
+constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
+constexpr int OFF_XCHG = OFF_C + NC * C_BYTES;
+constexpr int OFF_TB = OFF_XCHG + 4 * XCHG_HALF;     // tile_begin of every group
+constexpr int OFF_BAR = OFF_TB + ((kMaxGroups * 4 + 255) / 256) * 256;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
 constexpr int NA = 256;          // dequant-producer threads (two per A row)
-constexpr int NB = 128;          // activation-producer threads
-constexpr int B_ROWS = BN * 8 / NB;  // rows per activation-producer thread (12)
-constexpr int EPI_WARP = 12;     // first of the four epilogue warps
-constexpr int MMA_WARP = 16;
-constexpr int THREADS = (MMA_WARP + 1) * 32;
+constexpr int CODE_WARP = 8;
+constexpr int ACT_WARP = 9;      // two activation-loader warps: 9 and 10
+constexpr int NB = 64;
+constexpr int B_ROWS = BN / 8;   // rows per activation-loader thread (24)
 constexpr int B_LAG = 2;
+constexpr int MMA_WARP = 11;
+constexpr int EPI_WARP = 12;     // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
+constexpr int THREADS = (EPI_WARP + 4) * 32;
 constexpr uint32_t TMEM_COLS = 512;
+
+static_assert(OFF_B % 1024 == 0 && OFF_C % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB aligned stages");
 
 struct Bars {
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
+  uint64_t cfull[NC];
+  uint64_t cempty[NC];
   uint64_t accf[2];
   uint64_t acce[2];
   uint64_t done;
@@ -65,34 +79,45 @@ struct Bars {
   int abort;
   int epi_ok[2][4];
 };
-
-// iterator over (tile, k-step) pairs of this CTA
-struct KIter {
-  int tile;
-  int ks;
-  int nks;
-  TileInfo ti;
-  bool valid;
-};
+static_assert(sizeof(Bars) <= BAR_BYTES, "barrier block");
 
 FM_DEV int tile_ksteps(const GemmArgs& a, const TileInfo& ti, int mode) {
   const int K = (mode == MODE_DOWN && ti.expert < 0) ? a.K_shared : a.K;
   return K / 64;
 }
 
-FM_DEV void kiter_load(KIter& it, const GemmArgs& a, int tile, int ntiles, int mode) {
+// iterator over the (tile, super-step) pairs of this CTA
+struct SIter {
+  int tile;
+  int ss;
+  int nss;
+  int nks;
+  TileInfo ti;
+  bool valid;
+};
+
+// tile table with a shared-memory copy of the groups' first tile ids
+struct TileDir {
+  const TileTable* tab;
+  const int* tb;
+  int ng;
+  FM_DEV TileInfo get(int tile) const { return decode_tile(tab, tb, ng, tile); }
+};
+
+FM_DEV void siter_load(SIter& it, const GemmArgs& a, const TileDir& dir, int tile, int ntiles, int mode) {
   it.tile = tile;
-  it.ks = 0;
+  it.ss = 0;
   it.valid = tile < ntiles;
   if (it.valid) {
-    it.ti = decode_tile(a.tab, tile);
+    it.ti = dir.get(tile);
     it.nks = tile_ksteps(a, it.ti, mode);
+    it.nss = (it.nks + KS_PER_SS - 1) / KS_PER_SS;
   }
 }
 
-FM_DEV void kiter_next(KIter& it, const GemmArgs& a, int ntiles, int mode) {
+FM_DEV void siter_next(SIter& it, const GemmArgs& a, const TileDir& dir, int ntiles, int mode) {
   if (!it.valid) return;
-  if (++it.ks >= it.nks) kiter_load(it, a, it.tile + gridDim.x, ntiles, mode);
+  if (++it.ss >= it.nss) siter_load(it, a, dir, it.tile + gridDim.x, ntiles, mode);
 }
 
 FM_DEV bool wait_done(uint64_t* bar, uint32_t parity, uint32_t* err) {  // ignores abort
@@ -117,8 +142,68 @@ FM_DEV void red_add_v2(float* p, float a, float b) {
   asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 
+// A row t (0..127 of the tile) -> row inside its weight matrix, and the matrix's
+// scale / bias arrays
 template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) {
+FM_DEV void a_row_info(const GemmArgs& a, const TileInfo& ti, int t, int& row, const uint16_t*& S,
+                       const uint16_t*& B) {
+  const bool sh = ti.expert < 0;
+  if (MODE == MODE_GATEUP) {
+    const bool up = t >= 64;
+    row = ti.rb * 64 + (t & 63);
+    S = up ? (sh ? a.ss1 : a.s1) : (sh ? a.ss0 : a.s0);
+    B = up ? (sh ? a.sb1 : a.b1) : (sh ? a.sb0 : a.b0);
+  } else {
+    row = ti.rb * 128 + t;
+    S = sh ? a.ss0 : a.s0;
+    B = sh ? a.sb0 : a.b0;
+  }
+}
+
+// Scale / bias of the group each of the super-step's (up to) 4 k-steps uses for this
+// thread's half row (one group per half k-step for group sizes 32 / 64 / 128).
+template <int MODE>
+FM_DEV void load_scales(const GemmArgs& a, const SIter& it, int t, int half, uint32_t (&sv)[4], uint32_t (&bv)[4]) {
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) sv[kk] = bv[kk] = 0u;
+  if (!it.valid) return;
+  const TileInfo& ti = it.ti;
+  const bool sh = ti.expert < 0;
+  const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
+  const int N = sh ? a.N_shared : a.N;
+  int row;
+  const uint16_t* S;
+  const uint16_t* B;
+  a_row_info<MODE>(a, ti, t, row, S, B);
+  if (row >= N) return;
+  const int gpr = K / a.gs;
+  const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + row;
+  const uint16_t* srow = S + r * gpr;
+  const uint16_t* brow = B ? B + r * gpr : nullptr;
+  if (a.gs == 64 && (gpr & 1) == 0) {
+    // groups g0..g0+3 as two 4-byte aligned pairs
+    const int g0 = it.ss * KS_PER_SS;
+    const uint32_t s0 = g0 < gpr ? __ldg(reinterpret_cast<const uint32_t*>(srow + g0)) : 0u;
+    const uint32_t s1 = g0 + 2 < gpr ? __ldg(reinterpret_cast<const uint32_t*>(srow + g0 + 2)) : 0u;
+    const uint32_t b0 = (brow && g0 < gpr) ? __ldg(reinterpret_cast<const uint32_t*>(brow + g0)) : 0u;
+    const uint32_t b1 = (brow && g0 + 2 < gpr) ? __ldg(reinterpret_cast<const uint32_t*>(brow + g0 + 2)) : 0u;
+    sv[0] = s0 & 0xffffu; sv[1] = s0 >> 16; sv[2] = s1 & 0xffffu; sv[3] = s1 >> 16;
+    bv[0] = b0 & 0xffffu; bv[1] = b0 >> 16; bv[2] = b1 & 0xffffu; bv[3] = b1 >> 16;
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int ks = it.ss * KS_PER_SS + kk;
+      if (ks < it.nks) {
+        const int g = (ks * 64 + 32 * half) / a.gs;
+        sv[kk] = __ldg(srow + g);
+        bv[kk] = brow ? __ldg(brow + g) : 0u;
+      }
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, const __grid_constant__ TcMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
@@ -133,6 +218,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
       mbar_init(&bars->full[s], NA + NB);
       mbar_init(&bars->empty[s], 1);
     }
+    for (int c = 0; c < NC; ++c) {
+      mbar_init(&bars->cfull[c], 1);
+      mbar_init(&bars->cempty[c], NA / 32);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->accf[b], 1);
       mbar_init(&bars->acce[b], 4);
@@ -145,180 +234,182 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
     tmem_alloc(&bars->tmem_base, TMEM_COLS);
     tmem_relinquish();
   }
+  int* s_tb = reinterpret_cast<int*>(smem + OFF_TB);
+  const int ngroups = ntiles > 0 ? min(a.tab->num_groups, kMaxGroups) : 0;
+  for (int i = tid; i < ngroups; i += THREADS) s_tb[i] = a.tab->g[i].tile_begin;
+  const TileDir dir{a.tab, s_tb, ngroups};
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
 
-  if (warp < 8) {
+  if (warp < NA / 32) {
     // ------------------------------------------------------------ dequant producers
     const int t = tid >> 1;    // A row
-    const int half = tid & 1;  // words [4 half, 4 half + 4) of the row's 8 per k-step
-    KIter cur, pf;
-    kiter_load(cur, a, blockIdx.x, ntiles, MODE);
-    pf = cur;
-    int pf_count = 0;
-    auto issue = [&](const KIter& k, int slot) {
-      const TileInfo& ti = k.ti;
-      const bool sh = ti.expert < 0;
-      const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
-      const int N = sh ? a.N_shared : a.N;
-      int row;
-      const uint32_t* W;
-      const uint16_t* S;
-      const uint16_t* B;
-      if (MODE == MODE_GATEUP) {
-        const bool up = t >= 64;
-        row = ti.rb * 64 + (t & 63);
-        W = up ? (sh ? a.sw1 : a.w1) : (sh ? a.sw0 : a.w0);
-        S = up ? (sh ? a.ss1 : a.s1) : (sh ? a.ss0 : a.s0);
-        B = up ? (sh ? a.sb1 : a.b1) : (sh ? a.sb0 : a.b0);
-      } else {
-        row = ti.rb * 128 + t;
-        W = sh ? a.sw0 : a.w0;
-        S = sh ? a.ss0 : a.s0;
-        B = sh ? a.sb0 : a.b0;
-      }
-      if (row < N) {
-        const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + row;
-        const int gpr = K / a.gs;
-        uint8_t* ring = smem + OFF_RING + slot * RING_BYTES;
-        cp_async16(smem_u32(ring + t * 32 + half * 16), W + r * (K / 8) + k.ks * 8 + half * 4);
-        // half 0 fetches the scale pair, half 1 the bias pair
-        const uint16_t* SB = half ? B : S;
-        uint8_t* dst = ring + RING_CODES + t * 8 + half * 4;
-        const int g0 = (k.ks * 64) / a.gs;
-        if (!SB) {
-          *reinterpret_cast<uint32_t*>(dst) = 0u;
-        } else if ((gpr & 1) == 0) {
-          // 4-byte aligned group pair holding this k-step's group(s)
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(SB + r * gpr + (g0 & ~1))
-                       : "memory");
-        } else {
-          // odd group count per row (group size >= 64, one group per k-step): scalar
-          // load, the value duplicated into both halves of the slot
-          *reinterpret_cast<uint32_t*>(dst) = static_cast<uint32_t>(__ldg(SB + r * gpr + g0)) * 0x10001u;
-        }
-      }
-    };
-    // prologue: NRING-1 k-steps in flight
-    for (int d = 0; d < NRING - 1; ++d) {
-      if (pf.valid) {
-        issue(pf, pf_count % NRING);
-        kiter_next(pf, a, ntiles, MODE);
-      }
-      ++pf_count;
-      cp_async_commit();
-    }
-    int it = 0;
-    while (cur.valid) {
-      if (pf.valid) {
-        issue(pf, pf_count % NRING);
-        kiter_next(pf, a, ntiles, MODE);
-      }
-      ++pf_count;
-      cp_async_commit();
-      cp_async_wait<NRING - 1>();
-      // the pair of threads of a row read each other's scale / bias word
-      __syncwarp();
-      const int slot = it % NRING, stage = it % STAGES;
-      if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) break;
+    const int half = tid & 1;  // 16-byte half of the row's 32 bytes of codes per k-step
+    SIter cur;
+    siter_load(cur, a, dir, blockIdx.x, ntiles, MODE);
+    uint32_t sv[4], bv[4];
+    load_scales<MODE>(a, cur, t, half, sv, bv);
+    int cs = 0, it = 0;
+    bool ok = true;
+    while (cur.valid && ok) {
+      SIter nx = cur;
+      siter_next(nx, a, dir, ntiles, MODE);
+      uint32_t nsv[4], nbv[4];
+      load_scales<MODE>(a, nx, t, half, nsv, nbv);  // a super-step ahead
+      const int slot = cs % NC;
+      if (!mbar_wait(&bars->cfull[slot], (cs / NC) & 1, abort_flag, a.err)) break;
       const TileInfo& ti = cur.ti;
       const bool sh = ti.expert < 0;
       const int N = sh ? a.N_shared : a.N;
       const int row = (MODE == MODE_GATEUP) ? ti.rb * 64 + (t & 63) : ti.rb * 128 + t;
-      if (row < N) {
-        const uint8_t* ring = smem + OFF_RING + slot * RING_BYTES;
-        const uint4 w = *reinterpret_cast<const uint4*>(ring + t * 32 + half * 16);
-        const uint32_t sp = *reinterpret_cast<const uint32_t*>(ring + RING_CODES + t * 8);
-        const uint32_t bp = *reinterpret_cast<const uint32_t*>(ring + RING_CODES + t * 8 + 4);
-        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-        uint8_t* As = smem + OFF_A + stage * A_BYTES;
-        const int g0 = (cur.ks * 64) / a.gs;
+      const uint8_t* code = smem + OFF_C + slot * C_BYTES + t * 128;
+      const int nk = min(KS_PER_SS, cur.nks - cur.ss * KS_PER_SS);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int cc = half * 4 + i;
-          const int gi = (cur.ks * 64 + 8 * cc) / a.gs;
-          const int hi = (gi - (g0 & ~1)) & 1;
-          const uint16_t sv = static_cast<uint16_t>(hi ? (sp >> 16) : (sp & 0xffffu));
-          const uint16_t bv = static_cast<uint16_t>(hi ? (bp >> 16) : (bp & 0xffffu));
-          const uint32_t s2u = static_cast<uint32_t>(sv) * 0x10001u, b2u = static_cast<uint32_t>(bv) * 0x10001u;
+      for (int kk = 0; kk < KS_PER_SS; ++kk) {
+        if (kk >= nk) break;
+        const int stage = it % STAGES;
+        if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) {
+          ok = false;
+          break;
+        }
+        if (row < N) {
+          const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + half) ^ (t & 7)) << 4));
+          const uint32_t s2u = sv[kk] * 0x10001u, b2u = bv[kk] * 0x10001u;
           const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
           const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&b2u);
-          uint4 o;
-          o.x = deq_pair(words[i], 0, s2, b2);
-          o.y = deq_pair(words[i], 1, s2, b2);
-          o.z = deq_pair(words[i], 2, s2, b2);
-          o.w = deq_pair(words[i], 3, s2, b2);
-          *reinterpret_cast<uint4*>(As + sw128_off(t, cc)) = o;
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+          uint8_t* As = smem + OFF_A + stage * A_BYTES;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 o;
+            o.x = deq_pair(words[i], 0, s2, b2);
+            o.y = deq_pair(words[i], 1, s2, b2);
+            o.z = deq_pair(words[i], 2, s2, b2);
+            o.w = deq_pair(words[i], 3, s2, b2);
+            *reinterpret_cast<uint4*>(As + sw128_off(t, half * 4 + i)) = o;
+          }
         }
+        fence_proxy_async();
+        mbar_arrive(&bars->full[stage]);
+        ++it;
       }
-      fence_proxy_async();
-      mbar_arrive(&bars->full[stage]);
-      ++it;
-      kiter_next(cur, a, ntiles, MODE);
+      if (!ok) break;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->cempty[slot]);
+      ++cs;
+      cur = nx;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        sv[kk] = nsv[kk];
+        bv[kk] = nbv[kk];
+      }
     }
-    cp_async_wait<0>();
-  } else if (warp < EPI_WARP) {
-    // ------------------------------------------------------------ activation producers
-    const int bt = tid - NA;
-    const int cc = bt & 7, rg = bt >> 3;  // 16-byte chunk of the row, first row (0..15)
-    // swizzled destination of row rg + 16 i: (rg + 16 i) * 128 + ((cc ^ (rg & 7)) << 4)
-    const uint32_t dst0 = static_cast<uint32_t>(rg) * 128u + ((static_cast<uint32_t>(cc ^ (rg & 7))) << 4);
-    int it = 0;
+  } else if (warp == CODE_WARP) {
+    // ------------------------------------------------------------ code loader (TMA)
+    if (lane == 0) {
+      SIter cur;
+      siter_load(cur, a, dir, blockIdx.x, ntiles, MODE);
+      int cs = 0;
+      while (cur.valid) {
+        const int slot = cs % NC;
+        if (!mbar_wait(&bars->cempty[slot], ((cs / NC) & 1) ^ 1, abort_flag, a.err)) break;
+        const TileInfo& ti = cur.ti;
+        const bool sh = ti.expert < 0;
+        const int N = sh ? a.N_shared : a.N;
+        const int erow = sh ? 0 : ti.expert * N;
+        const uint32_t dst = smem_u32(smem + OFF_C + slot * C_BYTES);
+        const int x = cur.ss * (KS_PER_SS * 8);
+        mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);
+        if (MODE == MODE_GATEUP) {
+          const int r0 = erow + ti.rb * 64;
+          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, r0, &bars->cfull[slot]);
+          tma_load_2d(dst + 64 * 128, &maps.code[sh ? 3 : 1], x, r0, &bars->cfull[slot]);
+        } else {
+          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + ti.rb * 128, &bars->cfull[slot]);
+        }
+        ++cs;
+        siter_next(cur, a, dir, ntiles, MODE);
+      }
+    }
+    __syncwarp();
+  } else if (warp == ACT_WARP || warp == ACT_WARP + 1) {
+    // ------------------------------------------------------------ activation loaders
+    const int bt = tid - ACT_WARP * 32;   // 0..63
+    const int cc = bt & 7, rg = bt >> 3;  // 16-byte chunk, first row (rows rg + 8 i)
+    // swizzled destination of row rg + 8 i: (rg + 8 i) * 128 + ((cc ^ rg) << 4)
+    const uint32_t dst0 = static_cast<uint32_t>(rg) * 128u + (static_cast<uint32_t>(cc ^ rg) << 4);
+    int it = 0, pend = 0;  // pend: oldest k-step whose cp.async rows are not yet published
     bool ok = true;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-      const TileInfo ti = decode_tile(a.tab, tile);
+      const TileInfo ti = dir.get(tile);
       const bool sh = ti.expert < 0;
       const int nks = tile_ksteps(a, ti, MODE);
+      const bool gather = (MODE != MODE_DOWN) && !sh;
+      uint32_t srow[B_ROWS];
       const uint16_t* base = sh ? a.act_shared : a.act;
       const uint64_t ld_bytes = static_cast<uint64_t>(sh ? a.act_shared_ld : a.act_ld) * 2u;
-      // source rows of this thread's rows (rg + 16 i), kept in registers
-      uint32_t srow[B_ROWS];
+      if (gather) {
 #pragma unroll
-      for (int i = 0; i < B_ROWS; ++i) {
-        const int r = rg + 16 * i;
-        uint32_t s = 0;
-        if (r < ti.nrows) {
-          const int p = ti.row0 + r;
-          s = static_cast<uint32_t>((MODE == MODE_DOWN || sh) ? p : a.sorted_token[p]);
+        for (int i = 0; i < B_ROWS; ++i) {
+          const int r = rg + 8 * i;
+          srow[i] = (r < ti.nrows) ? static_cast<uint32_t>(a.sorted_token[ti.row0 + r]) : 0u;
         }
-        srow[i] = s;
       }
-      const int nvalid = ti.nrows;
+      const int nblk = (ti.nrows + 63) >> 6;
       for (int ks = 0; ks < nks; ++ks) {
         const int stage = it % STAGES;
         if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) {
           ok = false;
           break;
         }
-        const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES) + dst0;
-        const uint64_t src_k = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(ks * 128 + cc * 16);
+        if (gather) {
+          const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES) + dst0;
+          const uint64_t src_k = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(ks * 128 + cc * 16);
 #pragma unroll
-        for (int i = 0; i < B_ROWS; ++i) {
-          if (rg + 16 * i < nvalid)
-            cp_async16(bs + static_cast<uint32_t>(i) * 2048u,
-                       reinterpret_cast<const void*>(src_k + static_cast<uint64_t>(srow[i]) * ld_bytes));
-        }
-        cp_async_commit();
-        if (it >= B_LAG) {
-          cp_async_wait<B_LAG>();
-          fence_proxy_async();
-          mbar_arrive(&bars->full[(it - B_LAG) % STAGES]);
+          for (int i = 0; i < B_ROWS; ++i) {
+            if (rg + 8 * i < ti.nrows)
+              cp_async16(bs + static_cast<uint32_t>(i) * 1024u,
+                         reinterpret_cast<const void*>(src_k + static_cast<uint64_t>(srow[i]) * ld_bytes));
+          }
+          cp_async_commit();
+          if (it - pend >= B_LAG) {  // publish the k-step B_LAG behind
+            cp_async_wait<B_LAG>();
+            fence_proxy_async();
+            mbar_arrive(&bars->full[pend % STAGES]);
+            ++pend;
+          }
+        } else {
+          if (pend < it) {  // publish every gathered k-step still in flight
+            cp_async_wait<0>();
+            fence_proxy_async();
+            for (; pend < it; ++pend) mbar_arrive(&bars->full[pend % STAGES]);
+          }
+          if (bt == 0) {
+            mbar_arrive_expect_tx(&bars->full[stage], static_cast<uint32_t>(nblk) * 8192u);
+            const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES);
+            const CUtensorMap* map = &maps.act[sh ? 1 : 0];
+            for (int b = 0; b < nblk; ++b)
+              tma_load_2d(bs + b * 8192, map, ks * 64, ti.row0 + b * 64, &bars->full[stage]);
+          } else {
+            mbar_arrive(&bars->full[stage]);
+          }
+          pend = it + 1;
         }
         ++it;
       }
     }
     cp_async_wait<0>();
     fence_proxy_async();
-    for (int j = (it >= B_LAG ? it - B_LAG : 0); j < it; ++j) mbar_arrive(&bars->full[j % STAGES]);
+    for (; pend < it; ++pend) mbar_arrive(&bars->full[pend % STAGES]);
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++lt) {
-        const TileInfo ti = decode_tile(a.tab, tile);
+        const TileInfo ti = dir.get(tile);
         const int nks = tile_ksteps(a, ti, MODE);
         const int buf = lt & 1;
         if (!mbar_wait(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
@@ -353,7 +444,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
     uint16_t* xchg = reinterpret_cast<uint16_t*>(smem + OFF_XCHG);
     int lt = 0, xit = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
-      const TileInfo ti = decode_tile(a.tab, tile);
+      const TileInfo ti = dir.get(tile);
       const bool sh = ti.expert < 0;
       const int N = sh ? a.N_shared : a.N;
       const int buf = lt & 1;
@@ -388,9 +479,9 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
           const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
           const int pn = perm8(n);  // even for n % 8 < 4: (n, n+4) share one 32-bit word
           const int c0 = (q < 2) ? 0 : 16;
+          uint32_t res[16];  // all 16 columns first: independent chains for the scheduler
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
-            const int col = j * 32 + c0 + c;
             float gv, uv;
             if (q < 2) {
               gv = rbf(v[c]);
@@ -399,10 +490,14 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
               gv = bf2f(to_up[c * 64 + r64]);
               uv = rbf(v[16 + c]);
             }
-            const uint32_t mine = f2bf(swiglu1(gv, uv));
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 4);
-            if (col < ti.nrows && (lane & 4) == 0 && n < N)
-              *reinterpret_cast<uint32_t*>(outb + static_cast<int64_t>(ti.row0 + col) * ld + pn) = mine | (other << 16);
+            res[c] = f2bf(swiglu1(gv, uv));
+          }
+          uint16_t* orow = outb + static_cast<int64_t>(ti.row0 + j * 32 + c0) * ld + pn;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, res[c], 4);
+            if (j * 32 + c0 + c < ti.nrows && (lane & 4) == 0 && n < N)
+              *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(c) * ld) = res[c] | (other << 16);
           }
         } else {
           // lanes (2m, 2m+1) hold rows (n, n+1); the even lane finishes column c and
@@ -410,16 +505,19 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
           const int n = ti.rb * 128 + row_in;
           const bool odd = lane & 1;
           const int n0 = n & ~1;
+          // lane c fetches column c's metadata once; the loop reads it by shuffle
+          const int pc = ti.row0 + min(j * 32 + lane, ti.nrows - 1);
+          const float my_score = (MODE == MODE_DOWN && !sh) ? a.sorted_score[pc] : 1.f;
+          const int my_dst = (MODE == MODE_DOWN) ? (sh ? pc : a.sorted_token[pc]) : a.sorted_flat[pc];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             const int col = j * 32 + c + (odd ? 1 : 0);
             const bool colok = col < ti.nrows;
-            const int p = ti.row0 + (colok ? col : 0);
+            const int dst_row = __shfl_sync(0xffffffffu, my_dst, c + (odd ? 1 : 0));
             float mine_c = v[c], mine_c1 = v[c + 1];
             if (MODE == MODE_DOWN && !sh) {  // bf16(bf16(d) * score) per MLX op
-              const int pe = ti.row0 + min(j * 32 + c, ti.nrows - 1);
-              const int po = ti.row0 + min(j * 32 + c + 1, ti.nrows - 1);
-              const float se = a.sorted_score[pe], so = a.sorted_score[po];
+              const float se = __shfl_sync(0xffffffffu, my_score, c);
+              const float so = __shfl_sync(0xffffffffu, my_score, c + 1);
               mine_c = rbf(rbf(mine_c) * se);
               mine_c1 = rbf(rbf(mine_c1) * so);
             }
@@ -430,15 +528,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a) 
             const float hi = odd ? mine_c1 : got2;   // row n0+1
             if (!colok || n0 >= N) continue;
             if (MODE == MODE_DOWN) {
-              if (sh) {
-                red_add_v2(a.ysh + static_cast<int64_t>(p) * a.y_ld + n0, lo, hi);
-              } else {
-                const int tok = a.sorted_token[p];
-                red_add_v2(a.y_acc + static_cast<int64_t>(tok) * a.y_ld + n0, lo, hi);
-              }
+              float* yb = sh ? a.ysh : a.y_acc;
+              red_add_v2(yb + static_cast<int64_t>(dst_row) * a.y_ld + n0, lo, hi);
             } else {
-              *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(a.sorted_flat[p]) * a.out_ld + n0) =
-                  pack_bf16x2(lo, hi);
+              *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(dst_row) * a.out_ld + n0) = pack_bf16x2(lo, hi);
             }
           }
         }
@@ -467,11 +560,11 @@ cudaError_t init() {
   return e;
 }
 
-cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a) {
+cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps) {
   switch (mode) {
-    case MODE_GATEUP: qgemm_tc_kernel<MODE_GATEUP><<<grid, THREADS, SMEM_BYTES, stream>>>(a); break;
-    case MODE_DOWN: qgemm_tc_kernel<MODE_DOWN><<<grid, THREADS, SMEM_BYTES, stream>>>(a); break;
-    default: qgemm_tc_kernel<MODE_PLAIN><<<grid, THREADS, SMEM_BYTES, stream>>>(a); break;
+    case MODE_GATEUP: qgemm_tc_kernel<MODE_GATEUP><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
+    case MODE_DOWN: qgemm_tc_kernel<MODE_DOWN><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
+    default: qgemm_tc_kernel<MODE_PLAIN><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
   }
   return cudaGetLastError();
 }
