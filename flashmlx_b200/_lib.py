@@ -11,7 +11,7 @@ import os
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libflashmoe.so")
 
-FM_OK, FM_EINVAL, FM_EUNSUPPORTED, FM_ECUDA, FM_ENCCL, FM_ETIMEOUT, FM_EDEVICE, FM_ENOMEM = range(8)
+FM_OK, FM_EINVAL, FM_EUNSUPPORTED, FM_ECUDA, FM_ENCCL, FM_ETIMEOUT, FM_EDEVICE, FM_ENOMEM, FM_ETOOLARGE = range(9)
 FM_PATH_AUTO, FM_PATH_GEMV, FM_PATH_TCGEN05 = 0, 1, 2
 
 # every function include/flashmoe.h declares: name -> (restype, argtypes)
@@ -63,6 +63,7 @@ SIGNATURES = {
     "fm_gather_qmm": (_i, [_p, _p, _i64, _i, _i, _p, _p, _p, _i, _i, _p, _p, _i64, _i, _i, _i, _i, _p]),
     "fm_moe_block": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p,
                           C.POINTER(MoEOutputs)]),
+    "fm_moe_block_noalloc": (_i, [_i, _p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p]),
 }
 
 _lib = None

@@ -43,6 +43,7 @@ struct fm_handle {
   int path = FM_PATH_AUTO;
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
+  bool borrowed_ws = false;  // ws is fixed scratch the handle must never grow or free
   // kernel timing (fm_profile_enable)
   bool profile = false;
   struct Pending {
@@ -122,6 +123,7 @@ Plan make_plan(int64_t T, int64_t x_rows, int H, int E, int k, int epad, int ksp
 
 int ensure_ws(fm_handle* h, size_t bytes) {
   if (bytes <= h->ws_bytes) return FM_OK;
+  if (h->borrowed_ws) return set_err(h, FM_ETOOLARGE, "request exceeds the fixed scratch");
   cudaError_t e = cudaStreamSynchronize(h->stream);
   if (e != cudaSuccess) return cuda_err(h, e, "cudaStreamSynchronize");
   if (h->ws) cudaFree(h->ws);
@@ -303,6 +305,7 @@ const char* fm_status_string(int s) {
     case FM_ETIMEOUT: return "device wait timed out";
     case FM_EDEVICE: return "device-side check failed";
     case FM_ENOMEM: return "out of device memory";
+    case FM_ETOOLARGE: return "request needs more than the fixed no-allocation scratch";
     default: return "unknown status";
   }
 }
@@ -707,3 +710,104 @@ int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------- no-allocation entry point
+//
+// fm_moe_block_noalloc runs the same kernels as fm_moe_block, but its scratch (the
+// routing tables, the expert-sorted activations and the fp32 combine buffers) lives in
+// the fixed array below instead of a handle-owned cudaMalloc workspace.  Every GPU
+// that loads this library holds the array until the process exits.  All calls on a
+// device share it and it keeps the last call's contents: each call clears the control
+// block (error word, grid-barrier counters) on its stream before use, and calls whose
+// execution overlaps on the GPU race on the array.
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+struct NoAllocDevice {
+  bool ready = false;
+  int status = FM_OK;
+  uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int num_sms = 0;
+  int route_blocks_per_sm = 0;
+  int gemv_blocks_per_sm = 0;
+};
+constexpr int kNoAllocMaxDevices = 64;
+NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+// One-time set-up for `device`, which must be current: resolve the array's device
+// address (host code only ever sees a host-side stand-in for its name), query the
+// launch parameters fm_create would, and clear the control block.
+int noalloc_setup(int device, NoAllocDevice& d) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  int cc_major = 0, cc_minor = 0;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, device);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, device);
+  if (e == cudaSuccess && !(cc_major == 10 && cc_minor == 0)) return FM_EUNSUPPORTED;
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
+  if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&d.gemv_blocks_per_sm);
+  if (e == cudaSuccess) e = fm::tc::init();
+  if (e == cudaSuccess) e = cudaMemset(p, 0, kCtrlBytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return FM_ECUDA;
+  }
+  d.scratch = static_cast<uint8_t*>(p);
+  d.gemv_blocks_per_sm = std::min(d.gemv_blocks_per_sm, 8);
+  return FM_OK;
+}
+
+}  // namespace
+
+extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_config* c, const fm_moe_weights* w,
+                                    const uint16_t* x, int64_t T, uint16_t* y) {
+  if (device < 0 || device >= kNoAllocMaxDevices || !c || T < 0) return FM_EINVAL;
+  int prev = -1;
+  if (cudaGetDevice(&prev) != cudaSuccess) return FM_ECUDA;
+  if (prev != device && cudaSetDevice(device) != cudaSuccess) {
+    cudaGetLastError();
+    return FM_ECUDA;
+  }
+  NoAllocDevice& d = g_noalloc_dev[device];
+  int rc = FM_OK;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready) {
+      d.status = noalloc_setup(device, d);
+      d.ready = true;
+    }
+    rc = d.status;
+  }
+  if (rc == FM_OK) {
+    fm_handle h;  // borrows the fixed scratch; never grows or frees it
+    h.device = device;
+    h.stream = static_cast<cudaStream_t>(stream);
+    h.num_sms = d.num_sms;
+    h.route_blocks_per_sm = d.route_blocks_per_sm;
+    h.gemv_blocks_per_sm = d.gemv_blocks_per_sm;
+    h.ws = d.scratch;
+    h.ws_bytes = kNoAllocScratchBytes;
+    h.borrowed_ws = true;
+    const int epad = (c->num_experts + 1 + 7) / 8 * 8;
+    const size_t need = make_plan(T, T, c->hidden, c->num_experts, c->top_k, epad, router_ksplit(&h, T, c->hidden),
+                                  c->inter, c->shared_inter, c->shared_inter > 0, true)
+                            .total;
+    if (need > kNoAllocScratchBytes) {
+      rc = FM_ETOOLARGE;
+    } else if (cudaMemsetAsync(d.scratch, 0, kCtrlBytes, h.stream) != cudaSuccess) {
+      cudaGetLastError();
+      rc = FM_ECUDA;
+    } else {
+      rc = fm_moe_block(&h, c, w, x, T, y, nullptr);
+    }
+  }
+  if (prev != device) cudaSetDevice(prev);
+  return rc;
+}

@@ -52,7 +52,8 @@ typedef enum fm_status {
   FM_ENCCL = 4,         /* expert-parallel transport failure */
   FM_ETIMEOUT = 5,      /* a bounded device-side wait ran out */
   FM_EDEVICE = 6,       /* a kernel reported a failed device-side check */
-  FM_ENOMEM = 7         /* workspace allocation failed */
+  FM_ENOMEM = 7,        /* workspace allocation failed */
+  FM_ETOOLARGE = 8      /* fm_moe_block_noalloc: the call needs more than its fixed scratch */
 } fm_status;
 
 typedef struct fm_handle fm_handle;
@@ -168,6 +169,24 @@ FM_API int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int
  * bf16(sigmoid(x.wg) * shared(x)) when the layer has a shared expert. */
 FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* x,
                  int64_t T, uint16_t* y, const fm_moe_outputs* outs);
+
+/* fm_moe_block without a handle and without any device allocation.  No counterpart in
+ * the reference (MLX allocates its own buffers).  It is for callers that cannot let a
+ * library allocate device memory: runtimes whose memory planner or caching allocator
+ * owns all device memory after start-up, and hot paths where cudaMalloc / cudaFree,
+ * which synchronize the device, are not acceptable.  Same arguments and results as
+ * fm_moe_block on `device` / `stream` (a cudaStream_t), but every call uses one fixed
+ * 16 MiB scratch array per GPU that the library holds from load until process exit;
+ * calls that need more (the routing tables, sorted activations and combine buffers
+ * grow with T) return FM_ETOOLARGE before launching anything.  For the
+ * Qwen1.5-MoE-shaped layer that is a few hundred tokens, i.e. decode batches.
+ * The first call on a device resolves the array's device address and queries launch
+ * parameters; make that first call before any stream capture.  All calls share the
+ * array: calls whose execution overlaps on the GPU (other streams, other threads) race
+ * and must be serialized by the caller.  Device-side failures (a bounded wait that ran
+ * out) are not reported by this entry point; fm_moe_block + fm_sync_status report them. */
+FM_API int fm_moe_block_noalloc(int device, void* stream, const fm_moe_config* cfg, const fm_moe_weights* w,
+                                const uint16_t* x, int64_t T, uint16_t* y);
 
 #ifdef __cplusplus
 }
