@@ -254,7 +254,7 @@ int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps
 int router_ksplit(const fm_handle* h, int64_t T, int H) {
   const int64_t ntt = (T + 15) / 16;
   const int64_t target = static_cast<int64_t>(h->num_sms) * 16;
-  int ks = static_cast<int>(std::min<int64_t>(16, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
+  int ks = static_cast<int>(std::min<int64_t>(fm::kRouterMaxKsplit, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
   ks = std::min(ks, std::max(1, H / 128));
   return ks;
 }
@@ -487,8 +487,10 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.x_rows = T;
   ra.zero0 = at<float>(h, p.y_acc);
   ra.zero0_n = T * H;
-  ra.zero1 = shared ? at<float>(h, p.ysh) : nullptr;
-  ra.zero1_n = shared ? T * H : 0;
+  // the tcgen05 down epilogue stores each shared-expert row once; only the GEMV path
+  // (K split of the shared down projection) accumulates into it
+  ra.zero1 = (shared && !tcp) ? at<float>(h, p.ysh) : nullptr;
+  ra.zero1_n = (shared && !tcp) ? T * H : 0;
   ra.topk_ids = at<int32_t>(h, p.topk_ids);
   ra.topk_score = at<float>(h, p.topk_score);
   ra.gate_sig = at<float>(h, p.gate_sig);

@@ -187,6 +187,7 @@ struct RouteArgs {
 };
 
 constexpr int kRouteThreads = 256;  // 8 warps
-constexpr int kRouteChunk = 64;     // tokens per counting chunk
+constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
+constexpr int kRouterMaxKsplit = 16;  // K slices of the router partial logits
 
 }  // namespace fm

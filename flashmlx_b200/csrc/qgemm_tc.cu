@@ -528,8 +528,10 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
             const float hi = odd ? mine_c1 : got2;   // row n0+1
             if (!colok || n0 >= N) continue;
             if (MODE == MODE_DOWN) {
-              float* yb = sh ? a.ysh : a.y_acc;
-              red_add_v2(yb + static_cast<int64_t>(dst_row) * a.y_ld + n0, lo, hi);
+              if (sh)  // each shared-expert element is produced by exactly one tile
+                *reinterpret_cast<float2*>(a.ysh + static_cast<int64_t>(dst_row) * a.y_ld + n0) = make_float2(lo, hi);
+              else
+                red_add_v2(a.y_acc + static_cast<int64_t>(dst_row) * a.y_ld + n0, lo, hi);
             } else {
               *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(dst_row) * a.out_ld + n0) = pack_bf16x2(lo, hi);
             }

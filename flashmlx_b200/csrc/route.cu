@@ -85,7 +85,7 @@ __device__ int block_exclusive_scan(int* a, int n, int* s_tmp /* >= 33 ints */) 
 }
 
 struct RouteSmem {
-  uint32_t mask[kMaxExperts][2];  // token bitmask of the current chunk, per expert
+  uint32_t mask[kMaxExperts];  // token bitmask of the current chunk, per expert
   int offs[kMaxExperts + 1];
   int cnt_a[kMaxGroups + 1];
   int cnt_b[kMaxGroups + 1];
@@ -177,6 +177,23 @@ __device__ void phase_zero(float* p, int64_t n) {
 }
 
 // ------------------------------------------------------------------ phase 2
+static_assert(kRouteChunk <= 32, "one bitmask word per expert and chunk");
+
+// fixed-order sum of the K-split router partials of (token t, logit e); all loads are
+// issued before the first add so their latencies overlap
+FM_DEV float sum_partials(const RouteArgs& a, int64_t t, int e) {
+  float v[kRouterMaxKsplit];
+  const float* p = a.partial + t * a.epad + e;
+  const int64_t stride = a.T * a.epad;
+#pragma unroll
+  for (int ks = 0; ks < kRouterMaxKsplit; ++ks) v[ks] = ks < a.ksplit ? p[ks * stride] : 0.f;
+  float s = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < kRouterMaxKsplit; ++ks)
+    if (ks < a.ksplit) s += v[ks];
+  return s;
+}
+
 __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl) {
   const int lane = threadIdx.x & 31;
   const int E = a.E, k = a.k;
@@ -189,16 +206,12 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
     const int e = lane + 32 * i;
     p[i] = -INFINITY;
     if (e < E) {
-      float s = 0.f;
-      for (int ks = 0; ks < a.ksplit; ++ks) s += a.partial[(static_cast<int64_t>(ks) * a.T + t) * a.epad + e];
-      float l = rbf(s);
+      float l = rbf(sum_partials(a, t, e));
       if (a.router_bias) l = rbf(l + bf2f(a.router_bias[e]));
       p[i] = l;
       mx = fmaxf(mx, l);
     } else if (e == E && a.shared_gate_w) {
-      float s = 0.f;
-      for (int ks = 0; ks < a.ksplit; ++ks) s += a.partial[(static_cast<int64_t>(ks) * a.T + t) * a.epad + e];
-      a.gate_sig[t] = rbf(sigmoid_f(rbf(s)));
+      a.gate_sig[t] = rbf(sigmoid_f(rbf(sum_partials(a, t, e))));
     }
   }
   mx = warp_max(mx);
@@ -265,7 +278,7 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
     a.topk_score[t * k + lane] = sc;
     if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
     if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
-    atomicOr(&sm.mask[se][tl >> 5], 1u << (tl & 31));
+    atomicOr(&sm.mask[se], 1u << tl);
   }
 }
 
@@ -282,7 +295,7 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) 
   a.topk_ids[r] = static_cast<int32_t>(e);
   a.topk_score[r] = 1.f;
   a.row_src[r] = static_cast<int32_t>(xb * a.M + m);
-  atomicOr(&sm.mask[e][tl >> 5], 1u << (tl & 31));
+  atomicOr(&sm.mask[e], 1u << tl);
 }
 
 __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
@@ -290,7 +303,7 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
   const int k = a.do_router ? a.k : 1;
   for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
-    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e][0] = sm.mask[e][1] = 0u;
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e] = 0u;
     __syncthreads();
     for (int i = 0; i < kRouteChunk / 8; ++i) {
       const int tl = warp * (kRouteChunk / 8) + i;
@@ -301,18 +314,14 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
     }
     __syncthreads();
     for (int e = threadIdx.x; e < a.E; e += blockDim.x)
-      a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] = __popc(sm.mask[e][0]) + __popc(sm.mask[e][1]);
+      a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] = __popc(sm.mask[e]);
     const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
     const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
     for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
       const int tl = i / k;
       const int e = a.topk_ids[(t0 + tl) * k + (i % k)];
       if (e < 0) continue;
-      const uint32_t m0 = sm.mask[e][0], m1 = sm.mask[e][1];
-      int rank;
-      if (tl < 32) rank = __popc(m0 & ((1u << tl) - 1u));
-      else rank = __popc(m0) + __popc(m1 & ((1u << (tl - 32)) - 1u));
-      a.pair_rank[(t0 + tl) * k + (i % k)] = rank;
+      a.pair_rank[(t0 + tl) * k + (i % k)] = __popc(sm.mask[e] & ((1u << tl) - 1u));
     }
     __syncthreads();
   }
