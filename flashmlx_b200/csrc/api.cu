@@ -24,12 +24,15 @@ namespace fm {
 __global__ void route_kernel(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
+__global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
+                                      const float* gate_sig, int64_t T, int H, uint16_t* y);
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
 cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
 int max_rows();
 cudaError_t init();
-cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps);
+cudaError_t max_pairs(int* n);
+cudaError_t launch(int mode, int pairs, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps);
 }  // namespace tc
 }  // namespace fm
 
@@ -40,6 +43,7 @@ struct fm_handle {
   int num_sms = 0;
   int route_blocks_per_sm = 0;
   int gemv_blocks_per_sm = 0;
+  int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
@@ -81,11 +85,13 @@ int cuda_err(fm_handle* h, cudaError_t e, const char* what) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 // Per-call workspace carve-up.
 struct Plan {
   size_t total = 0;
   size_t partial, x_perm, topk_ids, topk_score, gate_sig, row_src, chunk_counts, pair_rank, totals, offsets,
-      sorted_token, sorted_score, sorted_flat, tab_a, tab_b, a_sorted, a_shared, y_acc, ysh;
+      sorted_token, sorted_score, sorted_flat, pair_pos, tab_a, tab_b, a_sorted, a_shared, y_acc, ysh, y_pairs, ysh16;
   size_t add(size_t bytes) {
     const size_t off = total;
     total = align_up(total + bytes, 256);
@@ -93,8 +99,10 @@ struct Plan {
   }
 };
 
+// tcp: the expert products run on the tcgen05 path (per-pair bf16 down rows combined
+// by finalize_pairs_kernel) rather than the GEMV path (fp32 atomic combine buffers)
 Plan make_plan(int64_t T, int64_t x_rows, int H, int E, int k, int epad, int ksplit, int64_t a_cols,
-               int64_t ash_cols, bool shared, bool moe) {
+               int64_t ash_cols, bool shared, bool moe, bool tcp) {
   Plan p;
   p.total = kCtrlBytes;
   const int64_t P = T * k;
@@ -112,12 +120,15 @@ Plan make_plan(int64_t T, int64_t x_rows, int H, int E, int k, int epad, int ksp
   p.sorted_token = p.add(sizeof(int32_t) * P);
   p.sorted_score = p.add(sizeof(float) * P);
   p.sorted_flat = p.add(sizeof(int32_t) * P);
+  p.pair_pos = p.add(moe && tcp ? sizeof(int32_t) * P : 0);
   p.tab_a = p.add(sizeof(TileTable));
   p.tab_b = p.add(moe ? sizeof(TileTable) : 0);
   p.a_sorted = p.add(moe ? sizeof(uint16_t) * P * a_cols : 0);
   p.a_shared = p.add(moe && shared ? sizeof(uint16_t) * T * ash_cols : 0);
-  p.y_acc = p.add(moe ? sizeof(float) * T * H : 0);
-  p.ysh = p.add(moe && shared ? sizeof(float) * T * H : 0);
+  p.y_acc = p.add(moe && !tcp ? sizeof(float) * T * H : 0);
+  p.ysh = p.add(moe && shared && !tcp ? sizeof(float) * T * H : 0);
+  p.y_pairs = p.add(moe && tcp ? sizeof(uint16_t) * P * H : 0);
+  p.ysh16 = p.add(moe && shared && tcp ? sizeof(uint16_t) * T * H : 0);
   return p;
 }
 
@@ -244,7 +255,7 @@ int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps
                                     {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain"}};
   if (tcgen05 && !maps) return set_err(h, FM_EINVAL, "tcgen05 launch without tensor maps");
   prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
-  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->num_sms, h->stream, ga, *maps)
+  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->tc_pairs, h->stream, ga, *maps)
                                 : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
   prof_end(h);
   if (e != cudaSuccess) return cuda_err(h, e, tcgen05 ? "qgemm_tc launch" : "qgemv launch");
@@ -330,6 +341,8 @@ int fm_create(fm_handle** out, int device, void* stream) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&h->gemv_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
+  if (e == cudaSuccess) e = fm::tc::max_pairs(&h->tc_pairs);
+  if (e == cudaSuccess && h->tc_pairs < 1) e = cudaErrorInvalidConfiguration;
   if (e != cudaSuccess) {
     cudaGetLastError();
     delete h;
@@ -444,10 +457,13 @@ int fm_reserve(fm_handle* h, const fm_moe_config* c, int64_t max_tokens) {
   if (!h || !c || max_tokens < 0) return FM_EINVAL;
   const int epad = (c->num_experts + 1 + 7) / 8 * 8;
   const int ksplit = router_ksplit(h, max_tokens, c->hidden);
-  Plan p = make_plan(max_tokens, max_tokens, c->hidden, c->num_experts, c->top_k, epad, 16, c->inter,
-                     c->shared_inter, c->shared_inter > 0, true);
   (void)ksplit;
-  return ensure_ws(h, p.total);
+  size_t need = 0;
+  for (bool tcp : {false, true})
+    need = std::max(need, make_plan(max_tokens, max_tokens, c->hidden, c->num_experts, c->top_k, epad, 16, c->inter,
+                                    c->shared_inter, c->shared_inter > 0, true, tcp)
+                              .total);
+  return ensure_ws(h, need);
 }
 
 int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
@@ -456,6 +472,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   int rc = check_moe(h, c, w);
   if (rc) return rc;
   if (T < 0 || (T > 0 && (!x || !y))) return set_err(h, FM_EINVAL, "bad x / y / T");
+  if (!aligned16(x) || !aligned16(y)) return set_err(h, FM_EINVAL, "x and y must be 16-byte aligned");
   if (T == 0) return FM_OK;
   if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
   const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k;
@@ -463,10 +480,10 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   const int epad = (E + 1 + 7) / 8 * 8;
   const int ksplit = router_ksplit(h, T, H);
   const int64_t P = T * k;
-  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true);
+  const bool tcp = use_tc(h, P, E);
+  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true, tcp);
   rc = ensure_ws(h, p.total);
   if (rc) return rc;
-  const bool tcp = use_tc(h, P, E);
 
   RouteArgs ra;
   std::memset(&ra, 0, sizeof(ra));
@@ -485,10 +502,10 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.partial = at<float>(h, p.partial);
   ra.x_perm = at<uint16_t>(h, p.x_perm);
   ra.x_rows = T;
-  ra.zero0 = at<float>(h, p.y_acc);
-  ra.zero0_n = T * H;
-  // the tcgen05 down epilogue stores each shared-expert row once; only the GEMV path
-  // (K split of the shared down projection) accumulates into it
+  // the GEMV path accumulates into fp32 combine buffers; the tcgen05 path stores
+  // every output row once and needs no clearing
+  ra.zero0 = tcp ? nullptr : at<float>(h, p.y_acc);
+  ra.zero0_n = tcp ? 0 : T * H;
   ra.zero1 = (shared && !tcp) ? at<float>(h, p.ysh) : nullptr;
   ra.zero1_n = (shared && !tcp) ? T * H : 0;
   ra.topk_ids = at<int32_t>(h, p.topk_ids);
@@ -502,12 +519,14 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.sorted_token = at<int32_t>(h, p.sorted_token);
   ra.sorted_score = at<float>(h, p.sorted_score);
   ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.pair_pos = tcp ? at<int32_t>(h, p.pair_pos) : nullptr;
   ra.tab_a = at<TileTable>(h, p.tab_a);
   ra.tab_b = at<TileTable>(h, p.tab_b);
-  ra.a_rows_per_block = 64;
+  ra.a_rows_per_block = tcp ? 128 : 64;
   ra.a_n = I;
   ra.a_n_shared = c->shared_inter;
   ra.b_n = H;
+  ra.b_rows_per_block = tcp ? 256 : 128;
   ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, I));
@@ -589,17 +608,25 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   gd.act_shared_ld = c->shared_inter;
   gd.out = nullptr;
   gd.out_shared = nullptr;
-  gd.y_acc = at<float>(h, p.y_acc);
-  gd.ysh = shared ? at<float>(h, p.ysh) : nullptr;
+  gd.y_acc = tcp ? nullptr : at<float>(h, p.y_acc);
+  gd.ysh = (shared && !tcp) ? at<float>(h, p.ysh) : nullptr;
+  gd.y_pairs = tcp ? at<uint16_t>(h, p.y_pairs) : nullptr;
+  gd.ysh16 = (shared && tcp) ? at<uint16_t>(h, p.ysh16) : nullptr;
   gd.y_ld = H;
   gd.tab = ra.tab_b;
   rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
   if (rc) return rc;
   // finalize: combine rounding + gated shared expert
-  const int64_t n4 = T * H / 4;
-  const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
   prof_begin(h, "finalize");
-  fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
+  if (tcp) {
+    const int64_t n8 = T * H / 8;
+    const int fb = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+    fm::finalize_pairs_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
+  } else {
+    const int64_t n4 = T * H / 4;
+    const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+    fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
+  }
   prof_end(h);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(h, e, "finalize launch");
@@ -619,12 +646,13 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   if (!lhs_indices && B % x_batches != 0) return set_err(h, FM_EINVAL, "x batch does not broadcast against rhs");
   if (B == 0) return FM_OK;
   if (!x || !w || !scales || !out || (!rhs_indices && E != 1)) return set_err(h, FM_EINVAL, "null pointer");
+  if (!aligned16(x) || !aligned16(out)) return set_err(h, FM_EINVAL, "x and out must be 16-byte aligned");
   if (K % 64 || N % 16) return set_err(h, FM_EUNSUPPORTED, "K must be a multiple of 64 and N of 16");
   const int64_t rows = B * M;
   if (rows > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
   bool tcp = use_tc(h, rows, E);
   if (K % 128) tcp = true;  // the GEMV path works in 128-wide K chunks
-  Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false);
+  Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false, tcp);
   int rc = ensure_ws(h, p.total);
   if (rc) return rc;
 
@@ -658,7 +686,7 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
   ra.tab_a = at<TileTable>(h, p.tab_a);
   ra.tab_b = nullptr;
-  ra.a_rows_per_block = 128;
+  ra.a_rows_per_block = tcp ? 256 : 128;
   ra.a_n = N;
   ra.a_n_shared = 0;
   ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
@@ -735,6 +763,7 @@ struct NoAllocDevice {
   int num_sms = 0;
   int route_blocks_per_sm = 0;
   int gemv_blocks_per_sm = 0;
+  int tc_pairs = 0;
 };
 constexpr int kNoAllocMaxDevices = 64;
 NoAllocDevice g_noalloc_dev[kNoAllocMaxDevices];
@@ -755,6 +784,8 @@ int noalloc_setup(int device, NoAllocDevice& d) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&d.gemv_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
+  if (e == cudaSuccess) e = fm::tc::max_pairs(&d.tc_pairs);
+  if (e == cudaSuccess && d.tc_pairs < 1) e = cudaErrorInvalidConfiguration;
   if (e == cudaSuccess) e = cudaMemset(p, 0, kCtrlBytes);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
@@ -794,12 +825,14 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
     h.num_sms = d.num_sms;
     h.route_blocks_per_sm = d.route_blocks_per_sm;
     h.gemv_blocks_per_sm = d.gemv_blocks_per_sm;
+    h.tc_pairs = d.tc_pairs;
     h.ws = d.scratch;
     h.ws_bytes = kNoAllocScratchBytes;
     h.borrowed_ws = true;
     const int epad = (c->num_experts + 1 + 7) / 8 * 8;
     const size_t need = make_plan(T, T, c->hidden, c->num_experts, c->top_k, epad, router_ksplit(&h, T, c->hidden),
-                                  c->inter, c->shared_inter, c->shared_inter > 0, true)
+                                  c->inter, c->shared_inter, c->shared_inter > 0, true,
+                                  use_tc(&h, T * c->top_k, c->num_experts))
                             .total;
     if (need > kNoAllocScratchBytes) {
       rc = FM_ETOOLARGE;

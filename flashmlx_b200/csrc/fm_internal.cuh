@@ -107,8 +107,10 @@ struct GemmArgs {
   uint16_t* out_shared;   // gate/up: a_shared [T, N_shared]
   int64_t out_ld;
   int64_t out_shared_ld;
-  float* y_acc;           // down: [T, H] fp32, sum_k bf16(d*score)
-  float* ysh;             // down: [T, H] fp32 shared-expert sums
+  float* y_acc;           // down (GEMV): [T, H] fp32, sum_k bf16(d*score)
+  float* ysh;             // down (GEMV): [T, H] fp32 shared-expert sums
+  uint16_t* y_pairs;      // down (tcgen05): [P, H] bf16(bf16(d)*score), expert-major rows
+  uint16_t* ysh16;        // down (tcgen05): [T, H] bf16 shared-expert rows
   int64_t y_ld;
   const TileTable* tab;
   uint32_t* err;
@@ -165,13 +167,15 @@ struct RouteArgs {
   int32_t* sorted_token;        // [T*k]
   float* sorted_score;          // [T*k]
   int32_t* sorted_flat;         // [T*k]
+  int32_t* pair_pos;            // [T*k] expert-major position of pair (t, j), or NULL
   // tile tables
   TileTable* tab_a;             // gate/up (or plain)
   TileTable* tab_b;             // down (NULL in plain mode)
-  int a_rows_per_block;         // 64 gate/up, 128 plain
+  int a_rows_per_block;         // GEMV: 64 gate/up, 128 plain; tcgen05 pairs: 128, 256
   int a_n;                      // routed output rows of table a
   int a_n_shared;               // shared output rows of table a (0 = no shared group)
   int b_n;                      // output rows of table b (H)
+  int b_rows_per_block;         // GEMV 128, tcgen05 pairs 256
   int chunk_max;                // token rows per chunk cap (32 GEMV, 256 tcgen05)
   int chunk_align;              // chunk size granularity (8 GEMV, 16 tcgen05)
   int b_ksplit_shared;          // K splits of the shared down group (GEMV)

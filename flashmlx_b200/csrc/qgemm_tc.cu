@@ -1,56 +1,74 @@
-// qgemm_tc.cu -- grouped 4-bit expert GEMM on the 5th-generation tensor cores.
+// qgemm_tc.cu -- grouped 4-bit expert GEMM on the 5th-generation tensor cores, run by
+// CTA pairs (2-CTA clusters) issuing tcgen05.mma.cta_group::2.
 //
 // Replaces mx::gather_qmm (sorted, model.cpp:703-721) and mx::quantized_matmul
-// (model.cpp:741-747) for prefill-sized batches.  One persistent CTA per SM walks a
-// device-built tile table (expert / shared-expert group, 128-row output block, chunk
-// of <= 192 activation rows).  D[128 x N] accumulates in TMEM:
-//   gate/up mode: A rows 0..63 = gate rows, 64..127 = the same up rows, so one
-//                 accumulator holds g and u of a row block; the epilogue applies
-//                 silu(g)*u and writes the pair-permuted activation rows for down.
-//   down mode:    A = 128 down rows; the epilogue rounds d, scales by the routing
-//                 weight and red.adds into the fp32 combine buffer (token-indexed).
-//   plain mode:   quantized_matmul / gather_qmm output, bf16.
+// (model.cpp:741-747) for prefill-sized batches.  Each pair walks a device-built tile
+// table (expert / shared-expert group, 256-row weight block, chunk of <= 256
+// activation rows).  One tile is D[256 x N] = A[256 x K] * B[N x K]^T:
+//   A (dequantized weights): rows 0..127 in CTA 0's shared memory, 128..255 in CTA 1's;
+//   B (activation rows):     rows 0..N/2-1 in CTA 0, N/2..N-1 in CTA 1;
+//   D (fp32, TMEM):          CTA r holds its 128 A rows x all N columns.
+// Per SM and 64-wide k-step that is 4 KB of codes and <= 16 KB of activations from
+// L2 for 4.2 MFLOP, half the L2 bytes per FLOP of a one-CTA 128 x 192 tile, which
+// the L2 -> SM bandwidth (~11 TB/s on B200) could not feed.
+//   gate/up mode: CTA r's A rows 0..63 = gate rows f0 + 64r .. +63, rows 64..127 =
+//                 the same up rows (f0 = 128 x block), so one CTA's accumulator holds
+//                 g and u of a row; the epilogue applies silu(g)*u and stores the
+//                 pair-permuted activation rows for down.
+//   down mode:    A = 128 down rows per CTA; the epilogue stores bf16(bf16(d)*score)
+//                 per routed pair (expert-major rows; the combine kernel sums the k
+//                 pairs of a token in a fixed order) or bf16(d) per shared row.
+//   plain mode:   quantized_matmul / gather_qmm output rows, bf16.
 //
-// Data movement: the packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows)
-// per load, 128B-swizzled, into a 3-deep ring.  Contiguous activation rows (down
-// projection, shared expert) arrive by TMA in 64-row boxes straight into the UMMA B
-// stage; token-gathered rows are copied with cp.async (the TMA unit's per-instruction
-// cost makes 4-row gather4 boxes too slow at 36-48 instructions per k-step).
+// Data movement: packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows) per
+// load, 128B-swizzled, into a 3-deep ring per CTA.  Contiguous activation rows arrive
+// by TMA in 64-row boxes straight into the UMMA B stage, completing on the leader
+// CTA's stage barrier; token-gathered rows are copied with cp.async.  Outputs go
+// through a shared-memory staging tile and leave as coalesced 16-byte stores.
 //
-// Roles (512 threads):
+// Roles (512 threads per CTA):
 //   warps 0-7   dequant producers: thread t owns half of A row t/2.  Per k-step: one
 //               16-byte code read, bf16 fma of the exact codes with the group's scale
-//               and bias (prefetched in registers a super-step ahead), four 16-byte
-//               stores into the 128B-swizzled K-major A stage.
+//               and bias (prefetched a super-step ahead), four 16-byte stores into the
+//               128B-swizzled K-major A stage; one arrival per warp on the leader's
+//               stage barrier.
 //   warp 8      code loader (one lane issues the TMA of each super-step).
-//   warps 9-10  activation loaders: cp.async gather of token rows (24 per thread, row
-//               indices in registers) or TMA of contiguous 64-row boxes.
-//   warp 11     TMEM allocator and single-thread tcgen05.mma issuer (M=128, N<=192,
-//               K=16 x 4 per stage); tcgen05.commit frees stages / publishes tiles.
+//   warps 9-10  activation loaders (this CTA's half of the tile's rows).
+//   warp 11     TMEM allocation (both CTAs) and, in the leader CTA only, the single
+//               tcgen05.mma issuer (M=256, N<=256, K=16 x 4 per stage); commits free
+//               the stage / publish the accumulator in both CTAs.
 //   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
 //               buffered accumulators (2 x 256 columns) overlap the next mainloop.
-// No cluster multicast anywhere; every TMA source is this GPU's own memory.  Every
-// wait is bounded.
+// Cross-CTA signalling: mbarrier arrivals on the peer's barriers through mapa
+// addresses, tcgen05.commit to each CTA's barrier, and the 2-CTA form of the TMA
+// load whose completion lands on the leader's barrier.  No load is multicast; every
+// TMA source is this GPU's own memory.  Every wait is bounded.
 #include "fm_internal.cuh"
 
 namespace fm {
 namespace tc {
 
-constexpr int BM = 128;
-constexpr int BN = 192;          // max activation rows per tile (MMA N)
+constexpr int BM = 128;          // A rows per CTA (M = 256 per pair)
+constexpr int BN = 256;          // max activation rows per pair tile (MMA N)
+constexpr int BNH = BN / 2;      // B rows per CTA
 constexpr int ACC_COLS = 256;    // TMEM columns per accumulator buffer
 constexpr int STAGES = 4;
 constexpr int NC = 3;            // code ring depth (super-steps of 4 k-steps)
 constexpr int KS_PER_SS = 4;
 constexpr int A_BYTES = BM * 128;
-constexpr int B_BYTES = BN * 128;
+constexpr int B_BYTES = BNH * 128;
 constexpr int C_BYTES = BM * 128;  // 128 rows x 32 words
-constexpr int XCHG_HALF = 16 * 64 * 2;
+constexpr int SC_GROUPS = 8;                     // max quant groups per row per super-step (gs 32)
+constexpr int SC_BYTES = 2 * BM * SC_GROUPS * 2; // scales + biases of one code slot
+constexpr int XCHG_BYTES = 2 * 2 * 16 * 64 * 2;  // gate/up halves, double-buffered
+constexpr int STG_BYTES = 32 * 256;              // 32 rows x 128 bf16 outputs
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
 constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
-constexpr int OFF_XCHG = OFF_C + NC * C_BYTES;
-constexpr int OFF_TB = OFF_XCHG + 4 * XCHG_HALF;     // tile_begin of every group
+constexpr int OFF_SC = OFF_C + NC * C_BYTES;
+constexpr int OFF_XCHG = OFF_SC + NC * SC_BYTES;
+constexpr int OFF_STG = OFF_XCHG + XCHG_BYTES;   // two staging tiles
+constexpr int OFF_TB = OFF_STG + 2 * STG_BYTES;  // tile_begin of every group
 constexpr int OFF_BAR = OFF_TB + ((kMaxGroups * 4 + 255) / 256) * 256;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
@@ -58,35 +76,130 @@ constexpr int NA = 256;          // dequant-producer threads (two per A row)
 constexpr int CODE_WARP = 8;
 constexpr int ACT_WARP = 9;      // two activation-loader warps: 9 and 10
 constexpr int NB = 64;
-constexpr int B_ROWS = BN / 8;   // rows per activation-loader thread (24)
+constexpr int B_ROWS = BNH / 8;  // rows per activation-loader thread (16)
 constexpr int B_LAG = 2;
 constexpr int MMA_WARP = 11;
 constexpr int EPI_WARP = 12;     // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
 constexpr int THREADS = (EPI_WARP + 4) * 32;
 constexpr uint32_t TMEM_COLS = 512;
+constexpr int FULL_ARRIVALS = 2 * (NA / 32 + NB / 32);  // per stage, both CTAs
+constexpr int CFULL_ARRIVALS = 1 + 32;  // code-loader lane 0 (meta + expect_tx) + one per lane's scale copies
+constexpr int ACCE_ARRIVALS = 2 * 4;                     // epilogue warps of both CTAs
 
 static_assert(OFF_B % 1024 == 0 && OFF_C % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB aligned stages");
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Bars {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[STAGES];   // leader: A and B of both CTAs ready
+  uint64_t empty[STAGES];  // each CTA: the MMAs reading the stage are done
   uint64_t cfull[NC];
   uint64_t cempty[NC];
-  uint64_t accf[2];
-  uint64_t acce[2];
+  uint64_t accf[2];        // each CTA: accumulator buffer complete
+  uint64_t acce[2];        // leader: accumulator buffer drained by both epilogues
   uint64_t done;
   uint32_t tmem_base;
   int abort;
   int epi_ok[2][4];
+  int slot_nk[NC];    // k-steps in the code slot's super-step; 0 marks the end of work
+  int slot_vlim[NC];  // A rows of this CTA inside the weight matrix (per 64-row half in gate/up)
 };
 static_assert(sizeof(Bars) <= BAR_BYTES, "barrier block");
+
+// ---------------------------------------------------------------- cluster helpers
+FM_DEV uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+FM_DEV uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+FM_DEV uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory location in CTA `rank`
+FM_DEV uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+FM_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrival on a barrier of either CTA of the pair, with the default (.release, .cta)
+// semantics: the data it publishes is read by the tensor core through the async
+// proxy (after fence.proxy.async) or by TMA completion, not by the peer's threads,
+// and a .cluster-scope release costs ~900 cycles per arrival on B200.
+FM_DEV void mbar_arrive_cluster(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+FM_DEV void mbar_arrive_expect_tx_cluster(uint32_t caddr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(caddr), "r"(bytes) : "memory");
+}
+// 2D TMA into this CTA's shared memory whose completion is counted on the pair
+// leader's barrier (caddr: shared::cluster address of that barrier)
+FM_DEV void tma_load_2d_pair(uint32_t dst, const void* map, int x, int y, uint32_t caddr) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(caddr)
+      : "memory");
+}
+
+// 4-byte cp.async that reads src_bytes (4 or 0) and zero-fills the rest
+FM_DEV void cp_async4(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// one arrival on *bar once every cp.async this thread issued so far has landed
+FM_DEV void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+FM_DEV void mbar_arrive_cnt(uint64_t* bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(n) : "memory");
+}
+
+// ---------------------------------------------------------------- 2-CTA tcgen05
+FM_DEV void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {  // one warp in each CTA
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+FM_DEV void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+FM_DEV void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem, both CTAs] (+)= A[smem, 256 rows over the pair] * B[smem, N rows over the pair]^T
+FM_DEV void umma2_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+// arrive once on the barrier at caddr (either CTA of the pair) when all previously
+// issued tcgen05.mma of this thread complete
+FM_DEV void umma2_commit(uint32_t caddr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(caddr)
+               : "memory");
+}
 
 FM_DEV int tile_ksteps(const GemmArgs& a, const TileInfo& ti, int mode) {
   const int K = (mode == MODE_DOWN && ti.expert < 0) ? a.K_shared : a.K;
   return K / 64;
 }
 
-// iterator over the (tile, super-step) pairs of this CTA
+// MMA N of a tile: rows rounded up to 16 (8 per CTA half)
+FM_DEV int tile_nmma(int nrows) { return max(16, (nrows + 15) & ~15); }
+
+// iterator over the (tile, super-step) pairs of this pair
 struct SIter {
   int tile;
   int ss;
@@ -115,9 +228,9 @@ FM_DEV void siter_load(SIter& it, const GemmArgs& a, const TileDir& dir, int til
   }
 }
 
-FM_DEV void siter_next(SIter& it, const GemmArgs& a, const TileDir& dir, int ntiles, int mode) {
+FM_DEV void siter_next(SIter& it, const GemmArgs& a, const TileDir& dir, int ntiles, int stride, int mode) {
   if (!it.valid) return;
-  if (++it.ss >= it.nss) siter_load(it, a, dir, it.tile + gridDim.x, ntiles, mode);
+  if (++it.ss >= it.nss) siter_load(it, a, dir, it.tile + stride, ntiles, mode);
 }
 
 FM_DEV bool wait_done(uint64_t* bar, uint32_t parity, uint32_t* err) {  // ignores abort
@@ -133,106 +246,130 @@ FM_DEV bool wait_done(uint64_t* bar, uint32_t parity, uint32_t* err) {  // ignor
 
 // silu(g) * u with the bf16 rounding of each MLX op (model.cpp:14-25); g, u already bf16
 FM_DEV float swiglu1(float g, float u) {
-  const float sg = rbf(__frcp_rn(1.0f + __expf(-g)));
+  const float sg = rbf(__fdividef(1.0f, 1.0f + __expf(-g)));
   const float h = rbf(g * sg);
   return rbf(h * u);
 }
 
-FM_DEV void red_add_v2(float* p, float a, float b) {
-  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
-}
-
-// A row t (0..127 of the tile) -> row inside its weight matrix, and the matrix's
-// scale / bias arrays
+// A row t (0..127 of this CTA's half) -> row inside its weight matrix, and the
+// matrix's scale / bias arrays
 template <int MODE>
-FM_DEV void a_row_info(const GemmArgs& a, const TileInfo& ti, int t, int& row, const uint16_t*& S,
+FM_DEV void a_row_info(const GemmArgs& a, const TileInfo& ti, int rank, int t, int& row, const uint16_t*& S,
                        const uint16_t*& B) {
   const bool sh = ti.expert < 0;
   if (MODE == MODE_GATEUP) {
     const bool up = t >= 64;
-    row = ti.rb * 64 + (t & 63);
+    row = ti.rb * 128 + rank * 64 + (t & 63);
     S = up ? (sh ? a.ss1 : a.s1) : (sh ? a.ss0 : a.s0);
     B = up ? (sh ? a.sb1 : a.b1) : (sh ? a.sb0 : a.b0);
   } else {
-    row = ti.rb * 128 + t;
+    row = ti.rb * 256 + rank * 128 + t;
     S = sh ? a.ss0 : a.s0;
     B = sh ? a.sb0 : a.b0;
   }
 }
 
-// Scale / bias of the group each of the super-step's (up to) 4 k-steps uses for this
-// thread's half row (one group per half k-step for group sizes 32 / 64 / 128).
+// The code-loader warp stages the scales and biases of one super-step (256 K values:
+// G = 256 / gs groups) of this CTA's 128 A rows into a code slot: sc[t][g], bi[t][g]
+// (u16, row stride SC_GROUPS).  Rows outside the matrix and groups past the row end
+// are zero-filled.  Aligned rows (an even number of groups per row) use 4-byte
+// cp.async tracked by the slot barrier; odd rows fall back to 2-byte loads + stores.
+// Every lane then counts one arrival on cfull.
 template <int MODE>
-FM_DEV void load_scales(const GemmArgs& a, const SIter& it, int t, int half, uint32_t (&sv)[4], uint32_t (&bv)[4]) {
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) sv[kk] = bv[kk] = 0u;
-  if (!it.valid) return;
+FM_DEV void stage_scales(const GemmArgs& a, const SIter& it, int rank, int lane, uint16_t* sc, uint16_t* bi,
+                         uint64_t* cfull) {
   const TileInfo& ti = it.ti;
   const bool sh = ti.expert < 0;
   const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
   const int N = sh ? a.N_shared : a.N;
-  int row;
-  const uint16_t* S;
-  const uint16_t* B;
-  a_row_info<MODE>(a, ti, t, row, S, B);
-  if (row >= N) return;
   const int gpr = K / a.gs;
-  const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + row;
-  const uint16_t* srow = S + r * gpr;
-  const uint16_t* brow = B ? B + r * gpr : nullptr;
-  if (a.gs == 64 && (gpr & 1) == 0) {
-    // groups g0..g0+3 as two 4-byte aligned pairs
-    const int g0 = it.ss * KS_PER_SS;
-    const uint32_t s0 = g0 < gpr ? __ldg(reinterpret_cast<const uint32_t*>(srow + g0)) : 0u;
-    const uint32_t s1 = g0 + 2 < gpr ? __ldg(reinterpret_cast<const uint32_t*>(srow + g0 + 2)) : 0u;
-    const uint32_t b0 = (brow && g0 < gpr) ? __ldg(reinterpret_cast<const uint32_t*>(brow + g0)) : 0u;
-    const uint32_t b1 = (brow && g0 + 2 < gpr) ? __ldg(reinterpret_cast<const uint32_t*>(brow + g0 + 2)) : 0u;
-    sv[0] = s0 & 0xffffu; sv[1] = s0 >> 16; sv[2] = s1 & 0xffffu; sv[3] = s1 >> 16;
-    bv[0] = b0 & 0xffffu; bv[1] = b0 >> 16; bv[2] = b1 & 0xffffu; bv[3] = b1 >> 16;
-  } else {
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int ks = it.ss * KS_PER_SS + kk;
-      if (ks < it.nks) {
-        const int g = (ks * 64 + 32 * half) / a.gs;
-        sv[kk] = __ldg(srow + g);
-        bv[kk] = brow ? __ldg(brow + g) : 0u;
+  const int G = 256 / a.gs;
+  const int g0 = it.ss * G;
+  const bool aligned = (gpr & 1) == 0;
+#pragma unroll 1
+  for (int i = 0; i < 4; ++i) {
+    const int t = lane + 32 * i;
+    int row;
+    const uint16_t* S;
+    const uint16_t* B;
+    a_row_info<MODE>(a, ti, rank, t, row, S, B);
+    const bool rv = row < N;
+    const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + (rv ? row : 0);
+    const uint16_t* srow = S + r * gpr;
+    const uint16_t* brow = B ? B + r * gpr : nullptr;
+    uint16_t* sdst = sc + t * SC_GROUPS;
+    uint16_t* bdst = bi + t * SC_GROUPS;
+    if (aligned) {
+      for (int g = 0; g < G; g += 2) {
+        const bool in = rv && g0 + g < gpr;  // gpr even: the pair is inside the row or past it
+        cp_async4(smem_u32(sdst + g), in ? srow + g0 + g : srow, in ? 4u : 0u);
+        cp_async4(smem_u32(bdst + g), (in && brow) ? brow + g0 + g : srow, (in && brow) ? 4u : 0u);
+      }
+    } else {
+      for (int g = 0; g < G; ++g) {
+        const bool in = rv && g0 + g < gpr;
+        sdst[g] = in ? __ldg(srow + g0 + g) : static_cast<uint16_t>(0);
+        bdst[g] = (in && brow) ? __ldg(brow + g0 + g) : static_cast<uint16_t>(0);
       }
     }
+  }
+  if (aligned) cp_async_arrive_noinc(cfull);
+  else mbar_arrive(cfull);
+}
+
+// The 128 epilogue threads copy a staged 32-row tile (row stride 256 B, `cols` bf16
+// columns per row) to global memory as 16-byte stores; staged row i goes to output
+// row dst_row(i), or nowhere when that is negative.
+template <class RowFn>
+FM_DEV void store_staged(const uint8_t* stg, int cols, uint16_t* base, int64_t ld, int col0, int ncols_valid,
+                         RowFn dst_row, int et) {
+  const int segs_per_row = cols / 8;
+  const int nseg = 32 * segs_per_row;
+  for (int s = et; s < nseg; s += 128) {
+    const int i = s / segs_per_row, part = s - i * segs_per_row;
+    const int64_t r = dst_row(i);
+    if (r < 0 || part * 8 >= ncols_valid) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(stg + i * 256 + part * 16);
+    *reinterpret_cast<uint4*>(base + r * ld + col0 + part * 8) = v;
   }
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, const __grid_constant__ TcMaps maps) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    qgemm_tc_kernel(const GemmArgs a, const __grid_constant__ TcMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   const int tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
+  const int rank = static_cast<int>(cluster_rank());
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(cluster_id_x());
+  const int npairs = static_cast<int>(num_clusters_x());
   // an earlier kernel of this call reported a device error: the tile table is not trusted
   const int ntiles = (*reinterpret_cast<volatile uint32_t*>(a.err) != 0u) ? 0 : a.tab->num_tiles;
   volatile int* abort_flag = &bars->abort;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&bars->full[s], NA + NB);
+      mbar_init(&bars->full[s], FULL_ARRIVALS);
       mbar_init(&bars->empty[s], 1);
     }
     for (int c = 0; c < NC; ++c) {
-      mbar_init(&bars->cfull[c], 1);
+      mbar_init(&bars->cfull[c], CFULL_ARRIVALS);
       mbar_init(&bars->cempty[c], NA / 32);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bars->accf[b], 1);
-      mbar_init(&bars->acce[b], 4);
+      mbar_init(&bars->acce[b], ACCE_ARRIVALS);
     }
     mbar_init(&bars->done, 1);
     bars->abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == MMA_WARP) {
-    tmem_alloc(&bars->tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc2(&bars->tmem_base, TMEM_COLS);
+    tmem_relinquish2();
   }
   int* s_tb = reinterpret_cast<int*>(smem + OFF_TB);
   const int ngroups = ntiles > 0 ? min(a.tab->num_groups, kMaxGroups) : 0;
@@ -240,41 +377,48 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
   const TileDir dir{a.tab, s_tb, ngroups};
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // the leader's stage / accumulator-drain barriers, as shared::cluster addresses
+  const uint32_t full0 = map_to_rank(&bars->full[0], 0);
+  const uint32_t acce0 = map_to_rank(&bars->acce[0], 0);
 
   if (warp < NA / 32) {
     // ------------------------------------------------------------ dequant producers
     const int t = tid >> 1;    // A row
     const int half = tid & 1;  // 16-byte half of the row's 32 bytes of codes per k-step
-    SIter cur;
-    siter_load(cur, a, dir, blockIdx.x, ntiles, MODE);
-    uint32_t sv[4], bv[4];
-    load_scales<MODE>(a, cur, t, half, sv, bv);
     int cs = 0, it = 0;
     bool ok = true;
-    while (cur.valid && ok) {
-      SIter nx = cur;
-      siter_next(nx, a, dir, ntiles, MODE);
-      uint32_t nsv[4], nbv[4];
-      load_scales<MODE>(a, nx, t, half, nsv, nbv);  // a super-step ahead
+    while (ok) {
       const int slot = cs % NC;
-      if (!mbar_wait(&bars->cfull[slot], (cs / NC) & 1, abort_flag, a.err)) break;
-      const TileInfo& ti = cur.ti;
-      const bool sh = ti.expert < 0;
-      const int N = sh ? a.N_shared : a.N;
-      const int row = (MODE == MODE_GATEUP) ? ti.rb * 64 + (t & 63) : ti.rb * 128 + t;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->cfull[slot], (cs / NC) & 1, abort_flag, a.err))) {
+        ok = false;
+        break;
+      }
+      const int nk = bars->slot_nk[slot];
+      if (nk == 0) break;  // end of this pair's tiles
+      const int vlim = bars->slot_vlim[slot];
+      const bool valid = ((MODE == MODE_GATEUP) ? (t & 63) : t) < vlim;
       const uint8_t* code = smem + OFF_C + slot * C_BYTES + t * 128;
-      const int nk = min(KS_PER_SS, cur.nks - cur.ss * KS_PER_SS);
+      const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + OFF_SC + slot * SC_BYTES) + t * SC_GROUPS;
+      const uint16_t* bi = sc + BM * SC_GROUPS;
+      uint32_t sv[4], bv[4];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int g = (kk * 64 + 32 * half) / a.gs;
+        sv[kk] = sc[g];
+        bv[kk] = bi[g];
+      }
 #pragma unroll
       for (int kk = 0; kk < KS_PER_SS; ++kk) {
         if (kk >= nk) break;
         const int stage = it % STAGES;
-        if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
           ok = false;
           break;
         }
-        if (row < N) {
+        if (valid) {
           const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + half) ^ (t & 7)) << 4));
           const uint32_t s2u = sv[kk] * 0x10001u, b2u = bv[kk] * 0x10001u;
           const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
@@ -291,48 +435,63 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
             *reinterpret_cast<uint4*>(As + sw128_off(t, half * 4 + i)) = o;
           }
         }
-        fence_proxy_async();
-        mbar_arrive(&bars->full[stage]);
+        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(full0 + stage * 8);
         ++it;
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->cempty[slot]);
       ++cs;
-      cur = nx;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        sv[kk] = nsv[kk];
-        bv[kk] = nbv[kk];
-      }
+    }
+    // drain: the last commits of every stage land before this CTA may exit
+    if (warp == 0 && ok) {
+      for (int i = it; i < it + STAGES; ++i)
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[i % STAGES], ((i / STAGES) & 1) ^ 1, abort_flag, a.err)))
+          break;
     }
   } else if (warp == CODE_WARP) {
     // ------------------------------------------------------------ code loader (TMA)
-    if (lane == 0) {
-      SIter cur;
-      siter_load(cur, a, dir, blockIdx.x, ntiles, MODE);
-      int cs = 0;
-      while (cur.valid) {
-        const int slot = cs % NC;
-        if (!mbar_wait(&bars->cempty[slot], ((cs / NC) & 1) ^ 1, abort_flag, a.err)) break;
-        const TileInfo& ti = cur.ti;
-        const bool sh = ti.expert < 0;
-        const int N = sh ? a.N_shared : a.N;
+    // Per super-step: the TMA of the codes (lane 0), the scales and biases (all lanes)
+    // and the slot metadata; after the last tile a slot with nk = 0 ends the consumers.
+    SIter cur;
+    siter_load(cur, a, dir, pair, ntiles, MODE);
+    int cs = 0;
+    while (true) {
+      const int slot = cs % NC;
+      if (!__all_sync(0xffffffffu, mbar_wait(&bars->cempty[slot], ((cs / NC) & 1) ^ 1, abort_flag, a.err))) break;
+      if (!cur.valid) {
+        if (lane == 0) {
+          bars->slot_nk[slot] = 0;
+          mbar_arrive_cnt(&bars->cfull[slot], CFULL_ARRIVALS);
+        }
+        break;
+      }
+      const TileInfo& ti = cur.ti;
+      const bool sh = ti.expert < 0;
+      const int N = sh ? a.N_shared : a.N;
+      uint16_t* sc = reinterpret_cast<uint16_t*>(smem + OFF_SC + slot * SC_BYTES);
+      stage_scales<MODE>(a, cur, rank, lane, sc, sc + BM * SC_GROUPS, &bars->cfull[slot]);
+      if (lane == 0) {
+        const int base = (MODE == MODE_GATEUP) ? ti.rb * 128 + rank * 64 : ti.rb * 256 + rank * 128;
+        bars->slot_nk[slot] = min(KS_PER_SS, cur.nks - cur.ss * KS_PER_SS);
+        bars->slot_vlim[slot] = max(0, N - base);
         const int erow = sh ? 0 : ti.expert * N;
         const uint32_t dst = smem_u32(smem + OFF_C + slot * C_BYTES);
         const int x = cur.ss * (KS_PER_SS * 8);
-        mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);
+        mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);  // also publishes the metadata
         if (MODE == MODE_GATEUP) {
-          const int r0 = erow + ti.rb * 64;
-          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, r0, &bars->cfull[slot]);
-          tma_load_2d(dst + 64 * 128, &maps.code[sh ? 3 : 1], x, r0, &bars->cfull[slot]);
+          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + base, &bars->cfull[slot]);
+          tma_load_2d(dst + 64 * 128, &maps.code[sh ? 3 : 1], x, erow + base, &bars->cfull[slot]);
         } else {
-          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + ti.rb * 128, &bars->cfull[slot]);
+          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + base, &bars->cfull[slot]);
         }
-        ++cs;
-        siter_next(cur, a, dir, ntiles, MODE);
       }
+      ++cs;
+      siter_next(cur, a, dir, ntiles, npairs, MODE);
     }
+    cp_async_wait<0>();
     __syncwarp();
   } else if (warp == ACT_WARP || warp == ACT_WARP + 1) {
     // ------------------------------------------------------------ activation loaders
@@ -342,11 +501,14 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
     const uint32_t dst0 = static_cast<uint32_t>(rg) * 128u + (static_cast<uint32_t>(cc ^ rg) << 4);
     int it = 0, pend = 0;  // pend: oldest k-step whose cp.async rows are not yet published
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+    for (int tile = pair; tile < ntiles && ok; tile += npairs) {
       const TileInfo ti = dir.get(tile);
       const bool sh = ti.expert < 0;
       const int nks = tile_ksteps(a, ti, MODE);
       const bool gather = (MODE != MODE_DOWN) && !sh;
+      const int hrows = tile_nmma(ti.nrows) / 2;              // B rows per CTA
+      const int rbeg = rank * hrows;                           // first tile row of this CTA
+      const int rmine = max(0, min(hrows, ti.nrows - rbeg));  // rows of this CTA holding data
       uint32_t srow[B_ROWS];
       const uint16_t* base = sh ? a.act_shared : a.act;
       const uint64_t ld_bytes = static_cast<uint64_t>(sh ? a.act_shared_ld : a.act_ld) * 2u;
@@ -354,13 +516,13 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
 #pragma unroll
         for (int i = 0; i < B_ROWS; ++i) {
           const int r = rg + 8 * i;
-          srow[i] = (r < ti.nrows) ? static_cast<uint32_t>(a.sorted_token[ti.row0 + r]) : 0u;
+          srow[i] = (r < rmine) ? static_cast<uint32_t>(a.sorted_token[ti.row0 + rbeg + r]) : 0u;
         }
       }
-      const int nblk = (ti.nrows + 63) >> 6;
+      const int nblk = (hrows + 63) >> 6;
       for (int ks = 0; ks < nks; ++ks) {
         const int stage = it % STAGES;
-        if (!mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err)) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
           ok = false;
           break;
         }
@@ -369,7 +531,7 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
           const uint64_t src_k = reinterpret_cast<uint64_t>(base) + static_cast<uint64_t>(ks * 128 + cc * 16);
 #pragma unroll
           for (int i = 0; i < B_ROWS; ++i) {
-            if (rg + 8 * i < ti.nrows)
+            if (rg + 8 * i < rmine)
               cp_async16(bs + static_cast<uint32_t>(i) * 1024u,
                          reinterpret_cast<const void*>(src_k + static_cast<uint64_t>(srow[i]) * ld_bytes));
           }
@@ -377,23 +539,26 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
           if (it - pend >= B_LAG) {  // publish the k-step B_LAG behind
             cp_async_wait<B_LAG>();
             fence_proxy_async();
-            mbar_arrive(&bars->full[pend % STAGES]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
             ++pend;
           }
         } else {
           if (pend < it) {  // publish every gathered k-step still in flight
             cp_async_wait<0>();
             fence_proxy_async();
-            for (; pend < it; ++pend) mbar_arrive(&bars->full[pend % STAGES]);
+            __syncwarp();
+            for (; pend < it; ++pend)
+              if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
           }
           if (bt == 0) {
-            mbar_arrive_expect_tx(&bars->full[stage], static_cast<uint32_t>(nblk) * 8192u);
+            mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nblk) * 8192u);
             const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES);
             const CUtensorMap* map = &maps.act[sh ? 1 : 0];
             for (int b = 0; b < nblk; ++b)
-              tma_load_2d(bs + b * 8192, map, ks * 64, ti.row0 + b * 64, &bars->full[stage]);
-          } else {
-            mbar_arrive(&bars->full[stage]);
+              tma_load_2d_pair(bs + b * 8192, map, ks * 64, ti.row0 + rbeg + b * 64, full0 + stage * 8);
+          } else if (lane == 0) {
+            mbar_arrive_cluster(full0 + stage * 8);
           }
           pend = it + 1;
         }
@@ -402,20 +567,23 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
     }
     cp_async_wait<0>();
     fence_proxy_async();
-    for (; pend < it; ++pend) mbar_arrive(&bars->full[pend % STAGES]);
+    __syncwarp();
+    for (; pend < it; ++pend)
+      if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
   } else if (warp == MMA_WARP) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      const uint32_t empty_l = map_to_rank(&bars->empty[0], 0), empty_p = map_to_rank(&bars->empty[0], 1);
+      const uint32_t accf_l = map_to_rank(&bars->accf[0], 0), accf_p = map_to_rank(&bars->accf[0], 1);
       int it = 0, lt = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++lt) {
+      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++lt) {
         const TileInfo ti = dir.get(tile);
         const int nks = tile_ksteps(a, ti, MODE);
         const int buf = lt & 1;
         if (!mbar_wait(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
         tc_fence_after();
-        const int nmma = max(16, (ti.nrows + 15) & ~15);
-        const uint32_t idesc = idesc_bf16(BM, nmma);
+        const uint32_t idesc = idesc_bf16(2 * BM, tile_nmma(ti.nrows));
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * ACC_COLS);
         for (int ks = 0; ks < nks; ++ks) {
           const int stage = it % STAGES;
@@ -427,23 +595,28 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
           const uint64_t ad = sdesc_sw128(smem_u32(smem + OFF_A + stage * A_BYTES));
           const uint64_t bd = sdesc_sw128(smem_u32(smem + OFF_B + stage * B_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
-          umma_commit(&bars->empty[stage]);
+          for (int kk = 0; kk < 4; ++kk) umma2_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+          umma2_commit(empty_l + stage * 8);
+          umma2_commit(empty_p + stage * 8);
           ++it;
         }
-        if (ok) umma_commit(&bars->accf[buf]);
+        if (ok) {
+          umma2_commit(accf_l + buf * 8);
+          umma2_commit(accf_p + buf * 8);
+        }
       }
-      umma_commit(&bars->done);
+      umma2_commit(map_to_rank(&bars->done, 0));
       wait_done(&bars->done, 0, a.err);
     }
     __syncwarp();
   } else if (warp >= EPI_WARP && warp < EPI_WARP + 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp - EPI_WARP;
-    const int row_in = q * 32 + lane;  // TMEM lane == A row
+    const int row_in = q * 32 + lane;    // TMEM lane == A row of this CTA
+    const int et = tid - EPI_WARP * 32;  // 0..127
     uint16_t* xchg = reinterpret_cast<uint16_t*>(smem + OFF_XCHG);
     int lt = 0, xit = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++lt) {
+    for (int tile = pair; tile < ntiles; tile += npairs, ++lt) {
       const TileInfo ti = dir.get(tile);
       const bool sh = ti.expert < 0;
       const int N = sh ? a.N_shared : a.N;
@@ -460,6 +633,9 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
       for (int j = 0; j < nchunks; ++j, ++xit) {
         float v[32];
         tmem_ld32(tbase + j * 32, v);
+        uint8_t* stg = smem + OFF_STG + (xit & 1) * STG_BYTES;
+        const int c_lim = ti.nrows - j * 32;  // valid columns of this chunk (may exceed 32)
+        const int prow = ti.row0 + j * 32;
         if (MODE == MODE_GATEUP) {
           // gate warps (q 0,1) finish columns 0..15, up warps (q 2,3) columns 16..31;
           // each hands the partner the other half of its rows through shared memory
@@ -474,12 +650,8 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
             for (int c = 0; c < 16; ++c) to_gate[c * 64 + r64] = f2bf(v[c]);
           }
           named_bar_sync(1, 128);
-          const int n = ti.rb * 64 + r64;
-          uint16_t* outb = sh ? a.out_shared : a.out;
-          const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
-          const int pn = perm8(n);  // even for n % 8 < 4: (n, n+4) share one 32-bit word
           const int c0 = (q < 2) ? 0 : 16;
-          uint32_t res[16];  // all 16 columns first: independent chains for the scheduler
+          uint32_t res[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             float gv, uv;
@@ -492,28 +664,29 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
             }
             res[c] = f2bf(swiglu1(gv, uv));
           }
-          uint16_t* orow = outb + static_cast<int64_t>(ti.row0 + j * 32 + c0) * ld + pn;
+          // staging row = token column (c0 + c), 64 outputs at their pair-permuted
+          // slots; lanes r64 and r64 ^ 4 share one 32-bit word
+          const int pn = perm8(r64);
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const uint32_t other = __shfl_xor_sync(0xffffffffu, res[c], 4);
-            if (j * 32 + c0 + c < ti.nrows && (lane & 4) == 0 && n < N)
-              *reinterpret_cast<uint32_t*>(orow + static_cast<int64_t>(c) * ld) = res[c] | (other << 16);
+            if ((lane & 4) == 0)
+              *reinterpret_cast<uint32_t*>(stg + (c0 + c) * 256 + pn * 2) = res[c] | (other << 16);
           }
+          named_bar_sync(1, 128);
+          uint16_t* outb = sh ? a.out_shared : a.out;
+          const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
+          const int col0 = ti.rb * 128 + rank * 64;
+          store_staged(stg, 64, outb, ld, col0, N - col0,
+                       [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(prow + i) : -1; }, et);
         } else {
-          // lanes (2m, 2m+1) hold rows (n, n+1); the even lane finishes column c and
-          // the odd lane column c+1, each as one 2-wide red / 4-byte store
-          const int n = ti.rb * 128 + row_in;
+          // staging row = token column c, 128 outputs; lanes (2m, 2m+1) hold rows
+          // (n, n+1): the even lane stores even columns, the odd lane odd columns
           const bool odd = lane & 1;
-          const int n0 = n & ~1;
-          // lane c fetches column c's metadata once; the loop reads it by shuffle
           const int pc = ti.row0 + min(j * 32 + lane, ti.nrows - 1);
           const float my_score = (MODE == MODE_DOWN && !sh) ? a.sorted_score[pc] : 1.f;
-          const int my_dst = (MODE == MODE_DOWN) ? (sh ? pc : a.sorted_token[pc]) : a.sorted_flat[pc];
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            const int col = j * 32 + c + (odd ? 1 : 0);
-            const bool colok = col < ti.nrows;
-            const int dst_row = __shfl_sync(0xffffffffu, my_dst, c + (odd ? 1 : 0));
             float mine_c = v[c], mine_c1 = v[c + 1];
             if (MODE == MODE_DOWN && !sh) {  // bf16(bf16(d) * score) per MLX op
               const float se = __shfl_sync(0xffffffffu, my_score, c);
@@ -521,33 +694,37 @@ __global__ void __launch_bounds__(THREADS, 1) qgemm_tc_kernel(const GemmArgs a, 
               mine_c = rbf(rbf(mine_c) * se);
               mine_c1 = rbf(rbf(mine_c1) * so);
             }
-            // even lane sends its column c+1 value, odd lane its column c value
             const float give = odd ? mine_c : mine_c1;
             const float got2 = __shfl_xor_sync(0xffffffffu, give, 1);
-            const float lo = odd ? got2 : mine_c;    // row n0, column (c or c+1)
-            const float hi = odd ? mine_c1 : got2;   // row n0+1
-            if (!colok || n0 >= N) continue;
-            if (MODE == MODE_DOWN) {
-              if (sh)  // each shared-expert element is produced by exactly one tile
-                *reinterpret_cast<float2*>(a.ysh + static_cast<int64_t>(dst_row) * a.y_ld + n0) = make_float2(lo, hi);
-              else
-                red_add_v2(a.y_acc + static_cast<int64_t>(dst_row) * a.y_ld + n0, lo, hi);
-            } else {
-              *reinterpret_cast<uint32_t*>(a.out + static_cast<int64_t>(dst_row) * a.out_ld + n0) = pack_bf16x2(lo, hi);
-            }
+            const float lo = odd ? got2 : mine_c;   // row n0, column (c or c+1)
+            const float hi = odd ? mine_c1 : got2;  // row n0+1
+            const int col = c + (odd ? 1 : 0);
+            *reinterpret_cast<uint32_t*>(stg + col * 256 + (row_in & ~1) * 2) = pack_bf16x2(lo, hi);
+          }
+          named_bar_sync(1, 128);
+          const int col0 = ti.rb * 256 + rank * 128;
+          if (MODE == MODE_DOWN) {
+            uint16_t* outb = sh ? a.ysh16 : a.y_pairs;
+            store_staged(stg, 128, outb, a.y_ld, col0, N - col0,
+                         [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(prow + i) : -1; }, et);
+          } else {
+            store_staged(
+                stg, 128, a.out, a.out_ld, col0, N - col0,
+                [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(a.sorted_flat[prow + i]) : -1; }, et);
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars->acce[buf]);
+      if (lane == 0) mbar_arrive_cluster(acce0 + buf * 8);
     }
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // no remote arrival or MMA read of this CTA's memory after this
   if (warp == MMA_WARP) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc2(tmem_base, TMEM_COLS);
   }
 }
 
@@ -562,7 +739,24 @@ cudaError_t init() {
   return e;
 }
 
-cudaError_t launch(int mode, int grid, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps) {
+// CTA pairs that can be resident at once (the persistent grid is twice that)
+cudaError_t max_pairs(int* n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaOccupancyMaxActiveClusters(n, qgemm_tc_kernel<MODE_GATEUP>, &cfg);
+}
+
+cudaError_t launch(int mode, int pairs, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps) {
+  const int grid = 2 * pairs;
   switch (mode) {
     case MODE_GATEUP: qgemm_tc_kernel<MODE_GATEUP><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
     case MODE_DOWN: qgemm_tc_kernel<MODE_DOWN><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;

@@ -250,4 +250,50 @@ __global__ void finalize_kernel(const float* __restrict__ y_acc, const float* __
   }
 }
 
+// TC path combine, y = bf16( bf16(sum_j y_pairs[pos(t, j)]) + bf16(gate * ysh16[t]) ):
+// the k routed rows of a token are summed in fp32 in the order j = 0..k-1 (MLX sums
+// the [T, k, H] product over axis -2; model.cpp:780-784), then the gated shared row
+// is added as in model.cpp:800-803.  One thread per 8 outputs (16-byte accesses).
+__global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, const int32_t* __restrict__ pair_pos,
+                                      int k, const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig,
+                                      int64_t T, int H, uint16_t* __restrict__ y) {
+  const int segs = H / 8;
+  const int64_t n = T * segs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / segs;
+    const int col = static_cast<int>(i - t * segs) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int pos = pair_pos[t * k + j];
+      if (pos < 0) continue;
+      const uint4 v = *reinterpret_cast<const uint4*>(y_pairs + static_cast<int64_t>(pos) * H + col);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += bf2f(static_cast<uint16_t>(w[q] & 0xffffu));
+        acc[2 * q + 1] += bf2f(static_cast<uint16_t>(w[q] >> 16));
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = rbf(acc[q]);
+    if (ysh16) {
+      const float gsv = gate_sig[t];
+      const uint4 s = *reinterpret_cast<const uint4*>(ysh16 + t * H + col);
+      const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = rbf(acc[2 * q] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] & 0xffffu))));
+        acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] >> 16))));
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(y + t * H + col) = o;
+  }
+}
+
 }  // namespace fm

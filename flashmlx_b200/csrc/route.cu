@@ -398,7 +398,8 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
       if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
     }
     plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
-    if (a.tab_b) plan_groups(a, sm, a.tab_b, 128, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
+    if (a.tab_b)
+      plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
   }
   const int k = a.do_router ? a.k : 1;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
@@ -408,8 +409,12 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
     for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
       const int64_t flat = t0 * k + i;
       const int e = a.topk_ids[flat];
-      if (e < 0) continue;
+      if (e < 0) {
+        if (a.pair_pos) a.pair_pos[flat] = -1;
+        continue;
+      }
       const int pos = sm.offs[e] + a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] + a.pair_rank[flat];
+      if (a.pair_pos) a.pair_pos[flat] = pos;
       const int64_t t = flat / k;
       a.sorted_token[pos] = a.do_router ? static_cast<int32_t>(t) : a.row_src[t];
       a.sorted_score[pos] = a.topk_score[flat];

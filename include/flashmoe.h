@@ -144,7 +144,11 @@ typedef struct fm_kernel_time {
 FM_API int fm_profile_enable(fm_handle* h, int on);
 FM_API int fm_profile_report(fm_handle* h, fm_kernel_time* out, int capacity, int* count, int reset);
 
-/* Operators ------------------------------------------------------------------ */
+/* Operators ------------------------------------------------------------------
+ * Activation and output pointers (x, y, out) must be 16-byte aligned (the kernels
+ * move rows in 16-byte units); FM_EINVAL otherwise.  Weight codes, scales and
+ * biases must be 16-byte aligned for the tcgen05 path's TMA descriptors (FM_ECUDA
+ * from the descriptor encoder otherwise). */
 
 /* out[M, N] = x[M, K] @ w_hat^T.  Replaces mx::quantized_matmul with transpose=true
  * (model.cpp:478-479, 509-511, 531-535, 741-747, 759-760, 793-796).
