@@ -244,9 +244,9 @@ bool encode_codes(CUtensorMap* m, const uint32_t* w, int64_t rows, int K, uint32
   return encode_2d(m, true, w, static_cast<uint64_t>(K / 8), static_cast<uint64_t>(rows), 32, box_rows);
 }
 
-// bf16 activation rows [rows, cols]: one-row boxes for gather4 or 64-row boxes
-bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols, bool gather) {
-  return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, gather ? 1 : 64);
+// bf16 activation rows [rows, cols], 128B-swizzled boxes of 64 columns x 32 rows
+bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols) {
+  return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, 32);
 }
 
 template <int MODE>
@@ -578,14 +578,14 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
               encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E) * I, H, 64) &&
               encode_codes(&maps_gu.code[2], shared ? w->shared_gate.w : nullptr, Is, H, 64) &&
               encode_codes(&maps_gu.code[3], shared ? w->shared_up.w : nullptr, Is, H, 64) &&
-              encode_act(&maps_gu.act[0], ra.x_perm, T, H, true) &&
-              encode_act(&maps_gu.act[1], shared ? ra.x_perm : nullptr, T, H, false) &&
+              encode_act(&maps_gu.act[0], ra.x_perm, T, H) &&
+              encode_act(&maps_gu.act[1], shared ? ra.x_perm : nullptr, T, H) &&
               encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E) * H, I, 128) &&
               encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
               encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
               encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
-              encode_act(&maps_dn.act[0], at<uint16_t>(h, p.a_sorted), P, I, false) &&
-              encode_act(&maps_dn.act[1], shared ? at<uint16_t>(h, p.a_shared) : nullptr, T, Is, false);
+              encode_act(&maps_dn.act[0], at<uint16_t>(h, p.a_sorted), P, I) &&
+              encode_act(&maps_dn.act[1], shared ? at<uint16_t>(h, p.a_shared) : nullptr, T, Is);
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
   rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
@@ -720,8 +720,8 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
     const bool ok = encode_codes(&maps.code[0], w, static_cast<int64_t>(E) * N, K, 128) &&
                     encode_codes(&maps.code[1], nullptr, 0, K, 128) && encode_codes(&maps.code[2], nullptr, 0, K, 128) &&
                     encode_codes(&maps.code[3], nullptr, 0, K, 128) &&
-                    encode_act(&maps.act[0], ra.x_perm, ra.x_rows, K, true) &&
-                    encode_act(&maps.act[1], nullptr, 0, K, false);
+                    encode_act(&maps.act[0], ra.x_perm, ra.x_rows, K) &&
+                    encode_act(&maps.act[1], nullptr, 0, K);
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
   return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps);

@@ -121,9 +121,10 @@ struct GemmArgs {
 //               {32 words = 4 k-steps, 64 rows (gate/up) | 128 rows (down, plain)}:
 //               gate/up: routed gate, routed up, shared gate, shared up;
 //               down / plain: routed, (unused), shared, (unused)
-//   act[0]:     routed activation rows, bf16 [rows, K], 128B swizzle; box {64, 1} for
-//               gather4 (gate/up, plain) or {64, 64} (down, contiguous rows)
-//   act[1]:     shared-expert activation rows, box {64, 64}
+//   act[0]:     routed activation rows, bf16 [rows, K], 128B swizzle, box {64, 32}
+//               (read by TMA only where the rows are contiguous: down; gate/up and
+//               plain gather their token rows with cp.async)
+//   act[1]:     shared-expert activation rows, box {64, 32}
 struct alignas(64) TcMaps {
   CUtensorMap code[4];
   CUtensorMap act[2];

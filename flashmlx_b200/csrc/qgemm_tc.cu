@@ -22,14 +22,15 @@
 //
 // Data movement: packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows) per
 // load, 128B-swizzled, into a 3-deep ring per CTA.  Contiguous activation rows arrive
-// by TMA in 64-row boxes straight into the UMMA B stage, completing on the leader
+// by TMA in 32-row boxes straight into the UMMA B stage, completing on the leader
 // CTA's stage barrier; token-gathered rows are copied with cp.async.  Outputs go
 // through a shared-memory staging tile and leave as coalesced 16-byte stores.
 //
 // Roles (512 threads per CTA):
-//   warps 0-7   dequant producers: thread t owns half of A row t/2.  Per k-step: one
-//               16-byte code read, bf16 fma of the exact codes with the group's scale
-//               and bias (prefetched a super-step ahead), four 16-byte stores into the
+//   warps 0-7   dequant producers in two groups of four that take alternate k-steps;
+//               thread t of a group owns A row t.  Per k-step: two 16-byte code reads,
+//               bf16 fma of the exact codes with the group's scale and bias (staged in
+//               shared memory by the code loader), eight 16-byte stores into the
 //               128B-swizzled K-major A stage; one arrival per warp on the leader's
 //               stage barrier.
 //   warp 8      code loader (one lane issues the TMA of each super-step).
@@ -72,7 +73,8 @@ constexpr int OFF_TB = OFF_STG + 2 * STG_BYTES;  // tile_begin of every group
 constexpr int OFF_BAR = OFF_TB + ((kMaxGroups * 4 + 255) / 256) * 256;
 constexpr int BAR_BYTES = 256;
 constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-constexpr int NA = 256;          // dequant-producer threads (two per A row)
+constexpr int NA = 256;          // dequant-producer threads: two groups of 128, one A row per thread
+constexpr int DQ_GROUPS = 2;     // group g dequantizes the k-steps with (k-step % 2) == g
 constexpr int CODE_WARP = 8;
 constexpr int ACT_WARP = 9;      // two activation-loader warps: 9 and 10
 constexpr int NB = 64;
@@ -82,7 +84,7 @@ constexpr int MMA_WARP = 11;
 constexpr int EPI_WARP = 12;     // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
 constexpr int THREADS = (EPI_WARP + 4) * 32;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int FULL_ARRIVALS = 2 * (NA / 32 + NB / 32);  // per stage, both CTAs
+constexpr int FULL_ARRIVALS = 2 * (NA / 32 / DQ_GROUPS + NB / 32);  // per stage, both CTAs
 constexpr int CFULL_ARRIVALS = 1 + 32;  // code-loader lane 0 (meta + expect_tx) + one per lane's scale copies
 constexpr int ACCE_ARRIVALS = 2 * 4;                     // epilogue warps of both CTAs
 
@@ -386,9 +388,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (warp < NA / 32) {
     // ------------------------------------------------------------ dequant producers
-    const int t = tid >> 1;    // A row
-    const int half = tid & 1;  // 16-byte half of the row's 32 bytes of codes per k-step
-    int cs = 0, it = 0;
+    const int grp = warp / 4;              // takes the k-steps with (k-step % DQ_GROUPS) == grp
+    const int t = (warp % 4) * 32 + lane;  // A row
+    int cs = 0, it0 = 0;                   // super-step, k-steps before it
     bool ok = true;
     while (ok) {
       const int slot = cs % NC;
@@ -403,48 +405,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint8_t* code = smem + OFF_C + slot * C_BYTES + t * 128;
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + OFF_SC + slot * SC_BYTES) + t * SC_GROUPS;
       const uint16_t* bi = sc + BM * SC_GROUPS;
-      uint32_t sv[4], bv[4];
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int g = (kk * 64 + 32 * half) / a.gs;
-        sv[kk] = sc[g];
-        bv[kk] = bi[g];
-      }
-#pragma unroll
-      for (int kk = 0; kk < KS_PER_SS; ++kk) {
+      for (int kk = grp; kk < KS_PER_SS; kk += DQ_GROUPS) {
         if (kk >= nk) break;
+        const int it = it0 + kk;
         const int stage = it % STAGES;
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
           ok = false;
           break;
         }
         if (valid) {
-          const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + half) ^ (t & 7)) << 4));
-          const uint32_t s2u = sv[kk] * 0x10001u, b2u = bv[kk] * 0x10001u;
-          const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
-          const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&b2u);
-          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
           uint8_t* As = smem + OFF_A + stage * A_BYTES;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 o;
-            o.x = deq_pair(words[i], 0, s2, b2);
-            o.y = deq_pair(words[i], 1, s2, b2);
-            o.z = deq_pair(words[i], 2, s2, b2);
-            o.w = deq_pair(words[i], 3, s2, b2);
-            *reinterpret_cast<uint4*>(As + sw128_off(t, half * 4 + i)) = o;
+          for (int h = 0; h < 2; ++h) {  // the two 32-element halves of the k-step
+            const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + h) ^ (t & 7)) << 4));
+            const int g = (kk * 64 + 32 * h) / a.gs;
+            const uint32_t s2u = static_cast<uint32_t>(sc[g]) * 0x10001u;
+            const uint32_t b2u = static_cast<uint32_t>(bi[g]) * 0x10001u;
+            const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
+            const __nv_bfloat162 b2 = *reinterpret_cast<const __nv_bfloat162*>(&b2u);
+            const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 o;
+              o.x = deq_pair(words[i], 0, s2, b2);
+              o.y = deq_pair(words[i], 1, s2, b2);
+              o.z = deq_pair(words[i], 2, s2, b2);
+              o.w = deq_pair(words[i], 3, s2, b2);
+              *reinterpret_cast<uint4*>(As + sw128_off(t, h * 4 + i)) = o;
+            }
           }
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(full0 + stage * 8);
-        ++it;
       }
       if (!ok) break;
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->cempty[slot]);
+      it0 += nk;
       ++cs;
     }
+    const int it = it0;
     // drain: the last commits of every stage land before this CTA may exit
     if (warp == 0 && ok) {
       for (int i = it; i < it + STAGES; ++i)
@@ -519,7 +521,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           srow[i] = (r < rmine) ? static_cast<uint32_t>(a.sorted_token[ti.row0 + rbeg + r]) : 0u;
         }
       }
-      const int nblk = (hrows + 63) >> 6;
+      const int nblk = (hrows + 31) >> 5;  // 32-row TMA boxes
       for (int ks = 0; ks < nks; ++ks) {
         const int stage = it % STAGES;
         if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
@@ -552,11 +554,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
           }
           if (bt == 0) {
-            mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nblk) * 8192u);
+            mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nblk) * 4096u);
             const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES);
             const CUtensorMap* map = &maps.act[sh ? 1 : 0];
             for (int b = 0; b < nblk; ++b)
-              tma_load_2d_pair(bs + b * 8192, map, ks * 64, ti.row0 + rbeg + b * 64, full0 + stage * 8);
+              tma_load_2d_pair(bs + b * 4096, map, ks * 64, ti.row0 + rbeg + b * 32, full0 + stage * 8);
           } else if (lane == 0) {
             mbar_arrive_cluster(full0 + stage * 8);
           }
