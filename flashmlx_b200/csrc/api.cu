@@ -270,7 +270,10 @@ int router_ksplit(const fm_handle* h, int64_t T, int H) {
   return ks;
 }
 
-bool use_tc(const fm_handle* h, int64_t pairs, int E) {
+// The GEMV path covers group sizes 64 and 128 (each 64-wide half of its 128-wide K
+// chunks lies inside one quant group); group size 32 always runs on tcgen05.
+bool use_tc(const fm_handle* h, int64_t pairs, int E, int gs) {
+  if (gs != 64 && gs != 128) return true;
   if (h->path == FM_PATH_GEMV) return false;
   if (h->path == FM_PATH_TCGEN05) return true;
   return pairs >= 24LL * E;  // ~24+ activation rows per matrix on average
@@ -480,7 +483,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   const int epad = (E + 1 + 7) / 8 * 8;
   const int ksplit = router_ksplit(h, T, H);
   const int64_t P = T * k;
-  const bool tcp = use_tc(h, P, E);
+  const bool tcp = use_tc(h, P, E, c->group_size);
   Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true, tcp);
   rc = ensure_ws(h, p.total);
   if (rc) return rc;
@@ -527,7 +530,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.a_n_shared = c->shared_inter;
   ra.b_n = H;
   ra.b_rows_per_block = tcp ? 256 : 128;
-  ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
+  ra.chunk_max = tcp ? fm::tc::max_rows() : 8;  // GEMV: one 8-row MMA column tile
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, I));
   ra.has_shared = shared ? 1 : 0;
@@ -650,7 +653,7 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   if (K % 64 || N % 16) return set_err(h, FM_EUNSUPPORTED, "K must be a multiple of 64 and N of 16");
   const int64_t rows = B * M;
   if (rows > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
-  bool tcp = use_tc(h, rows, E);
+  bool tcp = use_tc(h, rows, E, group_size);
   if (K % 128) tcp = true;  // the GEMV path works in 128-wide K chunks
   Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false, tcp);
   int rc = ensure_ws(h, p.total);
@@ -689,7 +692,7 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   ra.a_rows_per_block = tcp ? 256 : 128;
   ra.a_n = N;
   ra.a_n_shared = 0;
-  ra.chunk_max = tcp ? fm::tc::max_rows() : 32;
+  ra.chunk_max = tcp ? fm::tc::max_rows() : 8;  // GEMV: one 8-row MMA column tile
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = 1;
   ra.gsync = grid_sync(h);
@@ -832,7 +835,7 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
     const int epad = (c->num_experts + 1 + 7) / 8 * 8;
     const size_t need = make_plan(T, T, c->hidden, c->num_experts, c->top_k, epad, router_ksplit(&h, T, c->hidden),
                                   c->inter, c->shared_inter, c->shared_inter > 0, true,
-                                  use_tc(&h, T * c->top_k, c->num_experts))
+                                  use_tc(&h, T * c->top_k, c->num_experts, c->group_size))
                             .total;
     if (need > kNoAllocScratchBytes) {
       rc = FM_ETOOLARGE;

@@ -177,7 +177,7 @@ struct RouteArgs {
   int a_n_shared;               // shared output rows of table a (0 = no shared group)
   int b_n;                      // output rows of table b (H)
   int b_rows_per_block;         // GEMV 128, tcgen05 pairs 256
-  int chunk_max;                // token rows per chunk cap (32 GEMV, 256 tcgen05)
+  int chunk_max;                // token rows per chunk cap (8 GEMV, 256 tcgen05)
   int chunk_align;              // chunk size granularity (8 GEMV, 16 tcgen05)
   int b_ksplit_shared;          // K splits of the shared down group (GEMV)
   int has_shared;

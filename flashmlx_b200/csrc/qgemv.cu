@@ -1,20 +1,33 @@
-// qgemv.cu -- small-batch expert products: 4-bit affine dequant GEMV on the legacy
-// tensor pipe (mma.sync m16n8k16), for decode-sized batches (few tokens per expert).
+// qgemv.cu -- small-batch expert products: 4-bit affine GEMV on the legacy tensor
+// pipe (mma.sync m16n8k16), for decode-sized batches (few tokens per expert).
 //
 // Replaces mx::gather_qmm / mx::quantized_matmul for the decode path
 // (model.cpp:703-721, 741-747; decode reaches them with T*k < 64 unsorted, or sorted
 // with a handful of tokens per expert).  The kernel is HBM-bound: every weight byte
-// of an active expert is read once with 128-bit loads; inactive experts are never
-// touched.
+// of an active expert is read from HBM once (a group with more than 8 rows re-reads
+// its weights from L2 per 8-row chunk); inactive experts are never touched.
 //
-// Work unit (one CTA of 4 warps): an output-row block x a chunk of <= 32 activation
-// rows x an optional K split.  Warp w owns two 16-row MMA tiles:
+// Arithmetic (the affine split MLX's own small-batch qmv uses): per quantization
+// group g of a weight row, y += s_g * sum_k(q_k x_k) + b_g * sum_k(x_k), in fp32, with
+// the exact codes q fed to the tensor core as bf16 (0x4300 | q == 128 + q, exact), so
+// a code costs ~1 ALU op instead of a bf16 dequantization (the dequantizing form was
+// issue-bound at a quarter of HBM bandwidth).  The 128 offset folds into the bias
+// term: s*sum((128+q)x) + (b - 128 s)*sum(x).  sum(x) per token and group comes from
+// one extra MMA against an all-ones A fragment.  Group sizes 64 and 128 (a 64-wide
+// half chunk never straddles a group); the host sends group size 32 to tcgen05.
+//
+// Work unit (one CTA of 4 warps): an output-row block x a chunk of <= 8 activation
+// rows (one MMA column tile) x an optional K split.  Warp w owns two 16-row MMA tiles:
 //   gate/up mode: gate rows [64 rb + 16 w, +16) and the same up rows (SwiGLU in regs)
 //   down / plain: rows [128 rb + 32 w, +16) and [.. + 16, +16)
-// Lane (g = lane/4, c = lane%4) loads 16 bytes (32 codes) of rows g and g+8 per
-// 128-wide K chunk; code pairs (q_i, q_{i+4}) become bf16x2 A fragments directly,
-// and the activation rows are stored with the matching within-8 pair permutation,
-// so each B fragment is one 32-bit word of a 16-byte load.
+// Per 128-wide K chunk, lane (g = lane/4, c = lane%4) loads words {2c, 2c+1} and
+// {8+2c, 9+2c} of rows g and g+8 (two 8-byte loads per row); MMA k-step j of half h
+// takes code pairs 2(j&1), 2(j&1)+1 of word 8h + 2c + j/2, which matches the within-8
+// pair order of the activation rows, so every k-step lies inside one quant group.
+// Codes and scales stream through a three-chunk register ring (two chunks in flight
+// per warp); the activation chunk of the unit is staged in shared memory by cp.async.
+#include <type_traits>
+
 #include "fm_internal.cuh"
 
 namespace fm {
@@ -22,16 +35,7 @@ namespace fm {
 namespace {
 
 constexpr int kGvThreads = 128;
-constexpr int kGvMaxNT = 4;  // 8-token MMA column tiles per work unit
-
-FM_DEV uint32_t word_of(const uint4& v, int i) {
-  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
-}
-
-FM_DEV __nv_bfloat162 bf2_splat(uint16_t b) {
-  const uint32_t u = static_cast<uint32_t>(b) * 0x10001u;
-  return *reinterpret_cast<const __nv_bfloat162*>(&u);
-}
+constexpr int kXStride = 132;  // staged activation row stride (bf16): 264 B keeps the 8-byte fragment reads conflict-free
 
 FM_DEV float swiglu1(float g, float u) {  // model.cpp:14-25, bf16 rounding per op
   const float gs = rbf(sigmoid_f(g));
@@ -39,17 +43,38 @@ FM_DEV float swiglu1(float g, float u) {  // model.cpp:14-25, bf16 rounding per 
   return rbf(h * u);
 }
 
+// code pair (q_p, q_{p+4}) of a packed word as bf16x2 (128 + q_p, 128 + q_{p+4})
+FM_DEV uint32_t code_pair_128(uint32_t w, int p) { return ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u; }
+
+FM_DEV uint2 ldg_nc_v2(const uint32_t* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+FM_DEV void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+
 }  // namespace
 
 template <int MODE>
-__global__ void __launch_bounds__(kGvThreads) qgemv_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const TileTable* tab = a.tab;
   if (*reinterpret_cast<volatile uint32_t*>(a.err) != 0u) return;  // an earlier kernel failed
   const int ntiles = tab->num_tiles;
+  // shared-memory copy of the groups' first tile ids (tile lookups stay on chip) and a
+  // three-slot ring of 8 activation rows x 128 K (the B operand of one chunk)
+  __shared__ int s_tb[kMaxGroups];
+  __shared__ __align__(16) uint16_t s_x[3][8][kXStride];
+  const int ngroups = min(tab->num_groups, kMaxGroups);
+  for (int i = threadIdx.x; i < ngroups; i += blockDim.x) s_tb[i] = tab->g[i].tile_begin;
+  __syncthreads();
+  const bool gs128 = a.gs == 128;  // else 64: two groups per 128-wide chunk
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-    const TileInfo ti = decode_tile(tab, tile);
+    const TileInfo ti = decode_tile(tab, s_tb, ngroups, tile);
     const bool sh = ti.expert < 0;
     const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
     const int N = sh ? a.N_shared : a.N;
@@ -74,139 +99,158 @@ __global__ void __launch_bounds__(kGvThreads) qgemv_kernel(const GemmArgs a) {
     }
     const bool mval0 = r0[0] < N, mval1 = r0[1] < N;  // N % 16 == 0 (host-checked)
 
-    const uint32_t* wrow[2][2];
-    const uint16_t* srow[2][2];
-    const uint16_t* brow[2][2];
+    // row g of each 16-row tile (row g + 8 is 8 rows further)
+    const uint32_t* wrow[2];
+    const uint16_t* srow[2];
+    const uint16_t* brow[2];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int64_t r = erow + min(r0[m] + g + 8 * h, N - 1);
-        wrow[m][h] = Wm[m] + r * kw;
-        srow[m][h] = Sm[m] + r * gpr;
-        brow[m][h] = Bm[m] ? Bm[m] + r * gpr : nullptr;
-      }
-
-    // activation rows of the chunk: n-tile j, column g -> slot 8j + g
-    const int nt = (ti.nrows + 7) >> 3;
-    const uint16_t* xrow[kGvMaxNT];
-#pragma unroll
-    for (int j = 0; j < kGvMaxNT; ++j) {
-      const int slot = 8 * j + g;
-      xrow[j] = nullptr;
-      if (j < nt && slot < ti.nrows) {
-        const int p = ti.row0 + slot;
-        int64_t src;
-        const uint16_t* base;
-        int64_t ld;
-        if (MODE == MODE_DOWN) {
-          src = p;
-          base = sh ? a.act_shared : a.act;
-          ld = sh ? a.act_shared_ld : a.act_ld;
-        } else {
-          src = sh ? p : a.sorted_token[p];
-          base = sh ? a.act_shared : a.act;
-          ld = sh ? a.act_shared_ld : a.act_ld;
-        }
-        xrow[j] = base + src * ld;
-      }
+    for (int m = 0; m < 2; ++m) {
+      const int64_t r = erow + min(r0[m] + g, N - 1);
+      wrow[m] = Wm[m] + r * kw + 2 * c;
+      srow[m] = Sm[m] + r * gpr;
+      brow[m] = Bm[m] ? Bm[m] + r * gpr : nullptr;
     }
 
     const int kchunks = K / 128;
     const int kc0 = kchunks * ti.ks / ti.ksplit, kc1 = kchunks * (ti.ks + 1) / ti.ksplit;
-    float acc[2][kGvMaxNT][4];
-#pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int j = 0; j < kGvMaxNT; ++j) acc[m][j][0] = acc[m][j][1] = acc[m][j][2] = acc[m][j][3] = 0.f;
+    __syncthreads();  // every warp is done reading the ring of the previous unit
+    // activation rows of the unit (<= 8): thread tid copies 16 bytes (two 8-byte copies)
+    // of row tid / 16 per chunk into the ring; rows past the unit are zero-filled
+    const int xr = threadIdx.x >> 4, xc = threadIdx.x & 15;
+    const uint16_t* xsrc = nullptr;
+    if (xr < ti.nrows) {
+      const int p = ti.row0 + xr;
+      const int64_t src = (MODE == MODE_DOWN || sh) ? p : a.sorted_token[p];
+      xsrc = (sh ? a.act_shared : a.act) + src * (sh ? a.act_shared_ld : a.act_ld) + xc * 8;
+    }
+    auto load_x = [&](int kc, int slot) {
+      uint16_t* d = &s_x[slot][xr][xc * 8];
+      if (kc < kc1 && xsrc) {
+        cp_async8(smem_u32(d), xsrc + kc * 128);
+        cp_async8(smem_u32(d + 4), xsrc + kc * 128 + 4);
+      } else {
+        *reinterpret_cast<uint2*>(d) = make_uint2(0, 0);
+        *reinterpret_cast<uint2*>(d + 4) = make_uint2(0, 0);
+      }
+      cp_async_commit();
+    };
 
-    const uint4 z4 = make_uint4(0, 0, 0, 0);
-    uint4 A[2][2];
+    float y[2][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-        A[m][h] = (kc0 < kc1 && (m == 0 ? mval0 : mval1)) ? ldg_nc_v4(wrow[m][h] + kc0 * 16 + 4 * c) : z4;
+    for (int m = 0; m < 2; ++m) y[m][0] = y[m][1] = y[m][2] = y[m][3] = 0.f;
 
-    for (int kc = kc0; kc < kc1; ++kc) {
-      // prefetch the next chunk's codes
-      uint4 An[2][2];
-      const bool more = kc + 1 < kc1;
-#pragma unroll
-      for (int m = 0; m < 2; ++m)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          An[m][h] = (more && (m == 0 ? mval0 : mval1)) ? ldg_nc_v4(wrow[m][h] + (kc + 1) * 16 + 4 * c) : z4;
-      // scales / biases of the group holding this lane's 32 codes
-      const int grp = (kc * 128 + 32 * c) / a.gs;
-      __nv_bfloat162 s2[2][2], b2[2][2];
+    // Three-slot register ring: chunk kc is consumed from slot 0 while chunks kc+1 and
+    // kc+2 are in flight: codes W[m][h][half] (2 words each) and the raw bf16 scale /
+    // bias pairs of rows g, g+8 (groups of the two halves, low half = first group).
+    constexpr int RING = 3;
+    uint2 W[RING][2][2][2];
+    uint32_t S2[RING][2][2], B2[RING][2][2];
+    auto load_chunk = [&](int kc, uint2 (&Wd)[2][2][2], uint32_t (&Sd)[2][2], uint32_t (&Bd)[2][2]) {
+      const bool in = kc < kc1;
 #pragma unroll
       for (int m = 0; m < 2; ++m)
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          s2[m][h] = bf2_splat(__ldg(srow[m][h] + grp));
-          b2[m][h] = bf2_splat(brow[m][h] ? __ldg(brow[m][h] + grp) : static_cast<uint16_t>(0));
-        }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        uint4 Bv[kGvMaxNT];
-#pragma unroll
-        for (int j = 0; j < kGvMaxNT; ++j)
-          Bv[j] = xrow[j] ? __ldg(reinterpret_cast<const uint4*>(xrow[j] + kc * 128 + 32 * c + 8 * i)) : z4;
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            if (!(m == 0 ? mval0 : mval1)) continue;
-            const uint32_t wg = word_of(A[m][0], i), wg8 = word_of(A[m][1], i);
-            const uint32_t a0 = deq_pair(wg, 2 * hh, s2[m][0], b2[m][0]);
-            const uint32_t a1 = deq_pair(wg8, 2 * hh, s2[m][1], b2[m][1]);
-            const uint32_t a2 = deq_pair(wg, 2 * hh + 1, s2[m][0], b2[m][0]);
-            const uint32_t a3 = deq_pair(wg8, 2 * hh + 1, s2[m][1], b2[m][1]);
-#pragma unroll
-            for (int j = 0; j < kGvMaxNT; ++j)
-              if (j < nt) mma_bf16_16816(acc[m][j], a0, a1, a2, a3, word_of(Bv[j], 2 * hh), word_of(Bv[j], 2 * hh + 1));
+          const bool v = in && (m == 0 ? mval0 : mval1);
+          const uint32_t* wp = wrow[m] + 8 * h * kw + kc * 16;
+          Wd[m][h][0] = v ? ldg_nc_v2(wp) : make_uint2(0, 0);
+          Wd[m][h][1] = v ? ldg_nc_v2(wp + 8) : make_uint2(0, 0);
+          const uint16_t* sp = srow[m] + 8 * h * gpr;
+          const uint16_t* bp = brow[m] ? brow[m] + 8 * h * gpr : nullptr;
+          if (gs128) {
+            const uint32_t sv = v ? static_cast<uint32_t>(__ldg(sp + kc)) : 0u;
+            const uint32_t bv = (v && bp) ? static_cast<uint32_t>(__ldg(bp + kc)) : 0u;
+            Sd[m][h] = sv * 0x10001u;
+            Bd[m][h] = bv * 0x10001u;
+          } else {  // groups 2kc, 2kc+1: one aligned 4-byte load (gpr is even)
+            Sd[m][h] = v ? __ldg(reinterpret_cast<const uint32_t*>(sp + 2 * kc)) : 0u;
+            Bd[m][h] = (v && bp) ? __ldg(reinterpret_cast<const uint32_t*>(bp + 2 * kc)) : 0u;
           }
         }
+    };
+#pragma unroll
+    for (int r = 0; r < RING; ++r) load_chunk(kc0 + r, W[r], S2[r], B2[r]);
+    load_x(kc0, 0);
+    load_x(kc0 + 1, 1);
+
+    const uint32_t ONES = 0x3F803F80u;  // bf16x2 (1, 1)
+    // Chunk kc lives in ring slot (kc - kc0) % 3; the loop is unrolled by the ring size
+    // so every slot is a fixed set of registers (a register copy between slots would
+    // wait for that slot's loads and collapse the ring to one chunk in flight).
+    auto step = [&](int kc, auto slot_c) {
+      constexpr int SL = decltype(slot_c)::value;
+      cp_async_wait<1>();  // this thread's copy of chunk kc has landed
+      __syncthreads();     // ... and every thread's; chunk kc-1's slot is free again
+      load_x(kc + 2, (SL + 2) % 3);
+      const uint16_t* xrowg = &s_x[SL][g][0];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        float acc[2][4], xsum[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[0][e] = acc[1][e] = xsum[e] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int wi = j >> 1, p0 = 2 * (j & 1);
+          const uint2 bx = *reinterpret_cast<const uint2*>(xrowg + (hf * 8 + 2 * c + wi) * 8 + 2 * p0);
+          mma_bf16_16816(xsum, ONES, ONES, ONES, ONES, bx.x, bx.y);
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {  // rows past N carry zero codes and scales
+            const uint32_t wg = wi ? W[SL][m][0][hf].y : W[SL][m][0][hf].x;
+            const uint32_t wg8 = wi ? W[SL][m][1][hf].y : W[SL][m][1][hf].x;
+            mma_bf16_16816(acc[m], code_pair_128(wg, p0), code_pair_128(wg8, p0), code_pair_128(wg, p0 + 1),
+                           code_pair_128(wg8, p0 + 1), bx.x, bx.y);
+          }
+        }
+        // this half's quant group: y += s * acc + (b - 128 s) * sum(x)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const float s0 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][0] >> 16 : S2[SL][m][0] & 0xffffu));
+          const float s8 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][1] >> 16 : S2[SL][m][1] & 0xffffu));
+          const float b0 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][0] >> 16 : B2[SL][m][0] & 0xffffu));
+          const float b8 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][1] >> 16 : B2[SL][m][1] & 0xffffu));
+          const float c0 = fmaf(-128.f, s0, b0), c8 = fmaf(-128.f, s8, b8);
+          y[m][0] = fmaf(s0, acc[m][0], fmaf(c0, xsum[0], y[m][0]));
+          y[m][1] = fmaf(s0, acc[m][1], fmaf(c0, xsum[1], y[m][1]));
+          y[m][2] = fmaf(s8, acc[m][2], fmaf(c8, xsum[2], y[m][2]));
+          y[m][3] = fmaf(s8, acc[m][3], fmaf(c8, xsum[3], y[m][3]));
+        }
       }
-#pragma unroll
-      for (int m = 0; m < 2; ++m)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) A[m][h] = An[m][h];
+      load_chunk(kc + RING, W[SL], S2[SL], B2[SL]);  // refill this slot RING chunks ahead
+    };
+    for (int kc = kc0; kc < kc1; kc += RING) {
+      step(kc, std::integral_constant<int, 0>{});
+      if (kc + 1 < kc1) step(kc + 1, std::integral_constant<int, 1>{});
+      if (kc + 2 < kc1) step(kc + 2, std::integral_constant<int, 2>{});
     }
 
-    // epilogue: acc[m][j][e] is (row r0[m] + g + 8*(e>>1), slot 8j + 2c + (e&1))
+    // epilogue: y[m][e] is (row r0[m] + g + 8*(e>>1), slot 2c + (e&1))
 #pragma unroll
-    for (int j = 0; j < kGvMaxNT; ++j) {
-      if (j >= nt) continue;
+    for (int e = 0; e < 4; ++e) {
+      const int slot = 2 * c + (e & 1);
+      if (slot >= ti.nrows) continue;
+      const int p = ti.row0 + slot;
+      if (MODE == MODE_GATEUP) {
+        if (!mval0) continue;
+        const int n = r0[0] + g + 8 * (e >> 1);
+        const float gv = rbf(y[0][e]), uv = rbf(y[1][e]);
+        uint16_t* out = sh ? a.out_shared + static_cast<int64_t>(p) * a.out_shared_ld
+                           : a.out + static_cast<int64_t>(p) * a.out_ld;
+        out[perm8(n)] = f2bf(swiglu1(gv, uv));
+      } else {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int slot = 8 * j + 2 * c + (e & 1);
-        if (slot >= ti.nrows) continue;
-        const int p = ti.row0 + slot;
-        if (MODE == MODE_GATEUP) {
-          if (!mval0) continue;
-          const int n = r0[0] + g + 8 * (e >> 1);
-          const float gv = rbf(acc[0][j][e]), uv = rbf(acc[1][j][e]);
-          uint16_t* out = sh ? a.out_shared + static_cast<int64_t>(p) * a.out_shared_ld
-                             : a.out + static_cast<int64_t>(p) * a.out_ld;
-          out[perm8(n)] = f2bf(swiglu1(gv, uv));
-        } else {
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            if (!(m == 0 ? mval0 : mval1)) continue;
-            const int n = r0[m] + g + 8 * (e >> 1);
-            const float v = acc[m][j][e];
-            if (MODE == MODE_DOWN) {
-              if (sh) {
-                red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v);
-              } else {
-                const int t = a.sorted_token[p];
-                red_add_f32(a.y_acc + static_cast<int64_t>(t) * a.y_ld + n, rbf(rbf(v) * a.sorted_score[p]));
-              }
+        for (int m = 0; m < 2; ++m) {
+          if (!(m == 0 ? mval0 : mval1)) continue;
+          const int n = r0[m] + g + 8 * (e >> 1);
+          const float v = y[m][e];
+          if (MODE == MODE_DOWN) {
+            if (sh) {
+              red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v);
             } else {
-              a.out[static_cast<int64_t>(a.sorted_flat[p]) * a.out_ld + n] = f2bf(v);
+              const int t = a.sorted_token[p];
+              red_add_f32(a.y_acc + static_cast<int64_t>(t) * a.y_ld + n, rbf(rbf(v) * a.sorted_score[p]));
             }
+          } else {
+            a.out[static_cast<int64_t>(a.sorted_flat[p]) * a.out_ld + n] = f2bf(v);
           }
         }
       }

@@ -14,11 +14,12 @@ ulp is large against the small output, so an element-wise relative bound would
 measure the cancellation, not the kernel.  The element-wise figure (rms floor) is
 still reported as max_rel_elem.
 
-The device feeds bf16 tensor cores, so each dequantized weight s*q+b is rounded once
-to bf16 (MLX's Metal qmm also dequantizes into bf16 tiles).  The oracle evaluated in
-that weight-rounding mode is the tight reference (TIGHT).  Against the exact-
-arithmetic oracle the bf16 weight rounding alone leaves mae_rel ~1.4e-3 on a single
-4-bit GEMM; EXACT_FLOOR bounds that documented gap.
+MLX evaluates a 4-bit product in one of two forms: its large-batch qmm rounds each
+dequantized weight s*q+b once to bf16 (bf16 threadgroup tiles), its small-batch qmv
+keeps the weights exact (s*sum(q x) + b*sum(x) in fp32).  The device's tcgen05 path
+follows qmm, its GEMV path qmv; the oracle evaluates either form (weight-rounding
+mode), and the form a path follows is the tight reference (TIGHT).  The two forms
+differ by mae_rel ~1.4e-3 on a single 4-bit GEMM; EXACT_FLOOR bounds that gap.
 """
 from __future__ import annotations
 

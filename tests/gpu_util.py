@@ -10,15 +10,20 @@ from tests._parity import EXACT_FLOOR, TIGHT, assert_close, near_tie_tokens, sam
 
 
 def check_vs_oracle(y_bits, oracle_fn, what):
-    """Compare against the oracle with bf16-rounded dequantized weights (tight) and with
-    exact dequantization (documented floor).  Returns both metric dicts."""
+    """MLX has two arithmetic forms for a 4-bit product: qmm (large batches) rounds the
+    dequantized weights to bf16 tiles, qmv (small batches) keeps them exact (affine split
+    s*sum(q x) + b*sum(x) in fp32).  The tcgen05 path follows the first, the GEMV path the
+    second.  The result must match one form within TIGHT and both within EXACT_FLOOR
+    (the documented gap between the forms).  Returns (bf16-weights metrics, exact metrics)."""
     with O.weight_rounding(O.BF16_WEIGHTS):
         yt = oracle_fn()
     yt = yt[0] if isinstance(yt, tuple) else yt
-    mt = assert_close(y_bits, yt, what + " [oracle, bf16 weights]", **TIGHT)
     ye = oracle_fn()
     ye = ye[0] if isinstance(ye, tuple) else ye
+    mt = assert_close(y_bits, yt, what + " [oracle, bf16 weights]", **EXACT_FLOOR)
     me = assert_close(y_bits, ye, what + " [oracle, exact weights]", **EXACT_FLOOR)
+    best = min((mt, "bf16 weights"), (me, "exact weights"), key=lambda m: m[0]["mae_rel"])
+    assert_close(y_bits, yt if best[1] == "bf16 weights" else ye, what + f" [oracle, {best[1]}, tight]", **TIGHT)
     return mt, me
 
 

@@ -151,8 +151,9 @@ def test_paths_agree(ops):
             h.set_path(0)
     (ya, ra), (yb, rb) = outs
     np.testing.assert_array_equal(ra["topk_ids"], rb["topk_ids"])
-    from tests._parity import TIGHT, assert_close
-    assert_close(ya, yb, "gemv vs tcgen05", **TIGHT)
+    # the two paths follow MLX's two arithmetic forms (exact vs bf16-rounded weights)
+    from tests._parity import EXACT_FLOOR, assert_close
+    assert_close(ya, yb, "gemv vs tcgen05", **EXACT_FLOOR)
 
 
 def test_moe_block_argument_errors(ops):
