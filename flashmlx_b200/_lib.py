@@ -64,6 +64,12 @@ SIGNATURES = {
     "fm_moe_block": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p,
                           C.POINTER(MoEOutputs)]),
     "fm_moe_block_noalloc": (_i, [_i, _p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p]),
+    "fm_ep_range": (_i, [_i, _i, _i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "fm_ep_set": (_i, [_p, _i, _i]),
+    "fm_ep_dispatch": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, C.POINTER(C.c_int32),
+                            C.POINTER(C.c_void_p)]),
+    "fm_ep_experts": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, C.POINTER(C.c_int32), _p]),
+    "fm_ep_combine": (_i, [_p, C.POINTER(MoEConfig), _p, _p]),
 }
 
 _lib = None

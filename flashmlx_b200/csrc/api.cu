@@ -26,6 +26,11 @@ __global__ void finalize_kernel(const float* y_acc, const float* ysh, const floa
                                 uint16_t* y);
 __global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
                                       const float* gate_sig, int64_t T, int H, uint16_t* y);
+__global__ void ep_plan_kernel(const EpPlanArgs a);
+__global__ void ep_gather_kernel(const uint16_t* x_perm, const int32_t* sorted_token, int64_t P, int H, uint16_t* send);
+__global__ void finalize_ep_kernel(const uint16_t* ret, const int32_t* pair_pos, const float* score, int k,
+                                   const float* ysh32, const uint16_t* ysh16, const float* gate_sig, int64_t T, int H,
+                                   uint16_t* y);
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
 cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
@@ -48,6 +53,17 @@ struct fm_handle {
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
   bool borrowed_ws = false;  // ws is fixed scratch the handle must never grow or free
+  // expert parallelism (fm_ep_*): this rank's place, the dispatch the next calls
+  // refer to, and the owner-side workspace (sized by the rows received)
+  int ep_rank = 0;
+  int ep_world = 1;
+  int64_t ep_T = -1;       // tokens of the last fm_ep_dispatch (-1: none)
+  int64_t ep_R = 0;        // rows received by the last fm_ep_experts
+  int ep_stage = 0;        // 1 after dispatch, 2 after experts
+  bool ep_ysh_bf16 = false;
+  bool ep_shared = false;
+  uint8_t* ep_ws = nullptr;
+  size_t ep_ws_bytes = 0;
   // kernel timing (fm_profile_enable)
   bool profile = false;
   struct Pending {
@@ -305,6 +321,104 @@ int check_moe(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w) {
   return FM_OK;
 }
 
+
+// ---------------------------------------------------------------- expert parallelism
+// Balanced contiguous expert ranges: the first E % world ranks own one expert more.
+void ep_range(int E, int rank, int world, int* first, int* count) {
+  const int base = E / world, rem = E % world;
+  *count = base + (rank < rem ? 1 : 0);
+  *first = rank * base + std::min(rank, rem);
+}
+
+// Token-side workspace (fm_ep_dispatch .. fm_ep_combine): routing state, the
+// pair-position map, and the send rows.
+struct EpPlan1 {
+  size_t total = 0;
+  size_t partial, x_perm, topk_ids, topk_score, gate_sig, row_src, chunk_counts, pair_rank, totals, offsets,
+      sorted_token, sorted_score, sorted_flat, pair_pos, send;
+  size_t add(size_t bytes) {
+    const size_t off = total;
+    total = align_up(total + bytes, 256);
+    return off;
+  }
+};
+
+EpPlan1 make_ep_plan1(int64_t T, int H, int E, int k, int epad, int ksplit) {
+  EpPlan1 p;
+  p.total = kCtrlBytes;
+  const int64_t P = T * k;
+  const int64_t nchunks = (T + fm::kRouteChunk - 1) / fm::kRouteChunk;
+  p.partial = p.add(sizeof(float) * ksplit * T * epad);
+  p.x_perm = p.add(sizeof(uint16_t) * T * H);
+  p.topk_ids = p.add(sizeof(int32_t) * P);
+  p.topk_score = p.add(sizeof(float) * P);
+  p.gate_sig = p.add(sizeof(float) * T);
+  p.row_src = p.add(sizeof(int32_t) * T);
+  p.chunk_counts = p.add(sizeof(int32_t) * nchunks * E);
+  p.pair_rank = p.add(sizeof(int32_t) * P);
+  p.totals = p.add(sizeof(int32_t) * E);
+  p.offsets = p.add(sizeof(int32_t) * (E + 1));
+  p.sorted_token = p.add(sizeof(int32_t) * P);
+  p.sorted_score = p.add(sizeof(float) * P);
+  p.sorted_flat = p.add(sizeof(int32_t) * P);
+  p.pair_pos = p.add(sizeof(int32_t) * P);
+  p.send = p.add(sizeof(uint16_t) * P * H);
+  return p;
+}
+
+// Owner-side workspace (fm_ep_experts): tile tables and expert intermediates for the
+// R received rows plus this rank's shared-expert rows.
+struct EpPlan2 {
+  size_t total = 0;
+  size_t tab_a, tab_b, recv_counts, recv_total, row_map, unit_score, a_sorted, a_shared, ysh;
+  size_t add(size_t bytes) {
+    const size_t off = total;
+    total = align_up(total + bytes, 256);
+    return off;
+  }
+};
+
+EpPlan2 make_ep_plan2(int64_t R, int64_t T, int H, int I, int Is, int nseg, bool shared) {
+  EpPlan2 p;
+  p.tab_a = p.add(sizeof(TileTable));
+  p.tab_b = p.add(sizeof(TileTable));
+  p.recv_counts = p.add(sizeof(int32_t) * nseg);
+  p.recv_total = p.add(sizeof(int32_t));
+  p.row_map = p.add(sizeof(int32_t) * std::max<int64_t>(R, 1));
+  p.unit_score = p.add(sizeof(float) * std::max<int64_t>(R, 1));
+  p.a_sorted = p.add(sizeof(uint16_t) * R * I);
+  p.a_shared = p.add(shared ? sizeof(uint16_t) * T * Is : 0);
+  p.ysh = p.add(shared ? sizeof(float) * T * H : 0);  // fp32 (GEMV) or bf16 (tcgen05) rows
+  return p;
+}
+
+int ensure_ep_ws(fm_handle* h, size_t bytes) {
+  if (bytes <= h->ep_ws_bytes) return FM_OK;
+  if (h->borrowed_ws) return set_err(h, FM_ETOOLARGE, "expert parallelism needs an allocating handle");
+  cudaError_t e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaStreamSynchronize");
+  if (h->ep_ws) cudaFree(h->ep_ws);
+  h->ep_ws = nullptr;
+  h->ep_ws_bytes = 0;
+  const size_t want = align_up(bytes + bytes / 8, 1 << 20);
+  e = cudaMalloc(&h->ep_ws, want);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_err(h, FM_ENOMEM, std::string("expert-parallel workspace allocation failed: ") + cudaGetErrorString(e));
+  }
+  h->ep_ws_bytes = want;
+  return FM_OK;
+}
+
+template <class T>
+T* ep_at(fm_handle* h, size_t off) {
+  return reinterpret_cast<T*>(h->ep_ws + off);
+}
+
+int grid_for(const fm_handle* h, int64_t work) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(h->num_sms) * 8)));
+}
+
 }  // namespace
 
 extern "C" {
@@ -370,6 +484,7 @@ int fm_destroy(fm_handle* h) {
   }
   for (auto e : h->event_pool) cudaEventDestroy(e);
   if (h->ws) cudaFree(h->ws);
+  if (h->ep_ws) cudaFree(h->ep_ws);
   delete h;
   return FM_OK;
 }
@@ -728,6 +843,278 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
   return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps);
+}
+
+
+// ---------------------------------------------------------------- expert parallelism
+int fm_ep_range(int num_experts, int rank, int world, int* first, int* count) {
+  if (num_experts <= 0 || world <= 0 || rank < 0 || rank >= world || !first || !count) return FM_EINVAL;
+  ep_range(num_experts, rank, world, first, count);
+  return FM_OK;
+}
+
+int fm_ep_set(fm_handle* h, int rank, int world) {
+  if (!h) return FM_EINVAL;
+  if (world <= 0 || rank < 0 || rank >= world) return set_err(h, FM_EINVAL, "bad expert-parallel rank / world");
+  h->ep_rank = rank;
+  h->ep_world = world;
+  h->ep_T = -1;
+  h->ep_stage = 0;
+  return FM_OK;
+}
+
+int fm_ep_dispatch(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
+                   int32_t* expert_counts, const uint16_t** send_rows) {
+  if (!h) return FM_EINVAL;
+  if (!c || !w || !expert_counts || !send_rows) return set_err(h, FM_EINVAL, "null argument");
+  if (c->hidden <= 0 || c->num_experts <= 0 || c->top_k <= 0 || c->top_k > c->num_experts || c->top_k > 16 ||
+      c->num_experts > fm::kMaxExperts)
+    return set_err(h, FM_EINVAL, "bad MoE dimensions");
+  if (c->hidden % 128) return set_err(h, FM_EUNSUPPORTED, "hidden must be a multiple of 128");
+  if (c->router_quantized || c->shared_gate_quantized)
+    return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
+  if (!w->router_w || (c->shared_inter > 0 && !w->shared_expert_gate_w))
+    return set_err(h, FM_EINVAL, "router weights missing");
+  if (T < 0 || (T > 0 && !x)) return set_err(h, FM_EINVAL, "bad x / T");
+  if (!aligned16(x)) return set_err(h, FM_EINVAL, "x must be 16-byte aligned");
+  if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
+  const int H = c->hidden, E = c->num_experts, k = c->top_k;
+  const bool shared = c->shared_inter > 0;
+  const int epad = (E + 1 + 7) / 8 * 8;
+  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
+  const int64_t P = T * k;
+  const EpPlan1 p = make_ep_plan1(T, H, E, k, epad, ksplit);
+  int rc = ensure_ws(h, p.total);
+  if (rc) return rc;
+  *send_rows = at<uint16_t>(h, p.send);
+  h->ep_T = T;
+  h->ep_stage = 1;
+  if (T == 0) {
+    std::memset(expert_counts, 0, sizeof(int32_t) * E);
+    return FM_OK;
+  }
+  RouteArgs ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.x = x;
+  ra.router_w = static_cast<const uint16_t*>(w->router_w);
+  ra.shared_gate_w = shared ? static_cast<const uint16_t*>(w->shared_expert_gate_w) : nullptr;
+  ra.router_bias = w->router_bias;
+  ra.T = T;
+  ra.H = H;
+  ra.E = E;
+  ra.k = k;
+  ra.norm_topk = c->norm_topk_prob;
+  ra.do_router = 1;
+  ra.ksplit = ksplit;
+  ra.epad = epad;
+  ra.partial = at<float>(h, p.partial);
+  ra.x_perm = at<uint16_t>(h, p.x_perm);
+  ra.x_rows = T;
+  ra.topk_ids = at<int32_t>(h, p.topk_ids);
+  ra.topk_score = at<float>(h, p.topk_score);
+  ra.gate_sig = at<float>(h, p.gate_sig);
+  ra.row_src = at<int32_t>(h, p.row_src);
+  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
+  ra.pair_rank = at<int32_t>(h, p.pair_rank);
+  ra.totals = at<int32_t>(h, p.totals);
+  ra.offsets = at<int32_t>(h, p.offsets);
+  ra.sorted_token = at<int32_t>(h, p.sorted_token);
+  ra.sorted_score = at<float>(h, p.sorted_score);
+  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.pair_pos = at<int32_t>(h, p.pair_pos);
+  ra.chunk_max = 8;
+  ra.chunk_align = 8;
+  ra.has_shared = shared ? 1 : 0;
+  ra.gsync = grid_sync(h);
+  ra.err = err_word(h);
+  ra.phase_ns = phase_ns(h);
+  rc = launch_route(h, ra, ((T + 15) / 16) * ksplit);
+  if (rc) return rc;
+  prof_begin(h, "ep_gather");
+  fm::ep_gather_kernel<<<grid_for(h, P * (H / 8)), 256, 0, h->stream>>>(ra.x_perm, ra.sorted_token, P, H,
+                                                                        at<uint16_t>(h, p.send));
+  prof_end(h);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_gather launch");
+  std::vector<int32_t> off(static_cast<size_t>(E) + 1);
+  e = cudaMemcpyAsync(off.data(), ra.offsets, sizeof(int32_t) * (E + 1), cudaMemcpyDeviceToHost, h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "expert counts");
+  uint32_t dev_err = 0;
+  e = cudaMemcpy(&dev_err, h->ws, sizeof(dev_err), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_err(h, e, "device error word");
+  if (dev_err) return set_err(h, FM_EDEVICE, "device-side check failed in routing");
+  for (int i = 0; i < E; ++i) expert_counts[i] = off[i + 1] - off[i];
+  return FM_OK;
+}
+
+int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* recv_rows,
+                  const int32_t* recv_counts, uint16_t* d_rows) {
+  if (!h) return FM_EINVAL;
+  if (h->ep_stage != 1) return set_err(h, FM_EINVAL, "fm_ep_experts must follow fm_ep_dispatch");
+  if (!c || !w || !recv_counts) return set_err(h, FM_EINVAL, "null argument");
+  int first = 0, E_local = 0;
+  ep_range(c->num_experts, h->ep_rank, h->ep_world, &first, &E_local);
+  const int nseg = h->ep_world * E_local;
+  if (nseg + 1 > fm::kMaxGroups) return set_err(h, FM_EUNSUPPORTED, "too many (rank, expert) segments");
+  int64_t R = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (recv_counts[i] < 0) return set_err(h, FM_EINVAL, "negative receive count");
+    R += recv_counts[i];
+  }
+  if (R > 0 && (!recv_rows || !d_rows)) return set_err(h, FM_EINVAL, "null receive / result rows");
+  if (!aligned16(recv_rows) || !aligned16(d_rows)) return set_err(h, FM_EINVAL, "rows must be 16-byte aligned");
+  const int64_t T = h->ep_T;
+  const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k, Is = c->shared_inter;
+  const bool shared = Is > 0 && T > 0;
+  if (I <= 0 || I % 128 || (Is > 0 && Is % 128) || !quant_ok(H, c->group_size, c->bits) ||
+      !quant_ok(I, c->group_size, c->bits))
+    return set_err(h, FM_EUNSUPPORTED, "inter / shared sizes must be multiples of 128, 4-bit affine");
+  if (R > 0 && (!w->gate.w || !w->up.w || !w->down.w || !w->gate.scales || !w->up.scales || !w->down.scales))
+    return set_err(h, FM_EINVAL, "local expert weights missing");
+  if (shared && (!w->shared_gate.w || !w->shared_up.w || !w->shared_down.w))
+    return set_err(h, FM_EINVAL, "shared expert weights missing");
+  const bool tcp = use_tc(h, R + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
+  const EpPlan2 p2 = make_ep_plan2(R, std::max<int64_t>(T, 0), H, I, Is, nseg, shared);
+  int rc = ensure_ep_ws(h, p2.total);
+  if (rc) return rc;
+  const EpPlan1 p1 = make_ep_plan1(std::max<int64_t>(T, 0), H, E, k, (E + 1 + 7) / 8 * 8,
+                                   router_ksplit(h, std::max<int64_t>(T, 1), H));
+  h->ep_ysh_bf16 = tcp;
+  h->ep_shared = shared;
+  h->ep_R = R;
+  h->ep_stage = 2;
+  cudaError_t e = cudaMemcpyAsync(ep_at<int32_t>(h, p2.recv_counts), recv_counts, sizeof(int32_t) * nseg,
+                                  cudaMemcpyHostToDevice, h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "receive counts");
+  if (shared && !tcp) {
+    e = cudaMemsetAsync(ep_at<float>(h, p2.ysh), 0, sizeof(float) * T * H, h->stream);
+    if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
+  }
+  fm::EpPlanArgs pa;
+  std::memset(&pa, 0, sizeof(pa));
+  pa.recv_counts = ep_at<int32_t>(h, p2.recv_counts);
+  pa.world = h->ep_world;
+  pa.E_local = E_local;
+  pa.T_shared = shared ? static_cast<int>(T) : 0;
+  pa.a_n = I;
+  pa.a_n_shared = Is;
+  pa.b_n = H;
+  pa.a_rows_per_block = tcp ? 128 : 64;
+  pa.b_rows_per_block = tcp ? 256 : 128;
+  pa.chunk_max = tcp ? fm::tc::max_rows() : 8;
+  pa.chunk_align = tcp ? 16 : 8;
+  pa.b_ksplit_shared = tcp ? 1 : std::max(1, Is / std::max(1, I));
+  pa.tab_a = ep_at<TileTable>(h, p2.tab_a);
+  pa.tab_b = ep_at<TileTable>(h, p2.tab_b);
+  pa.row_map = ep_at<int32_t>(h, p2.row_map);
+  pa.unit_score = ep_at<float>(h, p2.unit_score);
+  pa.recv_total = ep_at<int32_t>(h, p2.recv_total);
+  pa.err = err_word(h);
+  prof_begin(h, "ep_plan");
+  fm::ep_plan_kernel<<<1, fm::kRouteThreads, 0, h->stream>>>(pa);
+  prof_end(h);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_plan launch");
+  if (R == 0 && !shared) return FM_OK;
+
+  uint16_t* x_perm = at<uint16_t>(h, p1.x_perm);
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  ga.gs = c->group_size;
+  ga.err = err_word(h);
+  ga.sorted_token = pa.row_map;
+  ga.sorted_score = pa.unit_score;
+  ga.sorted_flat = pa.row_map;
+  ga.K = H;
+  ga.K_shared = H;
+  ga.N = I;
+  ga.N_shared = Is;
+  ga.w0 = w->gate.w; ga.s0 = w->gate.scales; ga.b0 = w->gate.biases;
+  ga.w1 = w->up.w; ga.s1 = w->up.scales; ga.b1 = w->up.biases;
+  if (shared) {
+    ga.sw0 = w->shared_gate.w; ga.ss0 = w->shared_gate.scales; ga.sb0 = w->shared_gate.biases;
+    ga.sw1 = w->shared_up.w; ga.ss1 = w->shared_up.scales; ga.sb1 = w->shared_up.biases;
+  }
+  ga.act = recv_rows;
+  ga.act_ld = H;
+  ga.act_shared = x_perm;
+  ga.act_shared_ld = H;
+  ga.out = ep_at<uint16_t>(h, p2.a_sorted);
+  ga.out_ld = I;
+  ga.out_shared = shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr;
+  ga.out_shared_ld = Is;
+  ga.tab = pa.tab_a;
+  fm::TcMaps maps_gu, maps_dn;
+  if (tcp) {
+    const bool ok =
+        encode_codes(&maps_gu.code[0], w->gate.w, static_cast<int64_t>(E_local) * I, H, 64) &&
+        encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E_local) * I, H, 64) &&
+        encode_codes(&maps_gu.code[2], shared ? w->shared_gate.w : nullptr, Is, H, 64) &&
+        encode_codes(&maps_gu.code[3], shared ? w->shared_up.w : nullptr, Is, H, 64) &&
+        encode_act(&maps_gu.act[0], R > 0 ? recv_rows : nullptr, R, H) &&
+        encode_act(&maps_gu.act[1], shared ? x_perm : nullptr, T, H) &&
+        encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E_local) * H, I, 128) &&
+        encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
+        encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
+        encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
+        encode_act(&maps_dn.act[0], R > 0 ? ep_at<uint16_t>(h, p2.a_sorted) : nullptr, R, I) &&
+        encode_act(&maps_dn.act[1], shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr, T, Is);
+    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+  }
+  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
+  if (rc) return rc;
+  GemmArgs gd = ga;
+  gd.K = I;
+  gd.K_shared = Is;
+  gd.N = H;
+  gd.N_shared = H;
+  gd.w0 = w->down.w; gd.s0 = w->down.scales; gd.b0 = w->down.biases;
+  gd.w1 = nullptr; gd.s1 = nullptr; gd.b1 = nullptr;
+  if (shared) {
+    gd.sw0 = w->shared_down.w; gd.ss0 = w->shared_down.scales; gd.sb0 = w->shared_down.biases;
+  }
+  gd.sw1 = nullptr; gd.ss1 = nullptr; gd.sb1 = nullptr;
+  gd.act = ga.out;
+  gd.act_ld = I;
+  gd.act_shared = ga.out_shared;
+  gd.act_shared_ld = Is;
+  gd.out = nullptr;
+  gd.out_shared = nullptr;
+  gd.y_pairs = d_rows;
+  gd.y_acc = nullptr;
+  gd.ysh = (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr;
+  gd.ysh16 = (shared && tcp) ? ep_at<uint16_t>(h, p2.ysh) : nullptr;
+  gd.y_ld = H;
+  gd.tab = pa.tab_b;
+  return launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
+}
+
+int fm_ep_combine(fm_handle* h, const fm_moe_config* c, const uint16_t* ret_rows, uint16_t* y) {
+  if (!h) return FM_EINVAL;
+  if (h->ep_stage != 2) return set_err(h, FM_EINVAL, "fm_ep_combine must follow fm_ep_experts");
+  if (!c) return set_err(h, FM_EINVAL, "null config");
+  const int64_t T = h->ep_T;
+  h->ep_stage = 0;
+  if (T == 0) return FM_OK;
+  if (!y || !ret_rows) return set_err(h, FM_EINVAL, "null rows");
+  if (!aligned16(ret_rows) || !aligned16(y)) return set_err(h, FM_EINVAL, "rows must be 16-byte aligned");
+  const int H = c->hidden, E = c->num_experts, k = c->top_k;
+  const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, router_ksplit(h, std::max<int64_t>(T, 1), H));
+  const int Is = c->shared_inter, I = c->inter;
+  int first = 0, E_local = 0;
+  ep_range(E, h->ep_rank, h->ep_world, &first, &E_local);
+  const EpPlan2 p2 = make_ep_plan2(h->ep_R, T, H, I, Is, h->ep_world * E_local, h->ep_shared);
+  const bool shared = h->ep_shared;
+  prof_begin(h, "ep_combine");
+  fm::finalize_ep_kernel<<<grid_for(h, T * (H / 8)), 256, 0, h->stream>>>(
+      ret_rows, at<int32_t>(h, p1.pair_pos), at<float>(h, p1.topk_score), k,
+      (shared && !h->ep_ysh_bf16) ? ep_at<float>(h, p2.ysh) : nullptr,
+      (shared && h->ep_ysh_bf16) ? ep_at<uint16_t>(h, p2.ysh) : nullptr, at<float>(h, p1.gate_sig), T, H, y);
+  prof_end(h);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_combine launch");
+  return FM_OK;
 }
 
 int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w,

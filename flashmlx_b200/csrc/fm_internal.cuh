@@ -191,6 +191,24 @@ struct RouteArgs {
   unsigned long long* phase_ns;  // [4] accumulated per-phase time of block 0 (profiling)
 };
 
+// Arguments of the expert-parallel plan kernel.
+struct EpPlanArgs {
+  const int32_t* recv_counts;  // [world, E_local] rows received per (source rank, local expert)
+  int world;
+  int E_local;
+  int T_shared;                // this rank's tokens for its shared-expert group (0: none)
+  int a_n, a_n_shared, b_n;    // output rows of the routed / shared matrices per table
+  int a_rows_per_block, b_rows_per_block;
+  int chunk_max, chunk_align;
+  int b_ksplit_shared;
+  TileTable* tab_a;
+  TileTable* tab_b;
+  int32_t* row_map;            // [R] identity (received row p is activation row p)
+  float* unit_score;           // [R] 1.0
+  int32_t* recv_total;         // R
+  uint32_t* err;
+};
+
 constexpr int kRouteThreads = 256;  // 8 warps
 constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
 constexpr int kRouterMaxKsplit = 16;  // K slices of the router partial logits

@@ -245,6 +245,8 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
           if (MODE == MODE_DOWN) {
             if (sh) {
               red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v);
+            } else if (a.y_pairs) {  // one output row per pair (expert-parallel owner side)
+              a.y_pairs[static_cast<int64_t>(p) * a.y_ld + n] = f2bf(rbf(rbf(v) * a.sorted_score[p]));
             } else {
               const int t = a.sorted_token[p];
               red_add_f32(a.y_acc + static_cast<int64_t>(t) * a.y_ld + n, rbf(rbf(v) * a.sorted_score[p]));
@@ -329,6 +331,65 @@ __global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, cons
       for (int q = 0; q < 4; ++q) {
         acc[2 * q] = rbf(acc[2 * q] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] & 0xffffu))));
         acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] >> 16))));
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(y + t * H + col) = o;
+  }
+}
+
+// Expert-parallel send buffer: row p = x_perm[sorted_token[p]] (the routed pairs in
+// expert-major order, so the rows bound for each owner rank are contiguous).
+__global__ void ep_gather_kernel(const uint16_t* __restrict__ x_perm, const int32_t* __restrict__ sorted_token,
+                                 int64_t P, int H, uint16_t* __restrict__ send) {
+  const int segs = H / 8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < P * segs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t p = i / segs;
+    const int col = static_cast<int>(i - p * segs) * 8;
+    *reinterpret_cast<uint4*>(send + p * H + col) =
+        *reinterpret_cast<const uint4*>(x_perm + static_cast<int64_t>(sorted_token[p]) * H + col);
+  }
+}
+
+// Expert-parallel combine on the token's rank: ret[pos] holds bf16(d) returned by the
+// owner of pair (t, j); y = bf16( bf16(sum_j bf16(d * score_j)) + bf16(gate * shared) ),
+// the sum over j = 0..k-1 in fp32 in that order (model.cpp:780-784, 800-803).  The
+// shared rows come as fp32 sums (GEMV path) or bf16 rows (tcgen05 path).
+__global__ void finalize_ep_kernel(const uint16_t* __restrict__ ret, const int32_t* __restrict__ pair_pos,
+                                   const float* __restrict__ score, int k, const float* __restrict__ ysh32,
+                                   const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig, int64_t T,
+                                   int H, uint16_t* __restrict__ y) {
+  const int segs = H / 8;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < T * segs;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / segs;
+    const int col = static_cast<int>(i - t * segs) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int pos = pair_pos[t * k + j];
+      if (pos < 0) continue;
+      const float sc = score[t * k + j];
+      const uint4 v = *reinterpret_cast<const uint4*>(ret + static_cast<int64_t>(pos) * H + col);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] += rbf(bf2f(static_cast<uint16_t>(w[q] & 0xffffu)) * sc);
+        acc[2 * q + 1] += rbf(bf2f(static_cast<uint16_t>(w[q] >> 16)) * sc);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = rbf(acc[q]);
+    if (ysh32 || ysh16) {
+      const float gsv = gate_sig[t];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float sv = ysh32 ? rbf(ysh32[t * H + col + q]) : bf2f(ysh16[t * H + col + q]);
+        acc[q] = rbf(acc[q] + rbf(gsv * sv));
       }
     }
     uint4 o;

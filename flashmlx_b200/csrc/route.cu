@@ -350,6 +350,34 @@ __device__ void phase_column_scan(const RouteArgs& a, RouteSmem& sm) {
 }
 
 // ------------------------------------------------------------------ phase 4
+// Group G's tiling: weight blocks of rows_per_block output rows, chunks of at most
+// chunk_max activation rows (balanced, rounded up to chunk_align), K splits.
+__device__ void plan_one(TileGroup& G, int n_out, int rows_per_block, int chunk_max, int chunk_align) {
+  G.nblocks = (n_out + rows_per_block - 1) / rows_per_block;
+  if (G.rows > 0) {
+    const int c0 = (G.rows + chunk_max - 1) / chunk_max;
+    int cr = (G.rows + c0 - 1) / c0;
+    cr = (cr + chunk_align - 1) / chunk_align * chunk_align;
+    G.chunk_rows = cr;
+    G.chunks = (G.rows + cr - 1) / cr;
+  } else {
+    G.chunk_rows = chunk_align;
+    G.chunks = 0;
+  }
+}
+
+// tile_begin of every group (exclusive scan of the tile counts) and the totals; cnt
+// holds each group's tile count on entry (one CTA)
+__device__ void finish_table(TileTable* tab, int ng, int* cnt, int* s_tmp) {
+  __syncthreads();
+  const int total = block_exclusive_scan(cnt, ng, s_tmp);
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) tab->g[gi].tile_begin = cnt[gi];
+  if (threadIdx.x == 0) {
+    tab->num_groups = ng;
+    tab->num_tiles = total;
+  }
+}
+
 __device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, int rows_per_block, int n_routed,
                             int n_shared, int ksplit_shared, int* cnt) {
   const int has_sh = (n_shared > 0) ? 1 : 0;
@@ -361,29 +389,12 @@ __device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, i
     G.expert = e;
     G.row_begin = sh ? 0 : sm.offs[e];
     G.rows = sh ? static_cast<int>(a.T) : (sm.offs[e + 1] - sm.offs[e]);
-    const int n = sh ? n_shared : n_routed;
-    G.nblocks = (n + rows_per_block - 1) / rows_per_block;
     G.ksplit = sh ? ksplit_shared : 1;
-    if (G.rows > 0) {
-      const int c0 = (G.rows + a.chunk_max - 1) / a.chunk_max;
-      int cr = (G.rows + c0 - 1) / c0;
-      cr = (cr + a.chunk_align - 1) / a.chunk_align * a.chunk_align;
-      G.chunk_rows = cr;
-      G.chunks = (G.rows + cr - 1) / cr;
-    } else {
-      G.chunk_rows = a.chunk_align;
-      G.chunks = 0;
-    }
+    plan_one(G, sh ? n_shared : n_routed, rows_per_block, a.chunk_max, a.chunk_align);
     tab->g[gi] = G;
     cnt[gi] = G.nblocks * G.chunks * G.ksplit;
   }
-  __syncthreads();
-  const int total = block_exclusive_scan(cnt, ng, sm.tmp);
-  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) tab->g[gi].tile_begin = cnt[gi];
-  if (threadIdx.x == 0) {
-    tab->num_groups = ng;
-    tab->num_tiles = total;
-  }
+  finish_table(tab, ng, cnt, sm.tmp);
 }
 
 __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
@@ -397,7 +408,7 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
       a.offsets[e] = sm.offs[e];
       if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
     }
-    plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
+    if (a.tab_a) plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
     if (a.tab_b)
       plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
   }
@@ -439,6 +450,51 @@ FM_DEV void phase_mark(const RouteArgs& a, int phase, unsigned long long& t) {
     atomicAdd(a.phase_ns + phase, now - t);
     t = now;
   }
+}
+
+// Expert-parallel plan (one CTA): the rows a rank received sit in source-rank order,
+// each source's rows in expert-major order, so every (source, local expert) segment is
+// one tile group over contiguous rows; the rank's own tokens form the shared-expert
+// group.  Also writes the identity row map and unit scores the expert kernels read
+// for the received rows (the owner returns bf16(d); the token's rank scales it).
+__global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const EpPlanArgs a) {
+  __shared__ int cnt_a[kMaxGroups + 1];
+  __shared__ int cnt_b[kMaxGroups + 1];
+  __shared__ int rbeg[kMaxGroups + 1];
+  __shared__ int s_tmp[40];
+  const int has_sh = a.T_shared > 0 ? 1 : 0;
+  const int nseg = a.world * a.E_local;
+  const int ng = nseg + has_sh;
+  if (ng > kMaxGroups) {
+    if (threadIdx.x == 0) report(a.err, DEVERR_CONFIG);
+    return;
+  }
+  for (int i = threadIdx.x; i < nseg; i += blockDim.x) rbeg[i] = a.recv_counts[i];
+  __syncthreads();
+  const int R = block_exclusive_scan(rbeg, nseg, s_tmp);
+  for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) {
+    const bool sh = has_sh && gi == 0;
+    const int sg = gi - has_sh;
+    TileGroup G;
+    G.expert = sh ? -1 : sg % a.E_local;
+    G.row_begin = sh ? 0 : rbeg[sg];
+    G.rows = sh ? a.T_shared : a.recv_counts[sg];
+    G.ksplit = 1;
+    plan_one(G, sh ? a.a_n_shared : a.a_n, a.a_rows_per_block, a.chunk_max, a.chunk_align);
+    a.tab_a->g[gi] = G;
+    cnt_a[gi] = G.nblocks * G.chunks;
+    G.ksplit = sh ? a.b_ksplit_shared : 1;
+    plan_one(G, a.b_n, a.b_rows_per_block, a.chunk_max, a.chunk_align);
+    a.tab_b->g[gi] = G;
+    cnt_b[gi] = G.nblocks * G.chunks * G.ksplit;
+  }
+  finish_table(a.tab_a, ng, cnt_a, s_tmp);
+  finish_table(a.tab_b, ng, cnt_b, s_tmp);
+  for (int p = threadIdx.x; p < R; p += blockDim.x) {
+    a.row_map[p] = p;
+    a.unit_score[p] = 1.0f;
+  }
+  if (threadIdx.x == 0) *a.recv_total = R;
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {

@@ -192,6 +192,36 @@ FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_wei
 FM_API int fm_moe_block_noalloc(int device, void* stream, const fm_moe_config* cfg, const fm_moe_weights* w,
                                 const uint16_t* x, int64_t T, uint16_t* y);
 
+/* Expert parallelism ------------------------------------------------------------
+ * No reference counterpart: the reference runs the whole MoE layer in one process
+ * (model.cpp:750-807).  These calls split fm_moe_block into the three stages of an
+ * expert-parallel layer so that the caller's collectives (NCCL all-to-all over NVLink)
+ * move the rows between them.  Rank r of world W owns the contiguous experts
+ * [first, first + count) given by fm_ep_range (the first E % W ranks one more).
+ *
+ *   fm_ep_dispatch   route this rank's T tokens (router, softmax, top-k, stable
+ *                    expert-major order); fills expert_counts[E] (host, the call
+ *                    synchronizes the stream) and points *send_rows at the T*k token rows
+ *                    (device, H bf16 each, within-8 pair order) in expert-major order, so
+ *                    the rows for each owner are contiguous.  Valid until the next dispatch.
+ *   fm_ep_experts    owner side: recv_rows holds the rows received from every source rank
+ *                    in source order, each source's rows in expert-major order;
+ *                    recv_counts[W * count] (host) gives the rows per (source, local
+ *                    expert).  w holds the router / shared tensors and the stacked weights
+ *                    of the local experts only.  Writes bf16(d) per received row to d_rows
+ *                    (same order) and runs this rank's shared expert over its own tokens.
+ *   fm_ep_combine    token side: ret_rows holds the d rows returned by the owners in the
+ *                    order fm_ep_dispatch sent them; y = the MoE block output (sum over j
+ *                    of bf16(d * score) in order j = 0..k-1, plus the gated shared expert).
+ * The three calls on one handle form one layer and must come in this order. */
+FM_API int fm_ep_range(int num_experts, int rank, int world, int* first, int* count);
+FM_API int fm_ep_set(fm_handle* h, int rank, int world);
+FM_API int fm_ep_dispatch(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* x,
+                          int64_t T, int32_t* expert_counts, const uint16_t** send_rows);
+FM_API int fm_ep_experts(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* recv_rows,
+                         const int32_t* recv_counts, uint16_t* d_rows);
+FM_API int fm_ep_combine(fm_handle* h, const fm_moe_config* cfg, const uint16_t* ret_rows, uint16_t* y);
+
 #ifdef __cplusplus
 }
 #endif
