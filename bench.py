@@ -13,7 +13,10 @@ prefill batch (synthetic seeded inputs and weights, MLX packed 4-bit layout).
 value  = tokens of all ranks / max-over-ranks device time per step (inputs resident)
 e2e    = the same through the public API with the step's x copied from pinned host
          memory and y read back to pinned host memory inside the timed region
-N > 1  = independent replicas (each rank runs its own batch on its own weights copy)
+N > 1  = expert parallelism (flashmlx_b200.ep): each rank holds the router, the shared
+         expert and 1/N of the routed experts, routes its own batch of the workload's
+         tokens, and rows move by NCCL all-to-all (weak scaling); --replicas runs N
+         independent single-GPU layers instead
 --impl reference: the CPU restatement of the reference's MLX path (the reference
 needs MLX + Metal, which this box cannot run) timed on the host cores, rank 0 only.
 """
@@ -46,6 +49,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--replicas", action="store_true", help="N > 1: independent replicas instead of expert parallelism")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -185,6 +189,23 @@ def kernel_work(shape, T, counts):
     }, active
 
 
+def ep_kernel_work(shape, T, R, recv_counts, E_local):
+    """Algorithmic FLOPs / bytes per launch of the owner-side expert kernels of one
+    expert-parallel step on this rank: R received rows over its local experts, plus the
+    shared expert over its own T tokens."""
+    import numpy as np
+    H, I, Is = shape.hidden, shape.inter, shape.shared_inter
+    per_w = S.layer_weight_bytes(shape)["per_weight"]
+    rc = np.asarray(recv_counts).reshape(-1, E_local).sum(axis=0)
+    active = int((rc > 0).sum())
+    f_gu = 2.0 * R * H * I * 2 + 2.0 * T * H * Is * 2
+    f_dn = 2.0 * R * I * H + 2.0 * T * Is * H
+    b_gu = active * 2 * H * I * per_w + 2 * H * Is * per_w + R * H * 2 + T * H * 2 + R * I * 2 + T * Is * 2
+    b_dn = active * H * I * per_w + H * Is * per_w + R * I * 2 + T * Is * 2 + R * H * 2 + T * H * 4
+    return {"qgemm_tc_gateup": (f_gu, b_gu), "qgemv_gateup": (f_gu, b_gu),
+            "qgemm_tc_down": (f_dn, b_dn), "qgemv_down": (f_dn, b_dn)}, active
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -198,20 +219,44 @@ def run_ours(args, rank, world, local_rank):
 
     shape = S.CONFIGS[args.config]
     T = shape.tokens
+    ep = world > 1 and not args.replicas
     layer_np = S.make_layer(shape, args.seed)
-    x_np = S.make_x(shape, args.seed + rank)  # each replica gets its own batch
-    W = ops.MoEWeightsT.from_numpy(layer_np, dev)
-    block = ops.MoEBlock(shape, W)
-    block.reserve(T)
+    x_np = S.make_x(shape, args.seed + rank)  # each rank routes its own batch
     h = ops.default_handle(local_rank)
     x = ops.bf16_from_numpy(x_np, dev)
     y = torch.empty_like(x)
-    # routing of this batch (for the algorithmic byte count of the decode path)
-    _, routing = block(x, return_routing=True)
-    h.sync()
-    counts = np.diff(routing["expert_offsets"].cpu().numpy())
+    if ep:
+        from flashmlx_b200.ep import MoEBlockEP, expert_range, local_layer
+        W = ops.MoEWeightsT.from_numpy(local_layer(layer_np, rank, world), dev)
+        ep_block = MoEBlockEP(shape, W)
+        E_local = expert_range(shape.num_experts, rank, world)[1]
+        recv_seen = {}
+        orig_experts = ep_block.stages.experts
+
+        def experts_spy(recv, recv_counts):  # records this rank's receive layout
+            recv_seen["R"], recv_seen["counts"] = recv.shape[0], list(recv_counts)
+            return orig_experts(recv, recv_counts)
+
+        ep_block.stages.experts = experts_spy
+
+        def step(xin, out):
+            out.copy_(ep_block(xin))
+        step(x, y)
+        h.sync()
+        counts = None
+    else:
+        W = ops.MoEWeightsT.from_numpy(layer_np, dev)
+        block = ops.MoEBlock(shape, W)
+        block.reserve(T)
+        # routing of this batch (for the algorithmic byte count of the decode path)
+        _, routing = block(x, return_routing=True)
+        h.sync()
+        counts = np.diff(routing["expert_offsets"].cpu().numpy())
+
+        def step(xin, out):
+            block(xin, out=out)
     for _ in range(args.warmup):
-        block(x, out=y)
+        step(x, y)
     h.sync()
     if world > 1:
         dist.barrier()
@@ -225,7 +270,7 @@ def run_ours(args, rank, world, local_rank):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        block(x, out=y)
+        step(x, y)
     e1.record(stream)
     torch.cuda.synchronize()
     h.sync()
@@ -246,7 +291,7 @@ def run_ours(args, rank, world, local_rank):
     e0.record(stream)
     for _ in range(args.steps):
         x_e2e.copy_(x_pin, non_blocking=True)
-        block(x_e2e, out=y)
+        step(x_e2e, y)
         y_pin.copy_(y, non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize()
@@ -260,10 +305,17 @@ def run_ours(args, rank, world, local_rank):
 
     if rank == 0:
         peaks, peak_src = load_peaks()
-        work, active = kernel_work(shape, T, counts)
+        if ep:
+            work, active = ep_kernel_work(shape, T, recv_seen["R"], recv_seen["counts"], E_local)
+        else:
+            work, active = kernel_work(shape, T, counts)
         # dominant kernel by device time
         name, (launches, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
         avg_ms = tot_ms / max(1, launches)
+        cand = [(n, v) for n, v in prof.items() if n in work]
+        if name not in work and cand:  # dominant kernel outside the expert products: report those
+            name, (launches, tot_ms) = max(cand, key=lambda kv: kv[1][1])
+            avg_ms = tot_ms / max(1, launches)
         flops, nbytes = work.get(name, (0.0, 0.0))
         tensor_bound = name.startswith("qgemm_tc")
         if tensor_bound:
@@ -276,7 +328,7 @@ def run_ours(args, rank, world, local_rank):
             roof = {"bound": "hbm", "unit": "GB/s"}
         traffic = None
         tfile = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tfile):
+        if os.path.exists(tfile) and not ep:
             with open(tfile) as f:
                 traffic = json.load(f).get(shape.name, {}).get(name)
         roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "traffic": traffic,
@@ -295,7 +347,7 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": shape.name, "tokens_per_rank": T, "hidden": shape.hidden,
                        "inter": shape.inter, "experts": shape.num_experts, "top_k": shape.top_k,
                        "shared_inter": shape.shared_inter, "active_experts": active,
-                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "parallelism": (f"ep{world}" if ep else f"replicas{world}") if world > 1 else "single",
                        "l2": "weights exceed L2 (no flush between steps)"},
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
