@@ -86,6 +86,7 @@ __device__ int block_exclusive_scan(int* a, int n, int* s_tmp /* >= 33 ints */) 
 
 struct RouteSmem {
   uint32_t mask[kMaxExperts];  // token bitmask of the current chunk, per expert
+  int ids[kRouteChunk * 16];   // expert ids of the current chunk's pairs (-1: dropped)
   int offs[kMaxExperts + 1];
   int cnt_a[kMaxGroups + 1];
   int cnt_b[kMaxGroups + 1];
@@ -231,50 +232,41 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
     const int e = lane + 32 * i;
     p[i] = (e < E) ? rbf(p[i] / sum) : -INFINITY;
   }
-  // top-k: k rounds of warp argmax, ties toward the lower expert id.  NaN scores (bad
-  // input) rank lowest, and every round still returns a distinct valid id.
-  float sel_p[16];
-  int sel_e[16];
-  uint32_t taken = 0u;
+  // top-k: k rounds of one warp max over 32-bit keys (bf16 probability bits << 16 |
+  // 0xFFFF - expert).  The probabilities are bf16 values >= 0, so their bits order like
+  // the values; equal probabilities go to the lower expert id.  NaN (bad input) ranks
+  // lowest, and every round still returns a distinct valid id.
+  uint32_t key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    const uint32_t pb = isnan(p[i]) ? 0u : static_cast<uint32_t>(f2bf(p[i]));
+    key[i] = (e < E) ? ((pb << 16) | static_cast<uint32_t>(0xFFFF - e)) : 0u;
+  }
+  // lane j keeps the pick of round j; the renormalisation sum runs in round order
+  float sp = 0.f, ssum = 0.f;
+  int se = 0;
   for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
-    int be = 0x7fffffff;
+    uint32_t best = 0u;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane + 32 * i;
-      if (e >= E || ((taken >> i) & 1u)) continue;
-      const float v = isnan(p[i]) ? -INFINITY : p[i];
-      if (v > bv || be == 0x7fffffff) {  // ascending e per lane: strict > keeps the lower id
-        bv = v;
-        be = e;
-      }
+    for (int i = 0; i < PER; ++i) best = max(best, key[i]);
+    best = __reduce_max_sync(0xffffffffu, best);
+    const int be = 0xFFFF - static_cast<int>(best & 0xFFFFu);
+    const float bp = bf2f(static_cast<uint16_t>(best >> 16));
+    if (lane == j) {
+      sp = bp;
+      se = be;
     }
+    ssum += bp;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) {
-        bv = ov;
-        be = oe;
-      }
-    }
-    sel_p[j] = bv;
-    sel_e[j] = be;
-    if ((be & 31) == lane) taken |= 1u << (be >> 5);
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i == be) key[i] = 0u;  // taken (a valid key is never 0: 0xFFFF - e > 0)
   }
-  float denom = 1.f;
-  if (a.norm_topk) {
-    float s = 0.f;
-    for (int j = 0; j < k; ++j) s += sel_p[j];
-    denom = rbf(s);
-  }
+  const float denom = a.norm_topk ? rbf(ssum) : 1.f;
   if (lane < k) {
-    float sp = 0.f;
-    int se = 0;
-    for (int j = 0; j < k; ++j)
-      if (j == lane) { sp = sel_p[j]; se = sel_e[j]; }
     const float sc = a.norm_topk ? rbf(sp / denom) : sp;
     a.topk_ids[t * k + lane] = se;
+    sm.ids[tl * k + lane] = se;
     a.topk_score[t * k + lane] = sc;
     if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
     if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
@@ -290,9 +282,11 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) 
   if (e >= static_cast<uint32_t>(a.E) || xb < 0 || xb >= a.x_batches) {
     report(a.err, DEVERR_BOUNDS);
     a.topk_ids[r] = -1;
+    sm.ids[tl] = -1;
     return;
   }
   a.topk_ids[r] = static_cast<int32_t>(e);
+  sm.ids[tl] = static_cast<int>(e);
   a.topk_score[r] = 1.f;
   a.row_src[r] = static_cast<int32_t>(xb * a.M + m);
   atomicOr(&sm.mask[e], 1u << tl);
@@ -319,7 +313,7 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
     const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
     for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
       const int tl = i / k;
-      const int e = a.topk_ids[(t0 + tl) * k + (i % k)];
+      const int e = sm.ids[i];
       if (e < 0) continue;
       a.pair_rank[(t0 + tl) * k + (i % k)] = __popc(sm.mask[e] & ((1u << tl) - 1u));
     }
