@@ -70,6 +70,10 @@ SIGNATURES = {
                             C.POINTER(C.c_void_p)]),
     "fm_ep_experts": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, C.POINTER(C.c_int32), _p]),
     "fm_ep_combine": (_i, [_p, C.POINTER(MoEConfig), _p, _p]),
+    "fm_ep_p2p_alloc": (_i, [_p, C.POINTER(MoEConfig), _i64, _p]),
+    "fm_ep_p2p_open": (_i, [_p, _p]),
+    "fm_ep_p2p_forward": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p]),
+    "fm_ep_p2p_close": (_i, [_p]),
 }
 
 _lib = None

@@ -18,8 +18,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libflashmoe.so")
-SOURCES = ["route.cu", "qgemv.cu", "qgemm_tc.cu", "api.cu"]
-HEADERS = ["fm_common.cuh", "fm_internal.cuh"]
+SOURCES = ["route.cu", "qgemv.cu", "qgemm_tc.cu", "ep.cu", "api.cu"]
+HEADERS = ["fm_common.cuh", "fm_internal.cuh", "fm_ep.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden", "--expt-relaxed-constexpr",

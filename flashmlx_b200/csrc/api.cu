@@ -31,6 +31,12 @@ __global__ void ep_gather_kernel(const uint16_t* x_perm, const int32_t* sorted_t
 __global__ void finalize_ep_kernel(const uint16_t* ret, const int32_t* pair_pos, const float* score, int k,
                                    const float* ysh32, const uint16_t* ysh16, const float* gate_sig, int64_t T, int H,
                                    uint16_t* y);
+__global__ void ep_dispatch_kernel(const EpP2PArgs a);
+__global__ void ep_p2p_plan_kernel(const EpP2PArgs a, EpPlanArgs pa);
+__global__ void ep_return_kernel(const EpP2PArgs a);
+__global__ void ep_combine_p2p_kernel(const EpP2PArgs a, const int32_t* pair_pos, const float* score, int k,
+                                      const float* ysh32, const uint16_t* ysh16, const float* gate_sig, int64_t T,
+                                      uint16_t* y);
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
 cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
@@ -64,6 +70,19 @@ struct fm_handle {
   bool ep_shared = false;
   uint8_t* ep_ws = nullptr;
   size_t ep_ws_bytes = 0;
+  // peer-memory exchange (fm_ep_p2p_*): this rank's region, every rank's mapping of it
+  struct P2P {
+    uint8_t* region = nullptr;  // own region (cudaMalloc, exported by CUDA IPC)
+    size_t bytes = 0;
+    uint8_t* peer[fm::kEpMaxWorld] = {};
+    bool mapped[fm::kEpMaxWorld] = {};  // peer[r] opened from an IPC handle
+    bool open = false;
+    int world = 0, E = 0, H = 0, k = 0;
+    int64_t max_tokens = 0;
+    int64_t off_flags = 0, off_counts = 0, off_recv = 0, off_ret = 0, cap_recv = 0, cap_ret = 0;
+    uint32_t epoch = 0;
+    int coop_blocks = 0;  // co-resident blocks of the dispatch kernel
+  } p2p;
   // kernel timing (fm_profile_enable)
   bool profile = false;
   struct Pending {
@@ -371,6 +390,7 @@ EpPlan1 make_ep_plan1(int64_t T, int H, int E, int k, int epad, int ksplit) {
 struct EpPlan2 {
   size_t total = 0;
   size_t tab_a, tab_b, recv_counts, recv_total, row_map, unit_score, a_sorted, a_shared, ysh;
+  size_t d_rows = 0, row_src = 0, row_pos = 0;  // peer-memory exchange only
   size_t add(size_t bytes) {
     const size_t off = total;
     total = align_up(total + bytes, 256);
@@ -389,6 +409,16 @@ EpPlan2 make_ep_plan2(int64_t R, int64_t T, int H, int I, int Is, int nseg, bool
   p.a_sorted = p.add(sizeof(uint16_t) * R * I);
   p.a_shared = p.add(shared ? sizeof(uint16_t) * T * Is : 0);
   p.ysh = p.add(shared ? sizeof(float) * T * H : 0);  // fp32 (GEMV) or bf16 (tcgen05) rows
+  return p;
+}
+
+// The same plus the received rows' d buffer and their (source rank, send position):
+// R is the receive capacity, the host does not learn the count.
+EpPlan2 make_ep_plan2_p2p(int64_t R, int64_t T, int H, int I, int Is, int nseg, bool shared) {
+  EpPlan2 p = make_ep_plan2(R, T, H, I, Is, nseg, shared);
+  p.d_rows = p.add(sizeof(uint16_t) * R * H);
+  p.row_src = p.add(sizeof(int32_t) * std::max<int64_t>(R, 1));
+  p.row_pos = p.add(sizeof(int32_t) * std::max<int64_t>(R, 1));
   return p;
 }
 
@@ -417,6 +447,202 @@ T* ep_at(fm_handle* h, size_t off) {
 
 int grid_for(const fm_handle* h, int64_t work) {
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(h->num_sms) * 8)));
+}
+
+// Routing of an expert-parallel call over this rank's T tokens (token-side workspace p).
+RouteArgs ep_route_args(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
+                        int ksplit, const EpPlan1& p) {
+  const int H = c->hidden, E = c->num_experts, k = c->top_k;
+  const bool shared = c->shared_inter > 0;
+  RouteArgs ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.x = x;
+  ra.router_w = static_cast<const uint16_t*>(w->router_w);
+  ra.shared_gate_w = shared ? static_cast<const uint16_t*>(w->shared_expert_gate_w) : nullptr;
+  ra.router_bias = w->router_bias;
+  ra.T = T;
+  ra.H = H;
+  ra.E = E;
+  ra.k = k;
+  ra.norm_topk = c->norm_topk_prob;
+  ra.do_router = 1;
+  ra.ksplit = ksplit;
+  ra.epad = (E + 1 + 7) / 8 * 8;
+  ra.partial = at<float>(h, p.partial);
+  ra.x_perm = at<uint16_t>(h, p.x_perm);
+  ra.x_rows = T;
+  ra.topk_ids = at<int32_t>(h, p.topk_ids);
+  ra.topk_score = at<float>(h, p.topk_score);
+  ra.gate_sig = at<float>(h, p.gate_sig);
+  ra.row_src = at<int32_t>(h, p.row_src);
+  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
+  ra.pair_rank = at<int32_t>(h, p.pair_rank);
+  ra.totals = at<int32_t>(h, p.totals);
+  ra.offsets = at<int32_t>(h, p.offsets);
+  ra.sorted_token = at<int32_t>(h, p.sorted_token);
+  ra.sorted_score = at<float>(h, p.sorted_score);
+  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.pair_pos = at<int32_t>(h, p.pair_pos);
+  ra.chunk_max = 8;
+  ra.chunk_align = 8;
+  ra.has_shared = shared ? 1 : 0;
+  ra.gsync = grid_sync(h);
+  ra.err = err_word(h);
+  ra.phase_ns = phase_ns(h);
+  return ra;
+}
+
+// Token-side checks of fm_ep_dispatch and fm_ep_p2p_forward.
+int check_ep_route(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T) {
+  if (!c || !w) return set_err(h, FM_EINVAL, "null argument");
+  if (c->hidden <= 0 || c->num_experts <= 0 || c->top_k <= 0 || c->top_k > c->num_experts || c->top_k > 16 ||
+      c->num_experts > fm::kMaxExperts)
+    return set_err(h, FM_EINVAL, "bad MoE dimensions");
+  if (c->hidden % 128) return set_err(h, FM_EUNSUPPORTED, "hidden must be a multiple of 128");
+  if (c->router_quantized || c->shared_gate_quantized)
+    return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
+  if (!w->router_w || (c->shared_inter > 0 && !w->shared_expert_gate_w))
+    return set_err(h, FM_EINVAL, "router weights missing");
+  if (T < 0 || (T > 0 && !x)) return set_err(h, FM_EINVAL, "bad x / T");
+  if (!aligned16(x)) return set_err(h, FM_EINVAL, "x must be 16-byte aligned");
+  if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
+  return FM_OK;
+}
+
+
+// Unmaps the peers' regions and frees this rank's own (every rank must have finished
+// its calls: the regions are written by peers during a call).
+void p2p_close(fm_handle* h) {
+  auto& q = h->p2p;
+  if (q.region || q.open) cudaStreamSynchronize(h->stream);
+  for (int r = 0; r < fm::kEpMaxWorld; ++r) {
+    if (q.mapped[r] && q.peer[r]) cudaIpcCloseMemHandle(q.peer[r]);
+    q.mapped[r] = false;
+    q.peer[r] = nullptr;
+  }
+  if (q.region) cudaFree(q.region);
+  q = fm_handle::P2P();
+}
+
+// Owner-side planner arguments (tile groups over the (source rank, local expert)
+// segments and the shared expert's own tokens).
+fm::EpPlanArgs ep_plan_args(fm_handle* h, const fm_moe_config* c, int E_local, int64_t T, bool shared, bool tcp,
+                            const EpPlan2& p2) {
+  fm::EpPlanArgs pa;
+  std::memset(&pa, 0, sizeof(pa));
+  pa.recv_counts = ep_at<int32_t>(h, p2.recv_counts);
+  pa.world = h->ep_world;
+  pa.E_local = E_local;
+  pa.T_shared = shared ? static_cast<int>(T) : 0;
+  pa.a_n = c->inter;
+  pa.a_n_shared = c->shared_inter;
+  pa.b_n = c->hidden;
+  pa.a_rows_per_block = tcp ? 128 : 64;
+  pa.b_rows_per_block = tcp ? 256 : 128;
+  pa.chunk_max = tcp ? fm::tc::max_rows() : 8;
+  pa.chunk_align = tcp ? 16 : 8;
+  pa.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, c->inter));
+  pa.tab_a = ep_at<TileTable>(h, p2.tab_a);
+  pa.tab_b = ep_at<TileTable>(h, p2.tab_b);
+  pa.row_map = ep_at<int32_t>(h, p2.row_map);
+  pa.unit_score = ep_at<float>(h, p2.unit_score);
+  pa.recv_total = ep_at<int32_t>(h, p2.recv_total);
+  pa.err = err_word(h);
+  return pa;
+}
+
+// Owner-side checks of fm_ep_experts and fm_ep_p2p_forward.
+int check_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, bool routed, bool shared) {
+  const int H = c->hidden, I = c->inter, Is = c->shared_inter;
+  if (I <= 0 || I % 128 || (Is > 0 && Is % 128) || !quant_ok(H, c->group_size, c->bits) ||
+      !quant_ok(I, c->group_size, c->bits))
+    return set_err(h, FM_EUNSUPPORTED, "inter / shared sizes must be multiples of 128, 4-bit affine");
+  if (routed && (!w->gate.w || !w->up.w || !w->down.w || !w->gate.scales || !w->up.scales || !w->down.scales))
+    return set_err(h, FM_EINVAL, "local expert weights missing");
+  if (shared && (!w->shared_gate.w || !w->shared_up.w || !w->shared_down.w))
+    return set_err(h, FM_EINVAL, "shared expert weights missing");
+  return FM_OK;
+}
+
+// Owner-side expert GEMMs of an expert-parallel call: gate/up + SwiGLU, then down into
+// d_rows (bf16(d), one row per received row, in receive order), over the tile tables
+// pa holds.  R rows of recv_rows may be read (the received rows, or their capacity when
+// the host does not know the count).  The shared expert runs on this rank's own tokens.
+int ep_gemms(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* recv_rows, int64_t R,
+             int64_t T, int E_local, bool shared, bool tcp, const EpPlan1& p1, const EpPlan2& p2,
+             const fm::EpPlanArgs& pa, uint16_t* d_rows) {
+  const int H = c->hidden, I = c->inter, Is = c->shared_inter;
+  int rc = FM_OK;
+  uint16_t* x_perm = at<uint16_t>(h, p1.x_perm);
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  ga.gs = c->group_size;
+  ga.err = err_word(h);
+  ga.sorted_token = pa.row_map;
+  ga.sorted_score = pa.unit_score;
+  ga.sorted_flat = pa.row_map;
+  ga.K = H;
+  ga.K_shared = H;
+  ga.N = I;
+  ga.N_shared = Is;
+  ga.w0 = w->gate.w; ga.s0 = w->gate.scales; ga.b0 = w->gate.biases;
+  ga.w1 = w->up.w; ga.s1 = w->up.scales; ga.b1 = w->up.biases;
+  if (shared) {
+    ga.sw0 = w->shared_gate.w; ga.ss0 = w->shared_gate.scales; ga.sb0 = w->shared_gate.biases;
+    ga.sw1 = w->shared_up.w; ga.ss1 = w->shared_up.scales; ga.sb1 = w->shared_up.biases;
+  }
+  ga.act = recv_rows;
+  ga.act_ld = H;
+  ga.act_shared = x_perm;
+  ga.act_shared_ld = H;
+  ga.out = ep_at<uint16_t>(h, p2.a_sorted);
+  ga.out_ld = I;
+  ga.out_shared = shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr;
+  ga.out_shared_ld = Is;
+  ga.tab = pa.tab_a;
+  fm::TcMaps maps_gu, maps_dn;
+  if (tcp) {
+    const bool ok =
+        encode_codes(&maps_gu.code[0], w->gate.w, static_cast<int64_t>(E_local) * I, H, 64) &&
+        encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E_local) * I, H, 64) &&
+        encode_codes(&maps_gu.code[2], shared ? w->shared_gate.w : nullptr, Is, H, 64) &&
+        encode_codes(&maps_gu.code[3], shared ? w->shared_up.w : nullptr, Is, H, 64) &&
+        encode_act(&maps_gu.act[0], R > 0 ? recv_rows : nullptr, R, H) &&
+        encode_act(&maps_gu.act[1], shared ? x_perm : nullptr, T, H) &&
+        encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E_local) * H, I, 128) &&
+        encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
+        encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
+        encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
+        encode_act(&maps_dn.act[0], R > 0 ? ep_at<uint16_t>(h, p2.a_sorted) : nullptr, R, I) &&
+        encode_act(&maps_dn.act[1], shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr, T, Is);
+    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+  }
+  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
+  if (rc) return rc;
+  GemmArgs gd = ga;
+  gd.K = I;
+  gd.K_shared = Is;
+  gd.N = H;
+  gd.N_shared = H;
+  gd.w0 = w->down.w; gd.s0 = w->down.scales; gd.b0 = w->down.biases;
+  gd.w1 = nullptr; gd.s1 = nullptr; gd.b1 = nullptr;
+  if (shared) {
+    gd.sw0 = w->shared_down.w; gd.ss0 = w->shared_down.scales; gd.sb0 = w->shared_down.biases;
+  }
+  gd.sw1 = nullptr; gd.ss1 = nullptr; gd.sb1 = nullptr;
+  gd.act = ga.out;
+  gd.act_ld = I;
+  gd.act_shared = ga.out_shared;
+  gd.act_shared_ld = Is;
+  gd.out = nullptr;
+  gd.out_shared = nullptr;
+  gd.y_pairs = d_rows;
+  gd.y_acc = nullptr;
+  gd.ysh = (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr;
+  gd.ysh16 = (shared && tcp) ? ep_at<uint16_t>(h, p2.ysh) : nullptr;
+  gd.y_ld = H;
+  gd.tab = pa.tab_b;
+  return launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
 }
 
 }  // namespace
@@ -483,6 +709,7 @@ int fm_destroy(fm_handle* h) {
     cudaEventDestroy(p.b);
   }
   for (auto e : h->event_pool) cudaEventDestroy(e);
+  p2p_close(h);
   if (h->ws) cudaFree(h->ws);
   if (h->ep_ws) cudaFree(h->ep_ws);
   delete h;
@@ -866,25 +1093,15 @@ int fm_ep_set(fm_handle* h, int rank, int world) {
 int fm_ep_dispatch(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
                    int32_t* expert_counts, const uint16_t** send_rows) {
   if (!h) return FM_EINVAL;
-  if (!c || !w || !expert_counts || !send_rows) return set_err(h, FM_EINVAL, "null argument");
-  if (c->hidden <= 0 || c->num_experts <= 0 || c->top_k <= 0 || c->top_k > c->num_experts || c->top_k > 16 ||
-      c->num_experts > fm::kMaxExperts)
-    return set_err(h, FM_EINVAL, "bad MoE dimensions");
-  if (c->hidden % 128) return set_err(h, FM_EUNSUPPORTED, "hidden must be a multiple of 128");
-  if (c->router_quantized || c->shared_gate_quantized)
-    return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
-  if (!w->router_w || (c->shared_inter > 0 && !w->shared_expert_gate_w))
-    return set_err(h, FM_EINVAL, "router weights missing");
-  if (T < 0 || (T > 0 && !x)) return set_err(h, FM_EINVAL, "bad x / T");
-  if (!aligned16(x)) return set_err(h, FM_EINVAL, "x must be 16-byte aligned");
-  if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
+  if (!expert_counts || !send_rows) return set_err(h, FM_EINVAL, "null argument");
+  int rc = check_ep_route(h, c, w, x, T);
+  if (rc) return rc;
   const int H = c->hidden, E = c->num_experts, k = c->top_k;
-  const bool shared = c->shared_inter > 0;
   const int epad = (E + 1 + 7) / 8 * 8;
   const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
   const int64_t P = T * k;
   const EpPlan1 p = make_ep_plan1(T, H, E, k, epad, ksplit);
-  int rc = ensure_ws(h, p.total);
+  rc = ensure_ws(h, p.total);
   if (rc) return rc;
   *send_rows = at<uint16_t>(h, p.send);
   h->ep_T = T;
@@ -893,41 +1110,7 @@ int fm_ep_dispatch(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w
     std::memset(expert_counts, 0, sizeof(int32_t) * E);
     return FM_OK;
   }
-  RouteArgs ra;
-  std::memset(&ra, 0, sizeof(ra));
-  ra.x = x;
-  ra.router_w = static_cast<const uint16_t*>(w->router_w);
-  ra.shared_gate_w = shared ? static_cast<const uint16_t*>(w->shared_expert_gate_w) : nullptr;
-  ra.router_bias = w->router_bias;
-  ra.T = T;
-  ra.H = H;
-  ra.E = E;
-  ra.k = k;
-  ra.norm_topk = c->norm_topk_prob;
-  ra.do_router = 1;
-  ra.ksplit = ksplit;
-  ra.epad = epad;
-  ra.partial = at<float>(h, p.partial);
-  ra.x_perm = at<uint16_t>(h, p.x_perm);
-  ra.x_rows = T;
-  ra.topk_ids = at<int32_t>(h, p.topk_ids);
-  ra.topk_score = at<float>(h, p.topk_score);
-  ra.gate_sig = at<float>(h, p.gate_sig);
-  ra.row_src = at<int32_t>(h, p.row_src);
-  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
-  ra.pair_rank = at<int32_t>(h, p.pair_rank);
-  ra.totals = at<int32_t>(h, p.totals);
-  ra.offsets = at<int32_t>(h, p.offsets);
-  ra.sorted_token = at<int32_t>(h, p.sorted_token);
-  ra.sorted_score = at<float>(h, p.sorted_score);
-  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
-  ra.pair_pos = at<int32_t>(h, p.pair_pos);
-  ra.chunk_max = 8;
-  ra.chunk_align = 8;
-  ra.has_shared = shared ? 1 : 0;
-  ra.gsync = grid_sync(h);
-  ra.err = err_word(h);
-  ra.phase_ns = phase_ns(h);
+  RouteArgs ra = ep_route_args(h, c, w, x, T, ksplit, p);
   rc = launch_route(h, ra, ((T + 15) / 16) * ksplit);
   if (rc) return rc;
   prof_begin(h, "ep_gather");
@@ -967,16 +1150,11 @@ int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w,
   const int64_t T = h->ep_T;
   const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k, Is = c->shared_inter;
   const bool shared = Is > 0 && T > 0;
-  if (I <= 0 || I % 128 || (Is > 0 && Is % 128) || !quant_ok(H, c->group_size, c->bits) ||
-      !quant_ok(I, c->group_size, c->bits))
-    return set_err(h, FM_EUNSUPPORTED, "inter / shared sizes must be multiples of 128, 4-bit affine");
-  if (R > 0 && (!w->gate.w || !w->up.w || !w->down.w || !w->gate.scales || !w->up.scales || !w->down.scales))
-    return set_err(h, FM_EINVAL, "local expert weights missing");
-  if (shared && (!w->shared_gate.w || !w->shared_up.w || !w->shared_down.w))
-    return set_err(h, FM_EINVAL, "shared expert weights missing");
+  int rc = check_ep_experts(h, c, w, R > 0, shared);
+  if (rc) return rc;
   const bool tcp = use_tc(h, R + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
   const EpPlan2 p2 = make_ep_plan2(R, std::max<int64_t>(T, 0), H, I, Is, nseg, shared);
-  int rc = ensure_ep_ws(h, p2.total);
+  rc = ensure_ep_ws(h, p2.total);
   if (rc) return rc;
   const EpPlan1 p1 = make_ep_plan1(std::max<int64_t>(T, 0), H, E, k, (E + 1 + 7) / 8 * 8,
                                    router_ksplit(h, std::max<int64_t>(T, 1), H));
@@ -991,26 +1169,7 @@ int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w,
     e = cudaMemsetAsync(ep_at<float>(h, p2.ysh), 0, sizeof(float) * T * H, h->stream);
     if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
   }
-  fm::EpPlanArgs pa;
-  std::memset(&pa, 0, sizeof(pa));
-  pa.recv_counts = ep_at<int32_t>(h, p2.recv_counts);
-  pa.world = h->ep_world;
-  pa.E_local = E_local;
-  pa.T_shared = shared ? static_cast<int>(T) : 0;
-  pa.a_n = I;
-  pa.a_n_shared = Is;
-  pa.b_n = H;
-  pa.a_rows_per_block = tcp ? 128 : 64;
-  pa.b_rows_per_block = tcp ? 256 : 128;
-  pa.chunk_max = tcp ? fm::tc::max_rows() : 8;
-  pa.chunk_align = tcp ? 16 : 8;
-  pa.b_ksplit_shared = tcp ? 1 : std::max(1, Is / std::max(1, I));
-  pa.tab_a = ep_at<TileTable>(h, p2.tab_a);
-  pa.tab_b = ep_at<TileTable>(h, p2.tab_b);
-  pa.row_map = ep_at<int32_t>(h, p2.row_map);
-  pa.unit_score = ep_at<float>(h, p2.unit_score);
-  pa.recv_total = ep_at<int32_t>(h, p2.recv_total);
-  pa.err = err_word(h);
+  const fm::EpPlanArgs pa = ep_plan_args(h, c, E_local, T, shared, tcp, p2);
   prof_begin(h, "ep_plan");
   fm::ep_plan_kernel<<<1, fm::kRouteThreads, 0, h->stream>>>(pa);
   prof_end(h);
@@ -1018,76 +1177,7 @@ int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w,
   if (e != cudaSuccess) return cuda_err(h, e, "ep_plan launch");
   if (R == 0 && !shared) return FM_OK;
 
-  uint16_t* x_perm = at<uint16_t>(h, p1.x_perm);
-  GemmArgs ga;
-  std::memset(&ga, 0, sizeof(ga));
-  ga.gs = c->group_size;
-  ga.err = err_word(h);
-  ga.sorted_token = pa.row_map;
-  ga.sorted_score = pa.unit_score;
-  ga.sorted_flat = pa.row_map;
-  ga.K = H;
-  ga.K_shared = H;
-  ga.N = I;
-  ga.N_shared = Is;
-  ga.w0 = w->gate.w; ga.s0 = w->gate.scales; ga.b0 = w->gate.biases;
-  ga.w1 = w->up.w; ga.s1 = w->up.scales; ga.b1 = w->up.biases;
-  if (shared) {
-    ga.sw0 = w->shared_gate.w; ga.ss0 = w->shared_gate.scales; ga.sb0 = w->shared_gate.biases;
-    ga.sw1 = w->shared_up.w; ga.ss1 = w->shared_up.scales; ga.sb1 = w->shared_up.biases;
-  }
-  ga.act = recv_rows;
-  ga.act_ld = H;
-  ga.act_shared = x_perm;
-  ga.act_shared_ld = H;
-  ga.out = ep_at<uint16_t>(h, p2.a_sorted);
-  ga.out_ld = I;
-  ga.out_shared = shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr;
-  ga.out_shared_ld = Is;
-  ga.tab = pa.tab_a;
-  fm::TcMaps maps_gu, maps_dn;
-  if (tcp) {
-    const bool ok =
-        encode_codes(&maps_gu.code[0], w->gate.w, static_cast<int64_t>(E_local) * I, H, 64) &&
-        encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E_local) * I, H, 64) &&
-        encode_codes(&maps_gu.code[2], shared ? w->shared_gate.w : nullptr, Is, H, 64) &&
-        encode_codes(&maps_gu.code[3], shared ? w->shared_up.w : nullptr, Is, H, 64) &&
-        encode_act(&maps_gu.act[0], R > 0 ? recv_rows : nullptr, R, H) &&
-        encode_act(&maps_gu.act[1], shared ? x_perm : nullptr, T, H) &&
-        encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E_local) * H, I, 128) &&
-        encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
-        encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
-        encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
-        encode_act(&maps_dn.act[0], R > 0 ? ep_at<uint16_t>(h, p2.a_sorted) : nullptr, R, I) &&
-        encode_act(&maps_dn.act[1], shared ? ep_at<uint16_t>(h, p2.a_shared) : nullptr, T, Is);
-    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
-  }
-  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
-  if (rc) return rc;
-  GemmArgs gd = ga;
-  gd.K = I;
-  gd.K_shared = Is;
-  gd.N = H;
-  gd.N_shared = H;
-  gd.w0 = w->down.w; gd.s0 = w->down.scales; gd.b0 = w->down.biases;
-  gd.w1 = nullptr; gd.s1 = nullptr; gd.b1 = nullptr;
-  if (shared) {
-    gd.sw0 = w->shared_down.w; gd.ss0 = w->shared_down.scales; gd.sb0 = w->shared_down.biases;
-  }
-  gd.sw1 = nullptr; gd.ss1 = nullptr; gd.sb1 = nullptr;
-  gd.act = ga.out;
-  gd.act_ld = I;
-  gd.act_shared = ga.out_shared;
-  gd.act_shared_ld = Is;
-  gd.out = nullptr;
-  gd.out_shared = nullptr;
-  gd.y_pairs = d_rows;
-  gd.y_acc = nullptr;
-  gd.ysh = (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr;
-  gd.ysh16 = (shared && tcp) ? ep_at<uint16_t>(h, p2.ysh) : nullptr;
-  gd.y_ld = H;
-  gd.tab = pa.tab_b;
-  return launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
+  return ep_gemms(h, c, w, recv_rows, R, T, E_local, shared, tcp, p1, p2, pa, d_rows);
 }
 
 int fm_ep_combine(fm_handle* h, const fm_moe_config* c, const uint16_t* ret_rows, uint16_t* y) {
@@ -1113,6 +1203,206 @@ int fm_ep_combine(fm_handle* h, const fm_moe_config* c, const uint16_t* ret_rows
       (shared && h->ep_ysh_bf16) ? ep_at<uint16_t>(h, p2.ysh) : nullptr, at<float>(h, p1.gate_sig), T, H, y);
   prof_end(h);
   cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_combine launch");
+  return FM_OK;
+}
+
+// ---------------------------------------------------------------- expert parallelism over peer memory
+// Region layout (identical on every rank of the group; offsets in bytes):
+//   [0, 256)      local control: the grid completion counter of the exchange kernels
+//   off_flags     u32 [3][W]      epoch of the last post per (kind, source rank)
+//   off_counts    i32 [W][E]      pairs of every source rank per global expert
+//   off_recv      bf16 [cap_recv][H]  rows received as an owner
+//   off_ret       bf16 [cap_ret][H]   d rows returned to this rank as a token owner
+int fm_ep_p2p_alloc(fm_handle* h, const fm_moe_config* c, int64_t max_tokens, void* ipc_handle_out) {
+  if (!h) return FM_EINVAL;
+  if (!c || !ipc_handle_out || max_tokens <= 0) return set_err(h, FM_EINVAL, "null argument or max_tokens <= 0");
+  if (h->borrowed_ws) return set_err(h, FM_ETOOLARGE, "expert parallelism needs an allocating handle");
+  const int W = h->ep_world, E = c->num_experts, H = c->hidden, k = c->top_k;
+  if (W > fm::kEpMaxWorld) return set_err(h, FM_EUNSUPPORTED, "peer-memory exchange supports up to 8 ranks");
+  if (H <= 0 || H % 128 || E <= 0 || k <= 0 || k > E || E > fm::kMaxExperts)
+    return set_err(h, FM_EINVAL, "bad MoE dimensions");
+  if (max_tokens > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "max_tokens too large");
+  p2p_close(h);
+  auto& q = h->p2p;
+  const int64_t e_local_max = (E + W - 1) / W;
+  q.world = W;
+  q.E = E;
+  q.H = H;
+  q.k = k;
+  q.max_tokens = max_tokens;
+  q.cap_recv = static_cast<int64_t>(W) * max_tokens * std::min<int64_t>(k, e_local_max);
+  q.cap_ret = max_tokens * k;
+  size_t off = 256;
+  q.off_flags = static_cast<int64_t>(off);
+  off = align_up(off + sizeof(uint32_t) * 3 * W, 256);
+  q.off_counts = static_cast<int64_t>(off);
+  off = align_up(off + sizeof(int32_t) * static_cast<size_t>(W) * E, 256);
+  q.off_recv = static_cast<int64_t>(off);
+  off = align_up(off + sizeof(uint16_t) * static_cast<size_t>(q.cap_recv) * H, 256);
+  q.off_ret = static_cast<int64_t>(off);
+  off = align_up(off + sizeof(uint16_t) * static_cast<size_t>(q.cap_ret) * H, 256);
+  q.bytes = off;
+  cudaError_t e = cudaMalloc(&q.region, q.bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    q = fm_handle::P2P();
+    return set_err(h, FM_ENOMEM, std::string("peer-exchange region allocation failed: ") + cudaGetErrorString(e));
+  }
+  e = cudaMemsetAsync(q.region, 0, static_cast<size_t>(q.off_recv), h->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+  cudaIpcMemHandle_t ipc;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&ipc, q.region);
+  int per_sm = 0;
+  if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fm::ep_dispatch_kernel, 256, 0);
+  if (e != cudaSuccess) {
+    p2p_close(h);
+    return cuda_err(h, e, "peer-exchange region setup");
+  }
+  q.coop_blocks = h->num_sms * std::max(1, std::min(per_sm, 4));
+  q.peer[h->ep_rank] = q.region;
+  std::memcpy(ipc_handle_out, &ipc, sizeof(ipc));
+  return FM_OK;
+}
+
+int fm_ep_p2p_open(fm_handle* h, const void* ipc_handles) {
+  if (!h) return FM_EINVAL;
+  auto& q = h->p2p;
+  if (!q.region) return set_err(h, FM_EINVAL, "fm_ep_p2p_open must follow fm_ep_p2p_alloc");
+  if (q.open) return set_err(h, FM_EINVAL, "peer regions already open");
+  if (!ipc_handles && q.world > 1) return set_err(h, FM_EINVAL, "null handles");
+  for (int r = 0; r < q.world; ++r) {
+    if (r == h->ep_rank) continue;
+    cudaIpcMemHandle_t ipc;
+    std::memcpy(&ipc, static_cast<const uint8_t*>(ipc_handles) + static_cast<size_t>(r) * sizeof(ipc), sizeof(ipc));
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, ipc, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int s = 0; s < r; ++s)
+        if (q.mapped[s]) {
+          cudaIpcCloseMemHandle(q.peer[s]);
+          q.mapped[s] = false;
+          q.peer[s] = nullptr;
+        }
+      return cuda_err(h, e, "cudaIpcOpenMemHandle");
+    }
+    q.peer[r] = static_cast<uint8_t*>(ptr);
+    q.mapped[r] = true;
+  }
+  q.open = true;
+  return FM_OK;
+}
+
+int fm_ep_p2p_close(fm_handle* h) {
+  if (!h) return FM_EINVAL;
+  p2p_close(h);
+  return FM_OK;
+}
+
+int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,
+                      uint16_t* y) {
+  if (!h) return FM_EINVAL;
+  auto& q = h->p2p;
+  if (!q.open) return set_err(h, FM_EINVAL, "peer regions not open (fm_ep_p2p_alloc, fm_ep_p2p_open)");
+  int rc = check_ep_route(h, c, w, x, T);
+  if (rc) return rc;
+  const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k, Is = c->shared_inter;
+  if (E != q.E || H != q.H || k != q.k || h->ep_world != q.world)
+    return set_err(h, FM_EINVAL, "config differs from the one the peer regions were sized for");
+  if (T > q.max_tokens) return set_err(h, FM_ETOOLARGE, "T exceeds the max_tokens of fm_ep_p2p_alloc");
+  if (T > 0 && !y) return set_err(h, FM_EINVAL, "null y");
+  if (!aligned16(y)) return set_err(h, FM_EINVAL, "y must be 16-byte aligned");
+  int first = 0, E_local = 0;
+  ep_range(E, h->ep_rank, h->ep_world, &first, &E_local);
+  const int nseg = h->ep_world * E_local;
+  if (nseg + 1 > fm::kMaxGroups) return set_err(h, FM_EUNSUPPORTED, "too many (rank, expert) segments");
+  const bool shared = Is > 0 && T > 0;
+  const bool routed = E_local > 0;
+  rc = check_ep_experts(h, c, w, routed, shared);
+  if (rc) return rc;
+  // the receive count is not known on the host: decide the path on this rank's own pairs
+  const bool tcp = use_tc(h, T * k + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
+  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
+  const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, ksplit);
+  rc = ensure_ws(h, p1.total);
+  if (rc) return rc;
+  const EpPlan2 p2 = make_ep_plan2_p2p(q.cap_recv, T, H, I, Is, nseg, shared);
+  rc = ensure_ep_ws(h, p2.total);
+  if (rc) return rc;
+  if (++q.epoch == 0) q.epoch = 1;
+  cudaError_t e = cudaMemsetAsync(q.region, 0, 256, h->stream);
+  if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
+  RouteArgs ra = ep_route_args(h, c, w, x, T, ksplit, p1);
+  if (T > 0) {
+    rc = launch_route(h, ra, ((T + 15) / 16) * ksplit);
+    if (rc) return rc;
+  } else {
+    e = cudaMemsetAsync(ra.offsets, 0, sizeof(int32_t) * (E + 1), h->stream);
+    if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
+  }
+  if (shared && !tcp) {
+    e = cudaMemsetAsync(ep_at<float>(h, p2.ysh), 0, sizeof(float) * T * H, h->stream);
+    if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
+  }
+  const fm::EpPlanArgs pa = ep_plan_args(h, c, E_local, T, shared, tcp, p2);
+  fm::EpP2PArgs a;
+  std::memset(&a, 0, sizeof(a));
+  for (int r = 0; r < q.world; ++r) a.peer[r] = q.peer[r];
+  a.rank = h->ep_rank;
+  a.world = q.world;
+  a.E = E;
+  a.H = H;
+  a.k = k;
+  a.epoch = q.epoch;
+  a.off_flags = q.off_flags;
+  a.off_counts = q.off_counts;
+  a.off_recv = q.off_recv;
+  a.off_ret = q.off_ret;
+  a.cap_recv = q.cap_recv;
+  a.cap_ret = q.cap_ret;
+  a.offsets = ra.offsets;
+  a.sorted_token = ra.sorted_token;
+  a.x_perm = ra.x_perm;
+  a.P = T * k;
+  a.row_src = ep_at<int32_t>(h, p2.row_src);
+  a.row_pos = ep_at<int32_t>(h, p2.row_pos);
+  a.d_rows = ep_at<uint16_t>(h, p2.d_rows);
+  a.recv_total = pa.recv_total;
+  a.done_counter = reinterpret_cast<int32_t*>(q.region);
+  a.err = err_word(h);
+
+  prof_begin(h, "ep_p2p_dispatch");
+  {
+    const int64_t want = (a.P * (H / 8) + 255) / 256;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, q.coop_blocks)));
+    void* args[] = {&a};
+    e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(fm::ep_dispatch_kernel), dim3(grid), dim3(256),
+                                    args, 0, h->stream);
+  }
+  prof_end(h);
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_dispatch launch");
+  prof_begin(h, "ep_p2p_plan");
+  fm::ep_p2p_plan_kernel<<<1, fm::kRouteThreads, 0, h->stream>>>(a, pa);
+  prof_end(h);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_plan launch");
+  if (routed || shared) {
+    uint16_t* recv = reinterpret_cast<uint16_t*>(q.region + q.off_recv);
+    rc = ep_gemms(h, c, w, recv, routed ? q.cap_recv : 0, T, E_local, shared, tcp, p1, p2, pa,
+                  ep_at<uint16_t>(h, p2.d_rows));
+    if (rc) return rc;
+  }
+  prof_begin(h, "ep_p2p_return");
+  fm::ep_return_kernel<<<h->num_sms * 2, 256, 0, h->stream>>>(a);
+  prof_end(h);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_return launch");
+  prof_begin(h, "ep_p2p_combine");
+  fm::ep_combine_p2p_kernel<<<grid_for(h, T * (H / 8)), 256, 0, h->stream>>>(
+      a, ra.pair_pos, ra.topk_score, k, (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr,
+      (shared && tcp) ? ep_at<uint16_t>(h, p2.ysh) : nullptr, ra.gate_sig, T, y);
+  prof_end(h);
+  e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(h, e, "ep_combine launch");
   return FM_OK;
 }

@@ -209,6 +209,30 @@ struct EpPlanArgs {
   uint32_t* err;
 };
 
+constexpr int kEpMaxWorld = 8;  // ranks of one peer-memory expert-parallel group
+
+// Arguments of the expert-parallel exchange kernels over peer memory (layout: ep.cu).
+struct EpP2PArgs {
+  uint8_t* peer[kEpMaxWorld];  // region base of every rank, mapped here (peer[rank] = own)
+  int rank, world;
+  int E, H, k;
+  uint32_t epoch;
+  int64_t off_flags, off_counts, off_recv, off_ret;  // byte offsets in a region
+  int64_t cap_recv, cap_ret;                         // rows of recv / ret
+  // dispatch (token side)
+  const int32_t* offsets;       // [E + 1] expert offsets of this rank's pairs
+  const int32_t* sorted_token;  // [P] token of each pair, expert-major
+  const uint16_t* x_perm;       // [T, H]
+  int64_t P;
+  // owner side
+  int32_t* row_src;             // [cap_recv] source rank of each received row
+  int32_t* row_pos;             // [cap_recv] its position in the source's send order
+  const uint16_t* d_rows;       // [cap_recv, H] bf16(d) of the received rows
+  const int32_t* recv_total;    // rows received (device)
+  int32_t* done_counter;        // grid completion counter, 0 between launches
+  uint32_t* err;
+};
+
 constexpr int kRouteThreads = 256;  // 8 warps
 constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
 constexpr int kRouterMaxKsplit = 16;  // K slices of the router partial logits

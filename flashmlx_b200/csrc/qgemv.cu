@@ -28,7 +28,7 @@
 // per warp); the activation chunk of the unit is staged in shared memory by cp.async.
 #include <type_traits>
 
-#include "fm_internal.cuh"
+#include "fm_ep.cuh"
 
 namespace fm {
 
@@ -360,10 +360,10 @@ __global__ void ep_gather_kernel(const uint16_t* __restrict__ x_perm, const int3
 // owner of pair (t, j); y = bf16( bf16(sum_j bf16(d * score_j)) + bf16(gate * shared) ),
 // the sum over j = 0..k-1 in fp32 in that order (model.cpp:780-784, 800-803).  The
 // shared rows come as fp32 sums (GEMV path) or bf16 rows (tcgen05 path).
-__global__ void finalize_ep_kernel(const uint16_t* __restrict__ ret, const int32_t* __restrict__ pair_pos,
-                                   const float* __restrict__ score, int k, const float* __restrict__ ysh32,
-                                   const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig, int64_t T,
-                                   int H, uint16_t* __restrict__ y) {
+__device__ __forceinline__ void combine_rows(const uint16_t* __restrict__ ret, const int32_t* __restrict__ pair_pos,
+                                             const float* __restrict__ score, int k, const float* __restrict__ ysh32,
+                                             const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig,
+                                             int64_t T, int H, uint16_t* __restrict__ y) {
   const int segs = H / 8;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < T * segs;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -399,6 +399,26 @@ __global__ void finalize_ep_kernel(const uint16_t* __restrict__ ret, const int32
     o.w = pack_bf16x2(acc[6], acc[7]);
     *reinterpret_cast<uint4*>(y + t * H + col) = o;
   }
+}
+
+__global__ void finalize_ep_kernel(const uint16_t* __restrict__ ret, const int32_t* __restrict__ pair_pos,
+                                   const float* __restrict__ score, int k, const float* __restrict__ ysh32,
+                                   const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig, int64_t T,
+                                   int H, uint16_t* __restrict__ y) {
+  combine_rows(ret, pair_pos, score, k, ysh32, ysh16, gate_sig, T, H, y);
+}
+
+// Peer-memory variant (ep.cu): wait until every owner returned its rows into this
+// rank's ret buffer, then combine as finalize_ep_kernel.
+__global__ void __launch_bounds__(256) ep_combine_p2p_kernel(const EpP2PArgs a, const int32_t* __restrict__ pair_pos,
+                                                             const float* __restrict__ score, int k,
+                                                             const float* __restrict__ ysh32,
+                                                             const uint16_t* __restrict__ ysh16,
+                                                             const float* __restrict__ gate_sig, int64_t T,
+                                                             uint16_t* __restrict__ y) {
+  if (ep_block_error(a)) return;
+  if (!ep_wait_all(a, 2)) return;
+  combine_rows(ep_rows(a, a.rank, a.off_ret), pair_pos, score, k, ysh32, ysh16, gate_sig, T, a.H, y);
 }
 
 }  // namespace fm

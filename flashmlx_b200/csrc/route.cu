@@ -14,7 +14,7 @@
 //   3  per expert: exclusive scan of the chunk counts (stable order across chunks)
 //   4  expert offsets, tile tables for the expert-product kernels, scatter of the
 //      pairs into expert-major order
-#include "fm_internal.cuh"
+#include "fm_ep.cuh"
 
 namespace fm {
 
@@ -451,7 +451,7 @@ FM_DEV void phase_mark(const RouteArgs& a, int phase, unsigned long long& t) {
 // one tile group over contiguous rows; the rank's own tokens form the shared-expert
 // group.  Also writes the identity row map and unit scores the expert kernels read
 // for the received rows (the owner returns bf16(d); the token's rank scales it).
-__global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const EpPlanArgs a) {
+__device__ void ep_plan_body(const EpPlanArgs& a) {
   __shared__ int cnt_a[kMaxGroups + 1];
   __shared__ int cnt_b[kMaxGroups + 1];
   __shared__ int rbeg[kMaxGroups + 1];
@@ -489,6 +489,51 @@ __global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const EpPlanArgs
     a.unit_score[p] = 1.0f;
   }
   if (threadIdx.x == 0) *a.recv_total = R;
+}
+
+__global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const EpPlanArgs a) { ep_plan_body(a); }
+
+// Peer-memory variant (ep.cu): wait for every source's rows, copy the (source, local
+// expert) counts of this owner from its board into the plan's count array, record each
+// received row's source rank and position in that source's send order, then plan.
+__global__ void __launch_bounds__(kRouteThreads) ep_p2p_plan_kernel(const EpP2PArgs a, EpPlanArgs pa) {
+  __shared__ int64_t s_off[kEpMaxWorld + 1], s_start[kEpMaxWorld];
+  if (ep_block_error(a)) return;
+  if (!ep_wait_all(a, 1)) return;
+  const int W = a.world, E = a.E, me = a.rank;
+  int first, count;
+  ep_owner_range(E, me, W, first, count);
+  const int32_t* cnt = ep_board(a, me);
+  int32_t* rc = const_cast<int32_t*>(pa.recv_counts);
+  for (int i = threadIdx.x; i < W * count; i += blockDim.x) {
+    const int s = i / count, e = i % count;
+    rc[i] = cnt[static_cast<int64_t>(s) * E + first + e];
+  }
+  if (threadIdx.x < W) {
+    int64_t start = 0;
+    for (int e = 0; e < first; ++e) start += cnt[static_cast<int64_t>(threadIdx.x) * E + e];
+    s_start[threadIdx.x] = start;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t off = 0;
+    for (int s = 0; s < W; ++s) {
+      s_off[s] = off;
+      for (int e = 0; e < count; ++e) off += rc[s * count + e];
+    }
+    s_off[W] = off;
+    if (off > a.cap_recv) report(a.err, DEVERR_BOUNDS);
+  }
+  __syncthreads();
+  const int64_t R = s_off[W] < a.cap_recv ? s_off[W] : a.cap_recv;
+  for (int64_t p = threadIdx.x; p < R; p += blockDim.x) {
+    int s = 0;
+    while (s + 1 < W && p >= s_off[s + 1]) ++s;
+    a.row_src[p] = s;
+    a.row_pos[p] = static_cast<int32_t>(s_start[s] + (p - s_off[s]));
+  }
+  if (ep_block_error(a)) return;  // a barrier: the count array is complete before planning reads it
+  ep_plan_body(pa);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {

@@ -18,6 +18,11 @@ has no reference counterpart.  One expert-parallel layer on rank r of W:
 
 `ep_forward` is the protocol; the stage objects supply 1, 4 and 6 (DeviceStages: the
 C ABI on this rank's GPU; the tests also drive it with an oracle on CPU ranks).
+
+`MoEBlockEPPeer` runs the same layer with steps 2, 3 and 5 done by the kernels
+themselves over NVLink peer memory (fm_ep_p2p_*): routed rows are written straight into
+their owners' receive buffers and d rows straight back, ordered by epoch flags, with no
+host synchronization and no collective library inside a call.
 """
 from __future__ import annotations
 
@@ -27,7 +32,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-__all__ = ["expert_range", "local_layer", "Exchange", "ep_forward", "DeviceStages", "MoEBlockEP"]
+__all__ = ["expert_range", "local_layer", "Exchange", "ep_forward", "DeviceStages", "MoEBlockEP", "MoEBlockEPPeer"]
 
 
 def expert_range(num_experts: int, rank: int, world: int) -> tuple[int, int]:
@@ -181,3 +186,64 @@ class MoEBlockEP:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return ep_forward(self.stages, self.exchange, x)
 
+
+class MoEBlockEPPeer:
+    """LlamaModel::moe_block with its experts split across the ranks of a process group
+    (one process per GPU of one NVLink domain, at most 8) and the rows moved over peer
+    memory by the kernels (fm_ep_p2p_*).  Constructed collectively: every rank allocates
+    its exchange region for up to `max_tokens` tokens per call and the CUDA IPC handles
+    travel once over the group.  Every rank then makes the same sequence of calls, each
+    with its own tokens; `close` (collective) releases the regions."""
+
+    def __init__(self, shape, local_weights, max_tokens: int, group=None):
+        from . import ops
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.shape = shape
+        self.device = local_weights.router_w.device
+        self.block = ops.MoEBlock(shape, local_weights)  # config + weight structs
+        self.h = ops.Handle(self.device.index)  # owns the region: one per layer object
+        self.h.bind_stream()
+        lib = self.h.lib
+        self.h.check(lib.fm_ep_set(self.h.h, self.rank, self.world))
+        ipc = (C.c_uint8 * 64)()
+        self.h.check(lib.fm_ep_p2p_alloc(self.h.h, C.byref(self.block.cfg), int(max_tokens), ipc))
+        key = (shape.hidden, shape.num_experts, shape.top_k, int(max_tokens))
+        got = [None] * self.world
+        dist.all_gather_object(got, (bytes(ipc), key), group=group)
+        if any(k != key for _, k in got):
+            self.h.check(lib.fm_ep_p2p_close(self.h.h))
+            raise ValueError("ranks disagree on (hidden, num_experts, top_k, max_tokens)")
+        handles = b"".join(b for b, _ in got)
+        self.h.check(lib.fm_ep_p2p_open(self.h.h, handles))
+        dist.barrier(group)
+        self.max_tokens = int(max_tokens)
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        H = self.shape.hidden
+        if x.dtype != torch.bfloat16 or x.device != self.device or x.shape[-1] != H:
+            raise ValueError("x must be a bf16 tensor [T, hidden] on this rank's device")
+        x = x.contiguous()
+        T = x.numel() // H
+        y = out if out is not None else torch.empty_like(x)
+        self.h.bind_stream()
+        self.h.check(self.h.lib.fm_ep_p2p_forward(self.h.h, C.byref(self.block.cfg), C.byref(self.block.W),
+                                                  C.c_void_p(x.data_ptr() if T else 0), T,
+                                                  C.c_void_p(y.data_ptr() if T else 0)))
+        return y
+
+    def sync(self):
+        """Wait for this rank's calls and raise on a device-side error (a peer that did not
+        take part shows up here as a timeout)."""
+        self.h.sync()
+
+    def close(self):
+        """Collective: every rank's calls complete, then the regions are unmapped and freed."""
+        if self.h is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(self.group)
+        self.h.check(self.h.lib.fm_ep_p2p_close(self.h.h))
+        self.h.close()
+        self.h = None

@@ -222,6 +222,33 @@ FM_API int fm_ep_experts(fm_handle* h, const fm_moe_config* cfg, const fm_moe_we
                          const int32_t* recv_counts, uint16_t* d_rows);
 FM_API int fm_ep_combine(fm_handle* h, const fm_moe_config* cfg, const uint16_t* ret_rows, uint16_t* y);
 
+/* Expert parallelism over peer memory: the same layer with no host synchronization and
+ * no collective library.  Every rank of the group (one process per GPU of one NVLink
+ * domain, at most 8) owns a device region of identical layout, exported by CUDA IPC;
+ * the kernels write the routed rows straight into their owners' regions and the d rows
+ * back into their token ranks' regions, and order the steps with epoch flags in the
+ * regions (bounded device-side waits: a rank that does not take part makes the others'
+ * calls fail with FM_ETIMEOUT at fm_sync_status, after which the group must close and
+ * reallocate its regions).
+ *
+ *   fm_ep_p2p_alloc    after fm_ep_set: allocate this rank's region for up to max_tokens
+ *                      tokens per call with cfg's hidden / experts / top_k (identical on
+ *                      every rank) and write its 64-byte CUDA IPC handle to ipc_handle_out.
+ *   fm_ep_p2p_open     ipc_handles = the W handles in rank order (this rank's own slot is
+ *                      ignored): map every peer's region.  Call after every rank's alloc.
+ *   fm_ep_p2p_forward  one layer on this rank's T tokens (T <= max_tokens, may be 0): y =
+ *                      the MoE block output, as fm_moe_block over the whole model's
+ *                      experts.  Asynchronous on the handle's stream; every rank of the
+ *                      group must make the same sequence of calls.
+ *   fm_ep_p2p_close    unmap the peers' regions and free this rank's (also done by
+ *                      fm_destroy).  Call on every rank only after every rank's last
+ *                      forward completed (a barrier after a stream synchronize). */
+FM_API int fm_ep_p2p_alloc(fm_handle* h, const fm_moe_config* cfg, int64_t max_tokens, void* ipc_handle_out);
+FM_API int fm_ep_p2p_open(fm_handle* h, const void* ipc_handles);
+FM_API int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* x,
+                             int64_t T, uint16_t* y);
+FM_API int fm_ep_p2p_close(fm_handle* h);
+
 #ifdef __cplusplus
 }
 #endif
