@@ -14,9 +14,10 @@ value  = tokens of all ranks / max-over-ranks device time per step (inputs resid
 e2e    = the same through the public API with the step's x copied from pinned host
          memory and y read back to pinned host memory inside the timed region
 N > 1  = expert parallelism (flashmlx_b200.ep): each rank holds the router, the shared
-         expert and 1/N of the routed experts, routes its own batch of the workload's
-         tokens, and rows move by NCCL all-to-all (weak scaling); --replicas runs N
-         independent single-GPU layers instead
+         expert and 1/N of the routed experts and routes its own batch of the workload's
+         tokens (weak scaling).  Rows move over NVLink peer memory, written by the
+         kernels themselves (--ep-impl peer, default), or by NCCL all-to-all between
+         staged calls (--ep-impl nccl); --replicas runs N independent single-GPU layers
 --impl reference: the CPU restatement of the reference's MLX path (the reference
 needs MLX + Metal, which this box cannot run) timed on the host cores, rank 0 only.
 """
@@ -50,6 +51,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent replicas instead of expert parallelism")
+    ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: rows over peer memory by the kernels, or NCCL all-to-all between staged calls")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -225,8 +228,10 @@ def run_ours(args, rank, world, local_rank):
     h = ops.default_handle(local_rank)
     x = ops.bf16_from_numpy(x_np, dev)
     y = torch.empty_like(x)
+    hp = h  # the handle whose launches are timed
+    peer_block = None
     if ep:
-        from flashmlx_b200.ep import MoEBlockEP, expert_range, local_layer
+        from flashmlx_b200.ep import MoEBlockEP, MoEBlockEPPeer, expert_range, local_layer
         W = ops.MoEWeightsT.from_numpy(local_layer(layer_np, rank, world), dev)
         ep_block = MoEBlockEP(shape, W)
         E_local = expert_range(shape.num_experts, rank, world)[1]
@@ -238,12 +243,23 @@ def run_ours(args, rank, world, local_rank):
             return orig_experts(recv, recv_counts)
 
         ep_block.stages.experts = experts_spy
-
-        def step(xin, out):
-            out.copy_(ep_block(xin))
-        step(x, y)
+        y_ref = ep_block(x)  # one staged step: the receive layout (same routing as every step)
         h.sync()
         counts = None
+        if args.ep_impl == "peer":
+            peer_block = MoEBlockEPPeer(shape, W, max_tokens=T)
+            hp = peer_block.h
+
+            def step(xin, out):
+                peer_block(xin, out=out)
+            step(x, y)
+            hp.sync()
+            # the two layers may pick different expert paths (GEMV / tcgen05): close, not equal
+            if not torch.allclose(y.float(), y_ref.float(), rtol=2e-2, atol=2e-2):
+                raise RuntimeError("peer-memory and NCCL expert-parallel layers disagree")
+        else:
+            def step(xin, out):
+                out.copy_(ep_block(xin))
     else:
         W = ops.MoEWeightsT.from_numpy(layer_np, dev)
         block = ops.MoEBlock(shape, W)
@@ -257,7 +273,7 @@ def run_ours(args, rank, world, local_rank):
             block(xin, out=out)
     for _ in range(args.warmup):
         step(x, y)
-    h.sync()
+    hp.sync()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
@@ -265,18 +281,18 @@ def run_ours(args, rank, world, local_rank):
     clocks = ClockSampler(local_rank)
     clocks.start()
     stream = torch.cuda.current_stream()
-    h.profile(True)
-    h.profile_report(reset=True)
+    hp.profile(True)
+    hp.profile_report(reset=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         step(x, y)
     e1.record(stream)
     torch.cuda.synchronize()
-    h.sync()
+    hp.sync()
     dev_ms = e0.elapsed_time(e1) / args.steps
-    prof_all = h.profile_report(reset=True)
-    h.profile(False)
+    prof_all = hp.profile_report(reset=True)
+    hp.profile(False)
     # "route.phaseN" entries split the routing kernel's time; they are not launches
     prof = {k: v for k, v in prof_all.items() if "." not in k}
     phases = {k: v[1] / max(1, v[0]) for k, v in prof_all.items() if "." in k}
@@ -347,7 +363,8 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": shape.name, "tokens_per_rank": T, "hidden": shape.hidden,
                        "inter": shape.inter, "experts": shape.num_experts, "top_k": shape.top_k,
                        "shared_inter": shape.shared_inter, "active_experts": active,
-                       "parallelism": (f"ep{world}" if ep else f"replicas{world}") if world > 1 else "single",
+                       "parallelism": ((f"ep{world}-{args.ep_impl}" if ep else f"replicas{world}")
+                                       if world > 1 else "single"),
                        "l2": "weights exceed L2 (no flush between steps)"},
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
@@ -359,6 +376,8 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    if peer_block is not None:
+        peer_block.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

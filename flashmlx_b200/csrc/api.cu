@@ -33,7 +33,7 @@ __global__ void finalize_ep_kernel(const uint16_t* ret, const int32_t* pair_pos,
                                    uint16_t* y);
 __global__ void ep_dispatch_kernel(const EpP2PArgs a);
 __global__ void ep_p2p_plan_kernel(const EpP2PArgs a, EpPlanArgs pa);
-__global__ void ep_return_kernel(const EpP2PArgs a);
+__global__ void ep_release_kernel(const EpP2PArgs a, int kind);
 __global__ void ep_combine_p2p_kernel(const EpP2PArgs a, const int32_t* pair_pos, const float* score, int k,
                                       const float* ysh32, const uint16_t* ysh16, const float* gate_sig, int64_t T,
                                       uint16_t* y);
@@ -390,7 +390,7 @@ EpPlan1 make_ep_plan1(int64_t T, int H, int E, int k, int epad, int ksplit) {
 struct EpPlan2 {
   size_t total = 0;
   size_t tab_a, tab_b, recv_counts, recv_total, row_map, unit_score, a_sorted, a_shared, ysh;
-  size_t d_rows = 0, row_src = 0, row_pos = 0;  // peer-memory exchange only
+  size_t row_dst = 0;  // peer-memory exchange only
   size_t add(size_t bytes) {
     const size_t off = total;
     total = align_up(total + bytes, 256);
@@ -412,13 +412,11 @@ EpPlan2 make_ep_plan2(int64_t R, int64_t T, int H, int I, int Is, int nseg, bool
   return p;
 }
 
-// The same plus the received rows' d buffer and their (source rank, send position):
-// R is the receive capacity, the host does not learn the count.
+// The same plus each received row's d destination (a row of its source rank's ret
+// buffer): R is the receive capacity, the host does not learn the count.
 EpPlan2 make_ep_plan2_p2p(int64_t R, int64_t T, int H, int I, int Is, int nseg, bool shared) {
   EpPlan2 p = make_ep_plan2(R, T, H, I, Is, nseg, shared);
-  p.d_rows = p.add(sizeof(uint16_t) * R * H);
-  p.row_src = p.add(sizeof(int32_t) * std::max<int64_t>(R, 1));
-  p.row_pos = p.add(sizeof(int32_t) * std::max<int64_t>(R, 1));
+  p.row_dst = p.add(sizeof(uint16_t*) * std::max<int64_t>(R, 1));
   return p;
 }
 
@@ -565,12 +563,13 @@ int check_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights*
 }
 
 // Owner-side expert GEMMs of an expert-parallel call: gate/up + SwiGLU, then down into
-// d_rows (bf16(d), one row per received row, in receive order), over the tile tables
+// d_rows (bf16(d), one row per received row, in receive order) or, with d_rowptr, into
+// the row each received row points at (another rank's memory), over the tile tables
 // pa holds.  R rows of recv_rows may be read (the received rows, or their capacity when
 // the host does not know the count).  The shared expert runs on this rank's own tokens.
 int ep_gemms(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* recv_rows, int64_t R,
              int64_t T, int E_local, bool shared, bool tcp, const EpPlan1& p1, const EpPlan2& p2,
-             const fm::EpPlanArgs& pa, uint16_t* d_rows) {
+             const fm::EpPlanArgs& pa, uint16_t* d_rows, uint16_t* const* d_rowptr = nullptr) {
   const int H = c->hidden, I = c->inter, Is = c->shared_inter;
   int rc = FM_OK;
   uint16_t* x_perm = at<uint16_t>(h, p1.x_perm);
@@ -636,7 +635,8 @@ int ep_gemms(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, cons
   gd.act_shared_ld = Is;
   gd.out = nullptr;
   gd.out_shared = nullptr;
-  gd.y_pairs = d_rows;
+  gd.y_pairs = d_rowptr ? nullptr : d_rows;
+  gd.y_rowptr = d_rowptr;
   gd.y_acc = nullptr;
   gd.ysh = (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr;
   gd.ysh16 = (shared && tcp) ? ep_at<uint16_t>(h, p2.ysh) : nullptr;
@@ -1364,10 +1364,7 @@ int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights
   a.sorted_token = ra.sorted_token;
   a.x_perm = ra.x_perm;
   a.P = T * k;
-  a.row_src = ep_at<int32_t>(h, p2.row_src);
-  a.row_pos = ep_at<int32_t>(h, p2.row_pos);
-  a.d_rows = ep_at<uint16_t>(h, p2.d_rows);
-  a.recv_total = pa.recv_total;
+  a.row_dst = ep_at<uint16_t*>(h, p2.row_dst);
   a.done_counter = reinterpret_cast<int32_t*>(q.region);
   a.err = err_word(h);
 
@@ -1389,14 +1386,14 @@ int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights
   if (routed || shared) {
     uint16_t* recv = reinterpret_cast<uint16_t*>(q.region + q.off_recv);
     rc = ep_gemms(h, c, w, recv, routed ? q.cap_recv : 0, T, E_local, shared, tcp, p1, p2, pa,
-                  ep_at<uint16_t>(h, p2.d_rows));
+                  nullptr, a.row_dst);
     if (rc) return rc;
   }
-  prof_begin(h, "ep_p2p_return");
-  fm::ep_return_kernel<<<h->num_sms * 2, 256, 0, h->stream>>>(a);
+  prof_begin(h, "ep_p2p_release");
+  fm::ep_release_kernel<<<1, 32, 0, h->stream>>>(a, 2);
   prof_end(h);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_err(h, e, "ep_return launch");
+  if (e != cudaSuccess) return cuda_err(h, e, "ep_release launch");
   prof_begin(h, "ep_p2p_combine");
   fm::ep_combine_p2p_kernel<<<grid_for(h, T * (H / 8)), 256, 0, h->stream>>>(
       a, ra.pair_pos, ra.topk_score, k, (shared && !tcp) ? ep_at<float>(h, p2.ysh) : nullptr,

@@ -18,8 +18,9 @@
 //   ep_p2p_plan_kernel   (owner) wait for flag 1 of every source; tile tables over the
 //                        (source, local expert) segments and, per received row, its source
 //                        rank and position in that source's send order
-//   the expert GEMMs     (unchanged kernels; d rows written locally)
-//   ep_return_kernel     write every d row into its source rank's ret buffer, release flag 2
+//   the expert GEMMs     gate/up on the received rows; the down GEMM's epilogue stores
+//                        every bf16(d) row straight into its source rank's ret buffer
+//   ep_release_kernel    release flag 2 on every rank
 //   ep_combine_p2p_kernel  wait for flag 2 of every owner, then combine as fm_ep_combine
 // Ranks run calls in lockstep: a rank can only start call e+1 after its combine of call e
 // saw every owner's returns, which every owner issues after its GEMMs of call e finished
@@ -78,26 +79,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpP2PArgs a) {
   ep_release_when_grid_done(a, 1);
 }
 
-// Owner side: every d row back into its source's ret buffer, then flag 2.
-__global__ void __launch_bounds__(256) ep_return_kernel(const EpP2PArgs a) {
+// Owner side, after the down GEMM wrote every d row into its source's ret buffer:
+// release flag 2 on every rank (one block; the GEMM's stores precede it in stream order).
+__global__ void ep_release_kernel(const EpP2PArgs a, int kind) {
   if (ep_block_error(a)) return;
-  const int64_t R = *a.recv_total;
-  const int segs = a.H / 8;
-  const int64_t n = R * segs;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t p = i / segs;
-    const int col = static_cast<int>(i - p * segs) * 8;
-    const int s = a.row_src[p];
-    const int64_t pos = a.row_pos[p];
-    if (pos < 0 || pos >= a.cap_ret) {
-      report(a.err, DEVERR_BOUNDS);
-      continue;
-    }
-    *reinterpret_cast<uint4*>(ep_rows(a, s, a.off_ret) + pos * a.H + col) =
-        *reinterpret_cast<const uint4*>(a.d_rows + p * a.H + col);
-  }
-  ep_release_when_grid_done(a, 2);
+  __threadfence_system();
+  if (threadIdx.x < a.world) st_release_sys(ep_flag(a, threadIdx.x, kind, a.rank), a.epoch);
 }
 
 }  // namespace fm

@@ -110,6 +110,8 @@ struct GemmArgs {
   float* y_acc;           // down (GEMV): [T, H] fp32, sum_k bf16(d*score)
   float* ysh;             // down (GEMV): [T, H] fp32 shared-expert sums
   uint16_t* y_pairs;      // down (tcgen05): [P, H] bf16(bf16(d)*score), expert-major rows
+  uint16_t* const* y_rowptr;  // down, instead of y_pairs: destination of each pair's row
+                              // (another rank's memory over NVLink, expert parallelism)
   uint16_t* ysh16;        // down (tcgen05): [T, H] bf16 shared-expert rows
   int64_t y_ld;
   const TileTable* tab;
@@ -225,10 +227,8 @@ struct EpP2PArgs {
   const uint16_t* x_perm;       // [T, H]
   int64_t P;
   // owner side
-  int32_t* row_src;             // [cap_recv] source rank of each received row
-  int32_t* row_pos;             // [cap_recv] its position in the source's send order
-  const uint16_t* d_rows;       // [cap_recv, H] bf16(d) of the received rows
-  const int32_t* recv_total;    // rows received (device)
+  uint16_t** row_dst;           // [cap_recv] where each received row's d goes: its source
+                                // rank's ret buffer, at its position in that rank's send order
   int32_t* done_counter;        // grid completion counter, 0 between launches
   uint32_t* err;
 };

@@ -320,19 +320,18 @@ FM_DEV void stage_scales(const GemmArgs& a, const SIter& it, int rank, int lane,
 }
 
 // The 128 epilogue threads copy a staged 32-row tile (row stride 256 B, `cols` bf16
-// columns per row) to global memory as 16-byte stores; staged row i goes to output
-// row dst_row(i), or nowhere when that is negative.
+// columns per row) to global memory as 16-byte stores; staged row i goes to the output
+// row starting at dst_row(i) (this GPU's memory or a peer's), or nowhere when null.
 template <class RowFn>
-FM_DEV void store_staged(const uint8_t* stg, int cols, uint16_t* base, int64_t ld, int col0, int ncols_valid,
-                         RowFn dst_row, int et) {
+FM_DEV void store_staged(const uint8_t* stg, int cols, int col0, int ncols_valid, RowFn dst_row, int et) {
   const int segs_per_row = cols / 8;
   const int nseg = 32 * segs_per_row;
   for (int s = et; s < nseg; s += 128) {
     const int i = s / segs_per_row, part = s - i * segs_per_row;
-    const int64_t r = dst_row(i);
-    if (r < 0 || part * 8 >= ncols_valid) continue;
+    uint16_t* row = dst_row(i);
+    if (!row || part * 8 >= ncols_valid) continue;
     const uint4 v = *reinterpret_cast<const uint4*>(stg + i * 256 + part * 16);
-    *reinterpret_cast<uint4*>(base + r * ld + col0 + part * 8) = v;
+    *reinterpret_cast<uint4*>(row + col0 + part * 8) = v;
   }
 }
 
@@ -679,8 +678,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           uint16_t* outb = sh ? a.out_shared : a.out;
           const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
           const int col0 = ti.rb * 128 + rank * 64;
-          store_staged(stg, 64, outb, ld, col0, N - col0,
-                       [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(prow + i) : -1; }, et);
+          store_staged(stg, 64, col0, N - col0,
+                       [&](int i) -> uint16_t* { return i < c_lim ? outb + static_cast<int64_t>(prow + i) * ld : nullptr; },
+                       et);
         } else {
           // staging row = token column c, 128 outputs; lanes (2m, 2m+1) hold rows
           // (n, n+1): the even lane stores even columns, the odd lane odd columns
@@ -706,13 +706,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           named_bar_sync(1, 128);
           const int col0 = ti.rb * 256 + rank * 128;
           if (MODE == MODE_DOWN) {
-            uint16_t* outb = sh ? a.ysh16 : a.y_pairs;
-            store_staged(stg, 128, outb, a.y_ld, col0, N - col0,
-                         [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(prow + i) : -1; }, et);
+            if (!sh && a.y_rowptr) {
+              store_staged(stg, 128, col0, N - col0,
+                           [&](int i) -> uint16_t* { return i < c_lim ? a.y_rowptr[prow + i] : nullptr; }, et);
+            } else {
+              uint16_t* outb = sh ? a.ysh16 : a.y_pairs;
+              store_staged(
+                  stg, 128, col0, N - col0,
+                  [&](int i) -> uint16_t* { return i < c_lim ? outb + static_cast<int64_t>(prow + i) * a.y_ld : nullptr; },
+                  et);
+            }
           } else {
-            store_staged(
-                stg, 128, a.out, a.out_ld, col0, N - col0,
-                [&](int i) -> int64_t { return i < c_lim ? static_cast<int64_t>(a.sorted_flat[prow + i]) : -1; }, et);
+            store_staged(stg, 128, col0, N - col0,
+                         [&](int i) -> uint16_t* {
+                           return i < c_lim ? a.out + static_cast<int64_t>(a.sorted_flat[prow + i]) * a.out_ld : nullptr;
+                         },
+                         et);
           }
         }
       }

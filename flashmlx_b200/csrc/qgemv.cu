@@ -245,6 +245,8 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
           if (MODE == MODE_DOWN) {
             if (sh) {
               red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v);
+            } else if (a.y_rowptr) {  // one output row per pair, at its destination (peer memory)
+              a.y_rowptr[p][n] = f2bf(rbf(rbf(v) * a.sorted_score[p]));
             } else if (a.y_pairs) {  // one output row per pair (expert-parallel owner side)
               a.y_pairs[static_cast<int64_t>(p) * a.y_ld + n] = f2bf(rbf(rbf(v) * a.sorted_score[p]));
             } else {

@@ -494,8 +494,9 @@ __device__ void ep_plan_body(const EpPlanArgs& a) {
 __global__ void __launch_bounds__(kRouteThreads) ep_plan_kernel(const EpPlanArgs a) { ep_plan_body(a); }
 
 // Peer-memory variant (ep.cu): wait for every source's rows, copy the (source, local
-// expert) counts of this owner from its board into the plan's count array, record each
-// received row's source rank and position in that source's send order, then plan.
+// expert) counts of this owner from its board into the plan's count array, point each
+// received row at its d row's destination (its source rank's ret buffer, at the row's
+// position in that rank's send order), then plan.
 __global__ void __launch_bounds__(kRouteThreads) ep_p2p_plan_kernel(const EpP2PArgs a, EpPlanArgs pa) {
   __shared__ int64_t s_off[kEpMaxWorld + 1], s_start[kEpMaxWorld];
   if (ep_block_error(a)) return;
@@ -529,8 +530,13 @@ __global__ void __launch_bounds__(kRouteThreads) ep_p2p_plan_kernel(const EpP2PA
   for (int64_t p = threadIdx.x; p < R; p += blockDim.x) {
     int s = 0;
     while (s + 1 < W && p >= s_off[s + 1]) ++s;
-    a.row_src[p] = s;
-    a.row_pos[p] = static_cast<int32_t>(s_start[s] + (p - s_off[s]));
+    const int64_t pos = s_start[s] + (p - s_off[s]);
+    if (pos >= a.cap_ret) {
+      report(a.err, DEVERR_BOUNDS);
+      a.row_dst[p] = nullptr;
+      continue;
+    }
+    a.row_dst[p] = ep_rows(a, s, a.off_ret) + pos * a.H;
   }
   if (ep_block_error(a)) return;  // a barrier: the count array is complete before planning reads it
   ep_plan_body(pa);
