@@ -178,6 +178,19 @@ FM_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {  // whole warp
 FM_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 FM_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
+// One lane of a converged warp (the lowest): lets the compiler keep the operands of a
+// single-thread tcgen05 / TMA instruction in the warp's uniform registers when the whole
+// warp computed them.
+FM_DEV bool elect_one() {
+  uint32_t p = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(p));
+  return p != 0;
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 in, fp32 accumulate)
 FM_DEV void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
   asm volatile(

@@ -342,7 +342,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Bars* bars = reinterpret_cast<Bars*>(smem + OFF_BAR);
   const int tid = threadIdx.x;
-  const int warp = tid >> 5, lane = tid & 31;
+  // warp index broadcast from lane 0: provably warp-uniform, so each role's values
+  // derived from it can live in uniform registers
+  const int warp = __shfl_sync(0xffffffffu, tid >> 5, 0), lane = tid & 31;
   const int rank = static_cast<int>(cluster_rank());
   const bool leader = rank == 0;
   const int pair = static_cast<int>(cluster_id_x());
@@ -389,6 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ dequant producers
     const int grp = warp / 4;              // takes the k-steps with (k-step % DQ_GROUPS) == grp
     const int t = (warp % 4) * 32 + lane;  // A row
+    const int gs_shift = __ffs(a.gs) - 1;  // group sizes are powers of two (32, 64, 128)
     int cs = 0, it0 = 0;                   // super-step, k-steps before it
     bool ok = true;
     while (ok) {
@@ -409,16 +412,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (kk >= nk) break;
         const int it = it0 + kk;
         const int stage = it % STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
-          ok = false;
-          break;
-        }
+        // the k-step's 64 weights into registers first (codes and scales are in the
+        // code slot already), so the math overlaps the wait for the stage to drain
+        uint4 o[8];
         if (valid) {
-          uint8_t* As = smem + OFF_A + stage * A_BYTES;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // the two 32-element halves of the k-step
             const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + h) ^ (t & 7)) << 4));
-            const int g = (kk * 64 + 32 * h) / a.gs;
+            const int g = (kk * 64 + 32 * h) >> gs_shift;
             const uint32_t s2u = static_cast<uint32_t>(sc[g]) * 0x10001u;
             const uint32_t b2u = static_cast<uint32_t>(bi[g]) * 0x10001u;
             const __nv_bfloat162 s2 = *reinterpret_cast<const __nv_bfloat162*>(&s2u);
@@ -426,14 +427,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-              uint4 o;
-              o.x = deq_pair(words[i], 0, s2, b2);
-              o.y = deq_pair(words[i], 1, s2, b2);
-              o.z = deq_pair(words[i], 2, s2, b2);
-              o.w = deq_pair(words[i], 3, s2, b2);
-              *reinterpret_cast<uint4*>(As + sw128_off(t, h * 4 + i)) = o;
+              o[h * 4 + i].x = deq_pair(words[i], 0, s2, b2);
+              o[h * 4 + i].y = deq_pair(words[i], 1, s2, b2);
+              o[h * 4 + i].z = deq_pair(words[i], 2, s2, b2);
+              o[h * 4 + i].w = deq_pair(words[i], 3, s2, b2);
             }
           }
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
+          ok = false;
+          break;
+        }
+        if (valid) {
+          uint8_t* As = smem + OFF_A + stage * A_BYTES;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(As + sw128_off(t, j)) = o[j];
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
         __syncwarp();
@@ -552,12 +560,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             for (; pend < it; ++pend)
               if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
           }
-          if (bt == 0) {
-            mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nblk) * 4096u);
+          if (warp == ACT_WARP) {  // the whole warp: operands warp-uniform, one lane issues
+            const int row_base = __shfl_sync(0xffffffffu, ti.row0 + rbeg, 0);
+            const int nb = __shfl_sync(0xffffffffu, nblk, 0);
+            const CUtensorMap* map = &maps.act[__shfl_sync(0xffffffffu, sh ? 1 : 0, 0)];
             const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES);
-            const CUtensorMap* map = &maps.act[sh ? 1 : 0];
-            for (int b = 0; b < nblk; ++b)
-              tma_load_2d_pair(bs + b * 4096, map, ks * 64, ti.row0 + rbeg + b * 32, full0 + stage * 8);
+            if (elect_one()) {
+              mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nb) * 4096u);
+              for (int b = 0; b < nb; ++b)
+                tma_load_2d_pair(bs + b * 4096, map, ks * 64, row_base + b * 32, full0 + stage * 8);
+            }
+            __syncwarp();
           } else if (lane == 0) {
             mbar_arrive_cluster(full0 + stage * 8);
           }
@@ -573,41 +586,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader)
-    if (leader && lane == 0) {
+    // The whole warp walks the loop with every MMA operand (TMEM address, descriptors,
+    // instruction descriptor) warp-uniform -- broadcast from lane 0 where it comes from
+    // memory -- and one elected lane issues.  A single thread computing them itself
+    // costs ~90 cycles of issue per MMA, more than an N = 128 MMA takes to run.
+    // elect.sync picks the same (lowest) lane every time, so the commits track that
+    // lane's MMAs.
+    if (leader) {
       const uint32_t empty_l = map_to_rank(&bars->empty[0], 0), empty_p = map_to_rank(&bars->empty[0], 1);
       const uint32_t accf_l = map_to_rank(&bars->accf[0], 0), accf_p = map_to_rank(&bars->accf[0], 1);
-      int it = 0, lt = 0;
+      const uint32_t tbase = __shfl_sync(0xffffffffu, tmem_base, 0);
+      const uint32_t a_base = smem_u32(smem + OFF_A), b_base = smem_u32(smem + OFF_B);
+      const int ntl = __shfl_sync(0xffffffffu, ntiles, 0);
+      int stage = 0, phase = 0, lt = 0;
       bool ok = true;
-      for (int tile = pair; tile < ntiles && ok; tile += npairs, ++lt) {
+      for (int tile = pair; tile < ntl && ok; tile += npairs, ++lt) {
         const TileInfo ti = dir.get(tile);
-        const int nks = tile_ksteps(a, ti, MODE);
+        const int nks = __shfl_sync(0xffffffffu, tile_ksteps(a, ti, MODE), 0);
+        const uint32_t idesc = __shfl_sync(0xffffffffu, idesc_bf16(2 * BM, tile_nmma(ti.nrows)), 0);
         const int buf = lt & 1;
-        if (!mbar_wait(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err))) break;
         tc_fence_after();
-        const uint32_t idesc = idesc_bf16(2 * BM, tile_nmma(ti.nrows));
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * ACC_COLS);
+        const uint32_t d = tbase + static_cast<uint32_t>(buf * ACC_COLS);
         for (int ks = 0; ks < nks; ++ks) {
-          const int stage = it % STAGES;
-          if (!mbar_wait(&bars->full[stage], (it / STAGES) & 1, abort_flag, a.err)) {
+          if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase, abort_flag, a.err))) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sdesc_sw128(smem_u32(smem + OFF_A + stage * A_BYTES));
-          const uint64_t bd = sdesc_sw128(smem_u32(smem + OFF_B + stage * B_BYTES));
+          const uint64_t ad = sdesc_sw128(a_base + static_cast<uint32_t>(stage * A_BYTES));
+          const uint64_t bd = sdesc_sw128(b_base + static_cast<uint32_t>(stage * B_BYTES));
+          if (elect_one()) {
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) umma2_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
-          umma2_commit(empty_l + stage * 8);
-          umma2_commit(empty_p + stage * 8);
-          ++it;
+            for (int kk = 0; kk < 4; ++kk) umma2_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+            umma2_commit(empty_l + stage * 8);
+            umma2_commit(empty_p + stage * 8);
+          }
+          __syncwarp();
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
         }
-        if (ok) {
+        if (ok && elect_one()) {
           umma2_commit(accf_l + buf * 8);
           umma2_commit(accf_p + buf * 8);
         }
+        __syncwarp();
       }
-      umma2_commit(map_to_rank(&bars->done, 0));
-      wait_done(&bars->done, 0, a.err);
+      if (elect_one()) {
+        umma2_commit(map_to_rank(&bars->done, 0));
+        wait_done(&bars->done, 0, a.err);
+      }
     }
     __syncwarp();
   } else if (warp >= EPI_WARP && warp < EPI_WARP + 4) {
