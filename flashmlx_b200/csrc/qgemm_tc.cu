@@ -271,54 +271,6 @@ FM_DEV void a_row_info(const GemmArgs& a, const TileInfo& ti, int rank, int t, i
   }
 }
 
-// The code-loader warp stages the scales and biases of one super-step (256 K values:
-// G = 256 / gs groups) of this CTA's 128 A rows into a code slot: sc[t][g], bi[t][g]
-// (u16, row stride SC_GROUPS).  Rows outside the matrix and groups past the row end
-// are zero-filled.  Aligned rows (an even number of groups per row) use 4-byte
-// cp.async tracked by the slot barrier; odd rows fall back to 2-byte loads + stores.
-// Every lane then counts one arrival on cfull.
-template <int MODE>
-FM_DEV void stage_scales(const GemmArgs& a, const SIter& it, int rank, int lane, uint16_t* sc, uint16_t* bi,
-                         uint64_t* cfull) {
-  const TileInfo& ti = it.ti;
-  const bool sh = ti.expert < 0;
-  const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
-  const int N = sh ? a.N_shared : a.N;
-  const int gpr = K / a.gs;
-  const int G = 256 / a.gs;
-  const int g0 = it.ss * G;
-  const bool aligned = (gpr & 1) == 0;
-#pragma unroll 1
-  for (int i = 0; i < 4; ++i) {
-    const int t = lane + 32 * i;
-    int row;
-    const uint16_t* S;
-    const uint16_t* B;
-    a_row_info<MODE>(a, ti, rank, t, row, S, B);
-    const bool rv = row < N;
-    const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + (rv ? row : 0);
-    const uint16_t* srow = S + r * gpr;
-    const uint16_t* brow = B ? B + r * gpr : nullptr;
-    uint16_t* sdst = sc + t * SC_GROUPS;
-    uint16_t* bdst = bi + t * SC_GROUPS;
-    if (aligned) {
-      for (int g = 0; g < G; g += 2) {
-        const bool in = rv && g0 + g < gpr;  // gpr even: the pair is inside the row or past it
-        cp_async4(smem_u32(sdst + g), in ? srow + g0 + g : srow, in ? 4u : 0u);
-        cp_async4(smem_u32(bdst + g), (in && brow) ? brow + g0 + g : srow, (in && brow) ? 4u : 0u);
-      }
-    } else {
-      for (int g = 0; g < G; ++g) {
-        const bool in = rv && g0 + g < gpr;
-        sdst[g] = in ? __ldg(srow + g0 + g) : static_cast<uint16_t>(0);
-        bdst[g] = (in && brow) ? __ldg(brow + g0 + g) : static_cast<uint16_t>(0);
-      }
-    }
-  }
-  if (aligned) cp_async_arrive_noinc(cfull);
-  else mbar_arrive(cfull);
-}
-
 // The 128 epilogue threads copy a staged 32-row tile (row stride 256 B, `cols` bf16
 // columns per row) to global memory as 16-byte stores; staged row i goes to the output
 // row starting at dst_row(i) (this GPU's memory or a peer's), or nowhere when null.
@@ -462,41 +414,96 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     }
   } else if (warp == CODE_WARP) {
     // ------------------------------------------------------------ code loader (TMA)
-    // Per super-step: the TMA of the codes (lane 0), the scales and biases (all lanes)
-    // and the slot metadata; after the last tile a slot with nk = 0 ends the consumers.
+    // Per super-step: the TMA of the codes (one elected lane, operands warp-uniform), the
+    // scales and biases (all lanes: 4 A rows each, row pointers set once per tile) and
+    // the slot metadata; after the last tile a slot with nk = 0 ends the consumers.
+    // Scales land as sc[t][g], bi[t][g] (u16, row stride SC_GROUPS, G = 256 / gs groups
+    // of the super-step); rows outside the matrix and groups past the row end are zero.
+    // Rows with an even group count use 4-byte cp.async tracked by the slot barrier,
+    // odd ones 2-byte loads and stores.  Every lane counts one arrival on cfull.
     SIter cur;
     siter_load(cur, a, dir, pair, ntiles, MODE);
+    const int gs_shift = __ffs(a.gs) - 1;  // group sizes are powers of two
+    const int G = 256 >> gs_shift;         // quant groups per row per super-step
+    const uint16_t* srow[4];
+    const uint16_t* brow[4];
+    bool rv[4];
+    int gpr = 0, tile_ready = -1;
+    int u_vlim = 0, u_row = 0, u_map0 = 0;
     int cs = 0;
     while (true) {
       const int slot = cs % NC;
       if (!__all_sync(0xffffffffu, mbar_wait(&bars->cempty[slot], ((cs / NC) & 1) ^ 1, abort_flag, a.err))) break;
       if (!cur.valid) {
-        if (lane == 0) {
+        if (elect_one()) {
           bars->slot_nk[slot] = 0;
           mbar_arrive_cnt(&bars->cfull[slot], CFULL_ARRIVALS);
         }
+        __syncwarp();
         break;
       }
-      const TileInfo& ti = cur.ti;
-      const bool sh = ti.expert < 0;
-      const int N = sh ? a.N_shared : a.N;
-      uint16_t* sc = reinterpret_cast<uint16_t*>(smem + OFF_SC + slot * SC_BYTES);
-      stage_scales<MODE>(a, cur, rank, lane, sc, sc + BM * SC_GROUPS, &bars->cfull[slot]);
-      if (lane == 0) {
-        const int base = (MODE == MODE_GATEUP) ? ti.rb * 128 + rank * 64 : ti.rb * 256 + rank * 128;
-        bars->slot_nk[slot] = min(KS_PER_SS, cur.nks - cur.ss * KS_PER_SS);
-        bars->slot_vlim[slot] = max(0, N - base);
-        const int erow = sh ? 0 : ti.expert * N;
-        const uint32_t dst = smem_u32(smem + OFF_C + slot * C_BYTES);
-        const int x = cur.ss * (KS_PER_SS * 8);
-        mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);  // also publishes the metadata
-        if (MODE == MODE_GATEUP) {
-          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + base, &bars->cfull[slot]);
-          tma_load_2d(dst + 64 * 128, &maps.code[sh ? 3 : 1], x, erow + base, &bars->cfull[slot]);
-        } else {
-          tma_load_2d(dst, &maps.code[sh ? 2 : 0], x, erow + base, &bars->cfull[slot]);
+      if (cur.tile != tile_ready) {  // a new tile: this lane's scale rows and the tile's TMA rows
+        tile_ready = cur.tile;
+        const TileInfo& ti = cur.ti;
+        const bool sh = ti.expert < 0;
+        const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
+        const int N = sh ? a.N_shared : a.N;
+        gpr = K >> gs_shift;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          int row;
+          const uint16_t* S;
+          const uint16_t* B;
+          a_row_info<MODE>(a, ti, rank, lane + 32 * i, row, S, B);
+          rv[i] = row < N;
+          const int64_t r = (sh ? 0 : static_cast<int64_t>(ti.expert) * N) + (rv[i] ? row : 0);
+          srow[i] = S + r * gpr;
+          brow[i] = B ? B + r * gpr : nullptr;
         }
+        const int base = (MODE == MODE_GATEUP) ? ti.rb * 128 + rank * 64 : ti.rb * 256 + rank * 128;
+        u_vlim = __shfl_sync(0xffffffffu, max(0, N - base), 0);
+        u_row = __shfl_sync(0xffffffffu, (sh ? 0 : ti.expert * N) + base, 0);
+        u_map0 = __shfl_sync(0xffffffffu, sh ? 2 : 0, 0);
       }
+      const int ss = __shfl_sync(0xffffffffu, cur.ss, 0);
+      const int nk = __shfl_sync(0xffffffffu, min(KS_PER_SS, cur.nks - cur.ss * KS_PER_SS), 0);
+      uint16_t* sc = reinterpret_cast<uint16_t*>(smem + OFF_SC + slot * SC_BYTES);
+      uint16_t* bi = sc + BM * SC_GROUPS;
+      const int g0 = ss * G;
+      if ((gpr & 1) == 0) {  // 4-byte copies: the pair of groups is inside the row or past it
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = lane + 32 * i;
+          for (int g = 0; g < G; g += 2) {
+            const bool in = rv[i] && g0 + g < gpr;
+            cp_async4(smem_u32(sc + t * SC_GROUPS + g), in ? srow[i] + g0 + g : srow[i], in ? 4u : 0u);
+            cp_async4(smem_u32(bi + t * SC_GROUPS + g), (in && brow[i]) ? brow[i] + g0 + g : srow[i],
+                      (in && brow[i]) ? 4u : 0u);
+          }
+        }
+        cp_async_arrive_noinc(&bars->cfull[slot]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int t = lane + 32 * i;
+          for (int g = 0; g < G; ++g) {
+            const bool in = rv[i] && g0 + g < gpr;
+            sc[t * SC_GROUPS + g] = in ? __ldg(srow[i] + g0 + g) : static_cast<uint16_t>(0);
+            bi[t * SC_GROUPS + g] = (in && brow[i]) ? __ldg(brow[i] + g0 + g) : static_cast<uint16_t>(0);
+          }
+        }
+        mbar_arrive(&bars->cfull[slot]);
+      }
+      const uint32_t dst = smem_u32(smem + OFF_C + slot * C_BYTES);
+      const int x = ss * (KS_PER_SS * 8);
+      if (elect_one()) {
+        bars->slot_nk[slot] = nk;
+        bars->slot_vlim[slot] = u_vlim;
+        mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);  // also publishes the metadata
+        tma_load_2d(dst, &maps.code[u_map0], x, u_row, &bars->cfull[slot]);
+        if (MODE == MODE_GATEUP) tma_load_2d(dst + 64 * 128, &maps.code[u_map0 + 1], x, u_row, &bars->cfull[slot]);
+      }
+      __syncwarp();
       ++cs;
       siter_next(cur, a, dir, ntiles, npairs, MODE);
     }
