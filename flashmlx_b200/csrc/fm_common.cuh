@@ -36,8 +36,14 @@ FM_DEV uint16_t f2bf(float f) {
 
 FM_DEV float rbf(float f) { return bf2f(f2bf(f)); }
 
-FM_DEV uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+FM_DEV uint32_t pack_bf16x2(float lo, float hi) {  // both rounded to nearest even, one instruction
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// bf16x2 product of two bf16 pairs, each rounded once (= rbf(a * b) per lane)
+FM_DEV uint32_t bmul2(uint32_t a, uint32_t b) {
+  __nv_bfloat162 r = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&a), *reinterpret_cast<const __nv_bfloat162*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
 }
 
 FM_DEV float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }

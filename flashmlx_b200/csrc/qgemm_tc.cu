@@ -676,40 +676,48 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const int prow = ti.row0 + j * 32;
         if (MODE == MODE_GATEUP) {
           // gate warps (q 0,1) finish columns 0..15, up warps (q 2,3) columns 16..31;
-          // each hands the partner the other half of its rows through shared memory
-          uint16_t* to_up = xchg + (xit & 1) * (2 * 16 * 64);  // gate values, cols 16..31
-          uint16_t* to_gate = to_up + 16 * 64;                  // up values, cols 0..15
+          // each hands the partner the other half of its rows through shared memory,
+          // as bf16 pairs of adjacent columns: xchg word [column pair][row]
+          uint32_t* to_up = reinterpret_cast<uint32_t*>(xchg) + (xit & 1) * (2 * 8 * 64);  // gate, cols 16..31
+          uint32_t* to_gate = to_up + 8 * 64;                                                // up, cols 0..15
           const int r64 = row_in & 63;
           if (q < 2) {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) to_up[c * 64 + r64] = f2bf(v[16 + c]);
+            for (int c = 0; c < 8; ++c) to_up[c * 64 + r64] = pack_bf16x2(v[16 + 2 * c], v[17 + 2 * c]);
           } else {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) to_gate[c * 64 + r64] = f2bf(v[c]);
+            for (int c = 0; c < 8; ++c) to_gate[c * 64 + r64] = pack_bf16x2(v[2 * c], v[2 * c + 1]);
           }
           named_bar_sync(1, 128);
           const int c0 = (q < 2) ? 0 : 16;
-          uint32_t res[16];
+          // silu(g) * u per MLX op, two columns at a time: sg = bf16(sigmoid(g)) from
+          // fp32, then h = bf16(g * sg) and bf16(h * u) as bf16x2 products (each
+          // rounded once, as the per-op rounding of swiglu1)
+          uint32_t res2[8];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            float gv, uv;
+          for (int c = 0; c < 8; ++c) {
+            uint32_t g2, u2;
             if (q < 2) {
-              gv = rbf(v[c]);
-              uv = bf2f(to_gate[c * 64 + r64]);
+              g2 = pack_bf16x2(v[2 * c], v[2 * c + 1]);
+              u2 = to_gate[c * 64 + r64];
             } else {
-              gv = bf2f(to_up[c * 64 + r64]);
-              uv = rbf(v[16 + c]);
+              g2 = to_up[c * 64 + r64];
+              u2 = pack_bf16x2(v[16 + 2 * c], v[17 + 2 * c]);
             }
-            res[c] = f2bf(swiglu1(gv, uv));
+            const float ga = __uint_as_float(g2 << 16), gb = __uint_as_float(g2 & 0xffff0000u);
+            const uint32_t s2 = pack_bf16x2(__fdividef(1.0f, 1.0f + __expf(-ga)), __fdividef(1.0f, 1.0f + __expf(-gb)));
+            res2[c] = bmul2(bmul2(g2, s2), u2);
           }
           // staging row = token column (c0 + c), 64 outputs at their pair-permuted
           // slots; lanes r64 and r64 ^ 4 share one 32-bit word
           const int pn = perm8(r64);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const uint32_t other = __shfl_xor_sync(0xffffffffu, res[c], 4);
-            if ((lane & 4) == 0)
-              *reinterpret_cast<uint32_t*>(stg + (c0 + c) * 256 + pn * 2) = res[c] | (other << 16);
+          for (int c = 0; c < 8; ++c) {
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, res2[c], 4);
+            if ((lane & 4) == 0) {
+              *reinterpret_cast<uint32_t*>(stg + (c0 + 2 * c) * 256 + pn * 2) = __byte_perm(res2[c], other, 0x5410);
+              *reinterpret_cast<uint32_t*>(stg + (c0 + 2 * c + 1) * 256 + pn * 2) = __byte_perm(res2[c], other, 0x7632);
+            }
           }
           named_bar_sync(1, 128);
           uint16_t* outb = sh ? a.out_shared : a.out;
