@@ -731,22 +731,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           // (n, n+1): the even lane stores even columns, the odd lane odd columns
           const bool odd = lane & 1;
           const int pc = ti.row0 + min(j * 32 + lane, ti.nrows - 1);
-          const float my_score = (MODE == MODE_DOWN && !sh) ? a.sorted_score[pc] : 1.f;
+          // routing scores are bf16 values, so bf16(bf16(d) * score) per MLX op is one
+          // bf16x2 product per column pair; lane c (even) holds the scores of columns c, c+1
+          uint32_t s_pair = 0x3F803F80u;  // (1, 1)
+          if (MODE == MODE_DOWN && !sh) {
+            const float my_score = a.sorted_score[pc];
+            s_pair = pack_bf16x2(my_score, __shfl_down_sync(0xffffffffu, my_score, 1));
+          }
+          const uint32_t psel = odd ? 0x7632u : 0x5410u;
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
-            float mine_c = v[c], mine_c1 = v[c + 1];
-            if (MODE == MODE_DOWN && !sh) {  // bf16(bf16(d) * score) per MLX op
-              const float se = __shfl_sync(0xffffffffu, my_score, c);
-              const float so = __shfl_sync(0xffffffffu, my_score, c + 1);
-              mine_c = rbf(rbf(mine_c) * se);
-              mine_c1 = rbf(rbf(mine_c1) * so);
-            }
-            const float give = odd ? mine_c : mine_c1;
-            const float got2 = __shfl_xor_sync(0xffffffffu, give, 1);
-            const float lo = odd ? got2 : mine_c;   // row n0, column (c or c+1)
-            const float hi = odd ? mine_c1 : got2;  // row n0+1
+            uint32_t r2 = pack_bf16x2(v[c], v[c + 1]);  // this row, columns c and c+1
+            if (MODE == MODE_DOWN && !sh) r2 = bmul2(r2, __shfl_sync(0xffffffffu, s_pair, c));
+            // lanes (2m, 2m+1) hold rows (n0, n0+1): the even lane stores column c, the
+            // odd lane column c+1, each word holding both rows
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, r2, 1);
+            const uint32_t w = odd ? __byte_perm(other, r2, psel) : __byte_perm(r2, other, psel);
             const int col = c + (odd ? 1 : 0);
-            *reinterpret_cast<uint32_t*>(stg + col * 256 + (row_in & ~1) * 2) = pack_bf16x2(lo, hi);
+            *reinterpret_cast<uint32_t*>(stg + col * 256 + (row_in & ~1) * 2) = w;
           }
           named_bar_sync(1, 128);
           const int col0 = ti.rb * 256 + rank * 128;
