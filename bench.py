@@ -274,9 +274,6 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.warmup):
         step(x, y)
     hp.sync()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
 
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -284,9 +281,16 @@ def run_ours(args, rank, world, local_rank):
     hp.profile(True)
     hp.profile_report(reset=True)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # all host-side set-up (sampler start-up varies per rank by tens of ms) before the
+    # barrier: otherwise early ranks would time their wait for late ones in the first step
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     e0.record(stream)
+    h0 = time.perf_counter()
     for _ in range(args.steps):
         step(x, y)
+    host_ms = (time.perf_counter() - h0) * 1e3 / args.steps  # host time to issue one step
     e1.record(stream)
     torch.cuda.synchronize()
     hp.sync()
@@ -315,9 +319,16 @@ def run_ours(args, rank, world, local_rank):
     clk = clocks.stop()
 
     if world > 1:
+        per_rank = torch.zeros(world, 2, device=dev, dtype=torch.float64)
+        per_rank[rank, 0], per_rank[rank, 1] = dev_ms, host_ms
+        dist.all_reduce(per_rank, op=dist.ReduceOp.SUM)
+        rank_ms = [round(v, 4) for v in per_rank[:, 0].tolist()]
+        rank_host_ms = [round(v, 4) for v in per_rank[:, 1].tolist()]
         t = torch.tensor([dev_ms, e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dev_ms, e2e_ms = t.tolist()
+    else:
+        rank_ms, rank_host_ms = [round(dev_ms, 4)], [round(host_ms, 4)]
 
     if rank == 0:
         peaks, peak_src = load_peaks()
@@ -369,6 +380,8 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
             "gpu_launches": ours_launches,
+            "rank_ms_per_step": rank_ms,
+            "rank_host_ms_per_step": rank_host_ms,
             "kernels": {kname: {"launches": n, "avg_ms": ms / max(1, n)} for kname, (n, ms) in prof.items()},
             "route_phases_ms": phases,
             "roofline": roof,

@@ -1344,7 +1344,8 @@ int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights
     e = cudaMemsetAsync(ep_at<float>(h, p2.ysh), 0, sizeof(float) * T * H, h->stream);
     if (e != cudaSuccess) return cuda_err(h, e, "cudaMemsetAsync");
   }
-  const fm::EpPlanArgs pa = ep_plan_args(h, c, E_local, T, shared, tcp, p2);
+  fm::EpPlanArgs pa = ep_plan_args(h, c, E_local, T, shared, tcp, p2);
+  pa.src_rot = h->ep_rank;  // see ep_plan_body: owners start their stores at different sources
   fm::EpP2PArgs a;
   std::memset(&a, 0, sizeof(a));
   for (int r = 0; r < q.world; ++r) a.peer[r] = q.peer[r];

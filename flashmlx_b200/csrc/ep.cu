@@ -65,11 +65,17 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpP2PArgs a) {
   if (ep_block_error(a)) return;
   const int segs = a.H / 8;
   const int64_t routed = a.offsets[E];  // pairs with an expert (at most P)
-  const int64_t n = (routed < a.P ? routed : a.P) * segs;
+  const int64_t Pv = routed < a.P ? routed : a.P;
+  const int64_t n = Pv * segs;
+  // The rows are owner-contiguous and the grid walks them in order, so every rank starts
+  // at its own rows and goes on to the next owners': at any moment the ranks write to
+  // different owners rather than all of them into one owner's memory.
+  const int64_t rot = s_start[me] < Pv ? s_start[me] : 0;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t p = i / segs;
-    const int col = static_cast<int>(i - p * segs) * 8;
+    const int64_t p0 = i / segs;
+    const int col = static_cast<int>(i - p0 * segs) * 8;
+    const int64_t p = (p0 + rot < Pv) ? p0 + rot : p0 + rot - Pv;
     int r = 0;
     while (r + 1 < W && p >= s_start[r + 1]) ++r;
     const int64_t row = s_off[r] + (p - s_start[r]);

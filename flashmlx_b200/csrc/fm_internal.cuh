@@ -198,6 +198,7 @@ struct EpPlanArgs {
   const int32_t* recv_counts;  // [world, E_local] rows received per (source rank, local expert)
   int world;
   int E_local;
+  int src_rot;                 // first source rank in the table's group order (then +1, ...)
   int T_shared;                // this rank's tokens for its shared-expert group (0: none)
   int a_n, a_n_shared, b_n;    // output rows of the routed / shared matrices per table
   int a_rows_per_block, b_rows_per_block;

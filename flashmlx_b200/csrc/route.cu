@@ -468,7 +468,12 @@ __device__ void ep_plan_body(const EpPlanArgs& a) {
   const int R = block_exclusive_scan(rbeg, nseg, s_tmp);
   for (int gi = threadIdx.x; gi < ng; gi += blockDim.x) {
     const bool sh = has_sh && gi == 0;
-    const int sg = gi - has_sh;
+    // routed groups in source order src_rot, src_rot + 1, ...: when every owner starts
+    // from a different source, the down GEMMs' stores of d rows into the sources' memory
+    // spread over all links instead of all owners writing to one source at a time
+    const int k = sh ? 0 : gi - has_sh;
+    const int src = (k / a.E_local + a.src_rot) % a.world;
+    const int sg = src * a.E_local + k % a.E_local;
     TileGroup G;
     G.expert = sh ? -1 : sg % a.E_local;
     G.row_begin = sh ? 0 : rbeg[sg];
