@@ -1,0 +1,32 @@
+"""An MoE layer loaded from an MLX-format checkpoint runs on the device exactly as the
+same arrays uploaded directly (fm_moe_block, both expert paths)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from flashmlx_b200 import checkpoint as CK
+from flashmlx_b200 import synthetic as S
+from tests.test_checkpoint import SHAPE, _write_model
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("path", [1, 2])  # FM_PATH_GEMV, FM_PATH_TCGEN05
+def test_checkpoint_layer_on_device(tmp_path, path):
+    from flashmlx_b200 import ops
+    layer = S.make_layer(SHAPE, 11)
+    _write_model(str(tmp_path), layer)
+    ck = CK.Checkpoint(str(tmp_path))
+    shape = ck.config.shape(48)
+    x = ops.bf16_from_numpy(S.make_x(shape, 11), "cuda")
+    h = ops.default_handle(torch.cuda.current_device())
+    h.set_path(path)
+    try:
+        ya = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(layer, "cuda"))(x)
+        yb = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(ck.moe_layer(0), "cuda"))(x)
+        torch.cuda.synchronize()
+    finally:
+        h.set_path(0)
+    np.testing.assert_array_equal(ops.bf16_to_numpy(ya), ops.bf16_to_numpy(yb))
