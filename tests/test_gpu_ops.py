@@ -53,6 +53,7 @@ def test_kat_quantized_matmul(ops, path):
 @pytest.mark.parametrize("M,K,N,gs", [
     (1, 2048, 1408, 64), (7, 2048, 1408, 64), (32, 1408, 2048, 64), (33, 2048, 5632, 64),
     (300, 2048, 1408, 64), (513, 1408, 2048, 64), (64, 2048, 256, 32), (100, 2048, 384, 128),
+    (100, 1408, 256, 128),  # 11 quant groups per row: the odd-count scale staging
 ])
 def test_quantized_matmul_parity(ops, path, M, K, N, gs):
     rng = np.random.default_rng(M + K + N + gs)
