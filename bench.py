@@ -11,8 +11,9 @@ workload: BASELINE configs[1], the Qwen1.5-MoE-A2.7B-shaped layer on a 4096-toke
 prefill batch (synthetic seeded inputs and weights, MLX packed 4-bit layout).
 
 value  = tokens of all ranks / max-over-ranks device time per step (inputs resident)
-e2e    = the same through the public API with the step's x copied from pinned host
-         memory and y read back to pinned host memory inside the timed region
+e2e    = the same through the public API with each step's x copied from pinned host
+         memory and its y read back to pinned host memory inside the timed region (copies
+         on their own streams, overlapping the neighbouring steps' compute)
 N > 1  = expert parallelism (flashmlx_b200.ep): each rank holds the router, the shared
          expert and 1/N of the routed experts and routes its own batch of the workload's
          tokens (weak scaling).  Rows move over NVLink peer memory, written by the
@@ -301,18 +302,44 @@ def run_ours(args, rank, world, local_rank):
     prof = {k: v for k, v in prof_all.items() if "." not in k}
     phases = {k: v[1] / max(1, v[0]) for k, v in prof_all.items() if "." in k}
 
-    # end-to-end through the public API: pinned host x -> device -> block -> pinned host y
+    # end-to-end through the public API: every step copies its tokens from pinned host
+    # memory, runs the layer and reads its result back into pinned host memory.  As in a
+    # serving loop, the copies run on their own streams (one per direction) and overlap the
+    # neighbouring steps' compute; the device buffers are double-buffered and events order
+    # every reuse (a buffer is refilled only after the step that read it, and a result
+    # buffer is rewritten only after its read-back).
     x_pin = torch.from_numpy(x_np.view(np.int16)).view(torch.bfloat16).pin_memory()
     y_pin = torch.empty_like(x_pin).pin_memory()
-    x_e2e = torch.empty_like(x)
+    xs = [torch.empty_like(x) for _ in range(2)]
+    ys = [torch.empty_like(y) for _ in range(2)]
+    h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]    # input b landed
+    ev_done = [torch.cuda.Event() for _ in range(2)]  # the step that used buffers b finished
+    ev_out = [torch.cuda.Event() for _ in range(2)]   # result b read back
+    for b in range(2):
+        ev_done[b].record(stream)
+        ev_out[b].record(stream)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0.record(stream)
-    for _ in range(args.steps):
-        x_e2e.copy_(x_pin, non_blocking=True)
-        step(x_e2e, y)
-        y_pin.copy_(y, non_blocking=True)
+    h2d.wait_stream(stream)
+    d2h.wait_stream(stream)
+    for i in range(args.steps):
+        b = i & 1
+        h2d.wait_event(ev_done[b])
+        with torch.cuda.stream(h2d):
+            xs[b].copy_(x_pin, non_blocking=True)
+        ev_in[b].record(h2d)
+        stream.wait_event(ev_in[b])
+        stream.wait_event(ev_out[b])
+        step(xs[b], ys[b])
+        ev_done[b].record(stream)
+        d2h.wait_event(ev_done[b])
+        with torch.cuda.stream(d2h):
+            y_pin.copy_(ys[b], non_blocking=True)
+        ev_out[b].record(d2h)
+    stream.wait_stream(d2h)  # the last read-back is inside the timed region
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
