@@ -33,11 +33,17 @@
 //               shared memory by the code loader), eight 16-byte stores into the
 //               128B-swizzled K-major A stage; one arrival per warp on the leader's
 //               stage barrier.
-//   warp 8      code loader (one lane issues the TMA of each super-step).
+//   warp 8      code loader (an elected lane issues the TMA of each super-step; all
+//               lanes copy the scales).
 //   warps 9-10  activation loaders (this CTA's half of the tile's rows).
-//   warp 11     TMEM allocation (both CTAs) and, in the leader CTA only, the single
-//               tcgen05.mma issuer (M=256, N<=256, K=16 x 4 per stage); commits free
-//               the stage / publish the accumulator in both CTAs.
+//   warp 11     TMEM allocation (both CTAs) and, in the leader CTA only, the
+//               tcgen05.mma issuer (M=256, N<=256, K=16 x 4 per stage): the whole warp
+//               walks the k-steps with warp-uniform operands, one elected lane issues;
+//               commits free the stage / publish the accumulator in both CTAs.
+// Single-thread tcgen05 / TMA instructions are issued from a converged warp through
+// elect.sync with operands the warp computed uniformly (warp index and values read
+// from memory broadcast from lane 0): a thread computing them on its own paid ~90
+// cycles of issue per MMA, more than an N = 128 MMA takes to execute.
 //   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
 //               buffered accumulators (2 x 256 columns) overlap the next mainloop.
 // Cross-CTA signalling: mbarrier arrivals on the peer's barriers through mapa
