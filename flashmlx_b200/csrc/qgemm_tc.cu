@@ -67,14 +67,12 @@ constexpr int B_BYTES = BNH * 128;
 constexpr int C_BYTES = BM * 128;  // 128 rows x 32 words
 constexpr int SC_GROUPS = 8;                     // max quant groups per row per super-step (gs 32)
 constexpr int SC_BYTES = 2 * BM * SC_GROUPS * 2; // scales + biases of one code slot
-constexpr int XCHG_BYTES = 2 * 2 * 16 * 64 * 2;  // gate/up halves, double-buffered
 constexpr int STG_BYTES = 32 * 256;              // 32 rows x 128 bf16 outputs
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
 constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
 constexpr int OFF_SC = OFF_C + NC * C_BYTES;
-constexpr int OFF_XCHG = OFF_SC + NC * SC_BYTES;
-constexpr int OFF_STG = OFF_XCHG + XCHG_BYTES;   // two staging tiles
+constexpr int OFF_STG = OFF_SC + NC * SC_BYTES;  // two staging tiles
 constexpr int OFF_TB = OFF_STG + 2 * STG_BYTES;  // tile_begin of every group
 constexpr int OFF_BAR = OFF_TB + ((kMaxGroups * 4 + 255) / 256) * 256;
 constexpr int BAR_BYTES = 256;
@@ -348,7 +346,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (warp < NA / 32) {
     // ------------------------------------------------------------ dequant producers
     const int grp = warp / 4;              // takes the k-steps with (k-step % DQ_GROUPS) == grp
-    const int t = (warp % 4) * 32 + lane;  // A row
+    const int t = (warp % 4) * 32 + lane;  // code / scale row in the slot
+    // A row (= TMEM lane) it dequantizes into: in gate/up mode code rows 0..63 are gate
+    // rows f and 64..127 the up rows f of the same outputs, and A interleaves them in
+    // blocks of 8 (gate f -> 16 (f / 8) + f % 8, up f -> the same + 8), so an epilogue
+    // warp holds both halves of its SwiGLUs in lanes L and L ^ 8, and the 8 lanes of a
+    // 16-byte store phase still cover all 8 chunk positions of the 128-byte swizzle
+    const int a_row = (MODE == MODE_GATEUP) ? 16 * ((t & 63) >> 3) + 8 * (t >> 6) + (t & 7) : t;
     const int gs_shift = __ffs(a.gs) - 1;  // group sizes are powers of two (32, 64, 128)
     int cs = 0, it0 = 0;                   // super-step, k-steps before it
     bool ok = true;
@@ -399,7 +403,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         if (valid) {
           uint8_t* As = smem + OFF_A + stage * A_BYTES;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(As + sw128_off(t, j)) = o[j];
+          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(As + sw128_off(a_row, j)) = o[j];
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
         __syncwarp();
@@ -658,7 +662,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int q = warp - EPI_WARP;
     const int row_in = q * 32 + lane;    // TMEM lane == A row of this CTA
     const int et = tid - EPI_WARP * 32;  // 0..127
-    uint16_t* xchg = reinterpret_cast<uint16_t*>(smem + OFF_XCHG);
     int lt = 0, xit = 0;
     for (int tile = pair; tile < ntiles; tile += npairs, ++lt) {
       const TileInfo ti = dir.get(tile);
@@ -681,46 +684,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const int c_lim = ti.nrows - j * 32;  // valid columns of this chunk (may exceed 32)
         const int prow = ti.row0 + j * 32;
         if (MODE == MODE_GATEUP) {
-          // gate warps (q 0,1) finish columns 0..15, up warps (q 2,3) columns 16..31;
-          // each hands the partner the other half of its rows through shared memory,
-          // as bf16 pairs of adjacent columns: xchg word [column pair][row]
-          uint32_t* to_up = reinterpret_cast<uint32_t*>(xchg) + (xit & 1) * (2 * 8 * 64);  // gate, cols 16..31
-          uint32_t* to_gate = to_up + 8 * 64;                                                // up, cols 0..15
-          const int r64 = row_in & 63;
-          if (q < 2) {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) to_up[c * 64 + r64] = pack_bf16x2(v[16 + 2 * c], v[17 + 2 * c]);
-          } else {
-#pragma unroll
-            for (int c = 0; c < 8; ++c) to_gate[c * 64 + r64] = pack_bf16x2(v[2 * c], v[2 * c + 1]);
-          }
-          named_bar_sync(1, 128);
-          const int c0 = (q < 2) ? 0 : 16;
+          // TMEM lane L of warp q holds gate row f and lane L ^ 8 up row f (the dequant
+          // warps interleave them in blocks of 8): the gate lane finishes columns 0..15,
+          // the up lane 16..31, trading the other half as bf16 pairs of adjacent columns
+          const bool is_up = lane & 8;
+          const int f = q * 16 + 8 * (lane >> 4) + (lane & 7);  // output row of this CTA's 64
+          const int c0 = is_up ? 16 : 0;
           // silu(g) * u per MLX op, two columns at a time: sg = bf16(sigmoid(g)) from
           // fp32, then h = bf16(g * sg) and bf16(h * u) as bf16x2 products (each
           // rounded once, as the per-op rounding of swiglu1)
           uint32_t res2[8];
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
-            uint32_t g2, u2;
-            if (q < 2) {
-              g2 = pack_bf16x2(v[2 * c], v[2 * c + 1]);
-              u2 = to_gate[c * 64 + r64];
-            } else {
-              g2 = to_up[c * 64 + r64];
-              u2 = pack_bf16x2(v[16 + 2 * c], v[17 + 2 * c]);
-            }
+            const uint32_t lo2 = pack_bf16x2(v[2 * c], v[2 * c + 1]);         // my row, columns 2c, 2c+1
+            const uint32_t hi2 = pack_bf16x2(v[16 + 2 * c], v[17 + 2 * c]);   // my row, columns 16+2c, 17+2c
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, is_up ? lo2 : hi2, 8);
+            const uint32_t g2 = is_up ? got : lo2;
+            const uint32_t u2 = is_up ? hi2 : got;
             const float ga = __uint_as_float(g2 << 16), gb = __uint_as_float(g2 & 0xffff0000u);
             const uint32_t s2 = pack_bf16x2(__fdividef(1.0f, 1.0f + __expf(-ga)), __fdividef(1.0f, 1.0f + __expf(-gb)));
             res2[c] = bmul2(bmul2(g2, s2), u2);
           }
           // staging row = token column (c0 + c), 64 outputs at their pair-permuted
-          // slots; lanes r64 and r64 ^ 4 share one 32-bit word
-          const int pn = perm8(r64);
+          // slots; outputs f and f ^ 4 (lanes L and L ^ 4) share one 32-bit word
+          const int pn = perm8(f);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const uint32_t other = __shfl_xor_sync(0xffffffffu, res2[c], 4);
-            if ((lane & 4) == 0) {
+            if ((f & 4) == 0) {
               *reinterpret_cast<uint32_t*>(stg + (c0 + 2 * c) * 256 + pn * 2) = __byte_perm(res2[c], other, 0x5410);
               *reinterpret_cast<uint32_t*>(stg + (c0 + 2 * c + 1) * 256 + pn * 2) = __byte_perm(res2[c], other, 0x7632);
             }
