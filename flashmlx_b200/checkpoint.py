@@ -20,8 +20,8 @@ Checkpoints written by mlx-lm keep the experts pre-stacked as
 layers.N.mlp.switch_mlp.{gate,up,down}_proj.*; those are taken as they are.
 
 The result of moe_layer() has the layout of synthetic.make_layer (bf16 as uint16 bits,
-packed codes as uint32), so ops.MoEWeightsT.from_numpy(layer, device) uploads it.  Tensors
-are memory-mapped, not read, until a layer is stacked.  A quantized router or shared-expert
+packed codes as uint32; arrays the layer owns), so ops.MoEWeightsT.from_numpy(layer,
+device) uploads it.  Tensors are memory-mapped, not read, until a layer is stacked.  A quantized router or shared-expert
 gate (gate.scales / shared_expert_gate.scales present) raises NotImplementedError, as the
 C ABI returns FM_EUNSUPPORTED for it.
 """
@@ -181,9 +181,10 @@ class Checkpoint:
         return [i for i in range(self.config.num_layers) if self.has(f"layers.{i}.mlp.gate.weight")]
 
     def _qmatrix(self, prefix: str) -> tuple[np.ndarray, np.ndarray, np.ndarray | None]:
-        w = np.ascontiguousarray(self.get(prefix + ".weight", "U32"))
-        s = np.ascontiguousarray(self.get(prefix + ".scales", "BF16"))
-        b = np.ascontiguousarray(self.get(prefix + ".biases", "BF16")) if self.has(prefix + ".biases") else None
+        # copies: a stacked layer owns its arrays (the mapped file stays read-only)
+        w = np.array(self.get(prefix + ".weight", "U32"))
+        s = np.array(self.get(prefix + ".scales", "BF16"))
+        b = np.array(self.get(prefix + ".biases", "BF16")) if self.has(prefix + ".biases") else None
         return w, s, b
 
     def _stacked(self, mlp: str, proj: str) -> tuple[np.ndarray, np.ndarray, np.ndarray | None]:
@@ -209,7 +210,7 @@ class Checkpoint:
             raise NotImplementedError(f"{mlp}.gate is quantized: a quantized router is not implemented")
         if c.bits != 4:
             raise NotImplementedError(f"quantization bits = {c.bits}: only 4-bit affine weights are implemented")
-        d = {"router_w": np.ascontiguousarray(self.get(mlp + ".gate.weight", "BF16"))}
+        d = {"router_w": np.array(self.get(mlp + ".gate.weight", "BF16"))}
         for proj, key in (("gate_proj", "gate"), ("up_proj", "up"), ("down_proj", "down")):
             d[key] = self._stacked(mlp, proj)
         if self.has(mlp + ".shared_expert.gate_proj.weight"):
@@ -217,8 +218,7 @@ class Checkpoint:
                 d[key] = self._qmatrix(f"{mlp}.shared_expert.{proj}")
             if self.has(mlp + ".shared_expert_gate.scales"):
                 raise NotImplementedError(f"{mlp}.shared_expert_gate is quantized: not implemented")
-            d["shared_expert_gate_w"] = np.ascontiguousarray(
-                self.get(mlp + ".shared_expert_gate.weight", "BF16")).reshape(1, -1)
+            d["shared_expert_gate_w"] = np.array(self.get(mlp + ".shared_expert_gate.weight", "BF16")).reshape(1, -1)
         self._check(i, d)
         return d
 

@@ -171,3 +171,15 @@ def test_loaded_layer_through_the_oracle(tmp_path):
     ya = O.Layer(SHAPE, layer).moe_block(x)[0]
     yb = O.Layer(SHAPE, loaded).moe_block(x)[0]
     np.testing.assert_array_equal(ya, yb)
+
+
+def test_moe_model_layer_discovery(tmp_path):
+    """MoEModel finds the layers with a router and rejects the others (no device work)."""
+    from flashmlx_b200.model import MoEModel
+    layer = S.make_layer(SHAPE, 7)
+    _write_model(str(tmp_path), layer)
+    m = MoEModel(str(tmp_path), device="cpu")
+    assert m.is_moe(0) and not m.is_moe(1)
+    assert m.shape.hidden == SHAPE.hidden and m.shape.num_experts == SHAPE.num_experts
+    with pytest.raises(KeyError):
+        MoEModel(str(tmp_path), device="cpu", layers=[1])

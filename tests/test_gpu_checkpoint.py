@@ -30,3 +30,19 @@ def test_checkpoint_layer_on_device(tmp_path, path):
     finally:
         h.set_path(0)
     np.testing.assert_array_equal(ops.bf16_to_numpy(ya), ops.bf16_to_numpy(yb))
+
+
+def test_moe_model_forward(tmp_path):
+    """MoEModel.moe_block(x, layer) over a [B, L, H] batch equals fm_moe_block on the same
+    layer's arrays uploaded directly."""
+    from flashmlx_b200 import ops
+    from flashmlx_b200.model import MoEModel
+    layer = S.make_layer(SHAPE, 12)
+    _write_model(str(tmp_path), layer)
+    m = MoEModel(str(tmp_path), device="cuda", max_tokens=64)
+    x = ops.bf16_from_numpy(S.make_x(SHAPE.with_tokens(48), 12), "cuda")
+    y = m.moe_block(x.view(2, 24, SHAPE.hidden), 0)
+    assert y.shape == (2, 24, SHAPE.hidden)
+    ref = ops.MoEBlock(SHAPE, ops.MoEWeightsT.from_numpy(layer, "cuda"))(x)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(ops.bf16_to_numpy(y.reshape(48, -1)), ops.bf16_to_numpy(ref))
