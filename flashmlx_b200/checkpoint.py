@@ -21,9 +21,9 @@ layers.N.mlp.switch_mlp.{gate,up,down}_proj.*; those are taken as they are.
 
 The result of moe_layer() has the layout of synthetic.make_layer (bf16 as uint16 bits,
 packed codes as uint32; arrays the layer owns), so ops.MoEWeightsT.from_numpy(layer,
-device) uploads it.  Tensors are memory-mapped, not read, until a layer is stacked.  A quantized router or shared-expert
-gate (gate.scales / shared_expert_gate.scales present) raises NotImplementedError, as the
-C ABI returns FM_EUNSUPPORTED for it.
+device) uploads it.  Tensors are memory-mapped, not read, until a layer is stacked.  A
+quantized router or shared-expert gate (gate.scales / shared_expert_gate.scales present)
+raises NotImplementedError, as the C ABI returns FM_EUNSUPPORTED for it.
 """
 from __future__ import annotations
 
