@@ -115,6 +115,24 @@ def make_layer(shape: MoEShape, seed: int) -> dict:
     return d
 
 
+def make_sigmoid_layer(shape: MoEShape, seed: int, correction_bias: bool = True) -> dict:
+    """One layer of the sigmoid-routed variant (Nemotron-H / DeepSeek style): router
+    [E, H] bf16, e_score_correction_bias [E] fp32, ungated experts fc1 [E, I, H] and
+    fc2 [E, H, I], ungated shared expert up [Is, H] / down [H, Is] (when shared_inter)."""
+    H, I, E = shape.hidden, shape.inter, shape.num_experts
+    gs, bits = shape.group_size, shape.bits
+    d = {"router_w": f32_to_bf16(_rng(seed, "router").standard_normal((E, H), dtype=np.float32) * 0.05)}
+    if correction_bias:
+        d["correction_bias"] = (_rng(seed, "correction").standard_normal(E) * 0.05).astype(np.float32)
+    d["fc1"] = make_qmatrix(seed, "fc1", (E,), I, H, gs, bits)
+    d["fc2"] = make_qmatrix(seed, "fc2", (E,), H, I, gs, bits)
+    if shape.shared_inter:
+        Is = shape.shared_inter
+        d["shared_up"] = make_qmatrix(seed, "shared_up", (), Is, H, gs, bits)
+        d["shared_down"] = make_qmatrix(seed, "shared_down", (), H, Is, gs, bits)
+    return d
+
+
 def layer_weight_bytes(shape: MoEShape) -> dict:
     """Bytes of one expert / the shared expert / the router in the packed layout."""
     H, I = shape.hidden, shape.inter

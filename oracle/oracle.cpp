@@ -182,7 +182,7 @@ struct orc_moe_weights {
   const uint16_t* router_bias;  // [E] bf16 additive logit bias (benchmark load skew), nullable
 };
 
-int orc_version() { return 1; }
+int orc_version() { return 2; }
 
 // 0: exact dequantization (default); 1: dequantized weights rounded to bf16.
 int orc_set_weight_rounding(int mode) {
@@ -472,6 +472,165 @@ int orc_moe_block(const orc_moe_config* cfg, const orc_moe_weights* wt, const ui
       float gv = rbf(sigmoidf(gl[t]));
       for (int h = 0; h < H; ++h) yr[t * H + h] = rbf(yr[t * H + h] + rbf(gv * sh[t * H + h]));
     }
+  }
+  for (int64_t i = 0; i < T * H; ++i) y[i] = f2bf(yr[i]);
+  return 0;
+}
+
+
+// ------------------------------------------------------------------ sigmoid-routed variant
+// The Nemotron-H / DeepSeek-style MoE block (server/src/nemotron_h.cpp:1010-1100):
+//   logits  = bf16(x @ Wr^T)                                   (1018)
+//   orig    = sigmoid(fp32(logits)); sel = orig + correction    (1025-1029)
+//   n_group > 1: group score = sum of the group's top-2 sel; the n_group - topk_group
+//            lowest groups get sel = 0                           (1030-1041)
+//   top-k of sel (ties -> lower id), scores = orig of the picks  (1043-1045)
+//   norm_topk_prob and k > 1: s / (sum s + 1e-20)               (1046-1049)
+//   s *= routed_scaling_factor                                  (1050)
+//   experts: h = fc2(relu2(fc1(x))), relu2 = bf16(max(x,0)^2)   (1053-1091, 53-58)
+//   y = bf16( sum_k fp32(h_k) * s_k )                           (1094-1095)
+//   shared (ungated): y = bf16(y + down(relu2(up(x))))          (1098-1106)
+// MLX leaves argpartition's order and the score sums' order unspecified; here the picks
+// are in selection order (highest sel first) and sums run in that order; equal group
+// scores zero the higher group id first.
+struct orc_sig_config {
+  int hidden, inter, num_experts, top_k, group_size, bits;
+  int norm_topk_prob;
+  int shared_inter;  // ungated shared expert (up -> relu2 -> down), 0 = none
+  int n_group, topk_group;
+  float routed_scaling_factor;
+};
+
+struct orc_sig_weights {
+  const uint16_t* router_w;      // [E, H] bf16
+  const float* correction_bias;  // [E] fp32, nullable
+  orc_qweight fc1, fc2;          // [E, I, H], [E, H, I]
+  orc_qweight shared_up, shared_down;
+};
+
+int orc_route_sigmoid(const uint16_t* x, int64_t T, int H, const uint16_t* router_w, const float* correction_bias,
+                      int E, int k, int n_group, int topk_group, int norm_topk, float scale, int32_t* ids,
+                      float* scores, int nthreads) {
+  if (T < 0 || E <= 0 || k <= 0 || k > E || n_group <= 0 || E % n_group || topk_group <= 0 ||
+      topk_group > n_group)
+    return 1;
+  const int gsz = E / n_group;
+  if (n_group > 1 && gsz < 2) return 1;
+  std::vector<float> wf(static_cast<size_t>(E) * H);
+  to_float(router_w, static_cast<int64_t>(E) * H, wf.data());
+  parallel_for(T, nthreads, [&](int64_t lo, int64_t hi) {
+    std::vector<float> xf(H), orig(E), sel(E), gscore(n_group);
+    std::vector<int> order(E), gorder(n_group);
+    for (int64_t t = lo; t < hi; ++t) {
+      to_float(x + t * H, H, xf.data());
+      for (int e = 0; e < E; ++e) {
+        const float l = rbf(dot(xf.data(), wf.data() + static_cast<int64_t>(e) * H, H));
+        orig[e] = 1.0f / (1.0f + std::exp(-l));
+        sel[e] = correction_bias ? orig[e] + correction_bias[e] : orig[e];
+      }
+      if (n_group > 1) {
+        for (int gi = 0; gi < n_group; ++gi) {
+          float m1 = -INFINITY, m2 = -INFINITY;
+          for (int e = gi * gsz; e < (gi + 1) * gsz; ++e) {
+            if (sel[e] > m1) {
+              m2 = m1;
+              m1 = sel[e];
+            } else if (sel[e] > m2) {
+              m2 = sel[e];
+            }
+          }
+          gscore[gi] = m1 + m2;
+        }
+        std::iota(gorder.begin(), gorder.end(), 0);
+        // lowest scores first; among equal ones the higher group id first
+        std::sort(gorder.begin(), gorder.end(), [&](int a, int b) {
+          return gscore[a] != gscore[b] ? gscore[a] < gscore[b] : a > b;
+        });
+        for (int z = 0; z < n_group - topk_group; ++z)
+          for (int e = gorder[z] * gsz; e < (gorder[z] + 1) * gsz; ++e) sel[e] = 0.0f;
+      }
+      std::iota(order.begin(), order.end(), 0);
+      std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return sel[a] > sel[b]; });
+      float denom = 1.0f;
+      if (norm_topk && k > 1) {
+        float s = 0.0f;
+        for (int j = 0; j < k; ++j) s += orig[order[j]];
+        denom = s + 1e-20f;
+      }
+      for (int j = 0; j < k; ++j) {
+        ids[t * k + j] = order[j];
+        const float sc = (norm_topk && k > 1) ? orig[order[j]] / denom : orig[order[j]];
+        scores[t * k + j] = sc * scale;
+      }
+    }
+  });
+  return 0;
+}
+
+int orc_moe_block_sigmoid(const orc_sig_config* cfg, const orc_sig_weights* wt, const uint16_t* x, int64_t T,
+                          const int32_t* forced_ids, const float* forced_scores, uint16_t* y, int32_t* ids_out,
+                          float* scores_out, int nthreads) {
+  const int H = cfg->hidden, I = cfg->inter, E = cfg->num_experts, k = cfg->top_k;
+  const int gs = cfg->group_size, bits = cfg->bits;
+  if (!valid_quant(H, gs, bits) || !valid_quant(I, gs, bits) || k <= 0 || k > E || T < 0) return 1;
+  const int64_t P = T * k;
+  std::vector<int32_t> ids(P);
+  std::vector<float> scores(P);
+  if (forced_ids) {
+    std::memcpy(ids.data(), forced_ids, P * sizeof(int32_t));
+    std::memcpy(scores.data(), forced_scores, P * sizeof(float));
+  } else {
+    int rc = orc_route_sigmoid(x, T, H, wt->router_w, wt->correction_bias, E, k, cfg->n_group, cfg->topk_group,
+                               cfg->norm_topk_prob, cfg->routed_scaling_factor, ids.data(), scores.data(), nthreads);
+    if (rc) return rc;
+  }
+  for (int64_t i = 0; i < P; ++i)
+    if (ids[i] < 0 || ids[i] >= E) return 1;
+  if (ids_out) std::memcpy(ids_out, ids.data(), P * sizeof(int32_t));
+  if (scores_out) std::memcpy(scores_out, scores.data(), P * sizeof(float));
+  QMat m1{wt->fc1.w, wt->fc1.s, wt->fc1.b, I, H, gs, bits};
+  QMat m2{wt->fc2.w, wt->fc2.s, wt->fc2.b, H, I, gs, bits};
+  std::vector<float> xf(static_cast<size_t>(T) * H);
+  to_float(x, T * H, xf.data());
+  // per (token, slot) pair: h = fc2(relu2(fc1(x))); every pair's arithmetic is the same in
+  // the sorted and unsorted gather_qmm paths
+  std::vector<float> d_pair(static_cast<size_t>(P) * H);
+  parallel_for(P, nthreads, [&](int64_t lo, int64_t hi) {
+    std::vector<float> u(I);
+    for (int64_t i = lo; i < hi; ++i) {
+      const float* xr = xf.data() + (i / k) * H;
+      grouped_rows(m1, ids[i], xr, 1, u.data(), 0, I);
+      for (int n = 0; n < I; ++n) {
+        const float r = std::max(u[n], 0.0f);
+        u[n] = rbf(r * r);
+      }
+      grouped_rows(m2, ids[i], u.data(), 1, &d_pair[static_cast<size_t>(i) * H], 0, H);
+    }
+  });
+  std::vector<float> yr(static_cast<size_t>(T) * H);
+  for (int64_t t = 0; t < T; ++t)
+    for (int h = 0; h < H; ++h) {
+      float acc = 0.0f;
+      for (int j = 0; j < k; ++j) acc += d_pair[static_cast<size_t>(t * k + j) * H + h] * scores[t * k + j];
+      yr[t * H + h] = rbf(acc);
+    }
+  if (cfg->shared_inter > 0) {
+    const int Is = cfg->shared_inter;
+    if (!valid_quant(Is, gs, bits)) return 1;
+    QMat su{wt->shared_up.w, wt->shared_up.s, wt->shared_up.b, Is, H, gs, bits};
+    QMat sd{wt->shared_down.w, wt->shared_down.s, wt->shared_down.b, H, Is, gs, bits};
+    parallel_for(T, nthreads, [&](int64_t lo, int64_t hi) {
+      std::vector<float> u(Is), sh(H);
+      for (int64_t t = lo; t < hi; ++t) {
+        grouped_rows(su, 0, xf.data() + t * H, 1, u.data(), 0, Is);
+        for (int n = 0; n < Is; ++n) {
+          const float r = std::max(u[n], 0.0f);
+          u[n] = rbf(r * r);
+        }
+        grouped_rows(sd, 0, u.data(), 1, sh.data(), 0, H);
+        for (int h = 0; h < H; ++h) yr[t * H + h] = rbf(yr[t * H + h] + sh[h]);
+      }
+    });
   }
   for (int64_t i = 0; i < T * H; ++i) y[i] = f2bf(yr[i]);
   return 0;

@@ -46,11 +46,21 @@ class MoEWeights(C.Structure):
     ]
 
 
+class SigConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in (
+        "hidden", "inter", "num_experts", "top_k", "group_size", "bits", "norm_topk_prob", "shared_inter",
+        "n_group", "topk_group")] + [("routed_scaling_factor", C.c_float)]
+
+
+class SigWeights(C.Structure):
+    _fields_ = [("router_w", C.c_void_p), ("correction_bias", C.c_void_p), ("fc1", QWeight), ("fc2", QWeight),
+                ("shared_up", QWeight), ("shared_down", QWeight)]
+
+
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(_LIB_PATH):
-            build()
+        build()  # (re)builds when the library is missing or older than oracle.cpp
         L = C.CDLL(_LIB_PATH)
         p, i, i64 = C.c_void_p, C.c_int, C.c_int64
         L.orc_quantized_matmul.argtypes = [p, i64, i, p, p, p, i, i, i, p, i]
@@ -59,8 +69,13 @@ def lib():
         L.orc_sort_pairs.argtypes = [p, i64, i, i, p, p, p]
         L.orc_moe_block.argtypes = [C.POINTER(MoEConfig), C.POINTER(MoEWeights), p, i64, p, p, p, p, p, i]
         L.orc_set_weight_rounding.argtypes = [i]
+        L.orc_route_sigmoid.argtypes = [p, i64, i, p, p, i, i, i, i, i, C.c_float, p, p, i]
+        L.orc_moe_block_sigmoid.argtypes = [C.POINTER(SigConfig), C.POINTER(SigWeights), p, i64, p, p, p, p, p, i]
+        L.orc_version.restype = C.c_int
+        if L.orc_version() < 2:
+            raise ImportError("liboracle.so is stale; rebuild it (python -m oracle.oracle or make -C oracle)")
         for f in ("orc_quantized_matmul", "orc_gather_qmm", "orc_route", "orc_sort_pairs", "orc_moe_block",
-                  "orc_set_weight_rounding"):
+                  "orc_set_weight_rounding", "orc_route_sigmoid", "orc_moe_block_sigmoid"):
             getattr(L, f).restype = C.c_int
         _lib = L
     return _lib
@@ -201,4 +216,69 @@ class Layer:
                                  _p(y), _p(ids), _p(sc), nthreads or NTHREADS)
         if rc:
             raise ValueError("orc_moe_block: invalid arguments")
+        return y, ids, sc
+
+
+class SigmoidLayer:
+    """One layer of the sigmoid-routed variant (Nemotron-H / DeepSeek style, see
+    oracle.cpp): `shape` is a synthetic.MoEShape (inter = the experts' fc1 rows,
+    shared_inter = the ungated shared expert's up rows, norm_topk_prob), `routing` a dict
+    with n_group, topk_group, routed_scaling_factor; weights: router_w [E, H] bf16,
+    correction_bias [E] fp32 (optional), fc1 / fc2 / shared_up / shared_down as
+    (w, s, b) tuples."""
+
+    def __init__(self, shape, weights: dict, routing: dict):
+        self.shape = shape
+        self.arrays = []
+        cfg = SigConfig()
+        cfg.hidden, cfg.inter, cfg.num_experts, cfg.top_k = shape.hidden, shape.inter, shape.num_experts, shape.top_k
+        cfg.group_size, cfg.bits = shape.group_size, shape.bits
+        cfg.norm_topk_prob = int(shape.norm_topk_prob)
+        cfg.shared_inter = shape.shared_inter
+        cfg.n_group = int(routing.get("n_group", 1))
+        cfg.topk_group = int(routing.get("topk_group", 1))
+        cfg.routed_scaling_factor = float(routing.get("routed_scaling_factor", 1.0))
+        self.cfg = cfg
+        W = SigWeights()
+        W.router_w = self._keep(weights["router_w"], np.uint16)
+        if weights.get("correction_bias") is not None:
+            W.correction_bias = self._keep(weights["correction_bias"], np.float32)
+        for name in ("fc1", "fc2", "shared_up", "shared_down"):
+            if name in weights:
+                qw, qs, qb = weights[name]
+                setattr(W, name, QWeight(self._keep(qw, np.uint32), self._keep(qs, np.uint16),
+                                         None if qb is None else self._keep(qb, np.uint16)))
+        self.weights = W
+
+    def _keep(self, a, dt):
+        a = np.ascontiguousarray(a, dtype=dt)
+        self.arrays.append(a)
+        return a.ctypes.data
+
+    def route(self, x, nthreads=None):
+        """ids [T, k] in selection order, scores [T, k] fp32."""
+        x = _c(x, np.uint16)
+        T, k = x.shape[0], self.shape.top_k
+        ids = np.empty((T, k), np.int32)
+        sc = np.empty((T, k), np.float32)
+        c, W = self.cfg, self.weights
+        rc = lib().orc_route_sigmoid(_p(x), T, c.hidden, W.router_w, W.correction_bias, c.num_experts, k,
+                                     c.n_group, c.topk_group, c.norm_topk_prob, c.routed_scaling_factor,
+                                     _p(ids), _p(sc), nthreads or NTHREADS)
+        if rc:
+            raise ValueError("orc_route_sigmoid: invalid arguments")
+        return ids, sc
+
+    def moe_block(self, x, forced_ids=None, forced_scores=None, nthreads=None):
+        """y [T, H] bf16 bits, ids [T, k], scores [T, k] fp32."""
+        x = _c(x, np.uint16)
+        T, k = x.shape[0], self.shape.top_k
+        y = np.empty_like(x)
+        ids = np.empty((T, k), np.int32)
+        sc = np.empty((T, k), np.float32)
+        rc = lib().orc_moe_block_sigmoid(C.byref(self.cfg), C.byref(self.weights), _p(x), T,
+                                         _p(_c(forced_ids, np.int32)), _p(_c(forced_scores, np.float32)),
+                                         _p(y), _p(ids), _p(sc), nthreads or NTHREADS)
+        if rc:
+            raise ValueError("orc_moe_block_sigmoid: invalid arguments")
         return y, ids, sc

@@ -67,3 +67,58 @@ def moe_block(layer: dict, shape, x, ids, scores):
         gs = rbf(1.0 / (1.0 + np.exp(-gl.astype(np.float64))))
         y = rbf(rbf(y) + rbf(gs * sh))
     return f32_to_bf16(y.astype(np.float32))
+
+
+def relu2(u):
+    """bf16(max(u, 0)^2) of bf16 bits u (nemotron_h.cpp:53-58)."""
+    r = np.maximum(bf16_to_f32(u), 0.0).astype(np.float32)
+    return f32_to_bf16(r * r)
+
+
+def sigmoid_route(x, router_w, bias, k, n_group=1, topk_group=1, norm=False, scale=1.0):
+    """The sigmoid routing of nemotron_h.cpp:1018-1050 in float64: ids [T, k] (selection
+    order), scores [T, k], and the selection scores [T, E] used to find near-ties."""
+    xf = bf16_to_f32(x).astype(np.float64)
+    logits = rbf((xf @ bf16_to_f32(router_w).astype(np.float64).T).astype(np.float32)).astype(np.float64)
+    orig = 1.0 / (1.0 + np.exp(-logits))
+    sel = orig + (np.asarray(bias, np.float64) if bias is not None else 0.0)
+    T, E = sel.shape
+    if n_group > 1:
+        g = sel.reshape(T, n_group, E // n_group)
+        gscore = np.sort(g, axis=-1)[..., -2:].sum(-1)
+        sel = sel.copy()
+        for t in range(T):
+            low = sorted(range(n_group), key=lambda gi: (gscore[t, gi], -gi))[: n_group - topk_group]
+            for gi in low:
+                sel[t, gi * (E // n_group):(gi + 1) * (E // n_group)] = 0.0
+    ids = np.argsort(-sel, axis=-1, kind="stable")[:, :k]
+    sc = np.take_along_axis(orig, ids, -1)
+    if norm and k > 1:
+        sc = sc / (sc.sum(-1, keepdims=True) + 1e-20)
+    return ids.astype(np.int32), sc * scale, sel
+
+
+def sigmoid_moe_block(layer: dict, shape, x, ids, scores):
+    """fc1 -> relu2 -> fc2 per routed pair, fp32-scaled sum, plus the ungated shared
+    expert (nemotron_h.cpp:1052-1106), for given routing."""
+    T, k, H = x.shape[0], shape.top_k, shape.hidden
+    xf = bf16_to_f32(x).astype(np.float64)
+    y = np.zeros((T, H), np.float64)
+    for t in range(T):
+        for j in range(k):
+            e = int(ids[t, j])
+            W1 = dequant(layer["fc1"][0][e], layer["fc1"][1][e], layer["fc1"][2][e])
+            W2 = dequant(layer["fc2"][0][e], layer["fc2"][1][e], layer["fc2"][2][e])
+            u = f32_to_bf16((xf[t] @ W1.T).astype(np.float32))
+            a = bf16_to_f32(relu2(u)).astype(np.float64)
+            d = rbf((a @ W2.T).astype(np.float32)).astype(np.float64)
+            y[t] += d * float(scores[t, j])
+    y = rbf(y.astype(np.float32))
+    if shape.shared_inter:
+        Wu = dequant(*layer["shared_up"])
+        Wd = dequant(*layer["shared_down"])
+        u = f32_to_bf16((xf @ Wu.T).astype(np.float32))
+        a = bf16_to_f32(relu2(u)).astype(np.float64)
+        sh = rbf((a @ Wd.T).astype(np.float32))
+        y = rbf(y + sh)
+    return f32_to_bf16(np.asarray(y, np.float32))
