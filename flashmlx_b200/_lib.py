@@ -43,6 +43,16 @@ class MoEOutputs(C.Structure):
                 ("expert_offsets", C.c_void_p)]
 
 
+class MoEVariant(C.Structure):
+    _fields_ = [("score_func", C.c_int), ("n_group", C.c_int), ("topk_group", C.c_int),
+                ("routed_scaling_factor", C.c_float), ("expert_act", C.c_int), ("shared_ungated", C.c_int),
+                ("correction_bias", C.c_void_p), ("topk_scores_f32", C.c_void_p)]
+
+
+FM_SCORE_SOFTMAX, FM_SCORE_SIGMOID = 0, 1
+FM_ACT_SWIGLU, FM_ACT_RELU2 = 0, 1
+
+
 class KernelTime(C.Structure):
     _fields_ = [("name", C.c_char_p), ("launches", C.c_int64), ("total_ms", C.c_double)]
 
@@ -64,6 +74,8 @@ SIGNATURES = {
     "fm_moe_block": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p,
                           C.POINTER(MoEOutputs)]),
     "fm_moe_block_noalloc": (_i, [_i, _p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p]),
+    "fm_moe_block_variant": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEVariant), C.POINTER(MoEWeights), _p, _i64,
+                                  _p, C.POINTER(MoEOutputs)]),
     "fm_ep_range": (_i, [_i, _i, _i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "fm_ep_set": (_i, [_p, _i, _i]),
     "fm_ep_dispatch": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, C.POINTER(C.c_int32),

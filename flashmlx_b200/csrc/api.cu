@@ -22,6 +22,7 @@
 
 namespace fm {
 __global__ void route_kernel(const RouteArgs a);
+__global__ void route_kernel_sigmoid(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
 __global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
@@ -53,6 +54,7 @@ struct fm_handle {
   std::string last_error;
   int num_sms = 0;
   int route_blocks_per_sm = 0;
+  int route_sig_blocks_per_sm = 0;  // route_kernel_sigmoid
   int gemv_blocks_per_sm = 0;
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
@@ -228,16 +230,17 @@ bool quant_ok(int K, int gs, int bits) {
   return bits == 4 && (gs == 32 || gs == 64 || gs == 128) && K > 0 && K % gs == 0;
 }
 
-int launch_route(fm_handle* h, RouteArgs& ra, int64_t items) {
-  const int max_blocks = h->route_blocks_per_sm * h->num_sms;
+int launch_route(fm_handle* h, RouteArgs& ra, int64_t items, bool sigmoid = false) {
+  const int max_blocks = (sigmoid ? h->route_sig_blocks_per_sm : h->route_blocks_per_sm) * h->num_sms;
   const int64_t nchunks = (ra.T + fm::kRouteChunk - 1) / fm::kRouteChunk;
   int64_t want = std::max<int64_t>((items + 7) / 8, nchunks);
   want = std::max<int64_t>(want, std::min<int64_t>(ra.E, h->num_sms));
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks)));
   void* args[] = {&ra};
   prof_begin(h, ra.do_router ? "route" : "route_given");
-  cudaError_t e = cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&fm::route_kernel), dim3(grid),
-                                              dim3(fm::kRouteThreads), args, 0, h->stream);
+  const void* fn = sigmoid ? reinterpret_cast<const void*>(&fm::route_kernel_sigmoid)
+                           : reinterpret_cast<const void*>(&fm::route_kernel);
+  cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(fm::kRouteThreads), args, 0, h->stream);
   prof_end(h);
   if (e != cudaSuccess) return cuda_err(h, e, "route_kernel launch");
   return FM_OK;
@@ -286,9 +289,10 @@ bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols) {
 
 template <int MODE>
 int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps* maps = nullptr) {
-  static const char* names[2][3] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain"},
-                                    {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain"}};
+  static const char* names[2][5] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain", "qgemv_relu2", "qgemv_down"},
+                                    {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain", "", ""}};
   if (tcgen05 && !maps) return set_err(h, FM_EINVAL, "tcgen05 launch without tensor maps");
+  if (tcgen05 && MODE > fm::MODE_PLAIN) return set_err(h, FM_EUNSUPPORTED, "variant modes run on the GEMV path");
   prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
   const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->tc_pairs, h->stream, ga, *maps)
                                 : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
@@ -682,6 +686,9 @@ int fm_create(fm_handle** out, int device, void* stream) {
   }
   if (e == cudaSuccess)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_sig_blocks_per_sm, fm::route_kernel_sigmoid,
+                                                      fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&h->gemv_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
   if (e == cudaSuccess) e = fm::tc::max_pairs(&h->tc_pairs);
@@ -972,6 +979,186 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
     const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
     fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
   }
+  prof_end(h);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_err(h, e, "finalize launch");
+  return FM_OK;
+}
+
+// The Nemotron-H / DeepSeek-style block and other variants (fm_moe_variant): the same
+// routing / sort / tile-plan kernel with sigmoid scoring when asked, then the GEMV expert
+// kernels (relu^2 fc1 or SwiGLU gate/up, then down with fp32 or bf16 score products) and
+// the fixed combine with the shared expert gated or not.
+int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_variant* v, const fm_moe_weights* w,
+                         const uint16_t* x, int64_t T, uint16_t* y, const fm_moe_outputs* outs) {
+  if (!h) return FM_EINVAL;
+  if (!v) return fm_moe_block(h, c, w, x, T, y, outs);
+  if (v->score_func != FM_SCORE_SOFTMAX && v->score_func != FM_SCORE_SIGMOID)
+    return set_err(h, FM_EINVAL, "score_func must be FM_SCORE_SOFTMAX or FM_SCORE_SIGMOID");
+  if (v->expert_act != FM_ACT_SWIGLU && v->expert_act != FM_ACT_RELU2)
+    return set_err(h, FM_EINVAL, "expert_act must be FM_ACT_SWIGLU or FM_ACT_RELU2");
+  const bool sig = v->score_func == FM_SCORE_SIGMOID, relu2 = v->expert_act == FM_ACT_RELU2;
+  const bool ungated = v->shared_ungated != 0;
+  if (!sig && !relu2 && !ungated) return fm_moe_block(h, c, w, x, T, y, outs);
+  if (!c || !w) return set_err(h, FM_EINVAL, "null config or weights");
+  const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k, Is = c->shared_inter;
+  if (H <= 0 || I <= 0 || E <= 0 || k <= 0 || k > E || Is < 0) return set_err(h, FM_EINVAL, "bad MoE dimensions");
+  if (E > fm::kMaxExperts || k > 16) return set_err(h, FM_EUNSUPPORTED, "num_experts > 512 or top_k > 16");
+  if (H % 128 || I % 128 || Is % 128)
+    return set_err(h, FM_EUNSUPPORTED, "hidden and intermediate sizes must be multiples of 128");
+  if (!quant_ok(H, c->group_size, c->bits) || !quant_ok(I, c->group_size, c->bits) ||
+      (c->group_size != 64 && c->group_size != 128))
+    return set_err(h, FM_EUNSUPPORTED, "variants run 4-bit affine weights with group size 64 or 128");
+  if (c->router_quantized || (Is > 0 && !ungated && c->shared_gate_quantized))
+    return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");
+  const int n_group = v->n_group > 0 ? v->n_group : 1;
+  if (sig && (n_group > 32 || E % n_group || (n_group > 1 && E / n_group < 2) || v->topk_group < 0 ||
+              v->topk_group > n_group || (n_group > 1 && v->topk_group < 1)))
+    return set_err(h, FM_EINVAL, "n_group must divide E (groups of >= 2, at most 32), 1 <= topk_group <= n_group");
+  if (sig && w && w->router_bias)
+    return set_err(h, FM_EINVAL, "router_bias applies to softmax routing; sigmoid routing takes correction_bias");
+  const fm_qweight& e1 = relu2 ? w->up : w->gate;
+  if (!w->router_w || !e1.w || !e1.scales || !w->down.w || !w->down.scales || (!relu2 && (!w->up.w || !w->up.scales)))
+    return set_err(h, FM_EINVAL, "expert weights missing");
+  if (Is > 0) {
+    if (!w->shared_up.w || !w->shared_up.scales || !w->shared_down.w || !w->shared_down.scales ||
+        (!relu2 && (!w->shared_gate.w || !w->shared_gate.scales)) || (!ungated && !w->shared_expert_gate_w))
+      return set_err(h, FM_EINVAL, "shared expert weights missing");
+  }
+  if (T < 0 || (T > 0 && (!x || !y))) return set_err(h, FM_EINVAL, "bad x / y / T");
+  if (!aligned16(x) || !aligned16(y)) return set_err(h, FM_EINVAL, "x and y must be 16-byte aligned");
+  if (T == 0) return FM_OK;
+  if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
+  const bool shared = Is > 0;
+  const int epad = (E + 1 + 7) / 8 * 8;
+  const int ksplit = router_ksplit(h, T, H);
+  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, Is, shared, true, false);
+  int rc = ensure_ws(h, p.total);
+  if (rc) return rc;
+
+  RouteArgs ra;
+  std::memset(&ra, 0, sizeof(ra));
+  ra.x = x;
+  ra.router_w = static_cast<const uint16_t*>(w->router_w);
+  ra.shared_gate_w = (shared && !ungated) ? static_cast<const uint16_t*>(w->shared_expert_gate_w) : nullptr;
+  ra.router_bias = w->router_bias;
+  ra.T = T;
+  ra.H = H;
+  ra.E = E;
+  ra.k = k;
+  ra.norm_topk = c->norm_topk_prob;
+  ra.do_router = 1;
+  ra.ksplit = ksplit;
+  ra.epad = epad;
+  ra.partial = at<float>(h, p.partial);
+  ra.x_perm = at<uint16_t>(h, p.x_perm);
+  ra.x_rows = T;
+  ra.zero0 = at<float>(h, p.y_acc);
+  ra.zero0_n = T * H;
+  ra.zero1 = shared ? at<float>(h, p.ysh) : nullptr;
+  ra.zero1_n = shared ? T * H : 0;
+  ra.topk_ids = at<int32_t>(h, p.topk_ids);
+  ra.topk_score = at<float>(h, p.topk_score);
+  ra.gate_sig = at<float>(h, p.gate_sig);
+  ra.row_src = at<int32_t>(h, p.row_src);
+  ra.chunk_counts = at<int32_t>(h, p.chunk_counts);
+  ra.pair_rank = at<int32_t>(h, p.pair_rank);
+  ra.totals = at<int32_t>(h, p.totals);
+  ra.offsets = at<int32_t>(h, p.offsets);
+  ra.sorted_token = at<int32_t>(h, p.sorted_token);
+  ra.sorted_score = at<float>(h, p.sorted_score);
+  ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
+  ra.tab_a = at<TileTable>(h, p.tab_a);
+  ra.tab_b = at<TileTable>(h, p.tab_b);
+  ra.a_rows_per_block = relu2 ? 128 : 64;  // relu^2: one matrix, 4 warps x 32 rows
+  ra.a_n = I;
+  ra.a_n_shared = Is;
+  ra.b_n = H;
+  ra.b_rows_per_block = 128;
+  ra.chunk_max = 8;
+  ra.chunk_align = 8;
+  ra.b_ksplit_shared = std::max(1, Is / std::max(1, I));
+  ra.has_shared = shared ? 1 : 0;
+  if (outs) {
+    ra.out_topk_ids = outs->topk_ids;
+    ra.out_topk_scores = outs->topk_scores;
+    ra.out_sorted_token = outs->sorted_token;
+    ra.out_offsets = outs->expert_offsets;
+  }
+  ra.n_group = n_group;
+  ra.topk_group = v->topk_group > 0 ? v->topk_group : n_group;
+  ra.routed_scale = (sig && v->routed_scaling_factor != 0.f) ? v->routed_scaling_factor : 1.f;
+  ra.corr_bias = sig ? v->correction_bias : nullptr;
+  ra.out_scores_f32 = v->topk_scores_f32;
+  ra.shared_ungated = (shared && ungated) ? 1 : 0;
+  ra.gsync = grid_sync(h);
+  ra.err = err_word(h);
+  ra.phase_ns = phase_ns(h);
+  rc = launch_route(h, ra, ((T + 15) / 16) * ksplit, sig);
+  if (rc) return rc;
+
+  GemmArgs ga;
+  std::memset(&ga, 0, sizeof(ga));
+  ga.gs = c->group_size;
+  ga.err = err_word(h);
+  ga.sorted_token = ra.sorted_token;
+  ga.sorted_score = ra.sorted_score;
+  ga.sorted_flat = ra.sorted_flat;
+  ga.K = H;
+  ga.K_shared = H;
+  ga.N = I;
+  ga.N_shared = Is;
+  if (relu2) {  // fc1 = up; shared: up only
+    ga.w0 = w->up.w; ga.s0 = w->up.scales; ga.b0 = w->up.biases;
+    if (shared) {
+      ga.sw0 = w->shared_up.w; ga.ss0 = w->shared_up.scales; ga.sb0 = w->shared_up.biases;
+    }
+  } else {
+    ga.w0 = w->gate.w; ga.s0 = w->gate.scales; ga.b0 = w->gate.biases;
+    ga.w1 = w->up.w; ga.s1 = w->up.scales; ga.b1 = w->up.biases;
+    if (shared) {
+      ga.sw0 = w->shared_gate.w; ga.ss0 = w->shared_gate.scales; ga.sb0 = w->shared_gate.biases;
+      ga.sw1 = w->shared_up.w; ga.ss1 = w->shared_up.scales; ga.sb1 = w->shared_up.biases;
+    }
+  }
+  ga.act = ra.x_perm;
+  ga.act_shared = ra.x_perm;
+  ga.act_ld = H;
+  ga.act_shared_ld = H;
+  ga.out = at<uint16_t>(h, p.a_sorted);
+  ga.out_ld = I;
+  ga.out_shared = shared ? at<uint16_t>(h, p.a_shared) : nullptr;
+  ga.out_shared_ld = Is;
+  ga.tab = ra.tab_a;
+  rc = relu2 ? launch_gemm<fm::MODE_RELU2>(h, ga, false) : launch_gemm<fm::MODE_GATEUP>(h, ga, false);
+  if (rc) return rc;
+  GemmArgs gd = ga;
+  gd.K = I;
+  gd.K_shared = Is;
+  gd.N = H;
+  gd.N_shared = H;
+  gd.w0 = w->down.w; gd.s0 = w->down.scales; gd.b0 = w->down.biases;
+  gd.w1 = nullptr; gd.s1 = nullptr; gd.b1 = nullptr;
+  gd.sw0 = shared ? w->shared_down.w : nullptr;
+  gd.ss0 = shared ? w->shared_down.scales : nullptr;
+  gd.sb0 = shared ? w->shared_down.biases : nullptr;
+  gd.sw1 = nullptr; gd.ss1 = nullptr; gd.sb1 = nullptr;
+  gd.act = ga.out;
+  gd.act_ld = I;
+  gd.act_shared = ga.out_shared;
+  gd.act_shared_ld = Is;
+  gd.out = nullptr;
+  gd.out_shared = nullptr;
+  gd.y_acc = at<float>(h, p.y_acc);
+  gd.ysh = shared ? at<float>(h, p.ysh) : nullptr;
+  gd.y_ld = H;
+  gd.tab = ra.tab_b;
+  rc = sig ? launch_gemm<fm::MODE_DOWN_F32>(h, gd, false) : launch_gemm<fm::MODE_DOWN>(h, gd, false);
+  if (rc) return rc;
+  prof_begin(h, "finalize");
+  const int64_t n4 = T * H / 4;
+  const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+  fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
   prof_end(h);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(h, e, "finalize launch");

@@ -77,7 +77,10 @@ FM_DEV TileInfo decode_tile(const TileTable* tab, const int* tile_begin, int ngr
   return tile_of_group(tab, lo, tile);
 }
 
-enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2 };
+// MODE_RELU2: one ungated matrix (fc1) per expert with relu^2, written like gate/up's
+// activation rows for the down matrix; MODE_DOWN_F32: down with fp32 routing scores, the
+// product d * score kept in fp32 (the sigmoid-routed variant's combine).  GEMV only.
+enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2, MODE_RELU2 = 3, MODE_DOWN_F32 = 4 };
 
 // Arguments of the expert-product kernels (GEMV and tcgen05 paths).
 struct GemmArgs {
@@ -188,6 +191,13 @@ struct RouteArgs {
   uint16_t* out_topk_scores;
   int32_t* out_sorted_token;
   int32_t* out_offsets;
+  // sigmoid-routed variant (route_kernel_sigmoid): scores sigmoid(logit) [+ correction
+  // bias for selection], group-limited top-k, fp32 renormalised and scaled scores
+  int n_group, topk_group;
+  float routed_scale;
+  const float* corr_bias;       // [E] fp32 or NULL
+  float* out_scores_f32;        // [T, k] fp32 scores as used (nullable, either routing)
+  int shared_ungated;           // the shared expert is added without a gate (gate_sig = 1)
   GridSync* gsync;
   uint32_t* err;
   unsigned long long* phase_ns;  // [4] accumulated per-phase time of block 0 (profiling)

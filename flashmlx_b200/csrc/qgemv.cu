@@ -43,6 +43,12 @@ FM_DEV float swiglu1(float g, float u) {  // model.cpp:14-25, bf16 rounding per 
   return rbf(h * u);
 }
 
+// relu^2 of a bf16 value, rounded to bf16 (nemotron_h.cpp:53-58: maximum(x, 0), square)
+FM_DEV float relu2_1(float v) {
+  const float r = fmaxf(v, 0.f);
+  return rbf(r * r);
+}
+
 // code pair (q_p, q_{p+4}) of a packed word as bf16x2 (128 + q_p, 128 + q_{p+4})
 FM_DEV uint32_t code_pair_128(uint32_t w, int p) { return ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u; }
 
@@ -60,6 +66,7 @@ FM_DEV void cp_async8(uint32_t dst, const void* src) {
 
 template <int MODE>
 __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) {
+  constexpr bool kDown = MODE == MODE_DOWN || MODE == MODE_DOWN_F32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const TileTable* tab = a.tab;
@@ -76,7 +83,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
     const TileInfo ti = decode_tile(tab, s_tb, ngroups, tile);
     const bool sh = ti.expert < 0;
-    const int K = (MODE == MODE_DOWN && sh) ? a.K_shared : a.K;
+    const int K = (kDown && sh) ? a.K_shared : a.K;
     const int N = sh ? a.N_shared : a.N;
     const int kw = K / 8;        // u32 words per weight row
     const int gpr = K / a.gs;    // quant groups per row
@@ -120,7 +127,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
     const uint16_t* xsrc = nullptr;
     if (xr < ti.nrows) {
       const int p = ti.row0 + xr;
-      const int64_t src = (MODE == MODE_DOWN || sh) ? p : a.sorted_token[p];
+      const int64_t src = (kDown || sh) ? p : a.sorted_token[p];
       xsrc = (sh ? a.act_shared : a.act) + src * (sh ? a.act_shared_ld : a.act_ld) + xc * 8;
     }
     auto load_x = [&](int kc, int slot) {
@@ -242,9 +249,16 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
           if (!(m == 0 ? mval0 : mval1)) continue;
           const int n = r0[m] + g + 8 * (e >> 1);
           const float v = y[m][e];
-          if (MODE == MODE_DOWN) {
+          if (MODE == MODE_RELU2) {  // fc1 -> relu^2, activation rows for the down matrix
+            uint16_t* out = sh ? a.out_shared + static_cast<int64_t>(p) * a.out_shared_ld
+                               : a.out + static_cast<int64_t>(p) * a.out_ld;
+            out[perm8(n)] = f2bf(relu2_1(rbf(v)));
+          } else if (kDown) {
             if (sh) {
               red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + n, v);
+            } else if (MODE == MODE_DOWN_F32) {  // sigmoid routing: fp32 d * score, summed in fp32
+              const int t = a.sorted_token[p];
+              red_add_f32(a.y_acc + static_cast<int64_t>(t) * a.y_ld + n, rbf(v) * a.sorted_score[p]);
             } else if (a.y_rowptr) {  // one output row per pair, at its destination (peer memory)
               a.y_rowptr[p][n] = f2bf(rbf(rbf(v) * a.sorted_score[p]));
             } else if (a.y_pairs) {  // one output row per pair (expert-parallel owner side)
@@ -266,6 +280,8 @@ cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs
   switch (mode) {
     case MODE_GATEUP: qgemv_kernel<MODE_GATEUP><<<grid, kGvThreads, 0, stream>>>(a); break;
     case MODE_DOWN: qgemv_kernel<MODE_DOWN><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_RELU2: qgemv_kernel<MODE_RELU2><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_DOWN_F32: qgemv_kernel<MODE_DOWN_F32><<<grid, kGvThreads, 0, stream>>>(a); break;
     default: qgemv_kernel<MODE_PLAIN><<<grid, kGvThreads, 0, stream>>>(a); break;
   }
   return cudaGetLastError();

@@ -215,6 +215,7 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
       a.gate_sig[t] = rbf(sigmoid_f(rbf(sum_partials(a, t, e))));
     }
   }
+  if (a.shared_ungated && lane == 0) a.gate_sig[t] = 1.0f;
   mx = warp_max(mx);
   // softmax(precise): fp32 exp; sum = lane-strided partial sums then xor butterfly
   float part = 0.f;
@@ -270,6 +271,132 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
     a.topk_score[t * k + lane] = sc;
     if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
     if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
+    if (a.out_scores_f32) a.out_scores_f32[t * k + lane] = sc;
+    atomicOr(&sm.mask[se], 1u << tl);
+  }
+}
+
+// fp32 -> 32-bit key with the same order (NaN lowest)
+FM_DEV uint32_t ordered_key(float f) {
+  if (isnan(f)) return 0u;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Sigmoid routing of one token by one warp (the Nemotron-H / DeepSeek-style block,
+// nemotron_h.cpp:1018-1050): orig = sigmoid(fp32(bf16 logit)); sel = orig + correction
+// bias; with n_group > 1 each group scores the sum of its two best sel and the
+// n_group - topk_group lowest groups (equal scores: the higher group id first) get
+// sel = 0; top-k of sel (equal: lower expert id) in k rounds of a 64-bit warp max; the
+// scores are the picks' orig, divided by (their sum in pick order + 1e-20) when
+// norm_topk and k > 1, times routed_scale, all fp32.
+__device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl) {
+  const int lane = threadIdx.x & 31;
+  const int E = a.E, k = a.k;
+  constexpr int PER = kMaxExperts / 32;
+  float orig[PER];
+  unsigned long long key[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    orig[i] = 0.f;
+    key[i] = 0ull;
+    if (e < E) {
+      const float l = rbf(sum_partials(a, t, e));
+      orig[i] = 1.0f / (1.0f + expf(-l));
+    } else if (e == E && a.shared_gate_w) {
+      a.gate_sig[t] = rbf(sigmoid_f(rbf(sum_partials(a, t, e))));
+    }
+  }
+  if (a.shared_ungated && lane == 0) a.gate_sig[t] = 1.0f;
+  float sel[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    sel[i] = (e < E) ? (a.corr_bias ? orig[i] + a.corr_bias[e] : orig[i]) : -INFINITY;
+  }
+  if (a.n_group > 1) {  // n_group <= 32 (host-checked): lane gi holds group gi's score
+    const int gsz = E / a.n_group;
+    float gmine = 0.f;
+    for (int gi = 0; gi < a.n_group; ++gi) {
+      float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        if (e < E && e / gsz == gi) {
+          const float v = sel[i];
+          if (v > m1) {
+            m2 = m1;
+            m1 = v;
+          } else if (v > m2) {
+            m2 = v;
+          }
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) {  // top two of the warp
+        const float b1 = __shfl_xor_sync(0xffffffffu, m1, off);
+        const float b2 = __shfl_xor_sync(0xffffffffu, m2, off);
+        const float n2 = fmaxf(fminf(m1, b1), fmaxf(m2, b2));
+        m1 = fmaxf(m1, b1);
+        m2 = n2;
+      }
+      if (lane == gi) gmine = m1 + m2;
+    }
+    int rank = 0;  // groups zeroed before this lane's group
+    for (int gj = 0; gj < a.n_group; ++gj) {
+      const float v = __shfl_sync(0xffffffffu, gmine, gj);
+      if (lane < a.n_group && (v < gmine || (v == gmine && gj > lane))) ++rank;
+    }
+    const uint32_t zmask = __ballot_sync(0xffffffffu, lane < a.n_group && rank < a.n_group - a.topk_group);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && ((zmask >> (e / gsz)) & 1u)) sel[i] = 0.f;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    if (e < E)  // a valid key is never 0: its low half is 0xFFFF - e > 0
+      key[i] = (static_cast<unsigned long long>(ordered_key(sel[i])) << 32) | static_cast<uint32_t>(0xFFFF - e);
+  }
+  float sp = 0.f, ssum = 0.f;
+  int se = 0;
+  for (int j = 0; j < k; ++j) {
+    unsigned long long best = 0ull;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) best = key[i] > best ? key[i] : best;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const unsigned long long o = __shfl_xor_sync(0xffffffffu, best, off);
+      best = o > best ? o : best;
+    }
+    const int be = 0xFFFF - static_cast<int>(best & 0xFFFFu);
+    float mine = 0.f;  // the pick's orig, from the lane that holds it
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (i == (be >> 5)) mine = orig[i];
+    const float bo = __shfl_sync(0xffffffffu, mine, be & 31);
+    if (lane == j) {
+      sp = bo;
+      se = be;
+    }
+    ssum += bo;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i == be) key[i] = 0ull;
+  }
+  const bool renorm = a.norm_topk && k > 1;
+  const float denom = renorm ? ssum + 1e-20f : 1.f;
+  if (lane < k) {
+    const float sc = (renorm ? sp / denom : sp) * a.routed_scale;
+    a.topk_ids[t * k + lane] = se;
+    sm.ids[tl * k + lane] = se;
+    a.topk_score[t * k + lane] = sc;
+    if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
+    if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
+    if (a.out_scores_f32) a.out_scores_f32[t * k + lane] = sc;
     atomicOr(&sm.mask[se], 1u << tl);
   }
 }
@@ -292,6 +419,7 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) 
   atomicOr(&sm.mask[e], 1u << tl);
 }
 
+template <bool SIGMOID>
 __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
   const int warp = threadIdx.x >> 5;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
@@ -303,8 +431,9 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
       const int tl = warp * (kRouteChunk / 8) + i;
       const int64_t t = static_cast<int64_t>(ch) * kRouteChunk + tl;
       if (t >= a.T) break;
-      if (a.do_router) route_token(a, t, sm, tl);
-      else given_row(a, t, sm, tl);
+      if (!a.do_router) given_row(a, t, sm, tl);
+      else if (SIGMOID) route_token_sigmoid(a, t, sm, tl);
+      else route_token(a, t, sm, tl);
     }
     __syncthreads();
     for (int e = threadIdx.x; e < a.E; e += blockDim.x)
@@ -547,8 +676,8 @@ __global__ void __launch_bounds__(kRouteThreads) ep_p2p_plan_kernel(const EpP2PA
   ep_plan_body(pa);
 }
 
-__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
-  __shared__ RouteSmem sm;
+template <bool SIGMOID>
+__device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   const unsigned nb = gridDim.x;
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   // phase 1
@@ -559,7 +688,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 0, t);
   // phase 2
-  phase_topk_count(a, sm);
+  phase_topk_count<SIGMOID>(a, sm);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 1, t);
   // phase 3
@@ -569,6 +698,18 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
   // phase 4
   phase_scatter(a, sm);
   phase_mark(a, 3, t);
+}
+
+// softmax routing (the reference's LlamaModel block) and sigmoid routing (the
+// Nemotron-H / DeepSeek-style block) as separate kernels, so the default one keeps its
+// registers and occupancy
+__global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_body<false>(a, sm);
+}
+__global__ void __launch_bounds__(kRouteThreads) route_kernel_sigmoid(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_body<true>(a, sm);
 }
 
 }  // namespace fm

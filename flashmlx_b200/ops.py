@@ -303,3 +303,67 @@ class MoEBlock:
         h.bind_stream()
         h.check(h.lib.fm_moe_block(h.h, C.byref(self.cfg), C.byref(self.W), _ptr(x), T, _ptr(y), C.byref(outs)))
         return (y, routing) if return_routing else y
+class MoEBlockVariant:
+    """fm_moe_block_variant: the MoE block with another routing / expert form, e.g.
+    NemotronHModel::moe_block (server/src/nemotron_h.cpp:1010-1106): sigmoid routing with
+    an e_score_correction_bias and group-limited top-k, fp32 scores times
+    routed_scaling_factor, ungated relu^2 experts (fc1 as weights.up, fc2 as weights.down)
+    and an ungated shared expert (shared_up, shared_down).  Runs the GEMV expert path."""
+
+    def __init__(self, shape, weights: MoEWeightsT, score_func: int = _lib.FM_SCORE_SIGMOID,
+                 expert_act: int = _lib.FM_ACT_RELU2, shared_ungated: bool = True, n_group: int = 1,
+                 topk_group: int = 1, routed_scaling_factor: float = 1.0,
+                 correction_bias: torch.Tensor | None = None, handle: Handle | None = None):
+        self.block = MoEBlock(shape, weights, handle)
+        self.shape = shape
+        if correction_bias is not None:
+            _need(correction_bias, "correction_bias", (torch.float32,), weights.router_w.device)
+        self.correction_bias = correction_bias
+        v = _lib.MoEVariant()
+        v.score_func, v.expert_act, v.shared_ungated = score_func, expert_act, int(shared_ungated)
+        v.n_group, v.topk_group, v.routed_scaling_factor = n_group, topk_group, routed_scaling_factor
+        v.correction_bias = correction_bias.data_ptr() if correction_bias is not None else None
+        self.variant = v
+
+    @staticmethod
+    def sigmoid_from_numpy(shape, layer: dict, device, n_group: int = 1, topk_group: int = 1,
+                           routed_scaling_factor: float = 1.0, handle: Handle | None = None) -> "MoEBlockVariant":
+        """The Nemotron-H form from a synthetic.make_sigmoid_layer-style dict."""
+        import numpy as np
+
+        def q(t):
+            w, sc, b = t
+            return (u32_from_numpy(w, device), bf16_from_numpy(sc, device),
+                    bf16_from_numpy(b, device) if b is not None else None)
+        W = MoEWeightsT(router_w=bf16_from_numpy(layer["router_w"], device), gate=None, up=q(layer["fc1"]),
+                        down=q(layer["fc2"]),
+                        shared_up=q(layer["shared_up"]) if "shared_up" in layer else None,
+                        shared_down=q(layer["shared_down"]) if "shared_down" in layer else None)
+        cb = layer.get("correction_bias")
+        cbt = torch.from_numpy(np.ascontiguousarray(cb, np.float32)).to(device) if cb is not None else None
+        return MoEBlockVariant(shape, W, n_group=n_group, topk_group=topk_group,
+                               routed_scaling_factor=routed_scaling_factor, correction_bias=cbt, handle=handle)
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False):
+        w = self.block.weights
+        _need(x, "x", (torch.bfloat16,), w.router_w.device)
+        if x.shape[-1] != self.shape.hidden:
+            raise ValueError("x last dim must equal hidden size")
+        T = x.numel() // self.shape.hidden
+        y = out if out is not None else torch.empty_like(x)
+        outs = MoEOutputs()
+        routing = None
+        self.variant.topk_scores_f32 = None
+        if return_routing:
+            k = self.shape.top_k
+            routing = {"topk_ids": torch.empty(T, k, dtype=torch.int32, device=x.device),
+                       "topk_scores_f32": torch.empty(T, k, dtype=torch.float32, device=x.device)}
+            outs.topk_ids = routing["topk_ids"].data_ptr()
+            self.variant.topk_scores_f32 = routing["topk_scores_f32"].data_ptr()
+        h = self.block._h(x.device)
+        h.bind_stream()
+        h.check(h.lib.fm_moe_block_variant(h.h, C.byref(self.block.cfg), C.byref(self.variant), C.byref(self.block.W),
+                                           _ptr(x), T, _ptr(y), C.byref(outs)))
+        return (y, routing) if return_routing else y
+
+

@@ -106,6 +106,35 @@ typedef struct fm_moe_outputs {
   int32_t* expert_offsets; /* [E+1] start of each expert's segment in that order */
 } fm_moe_outputs;
 
+/* Routing / expert variant of an MoE block.  All zero (or cfg-only calls through
+ * fm_moe_block) is the reference's LlamaModel block: softmax routing, SwiGLU gate/up/down
+ * experts, a sigmoid-gated shared expert.  The Nemotron-H / DeepSeek-style block of
+ * NemotronHModel::moe_block (nemotron_h.cpp:1010-1106) is score_func = FM_SCORE_SIGMOID,
+ * expert_act = FM_ACT_RELU2, shared_ungated = 1:
+ *   orig = sigmoid(fp32(bf16 logits)), sel = orig + correction_bias; with n_group > 1 each
+ *   of the n_group equal expert groups scores the sum of its two best sel and the
+ *   n_group - topk_group lowest groups get sel = 0; the top-k of sel take their orig as
+ *   scores, divided by (their sum + 1e-20) when norm_topk_prob and k > 1, times
+ *   routed_scaling_factor, in fp32; experts h = fc2(relu2(fc1(x))) with fc1 passed as
+ *   weights.up and fc2 as weights.down (weights.gate unused); y = bf16(sum_k h_k * s_k)
+ *   in fp32, plus bf16(shared_down(relu2(shared_up(x)))) unweighted when the layer has a
+ *   shared expert (shared_inter > 0; weights.shared_gate and shared_expert_gate_w unused). */
+#define FM_SCORE_SOFTMAX 0
+#define FM_SCORE_SIGMOID 1
+#define FM_ACT_SWIGLU 0
+#define FM_ACT_RELU2 1
+
+typedef struct fm_moe_variant {
+  int score_func;               /* FM_SCORE_SOFTMAX | FM_SCORE_SIGMOID */
+  int n_group;                  /* sigmoid: expert groups for group-limited top-k (<= 32); 0 or 1 = off */
+  int topk_group;               /* sigmoid: groups kept */
+  float routed_scaling_factor;  /* sigmoid: multiplies the scores; 0 reads as 1 */
+  int expert_act;               /* FM_ACT_SWIGLU | FM_ACT_RELU2 */
+  int shared_ungated;           /* 1: the shared expert's output is added without the sigmoid gate */
+  const float* correction_bias; /* sigmoid: [E] fp32 e_score_correction_bias (selection only), or NULL */
+  float* topk_scores_f32;       /* optional [T, k] fp32 scores as applied (device) */
+} fm_moe_variant;
+
 /* Handle lifecycle -------------------------------------------------------- */
 
 /* Creates a handle on `device`, issuing work on `stream` (a cudaStream_t, NULL =
@@ -171,6 +200,15 @@ FM_API int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int
  * router logits (bf16), softmax (fp32 inside, bf16 out), top-k, optional renorm,
  * gate/up/down expert products with silu(g)*u, bf16(d*score) summed over k, plus
  * bf16(sigmoid(x.wg) * shared(x)) when the layer has a shared expert. */
+/* fm_moe_block for a variant of the block (fm_moe_variant above; NULL = fm_moe_block).
+ * The default variant runs fm_moe_block itself; the others run the GEMV expert path at
+ * every batch size (correct at any size, not tuned for prefill).  No reference
+ * interface is replaced: NemotronHModel::moe_block (nemotron_h.cpp:1010-1106) is what
+ * a caller would switch. */
+FM_API int fm_moe_block_variant(fm_handle* h, const fm_moe_config* cfg, const fm_moe_variant* v,
+                                const fm_moe_weights* w, const uint16_t* x, int64_t T, uint16_t* y,
+                                const fm_moe_outputs* outs);
+
 FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_weights* w, const uint16_t* x,
                  int64_t T, uint16_t* y, const fm_moe_outputs* outs);
 

@@ -1,0 +1,69 @@
+"""The Nemotron-H / DeepSeek-style block (fm_moe_block_variant: sigmoid routing with a
+correction bias and group-limited top-k, fp32 scaled scores, ungated relu^2 experts and
+shared expert; server/src/nemotron_h.cpp:1010-1106) on the device against the CPU
+oracle's restatement: the routing against the oracle's own routing where no near-tie
+decides a pick, the block against the oracle under the device's routing."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from flashmlx_b200 import synthetic as S
+from oracle import oracle as O
+from tests import numpy_ref as R
+from tests.gpu_util import check_vs_oracle, host_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def _shape(tokens, shared):
+    return S.MoEShape("sig", 512, 256, 32, 4, tokens, True, shared)
+
+
+@pytest.mark.parametrize("tokens", [1, 7, 48, 300])
+@pytest.mark.parametrize("groups", [(1, 1), (4, 2)])
+@pytest.mark.parametrize("shared", [0, 256])
+def test_sigmoid_block_vs_oracle(tokens, groups, shared):
+    from flashmlx_b200 import ops
+    shape = _shape(tokens, shared)
+    layer = S.make_sigmoid_layer(shape, 21)
+    x_np = S.make_x(shape, 21)
+    routing = {"n_group": groups[0], "topk_group": groups[1], "routed_scaling_factor": 2.5}
+    blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", **routing)
+    y, r = blk(ops.bf16_from_numpy(x_np, "cuda"), return_routing=True)
+    torch.cuda.synchronize()
+    ids = r["topk_ids"].cpu().numpy()
+    sc = r["topk_scores_f32"].cpu().numpy()
+    L = O.SigmoidLayer(shape, layer, routing)
+    # routing: the same picks (as sets) and scores where the k-th pick is clear of the next
+    oid, osc = L.route(x_np)
+    _, _, sel = R.sigmoid_route(x_np, layer["router_w"], layer["correction_bias"], shape.top_k, groups[0],
+                                groups[1], True, 2.5)
+    srt = np.sort(sel, axis=-1)[:, ::-1]
+    clear = np.abs(srt[:, shape.top_k - 1] - srt[:, shape.top_k]) > 5e-3
+    assert clear.mean() > 0.6
+    for t in np.nonzero(clear)[0]:
+        assert set(ids[t]) == set(oid[t]), (t, ids[t], oid[t])
+        dev = dict(zip(ids[t].tolist(), sc[t].tolist()))
+        for e, s in zip(oid[t].tolist(), osc[t].tolist()):
+            assert abs(dev[e] - s) <= 2e-2 * abs(s) + 1e-6, (t, e, dev[e], s)
+    # the block under the device's routing (ids and fp32 scores as applied)
+    check_vs_oracle(host_bf16(y), lambda: L.moe_block(x_np, forced_ids=ids, forced_scores=sc),
+                    f"sigmoid block T={tokens} groups={groups} shared={shared}")
+
+
+def test_variant_rejects_bad_arguments():
+    from flashmlx_b200 import ops
+    from flashmlx_b200._lib import FlashMoEError
+    shape = _shape(4, 0)
+    layer = S.make_sigmoid_layer(shape, 22)
+    x = ops.bf16_from_numpy(S.make_x(shape, 22), "cuda")
+    with pytest.raises(FlashMoEError):  # 32 experts in 3 groups
+        ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", n_group=3, topk_group=1)(x)
+    with pytest.raises(FlashMoEError):  # more groups kept than exist
+        ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", n_group=4, topk_group=5)(x)
+    blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda")
+    blk.block.W.router_bias = blk.block.weights.router_w.data_ptr()  # a softmax-only logit bias
+    with pytest.raises(FlashMoEError):
+        blk(x)
