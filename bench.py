@@ -47,7 +47,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(S.CONFIGS))
+    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(S.CONFIGS) + sorted(S.VARIANT_CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -121,11 +121,28 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU
-def cpu_oracle_throughput(shape, layer_np, x_np, min_seconds=10.0):
-    """Tokens/s of the CPU restatement on a bounded sample (all host threads)."""
+def oracle_layer(config, shape, layer_np):
+    """The CPU restatement of the workload's block (the variant's for variant configs)."""
     from oracle import oracle as O
     O.build()
-    L = O.Layer(shape, layer_np)
+    if config in S.VARIANT_CONFIGS:
+        return O.SigmoidLayer(shape, layer_np, S.VARIANT_CONFIGS[config][1])
+    return O.Layer(shape, layer_np)
+
+
+def workload(config, seed):
+    """(shape, numpy layer) of a bench workload."""
+    if config in S.VARIANT_CONFIGS:
+        shape = S.VARIANT_CONFIGS[config][0]
+        return shape, S.make_sigmoid_layer(shape, seed)
+    shape = S.CONFIGS[config]
+    return shape, S.make_layer(shape, seed)
+
+
+def cpu_oracle_throughput(shape, layer_np, x_np, min_seconds=10.0, config=None):
+    """Tokens/s of the CPU restatement on a bounded sample (all host threads)."""
+    from oracle import oracle as O
+    L = oracle_layer(config, shape, layer_np)
     n = min(CPU_SAMPLE_TOKENS, x_np.shape[0])
     sample = x_np[:n]
     done, t0 = 0, time.perf_counter()
@@ -144,12 +161,10 @@ def run_reference(args, rank, world):
     """--impl reference: the CPU port of the reference path; rank 0 only."""
     if rank != 0:
         return
-    shape = S.CONFIGS[args.config]
-    layer_np = S.make_layer(shape, args.seed)
+    shape, layer_np = workload(args.config, args.seed)
     x_np = S.make_x(shape, args.seed)
     from oracle import oracle as O
-    O.build()
-    L = O.Layer(shape, layer_np)
+    L = oracle_layer(args.config, shape, layer_np)
     n = min(CPU_SAMPLE_TOKENS, x_np.shape[0])
     for _ in range(args.warmup):
         L.moe_block(x_np[:n])
@@ -186,7 +201,11 @@ def kernel_work(shape, T, counts):
     b_dn = active * H * I * per_w + H * Is * per_w + P * I * 2 + T * Is * 2 + T * H * 4 * (2 if Is else 1)
     f_rt = 2.0 * T * H * (E + (1 if Is else 0))
     b_rt = E * H * 2 + T * H * 2 * 2 + T * H * 4 * (2 if Is else 1)
+    # the variant's ungated fc1 (relu^2): one matrix instead of gate and up
+    f_r2 = 2.0 * P * H * I + 2.0 * T * H * Is
+    b_r2 = active * H * I * per_w + H * Is * per_w + T * H * 2 + P * I * 2 + T * Is * 2
     return {
+        "qgemv_relu2": (f_r2, b_r2),
         "qgemm_tc_gateup": (f_gu, b_gu), "qgemv_gateup": (f_gu, b_gu),
         "qgemm_tc_down": (f_dn, b_dn), "qgemv_down": (f_dn, b_dn),
         "route": (f_rt, b_rt), "finalize": (0.0, T * H * (4 + 4 + 2) if Is else T * H * 6),
@@ -221,10 +240,12 @@ def run_ours(args, rank, world, local_rank):
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
     from flashmlx_b200 import ops
 
-    shape = S.CONFIGS[args.config]
+    shape, layer_np = workload(args.config, args.seed)
+    variant = args.config in S.VARIANT_CONFIGS
     T = shape.tokens
     ep = world > 1 and not args.replicas
-    layer_np = S.make_layer(shape, args.seed)
+    if ep and variant:
+        raise SystemExit("variant workloads run on one GPU or as --replicas")
     x_np = S.make_x(shape, args.seed + rank)  # each rank routes its own batch
     h = ops.default_handle(local_rank)
     x = ops.bf16_from_numpy(x_np, dev)
@@ -261,6 +282,15 @@ def run_ours(args, rank, world, local_rank):
         else:
             def step(xin, out):
                 out.copy_(ep_block(xin))
+    elif variant:
+        block = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer_np, dev, **S.VARIANT_CONFIGS[args.config][1])
+        block.block.reserve(T)
+        _, routing = block(x, return_routing=True)
+        h.sync()
+        counts = np.bincount(routing["topk_ids"].cpu().numpy().ravel(), minlength=shape.num_experts)
+
+        def step(xin, out):
+            block(xin, out=out)
     else:
         W = ops.MoEWeightsT.from_numpy(layer_np, dev)
         block = ops.MoEBlock(shape, W)
@@ -390,7 +420,7 @@ def run_ours(args, rank, world, local_rank):
                      "algorithmic": flops if tensor_bound else nbytes})
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            v, info = cpu_oracle_throughput(shape, layer_np, x_np)
+            v, info = cpu_oracle_throughput(shape, layer_np, x_np, config=args.config)
             cpu = {"value": v, "unit": "tokens/s", **info}
         ours_launches = sum(n for kname, (n, _) in prof.items())
         line = {
