@@ -9,7 +9,8 @@ Follows the reference's loader for the MoE layers:
                          with the same defaults
   Checkpoint             LlamaModel::load_weights (148-184): every *.safetensors file of the
                          directory in sorted order, later files overriding earlier keys,
-                         a leading "model." stripped from every key
+                         a leading "model." (or Nemotron-H's "backbone.") stripped from
+                         every key
   Checkpoint.moe_layer   build_moe_weight_cache (368-470): a layer is MoE when it has
                          layers.N.mlp.gate.weight; the experts'
                          experts.E.{gate,up,down}_proj.{weight,scales,biases} are stacked
@@ -18,6 +19,13 @@ Follows the reference's loader for the MoE layers:
                          shared_expert_gate.weight
 Checkpoints written by mlx-lm keep the experts pre-stacked as
 layers.N.mlp.switch_mlp.{gate,up,down}_proj.*; those are taken as they are.
+
+Nemotron-H checkpoints (NemotronHModel, server/src/nemotron_h.cpp: config 244-261,
+pattern 272-285, MoE weights 444-468) mark their MoE layers 'E' in
+hybrid_override_pattern and keep them under layers.N.mixer: gate.weight,
+gate.e_score_correction_bias, switch_mlp.fc1 / fc2 (stacked), shared_experts.up_proj /
+down_proj; Checkpoint.sigmoid_moe_layer() reads one into the layout of
+synthetic.make_sigmoid_layer for ops.MoEBlockVariant.
 
 The result of moe_layer() has the layout of synthetic.make_layer (bf16 as uint16 bits,
 packed codes as uint32; arrays the layer owns), so ops.MoEWeightsT.from_numpy(layer,
@@ -123,6 +131,21 @@ class MoEModelConfig:
     norm_topk_prob: bool
     bits: int
     group_size: int
+    # Nemotron-H / DeepSeek-style routing (defaults: off)
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+    hybrid_override_pattern: str = ""
+
+    @property
+    def sigmoid_routed(self) -> bool:
+        """A Nemotron-H model (MoE layers marked 'E' in hybrid_override_pattern)."""
+        return "E" in self.hybrid_override_pattern
+
+    def routing(self) -> dict:
+        """The variant's routing parameters (ops.MoEBlockVariant keyword arguments)."""
+        return {"n_group": self.n_group, "topk_group": self.topk_group,
+                "routed_scaling_factor": self.routed_scaling_factor}
 
     def shape(self, tokens: int, name: str = "checkpoint") -> MoEShape:
         """The layer shape for a batch of `tokens` (the MoEBlock / bench description)."""
@@ -137,16 +160,22 @@ def load_config(model_dir: str) -> MoEModelConfig:
     q = c.get("quantization")
     if not isinstance(q, dict):
         q = {}
+    pattern = c.get("hybrid_override_pattern") or ""
     return MoEModelConfig(
         hidden=int(c.get("hidden_size", 4096)),
         num_layers=int(c.get("num_hidden_layers", 32)),
-        num_experts=int(c.get("num_experts", 0)),
+        num_experts=int(c.get("num_experts", 0) or c.get("n_routed_experts", 0)),
         top_k=int(c.get("num_experts_per_tok", 0)),
         inter=int(c.get("moe_intermediate_size", 0)),
-        shared_inter=int(c.get("shared_expert_intermediate_size", 0)),
+        shared_inter=int(c.get("shared_expert_intermediate_size", 0) or
+                         (c.get("moe_shared_expert_intermediate_size", 0) if c.get("n_shared_experts", 1) else 0)),
         norm_topk_prob=bool(c.get("norm_topk_prob", False)),
         bits=int(q.get("bits", 0)),
         group_size=int(q.get("group_size", 64)),
+        n_group=int(c.get("n_group", 1)),
+        topk_group=int(c.get("topk_group", 1)),
+        routed_scaling_factor=float(c.get("routed_scaling_factor", 1.0)),
+        hybrid_override_pattern=str(pattern),
     )
 
 
@@ -163,7 +192,12 @@ class Checkpoint:
         for path in files:
             t, _ = read_safetensors(path)
             for key, v in t.items():
-                self.tensors[key[6:] if key.startswith("model.") else key] = v
+                # "model." (LlamaModel::load_weights) or "backbone." (NemotronHModel, 333-337)
+                for pre in ("model.", "backbone."):
+                    if key.startswith(pre):
+                        key = key[len(pre):]
+                        break
+                self.tensors[key] = v
 
     def has(self, key: str) -> bool:
         return key in self.tensors
@@ -177,8 +211,56 @@ class Checkpoint:
         return arr
 
     def moe_layers(self) -> list[int]:
-        """Indices of the layers with a router (layers.N.mlp.gate.weight)."""
-        return [i for i in range(self.config.num_layers) if self.has(f"layers.{i}.mlp.gate.weight")]
+        """Indices of the layers with a router: layers.N.mlp.gate.weight, or for a
+        Nemotron-H model the 'E' layers of hybrid_override_pattern (layers.N.mixer)."""
+        c = self.config
+        if c.sigmoid_routed:
+            if len(c.hybrid_override_pattern) != c.num_layers:
+                raise ValueError("hybrid_override_pattern length differs from num_hidden_layers")
+            return [i for i, b in enumerate(c.hybrid_override_pattern) if b == "E"]
+        return [i for i in range(c.num_layers) if self.has(f"layers.{i}.mlp.gate.weight")]
+
+    def sigmoid_moe_layer(self, i: int) -> dict:
+        """Nemotron-H MoE layer i in the layout of synthetic.make_sigmoid_layer."""
+        c = self.config
+        mx = f"layers.{i}.mixer"
+        if not self.has(mx + ".gate.weight"):
+            raise KeyError(f"layer {i} has no router ({mx}.gate.weight)")
+        if self.has(mx + ".gate.scales"):
+            raise NotImplementedError(f"{mx}.gate is quantized: a quantized router is not implemented")
+        if c.bits != 4:
+            raise NotImplementedError(f"quantization bits = {c.bits}: only 4-bit affine weights are implemented")
+        d = {"router_w": np.array(self.get(mx + ".gate.weight", "BF16"))}
+        if self.has(mx + ".gate.e_score_correction_bias"):
+            dt, arr = self.tensors[mx + ".gate.e_score_correction_bias"]
+            if dt == "F32":
+                d["correction_bias"] = np.array(arr, np.float32)
+            elif dt == "BF16":
+                d["correction_bias"] = (np.asarray(arr, np.uint32) << 16).view(np.float32).copy()
+            else:
+                raise ValueError(f"{mx}.gate.e_score_correction_bias: {dt}, expected F32 or BF16")
+        d["fc1"] = self._qmatrix(mx + ".switch_mlp.fc1")
+        d["fc2"] = self._qmatrix(mx + ".switch_mlp.fc2")
+        if self.has(mx + ".shared_experts.up_proj.weight"):
+            d["shared_up"] = self._qmatrix(mx + ".shared_experts.up_proj")
+            d["shared_down"] = self._qmatrix(mx + ".shared_experts.down_proj")
+        E, H, I, Is, gs, pw = c.num_experts, c.hidden, c.inter, c.shared_inter, c.group_size, 32 // c.bits
+        shapes = {"router_w": (E, H), "fc1": (E, I, H), "fc2": (E, H, I), "shared_up": (Is, H), "shared_down": (H, Is)}
+        for key, shp in shapes.items():
+            if key not in d:
+                if key.startswith("shared") and Is:
+                    raise ValueError(f"layer {i}: config has a shared expert ({Is}) but the checkpoint has none")
+                continue
+            if key == "router_w":
+                got, want = d[key].shape, shp
+            else:
+                got = d[key][0].shape + d[key][1].shape[-1:]
+                want = shp[:-1] + (shp[-1] // pw, shp[-1] // gs)
+            if tuple(got) != tuple(want):
+                raise ValueError(f"layer {i} {key}: shape {tuple(got)}, config gives {tuple(want)}")
+        if "correction_bias" in d and d["correction_bias"].shape != (E,):
+            raise ValueError(f"layer {i} correction bias: shape {d['correction_bias'].shape}, config gives ({E},)")
+        return d
 
     def _qmatrix(self, prefix: str) -> tuple[np.ndarray, np.ndarray, np.ndarray | None]:
         # copies: a stacked layer owns its arrays (the mapped file stays read-only)

@@ -1,5 +1,6 @@
 """The MoE layers of an MLX-format checkpoint on one GPU, called the way the reference's
-decoder layer calls them.
+decoder layer calls them (LlamaModel, and NemotronHModel's 'E' layers through the
+sigmoid-routed variant).
 
 LlamaModel's layer (server/src/model.cpp:825-839) normalises the attention output and
 dispatches the MLP: moe_block(normed, layer) when the layer has a router
@@ -33,11 +34,18 @@ class MoEModel:
                 raise KeyError(f"layers {missing} are not MoE layers of {model_dir}")
             moe = sorted(layers)
         self.shape = self.config.shape(max_tokens or 1, name=model_dir)
-        self.blocks = {i: ops.MoEBlock(self.shape, ops.MoEWeightsT.from_numpy(self.checkpoint.moe_layer(i), self.device),
-                                       handle)
-                       for i in moe}
+        if self.config.sigmoid_routed:  # Nemotron-H: NemotronHModel::moe_block through fm_moe_block_variant
+            self.blocks = {i: ops.MoEBlockVariant.sigmoid_from_numpy(self.shape, self.checkpoint.sigmoid_moe_layer(i),
+                                                                     self.device, handle=handle,
+                                                                     **self.config.routing())
+                           for i in moe}
+        else:
+            self.blocks = {i: ops.MoEBlock(self.shape,
+                                           ops.MoEWeightsT.from_numpy(self.checkpoint.moe_layer(i), self.device), handle)
+                           for i in moe}
         if max_tokens and self.blocks:
-            next(iter(self.blocks.values())).reserve(max_tokens, self.device)
+            first = next(iter(self.blocks.values()))
+            (first.block if isinstance(first, ops.MoEBlockVariant) else first).reserve(max_tokens, self.device)
 
     def is_moe(self, layer: int) -> bool:
         """layer_is_moe_[layer]: the layer has a router and its experts are loaded."""

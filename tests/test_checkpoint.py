@@ -183,3 +183,59 @@ def test_moe_model_layer_discovery(tmp_path):
     assert m.shape.hidden == SHAPE.hidden and m.shape.num_experts == SHAPE.num_experts
     with pytest.raises(KeyError):
         MoEModel(str(tmp_path), device="cpu", layers=[1])
+
+
+NEMO = S.MoEShape("nemo", 256, 128, 8, 2, 8, True, 256)
+
+
+def _write_nemotron(path, layer):
+    """A 4-layer Nemotron-H model 'ME*E' whose two MoE layers are written from `layer`."""
+    c = {"hidden_size": NEMO.hidden, "num_hidden_layers": 4, "hybrid_override_pattern": "ME*E",
+         "n_routed_experts": NEMO.num_experts, "num_experts_per_tok": NEMO.top_k,
+         "moe_intermediate_size": NEMO.inter, "moe_shared_expert_intermediate_size": NEMO.shared_inter,
+         "n_shared_experts": 1, "n_group": 2, "topk_group": 1, "routed_scaling_factor": 2.5,
+         "norm_topk_prob": True, "quantization": {"group_size": 64, "bits": 4}}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(c, f)
+    t = {}
+    for li in (1, 3):
+        mx = f"backbone.layers.{li}.mixer"
+        t[f"{mx}.gate.weight"] = layer["router_w"]
+        t[f"{mx}.gate.e_score_correction_bias"] = ("F32", layer["correction_bias"])
+        for key, name in (("fc1", "switch_mlp.fc1"), ("fc2", "switch_mlp.fc2"),
+                          ("shared_up", "shared_experts.up_proj"), ("shared_down", "shared_experts.down_proj")):
+            w, s, b = layer[key]
+            t[f"{mx}.{name}.weight"], t[f"{mx}.{name}.scales"], t[f"{mx}.{name}.biases"] = w, s, b
+    t["backbone.layers.0.mixer.A_log"] = ("F32", np.zeros(4, np.float32))
+    CK.write_safetensors(os.path.join(path, "model.safetensors"), t)
+
+
+def test_nemotron_checkpoint(tmp_path):
+    layer = S.make_sigmoid_layer(NEMO, 13)
+    _write_nemotron(str(tmp_path), layer)
+    ck = CK.Checkpoint(str(tmp_path))
+    c = ck.config
+    assert c.sigmoid_routed and ck.moe_layers() == [1, 3]
+    assert (c.num_experts, c.shared_inter) == (NEMO.num_experts, NEMO.shared_inter)
+    assert c.routing() == {"n_group": 2, "topk_group": 1, "routed_scaling_factor": 2.5}
+    assert ck.has("layers.0.mixer.A_log")  # "backbone." stripped
+    got = ck.sigmoid_moe_layer(3)
+    np.testing.assert_array_equal(got["router_w"], layer["router_w"])
+    np.testing.assert_array_equal(got["correction_bias"], layer["correction_bias"])
+    for key in ("fc1", "fc2", "shared_up", "shared_down"):
+        for x, y in zip(got[key], layer[key]):
+            np.testing.assert_array_equal(x, y)
+    with pytest.raises(KeyError):
+        ck.sigmoid_moe_layer(2)
+
+
+def test_nemotron_checkpoint_through_the_oracle(tmp_path):
+    """The oracle's variant block over the loaded layer equals it over the source arrays."""
+    from oracle import oracle as O
+    layer = S.make_sigmoid_layer(NEMO, 14)
+    _write_nemotron(str(tmp_path), layer)
+    ck = CK.Checkpoint(str(tmp_path))
+    x = S.make_x(NEMO, 14)
+    ya = O.SigmoidLayer(NEMO, layer, ck.config.routing()).moe_block(x)[0]
+    yb = O.SigmoidLayer(NEMO, ck.sigmoid_moe_layer(1), ck.config.routing()).moe_block(x)[0]
+    np.testing.assert_array_equal(ya, yb)
