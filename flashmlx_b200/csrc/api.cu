@@ -1004,10 +1004,12 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k, Is = c->shared_inter;
   if (H <= 0 || I <= 0 || E <= 0 || k <= 0 || k > E || Is < 0) return set_err(h, FM_EINVAL, "bad MoE dimensions");
   if (E > fm::kMaxExperts || k > 16) return set_err(h, FM_EUNSUPPORTED, "num_experts > 512 or top_k > 16");
-  if (H % 128 || I % 128 || Is % 128)
-    return set_err(h, FM_EUNSUPPORTED, "hidden and intermediate sizes must be multiples of 128");
+  // the GEMV expert path reads K in 128-wide chunks plus at most one 64-wide half
+  // (group size 64), so the expert widths (the down matrices' K) need only be multiples of 64
+  if (H % 128 || I % 64 || Is % 64)
+    return set_err(h, FM_EUNSUPPORTED, "hidden must be a multiple of 128, the intermediate sizes of 64");
   if (!quant_ok(H, c->group_size, c->bits) || !quant_ok(I, c->group_size, c->bits) ||
-      (c->group_size != 64 && c->group_size != 128))
+      (Is > 0 && !quant_ok(Is, c->group_size, c->bits)) || (c->group_size != 64 && c->group_size != 128))
     return set_err(h, FM_EUNSUPPORTED, "variants run 4-bit affine weights with group size 64 or 128");
   if (c->router_quantized || (Is > 0 && !ungated && c->shared_gate_quantized))
     return set_err(h, FM_EUNSUPPORTED, "quantized router / shared-expert gate not implemented");

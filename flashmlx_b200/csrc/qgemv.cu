@@ -15,6 +15,9 @@
 // term: s*sum((128+q)x) + (b - 128 s)*sum(x).  sum(x) per token and group comes from
 // one extra MMA against an all-ones A fragment.  Group sizes 64 and 128 (a 64-wide
 // half chunk never straddles a group); the host sends group size 32 to tcgen05.
+// K is a multiple of 128, or of 64 with group size 64 (K = 128 n + 64, e.g. the
+// expert width 1856 of Nemotron-3-Nano): the last chunk then holds one half, and its
+// second half runs with zero codes, scales, biases and activations.
 //
 // Work unit (one CTA of 4 warps): an output-row block x a chunk of <= 8 activation
 // rows (one MMA column tile) x an optional K split.  Warp w owns two 16-row MMA tiles:
@@ -118,7 +121,9 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
       brow[m] = Bm[m] ? Bm[m] + r * gpr : nullptr;
     }
 
-    const int kchunks = K / 128;
+    const int kfull = K / 128;                   // chunks with both 64-wide halves
+    const int kchunks = kfull + ((K & 127) != 0);  // + a trailing half chunk
+    const bool odd_gpr = gpr & 1;                // only with a trailing half (group size 64)
     const int kc0 = kchunks * ti.ks / ti.ksplit, kc1 = kchunks * (ti.ks + 1) / ti.ksplit;
     __syncthreads();  // every warp is done reading the ring of the previous unit
     // activation rows of the unit (<= 8): thread tid copies 16 bytes (two 8-byte copies)
@@ -132,7 +137,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
     }
     auto load_x = [&](int kc, int slot) {
       uint16_t* d = &s_x[slot][xr][xc * 8];
-      if (kc < kc1 && xsrc) {
+      if (kc < kc1 && xsrc && (kc < kfull || xc < 8)) {
         cp_async8(smem_u32(d), xsrc + kc * 128);
         cp_async8(smem_u32(d + 4), xsrc + kc * 128 + 4);
       } else {
@@ -153,7 +158,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
     uint2 W[RING][2][2][2];
     uint32_t S2[RING][2][2], B2[RING][2][2];
     auto load_chunk = [&](int kc, uint2 (&Wd)[2][2][2], uint32_t (&Sd)[2][2], uint32_t (&Bd)[2][2]) {
-      const bool in = kc < kc1;
+      const bool in = kc < kc1, full = kc < kfull;
 #pragma unroll
       for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -161,7 +166,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
           const bool v = in && (m == 0 ? mval0 : mval1);
           const uint32_t* wp = wrow[m] + 8 * h * kw + kc * 16;
           Wd[m][h][0] = v ? ldg_nc_v2(wp) : make_uint2(0, 0);
-          Wd[m][h][1] = v ? ldg_nc_v2(wp + 8) : make_uint2(0, 0);
+          Wd[m][h][1] = (v && full) ? ldg_nc_v2(wp + 8) : make_uint2(0, 0);
           const uint16_t* sp = srow[m] + 8 * h * gpr;
           const uint16_t* bp = brow[m] ? brow[m] + 8 * h * gpr : nullptr;
           if (gs128) {
@@ -169,9 +174,16 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
             const uint32_t bv = (v && bp) ? static_cast<uint32_t>(__ldg(bp + kc)) : 0u;
             Sd[m][h] = sv * 0x10001u;
             Bd[m][h] = bv * 0x10001u;
-          } else {  // groups 2kc, 2kc+1: one aligned 4-byte load (gpr is even)
+          } else if (!odd_gpr) {  // groups 2kc, 2kc+1: one aligned 4-byte load (gpr is even)
             Sd[m][h] = v ? __ldg(reinterpret_cast<const uint32_t*>(sp + 2 * kc)) : 0u;
             Bd[m][h] = (v && bp) ? __ldg(reinterpret_cast<const uint32_t*>(bp + 2 * kc)) : 0u;
+          } else {  // odd gpr: rows start on 2-byte boundaries; group 2kc+1 exists iff the chunk is full
+            const uint32_t slo = v ? static_cast<uint32_t>(__ldg(sp + 2 * kc)) : 0u;
+            const uint32_t shi = (v && full) ? static_cast<uint32_t>(__ldg(sp + 2 * kc + 1)) : 0u;
+            const uint32_t blo = (v && bp) ? static_cast<uint32_t>(__ldg(bp + 2 * kc)) : 0u;
+            const uint32_t bhi = (v && bp && full) ? static_cast<uint32_t>(__ldg(bp + 2 * kc + 1)) : 0u;
+            Sd[m][h] = slo | (shi << 16);
+            Bd[m][h] = blo | (bhi << 16);
           }
         }
     };

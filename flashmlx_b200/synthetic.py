@@ -116,11 +116,11 @@ def make_layer(shape: MoEShape, seed: int) -> dict:
 
 
 # The sigmoid-routed variant (fm_moe_block_variant), shaped like Nemotron-3-Nano's MoE
-# layers (hidden 2688, 128 experts, top-6, shared 3712, routed_scaling_factor 2.5,
-# renormalised) with the expert width rounded to a multiple of 128 (1856 -> 1792; the
-# kernels take multiples of 128).  Single-GPU bench workloads, not BASELINE configs.
+# layers (hidden 2688, 128 experts, top-6, expert width 1856, shared 3712,
+# routed_scaling_factor 2.5, renormalised).  Single-GPU bench workloads, not BASELINE
+# configs.
 VARIANT_CONFIGS = {
-    "nemotron_decode": (MoEShape("nemotron_decode", 2688, 1792, 128, 6, 32, True, 3712),
+    "nemotron_decode": (MoEShape("nemotron_decode", 2688, 1856, 128, 6, 32, True, 3712),
                         {"n_group": 1, "topk_group": 1, "routed_scaling_factor": 2.5}),
 }
 

@@ -25,10 +25,24 @@ def _shape(tokens, shared):
 @pytest.mark.parametrize("groups", [(1, 1), (4, 2)])
 @pytest.mark.parametrize("shared", [0, 256])
 def test_sigmoid_block_vs_oracle(tokens, groups, shared):
+    _check_sigmoid(_shape(tokens, shared), groups, 21)
+
+
+@pytest.mark.parametrize("tokens", [1, 9, 300])
+@pytest.mark.parametrize("widths", [(320, 0), (192, 448), (1856, 3712)])
+def test_sigmoid_block_half_chunk_widths(tokens, widths):
+    """Expert widths that are multiples of 64 but not 128 (Nemotron-3-Nano's 1856): the
+    down matrices' K ends in a 64-wide half chunk with an odd number of quant groups
+    per row; (192, 448) also splits the shared down's K over two work units."""
+    inter, shared = widths
+    _check_sigmoid(S.MoEShape("sig64", 512, inter, 32, 4, tokens, True, shared), (4, 2), 23)
+
+
+def _check_sigmoid(shape, groups, seed):
     from flashmlx_b200 import ops
-    shape = _shape(tokens, shared)
-    layer = S.make_sigmoid_layer(shape, 21)
-    x_np = S.make_x(shape, 21)
+    tokens, shared = shape.tokens, shape.shared_inter
+    layer = S.make_sigmoid_layer(shape, seed)
+    x_np = S.make_x(shape, seed)
     routing = {"n_group": groups[0], "topk_group": groups[1], "routed_scaling_factor": 2.5}
     blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", **routing)
     y, r = blk(ops.bf16_from_numpy(x_np, "cuda"), return_routing=True)
