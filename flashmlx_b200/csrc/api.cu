@@ -1029,6 +1029,18 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   }
   if (T < 0 || (T > 0 && (!x || !y))) return set_err(h, FM_EINVAL, "bad x / y / T");
   if (!aligned16(x) || !aligned16(y)) return set_err(h, FM_EINVAL, "x and y must be 16-byte aligned");
+  // A down K (I or Is) of 128 n + 64 runs the GEMV's half-chunk instance, which stages a
+  // work unit's scales / biases in shared memory by aligned 4-byte copies: at most 62
+  // groups per row and unit, 4-byte aligned scale / bias arrays
+  const int ksplit_sh = std::max(1, Is / std::max(1, I));
+  if ((I % 128) || (Is % 128)) {
+    auto a4 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; };
+    const int unit_sh = ((Is + 127) / 128 + ksplit_sh - 1) / ksplit_sh;  // 128-wide chunks per shared unit
+    if (I / 64 > 62 || 2 * unit_sh > 62)
+      return set_err(h, FM_EUNSUPPORTED, "expert widths of 128 n + 64 are implemented up to 3968");
+    if (!a4(w->down.scales) || !a4(w->down.biases) || (Is > 0 && (!a4(w->shared_down.scales) || !a4(w->shared_down.biases))))
+      return set_err(h, FM_EINVAL, "down scales / biases must be 4-byte aligned");
+  }
   if (T == 0) return FM_OK;
   if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
   const bool shared = Is > 0;
@@ -1079,7 +1091,7 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   ra.b_rows_per_block = 128;
   ra.chunk_max = 8;
   ra.chunk_align = 8;
-  ra.b_ksplit_shared = std::max(1, Is / std::max(1, I));
+  ra.b_ksplit_shared = ksplit_sh;
   ra.has_shared = shared ? 1 : 0;
   if (outs) {
     ra.out_topk_ids = outs->topk_ids;

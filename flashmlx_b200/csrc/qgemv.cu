@@ -15,9 +15,13 @@
 // term: s*sum((128+q)x) + (b - 128 s)*sum(x).  sum(x) per token and group comes from
 // one extra MMA against an all-ones A fragment.  Group sizes 64 and 128 (a 64-wide
 // half chunk never straddles a group); the host sends group size 32 to tcgen05.
-// K is a multiple of 128, or of 64 with group size 64 (K = 128 n + 64, e.g. the
-// expert width 1856 of Nemotron-3-Nano): the last chunk then holds one half, and its
-// second half runs with zero codes, scales, biases and activations.
+// K is a multiple of 128, or -- down matrices only, in the HALF instances -- of 64
+// with group size 64 (K = 128 n + 64, e.g. the expert width 1856 of Nemotron-3-Nano):
+// the last chunk then holds one half, and its second half runs with zero codes,
+// scales, biases and activations.  Such rows hold an odd number of quant groups, so
+// their scale / bias pairs are not 4-byte aligned; the HALF instances stage the unit's
+// scales and biases in shared memory once per unit (4-byte cp.async of the aligned
+// words around each row's range) instead of streaming them through the register ring.
 //
 // Work unit (one CTA of 4 warps): an output-row block x a chunk of <= 8 activation
 // rows (one MMA column tile) x an optional K split.  Warp w owns two 16-row MMA tiles:
@@ -39,6 +43,8 @@ namespace {
 
 constexpr int kGvThreads = 128;
 constexpr int kXStride = 132;  // staged activation row stride (bf16): 264 B keeps the 8-byte fragment reads conflict-free
+constexpr int kSbGroups = 62;  // HALF instances: at most 62 quant groups per row in one unit (host-checked)
+constexpr int kSbStride = 66;  // u16 per staged row: <= 32 words of groups; 33 words keep the 8 rows' reads conflict-free
 
 FM_DEV float swiglu1(float g, float u) {  // model.cpp:14-25, bf16 rounding per op
   const float gs = rbf(sigmoid_f(g));
@@ -65,11 +71,16 @@ FM_DEV void cp_async8(uint32_t dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
 }
 
+FM_DEV void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+
 }  // namespace
 
-template <int MODE>
+template <int MODE, bool HALF>
 __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) {
   constexpr bool kDown = MODE == MODE_DOWN || MODE == MODE_DOWN_F32;
+  static_assert(!HALF || kDown, "half chunks only on the down matrices");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const TileTable* tab = a.tab;
@@ -79,6 +90,12 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
   // three-slot ring of 8 activation rows x 128 K (the B operand of one chunk)
   __shared__ int s_tb[kMaxGroups];
   __shared__ __align__(16) uint16_t s_x[3][8][kXStride];
+  // HALF: scales [0, 128) and biases [128, 256) of the unit's rows (row 32 warp + 16 m + 8 h + g)
+  uint16_t* sb = nullptr;
+  if constexpr (HALF) {
+    __shared__ __align__(16) uint16_t s_sb[2 * kGvThreads * kSbStride];
+    sb = s_sb;
+  }
   const int ngroups = min(tab->num_groups, kMaxGroups);
   for (int i = threadIdx.x; i < ngroups; i += blockDim.x) s_tb[i] = tab->g[i].tile_begin;
   __syncthreads();
@@ -121,11 +138,50 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
       brow[m] = Bm[m] ? Bm[m] + r * gpr : nullptr;
     }
 
-    const int kfull = K / 128;                   // chunks with both 64-wide halves
-    const int kchunks = kfull + ((K & 127) != 0);  // + a trailing half chunk
-    const bool odd_gpr = gpr & 1;                // only with a trailing half (group size 64)
+    const int kfull = K / 128;  // chunks with both 64-wide halves
+    const int kchunks = HALF ? kfull + ((K & 127) != 0) : kfull;  // + a trailing half chunk
     const int kc0 = kchunks * ti.ks / ti.ksplit, kc1 = kchunks * (ti.ks + 1) / ti.ksplit;
-    __syncthreads();  // every warp is done reading the ring of the previous unit
+    __syncthreads();  // every warp is done reading the ring (and the staged scales) of the previous unit
+    // HALF: u16 index in sb of (row g + 8h of tile m, the unit's first group), biases + kBias
+    constexpr int kBias = kGvThreads * kSbStride;
+    uint32_t sbo[2][2] = {{0u, 0u}, {0u, 0u}};
+    if constexpr (HALF) {
+      const int gbase = 2 * kc0;                       // the unit's first quant group (group size 64)
+      const int ng = min(2 * (kc1 - kc0), gpr - gbase);  // its groups
+      if (ng > kSbGroups) {  // the host splits K so that this never happens
+        if (threadIdx.x == 0) report(a.err, DEVERR_CONFIG);
+        continue;
+      }
+      // staged rows: a warp's 32 rows (16 m + 8 h + j) of scales, then of biases, each
+      // from the aligned word holding group gbase on; lpr consecutive lanes copy
+      // consecutive words of one row (coalesced), 32 / lpr rows per pass
+      const int lpr = ng <= 30 ? 16 : 32;  // a row's words: at most (ng + 2) / 2 <= 32
+      for (int rw = lane / lpr; ng > 0 && rw < 64; rw += 32 / lpr) {  // rw = 32 * (bias) + local row;
+                                                                      // an empty unit copies nothing
+        const int w = lane & (lpr - 1);
+        const int lr = rw & 31;
+        const int rl = r0[0] + lr;  // down modes: the warp's rows are contiguous (r0[1] = r0[0] + 16)
+        if (rl >= N) continue;      // whole 16-row tile past N: never read
+        const uint16_t* base = (rw >> 5) ? Bm[0] : Sm[0];  // one matrix in the down modes
+        if (!base) continue;
+        const int64_t e = (erow + rl) * gpr + gbase;
+        const int off = static_cast<int>(e & 1);
+        // words [e - off, e - off + 2 nw) cover the row's groups [e, e + ng); the one u16
+        // past them (off + ng odd) lies inside the array, whose length (rows x groups, rows
+        // a multiple of 16) is even from a 4-byte aligned base
+        if (w >= ((off + ng + 1) >> 1)) continue;
+        uint16_t* d = sb + (rw >> 5) * kBias + (warp * 32 + lr) * kSbStride + 2 * w;
+        cp_async4(smem_u32(d), base + (e - off) + 2 * w);
+      }
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int rl = min(r0[m] + g + 8 * h, N - 1);
+          const int off = static_cast<int>(((erow + rl) * gpr + gbase) & 1);
+          sbo[m][h] = (warp * 32 + 16 * m + 8 * h + g) * kSbStride + off;
+        }
+    }
     // activation rows of the unit (<= 8): thread tid copies 16 bytes (two 8-byte copies)
     // of row tid / 16 per chunk into the ring; rows past the unit are zero-filled
     const int xr = threadIdx.x >> 4, xc = threadIdx.x & 15;
@@ -137,7 +193,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
     }
     auto load_x = [&](int kc, int slot) {
       uint16_t* d = &s_x[slot][xr][xc * 8];
-      if (kc < kc1 && xsrc && (kc < kfull || xc < 8)) {
+      if (kc < kc1 && xsrc && (!HALF || kc < kfull || xc < 8)) {
         cp_async8(smem_u32(d), xsrc + kc * 128);
         cp_async8(smem_u32(d + 4), xsrc + kc * 128 + 4);
       } else {
@@ -158,7 +214,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
     uint2 W[RING][2][2][2];
     uint32_t S2[RING][2][2], B2[RING][2][2];
     auto load_chunk = [&](int kc, uint2 (&Wd)[2][2][2], uint32_t (&Sd)[2][2], uint32_t (&Bd)[2][2]) {
-      const bool in = kc < kc1, full = kc < kfull;
+      const bool in = kc < kc1, full = !HALF || kc < kfull;
 #pragma unroll
       for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -167,6 +223,7 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
           const uint32_t* wp = wrow[m] + 8 * h * kw + kc * 16;
           Wd[m][h][0] = v ? ldg_nc_v2(wp) : make_uint2(0, 0);
           Wd[m][h][1] = (v && full) ? ldg_nc_v2(wp + 8) : make_uint2(0, 0);
+          if constexpr (HALF) continue;  // scales and biases come from shared memory
           const uint16_t* sp = srow[m] + 8 * h * gpr;
           const uint16_t* bp = brow[m] ? brow[m] + 8 * h * gpr : nullptr;
           if (gs128) {
@@ -174,16 +231,9 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
             const uint32_t bv = (v && bp) ? static_cast<uint32_t>(__ldg(bp + kc)) : 0u;
             Sd[m][h] = sv * 0x10001u;
             Bd[m][h] = bv * 0x10001u;
-          } else if (!odd_gpr) {  // groups 2kc, 2kc+1: one aligned 4-byte load (gpr is even)
+          } else {  // groups 2kc, 2kc+1: one aligned 4-byte load (gpr is even)
             Sd[m][h] = v ? __ldg(reinterpret_cast<const uint32_t*>(sp + 2 * kc)) : 0u;
             Bd[m][h] = (v && bp) ? __ldg(reinterpret_cast<const uint32_t*>(bp + 2 * kc)) : 0u;
-          } else {  // odd gpr: rows start on 2-byte boundaries; group 2kc+1 exists iff the chunk is full
-            const uint32_t slo = v ? static_cast<uint32_t>(__ldg(sp + 2 * kc)) : 0u;
-            const uint32_t shi = (v && full) ? static_cast<uint32_t>(__ldg(sp + 2 * kc + 1)) : 0u;
-            const uint32_t blo = (v && bp) ? static_cast<uint32_t>(__ldg(bp + 2 * kc)) : 0u;
-            const uint32_t bhi = (v && bp && full) ? static_cast<uint32_t>(__ldg(bp + 2 * kc + 1)) : 0u;
-            Sd[m][h] = slo | (shi << 16);
-            Bd[m][h] = blo | (bhi << 16);
           }
         }
     };
@@ -223,10 +273,20 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
         // this half's quant group: y += s * acc + (b - 128 s) * sum(x)
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
-          const float s0 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][0] >> 16 : S2[SL][m][0] & 0xffffu));
-          const float s8 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][1] >> 16 : S2[SL][m][1] & 0xffffu));
-          const float b0 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][0] >> 16 : B2[SL][m][0] & 0xffffu));
-          const float b8 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][1] >> 16 : B2[SL][m][1] & 0xffffu));
+          float s0, s8, b0, b8;
+          if constexpr (HALF) {  // group 2(kc - kc0) + hf of the unit; the empty half of a trailing chunk is 0
+            const bool gv = hf == 0 || kc < kfull;
+            const uint32_t q = 2 * (kc - kc0) + hf;
+            s0 = gv ? bf2f(sb[sbo[m][0] + q]) : 0.f;
+            s8 = gv ? bf2f(sb[sbo[m][1] + q]) : 0.f;
+            b0 = (gv && Bm[m]) ? bf2f(sb[kBias + sbo[m][0] + q]) : 0.f;
+            b8 = (gv && Bm[m]) ? bf2f(sb[kBias + sbo[m][1] + q]) : 0.f;
+          } else {
+            s0 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][0] >> 16 : S2[SL][m][0] & 0xffffu));
+            s8 = bf2f(static_cast<uint16_t>(hf ? S2[SL][m][1] >> 16 : S2[SL][m][1] & 0xffffu));
+            b0 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][0] >> 16 : B2[SL][m][0] & 0xffffu));
+            b8 = bf2f(static_cast<uint16_t>(hf ? B2[SL][m][1] >> 16 : B2[SL][m][1] & 0xffffu));
+          }
           const float c0 = fmaf(-128.f, s0, b0), c8 = fmaf(-128.f, s8, b8);
           y[m][0] = fmaf(s0, acc[m][0], fmaf(c0, xsum[0], y[m][0]));
           y[m][1] = fmaf(s0, acc[m][1], fmaf(c0, xsum[1], y[m][1]));
@@ -288,19 +348,32 @@ __global__ void __launch_bounds__(kGvThreads, 3) qgemv_kernel(const GemmArgs a) 
   }
 }
 
+// A K (routed or shared) that is not a multiple of 128 takes the HALF instance of a
+// down mode; the host checks group size 64, 4-byte aligned scales / biases and at most
+// kSbGroups groups per row and unit.
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a) {
+  const bool half = (a.K & 127) || ((mode == MODE_DOWN || mode == MODE_DOWN_F32) && a.N_shared > 0 && (a.K_shared & 127));
+  if (half) {
+    if (a.gs != 64) return cudaErrorInvalidValue;
+    switch (mode) {
+      case MODE_DOWN: qgemv_kernel<MODE_DOWN, true><<<grid, kGvThreads, 0, stream>>>(a); break;
+      case MODE_DOWN_F32: qgemv_kernel<MODE_DOWN_F32, true><<<grid, kGvThreads, 0, stream>>>(a); break;
+      default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+  }
   switch (mode) {
-    case MODE_GATEUP: qgemv_kernel<MODE_GATEUP><<<grid, kGvThreads, 0, stream>>>(a); break;
-    case MODE_DOWN: qgemv_kernel<MODE_DOWN><<<grid, kGvThreads, 0, stream>>>(a); break;
-    case MODE_RELU2: qgemv_kernel<MODE_RELU2><<<grid, kGvThreads, 0, stream>>>(a); break;
-    case MODE_DOWN_F32: qgemv_kernel<MODE_DOWN_F32><<<grid, kGvThreads, 0, stream>>>(a); break;
-    default: qgemv_kernel<MODE_PLAIN><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_GATEUP: qgemv_kernel<MODE_GATEUP, false><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_DOWN: qgemv_kernel<MODE_DOWN, false><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_RELU2: qgemv_kernel<MODE_RELU2, false><<<grid, kGvThreads, 0, stream>>>(a); break;
+    case MODE_DOWN_F32: qgemv_kernel<MODE_DOWN_F32, false><<<grid, kGvThreads, 0, stream>>>(a); break;
+    default: qgemv_kernel<MODE_PLAIN, false><<<grid, kGvThreads, 0, stream>>>(a); break;
   }
   return cudaGetLastError();
 }
 
 cudaError_t qgemv_blocks_per_sm(int* n) {
-  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, qgemv_kernel<MODE_GATEUP>, kGvThreads, 0);
+  return cudaOccupancyMaxActiveBlocksPerMultiprocessor(n, qgemv_kernel<MODE_GATEUP, false>, kGvThreads, 0);
 }
 
 // y = bf16( bf16(y_acc) + bf16( bf16(sigmoid(gate)) * bf16(ysh) ) )   (model.cpp:800-803)
