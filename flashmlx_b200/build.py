@@ -1,4 +1,5 @@
-"""Builds libflashmoe.so (the C-ABI library) in-tree with nvcc for sm_100a.
+"""Builds libflashmoe.so (the C-ABI library) in-tree with nvcc for sm_100a, and the C++
+host layer's driver program fm_host (flashmlx_b200/host) with g++.
 
     python -m flashmlx_b200.build [--force]
 
@@ -62,5 +63,36 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+HOST = os.path.join(PKG, "host")
+HOST_SOURCES = ["checkpoint.cpp", "moe_model.cpp", "fm_host.cpp"]
+HOST_HEADERS = ["checkpoint.hpp", "moe_model.hpp", "flashmoe.hpp", "json.hpp"]
+HOST_EXE = os.path.join(LIB_DIR, "fm_host")
+
+
+def cuda_home() -> str:
+    return os.path.dirname(os.path.dirname(os.path.realpath(nvcc())))
+
+
+def build_host(force: bool = False) -> str:
+    """The C++ host layer's driver program (flashmlx_b200/host): g++, linked against
+    libflashmoe.so (found next to it at run time) and the static CUDA runtime.  Rebuilt
+    when a host source or the C header is newer; the CUDA library is built only if absent."""
+    if not os.path.exists(LIB):
+        build()
+    deps = [os.path.join(HOST, f) for f in HOST_SOURCES + HOST_HEADERS] + [os.path.join(INCLUDE, "flashmoe.h")]
+    if not force and os.path.exists(HOST_EXE) and all(os.path.getmtime(d) <= os.path.getmtime(HOST_EXE) for d in deps):
+        return HOST_EXE
+    cuda = cuda_home()
+    tmp = HOST_EXE + ".tmp"
+    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-I", INCLUDE, "-I", HOST,
+           "-I", os.path.join(cuda, "include"), *[os.path.join(HOST, f) for f in HOST_SOURCES],
+           "-L", LIB_DIR, "-lflashmoe", "-Wl,-rpath,$ORIGIN", "-L", os.path.join(cuda, "lib64"), "-lcudart_static",
+           "-ldl", "-lpthread", "-lrt", "-o", tmp]
+    subprocess.check_call(cmd)
+    os.replace(tmp, HOST_EXE)
+    return HOST_EXE
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_host(force="--force" in sys.argv))
