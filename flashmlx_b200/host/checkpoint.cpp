@@ -52,7 +52,8 @@ std::vector<T> copy_out(const TensorView& t) {
 }
 
 int to_int(double v, const char* key) {
-  if (v != static_cast<double>(static_cast<int>(v))) throw err(std::string("config.json: ") + key + " is not an integer");
+  if (!(v >= -2147483648.0 && v <= 2147483647.0) || v != static_cast<double>(static_cast<int>(v)))
+    throw err(std::string("config.json: ") + key + " is not an integer");
   return static_cast<int>(v);
 }
 
@@ -167,7 +168,9 @@ SafetensorsFile::SafetensorsFile(const std::string& path) {
     const json::Value* shape = info.find("shape");
     const json::Value* offs = info.find("data_offsets");
     if (!dt || dt->kind != json::Value::String || !shape || shape->kind != json::Value::Array || !offs ||
-        offs->kind != json::Value::Array || offs->arr.size() != 2) {
+        offs->kind != json::Value::Array || offs->arr.size() != 2 || offs->arr[0].kind != json::Value::Number ||
+        offs->arr[1].kind != json::Value::Number || offs->arr[0].num < 0 || offs->arr[1].num < 0 ||
+        offs->arr[0].num > 9.0e15 || offs->arr[1].num > 9.0e15) {
       unmap();
       throw err(path + ": " + name + ": malformed tensor record");
     }
@@ -179,7 +182,7 @@ SafetensorsFile::SafetensorsFile(const std::string& path) {
     }
     uint64_t numel = 1;
     for (const auto& d : shape->arr) {
-      if (d.kind != json::Value::Number || d.num < 0) {
+      if (d.kind != json::Value::Number || d.num < 0 || d.num > 9.0e15 || d.num != static_cast<double>(static_cast<int64_t>(d.num))) {
         unmap();
         throw err(path + ": " + name + ": bad shape");
       }
