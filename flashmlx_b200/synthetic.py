@@ -115,6 +115,66 @@ def make_layer(shape: MoEShape, seed: int) -> dict:
     return d
 
 
+@dataclasses.dataclass(frozen=True)
+class DecoderShape:
+    """A full decoder (LlamaModel with MoE layers): attention shape, vocabulary, norms,
+    and the MoE layer shape of every layer (tokens unused)."""
+    name: str
+    hidden: int
+    layers: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    rope_theta: float
+    rms_eps: float
+    moe: MoEShape
+    attn_bias: bool = True            # q/k/v biases (Qwen2-MoE), model.cpp:560-566
+    tie_word_embeddings: bool = False
+    group_size: int = 64
+    bits: int = 4
+
+
+# configs[2]: the 24-layer Qwen1.5-MoE-A2.7B-shaped decoder, every MoE block as configs[0]
+DECODER_CONFIGS = {
+    "qwen15_decoder": DecoderShape("qwen15_decoder", 2048, 24, 16, 16, 128, 151936, 1e6, 1e-6,
+                                   MoEShape("qwen15_moe", 2048, 1408, 60, 4, 0, False, 5632)),
+}
+
+
+def make_decoder(shape: DecoderShape, seed: int) -> dict:
+    """Random-init weights of a decoder (numpy, bf16 as uint16): the 4-bit embedding
+    `embed` (w, s, b) [V, H]; per layer `in_norm`, `post_norm` [H], 4-bit `q`, `k`, `v`, `o`,
+    bf16 `q_bias`, `k_bias`, `v_bias`, and the MoE layer `moe` (make_layer); `norm` [H] and
+    the 4-bit `lm_head` [V, H] unless the embeddings are tied."""
+    H, nh, nkv, d = shape.hidden, shape.n_heads, shape.n_kv_heads, shape.head_dim
+    gs, bits = shape.group_size, shape.bits
+
+    def norm_w(name):  # around 1, as trained RMSNorm weights are
+        return f32_to_bf16(1.0 + 0.1 * _rng(seed, name).standard_normal(H, dtype=np.float32))
+
+    def bias(name, n):
+        return f32_to_bf16(0.02 * _rng(seed, name).standard_normal(n, dtype=np.float32))
+
+    w = {"embed": make_qmatrix(seed, "embed", (), shape.vocab, H, gs, bits, scale_std=0.1),
+         "norm": norm_w("norm"), "layers": []}
+    if not shape.tie_word_embeddings:
+        w["lm_head"] = make_qmatrix(seed, "lm_head", (), shape.vocab, H, gs, bits)
+    for li in range(shape.layers):
+        p = f"layers.{li}."
+        lw = {"in_norm": norm_w(p + "in_norm"), "post_norm": norm_w(p + "post_norm"),
+              "q": make_qmatrix(seed, p + "q", (), nh * d, H, gs, bits),
+              "k": make_qmatrix(seed, p + "k", (), nkv * d, H, gs, bits),
+              "v": make_qmatrix(seed, p + "v", (), nkv * d, H, gs, bits),
+              "o": make_qmatrix(seed, p + "o", (), H, nh * d, gs, bits),
+              "moe": make_layer(shape.moe, seed * 1000 + li)}
+        if shape.attn_bias:
+            lw["q_bias"], lw["k_bias"], lw["v_bias"] = bias(p + "qb", nh * d), bias(p + "kb", nkv * d), bias(
+                p + "vb", nkv * d)
+        w["layers"].append(lw)
+    return w
+
+
 # The sigmoid-routed variant (fm_moe_block_variant), shaped like Nemotron-3-Nano's MoE
 # layers (hidden 2688, 128 experts, top-6, expert width 1856, shared 3712,
 # routed_scaling_factor 2.5, renormalised).  Single-GPU bench workloads, not BASELINE
