@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libflashmoe.so")
-SOURCES = ["route.cu", "qgemv.cu", "qgemm_tc.cu", "ep.cu", "api.cu"]
+SOURCES = ["route.cu", "qgemv.cu", "qgemm_tc.cu", "ep.cu", "decoder.cu", "api.cu"]
 HEADERS = ["fm_common.cuh", "fm_internal.cuh", "fm_ep.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -64,8 +64,10 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 
 HOST = os.path.join(PKG, "host")
-HOST_SOURCES = ["checkpoint.cpp", "moe_model.cpp", "fm_host.cpp"]
-HOST_HEADERS = ["checkpoint.hpp", "moe_model.hpp", "flashmoe.hpp", "json.hpp"]
+HOST_LIB_SOURCES = ["checkpoint.cpp", "moe_model.cpp", "decoder.cpp"]
+HOST_HEADERS = ["checkpoint.hpp", "moe_model.hpp", "decoder.hpp", "device_store.hpp", "flashmoe.hpp", "json.hpp",
+                "fmh.h"]
+HOST_LIB = os.path.join(LIB_DIR, "libflashmoe_host.so")
 HOST_EXE = os.path.join(LIB_DIR, "fm_host")
 
 
@@ -74,21 +76,31 @@ def cuda_home() -> str:
 
 
 def build_host(force: bool = False) -> str:
-    """The C++ host layer's driver program (flashmlx_b200/host): g++, linked against
-    libflashmoe.so (found next to it at run time) and the static CUDA runtime.  Rebuilt
-    when a host source or the C header is newer; the CUDA library is built only if absent."""
+    """The C++ host layer (flashmlx_b200/host) with g++: libflashmoe_host.so (loader,
+    MoEModel, Decoder and its C interface fmh.h) and the fm_host driver program, linked
+    against libflashmoe.so (found next to them at run time) and the static CUDA runtime
+    (its symbols kept private).  Rebuilt when a host source or a C header is newer; the
+    CUDA library is built only if absent."""
     if not os.path.exists(LIB):
         build()
-    deps = [os.path.join(HOST, f) for f in HOST_SOURCES + HOST_HEADERS] + [os.path.join(INCLUDE, "flashmoe.h")]
-    if not force and os.path.exists(HOST_EXE) and all(os.path.getmtime(d) <= os.path.getmtime(HOST_EXE) for d in deps):
+    deps = [os.path.join(HOST, f) for f in HOST_LIB_SOURCES + HOST_HEADERS + ["fm_host.cpp"]]
+    deps.append(os.path.join(INCLUDE, "flashmoe.h"))
+    outs = (HOST_LIB, HOST_EXE)
+    if not force and all(os.path.exists(o) for o in outs) and \
+            max(os.path.getmtime(d) for d in deps) <= min(os.path.getmtime(o) for o in outs):
         return HOST_EXE
     cuda = cuda_home()
+    cxx = shutil.which("g++") or "g++"
+    common = ["-std=c++17", "-O2", "-Wall", "-Wextra", "-I", INCLUDE, "-I", HOST, "-I", os.path.join(cuda, "include")]
+    cudart = ["-L", os.path.join(cuda, "lib64"), "-lcudart_static", "-ldl", "-lpthread", "-lrt"]
+    tmp = HOST_LIB + ".tmp"
+    subprocess.check_call([cxx, *common, "-fPIC", "-shared", *[os.path.join(HOST, f) for f in HOST_LIB_SOURCES],
+                           "-L", LIB_DIR, "-lflashmoe", "-Wl,-rpath,$ORIGIN", "-Wl,--exclude-libs,ALL", *cudart,
+                           "-o", tmp])
+    os.replace(tmp, HOST_LIB)
     tmp = HOST_EXE + ".tmp"
-    cmd = [shutil.which("g++") or "g++", "-std=c++17", "-O2", "-Wall", "-Wextra", "-I", INCLUDE, "-I", HOST,
-           "-I", os.path.join(cuda, "include"), *[os.path.join(HOST, f) for f in HOST_SOURCES],
-           "-L", LIB_DIR, "-lflashmoe", "-Wl,-rpath,$ORIGIN", "-L", os.path.join(cuda, "lib64"), "-lcudart_static",
-           "-ldl", "-lpthread", "-lrt", "-o", tmp]
-    subprocess.check_call(cmd)
+    subprocess.check_call([cxx, *common, os.path.join(HOST, "fm_host.cpp"), "-L", LIB_DIR, "-lflashmoe_host",
+                           "-lflashmoe", "-Wl,-rpath,$ORIGIN", *cudart, "-o", tmp])
     os.replace(tmp, HOST_EXE)
     return HOST_EXE
 

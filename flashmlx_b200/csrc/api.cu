@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 #include <cstdio>
 #include <cstring>
@@ -39,6 +40,17 @@ __global__ void ep_combine_p2p_kernel(const EpP2PArgs a, const int32_t* pair_pos
                                       const float* ysh32, const uint16_t* ysh16, const float* gate_sig, int64_t T,
                                       uint16_t* y);
 cudaError_t launch_qgemv(int mode, int grid, cudaStream_t stream, const GemmArgs& a);
+cudaError_t launch_dequant(const uint32_t* w, const uint16_t* s, const uint16_t* b, int64_t N, int K, int gs,
+                           uint16_t* out, int num_sms, cudaStream_t st);
+cudaError_t launch_embed(const uint16_t* table, int64_t V, int H, const int32_t* ids, int64_t T, uint16_t* y,
+                         uint32_t* err, int num_sms, cudaStream_t st);
+cudaError_t launch_rms_norm(const uint16_t* x, const uint16_t* r, const uint16_t* w, int64_t T, int H, float eps,
+                            uint16_t* h_out, uint16_t* y, cudaStream_t st);
+cudaError_t attn_init();
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t st);
+cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out, int num_sms,
+                          cudaStream_t st);
+cudaError_t launch_argmax(const uint16_t* logits, int64_t T, int64_t V, int32_t* ids, cudaStream_t st);
 cudaError_t qgemv_blocks_per_sm(int* n);
 namespace tc {
 int max_rows();
@@ -693,6 +705,7 @@ int fm_create(fm_handle** out, int device, void* stream) {
   if (e == cudaSuccess) e = fm::tc::init();
   if (e == cudaSuccess) e = fm::tc::max_pairs(&h->tc_pairs);
   if (e == cudaSuccess && h->tc_pairs < 1) e = cudaErrorInvalidConfiguration;
+  if (e == cudaSuccess) e = fm::attn_init();
   if (e != cudaSuccess) {
     cudaGetLastError();
     delete h;
@@ -1616,6 +1629,122 @@ int fm_quantized_matmul(fm_handle* h, const uint16_t* x, int64_t M, int K, const
   // one expert, one batch of M rows: gather_qmm with E = 1 and no indices
   return fm_gather_qmm(h, x, 1, static_cast<int>(M), K, w, scales, biases, 1, N, nullptr, nullptr, 1, transpose,
                        group_size, bits, 1, out);
+}
+
+// ---------------------------------------------------------------- decoder ops (decoder.cu)
+
+int fm_dequantize(fm_handle* h, const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int64_t N, int K,
+                  int group_size, int bits, uint16_t* out) {
+  if (!h) return FM_EINVAL;
+  if (!quant_ok(K, group_size, bits) || K % 8) return set_err(h, FM_EUNSUPPORTED, "only 4-bit affine, group 32/64/128");
+  if (N < 0) return set_err(h, FM_EINVAL, "negative N");
+  if (N == 0) return FM_OK;
+  if (!w || !scales || !out) return set_err(h, FM_EINVAL, "null pointer");
+  if (!aligned16(out) || (reinterpret_cast<uintptr_t>(w) & 3)) return set_err(h, FM_EINVAL, "misaligned pointer");
+  prof_begin(h, "dequantize");
+  const cudaError_t e = fm::launch_dequant(w, scales, biases, N, K, group_size, out, h->num_sms, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "dequantize launch");
+}
+
+int fm_embed(fm_handle* h, const uint16_t* table, int64_t V, int H, const int32_t* ids, int64_t T, uint16_t* y) {
+  if (!h) return FM_EINVAL;
+  if (V <= 0 || H <= 0 || H % 8 || T < 0) return set_err(h, FM_EINVAL, "bad sizes (H % 8 == 0)");
+  if (T == 0) return FM_OK;
+  if (!table || !ids || !y) return set_err(h, FM_EINVAL, "null pointer");
+  if (!aligned16(table) || !aligned16(y)) return set_err(h, FM_EINVAL, "table and y must be 16-byte aligned");
+  prof_begin(h, "embed");
+  const cudaError_t e = fm::launch_embed(table, V, H, ids, T, y, err_word(h), h->num_sms, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "embed launch");
+}
+
+int fm_rms_norm(fm_handle* h, const uint16_t* x, const uint16_t* residual, const uint16_t* weight, int64_t T, int H,
+                float eps, uint16_t* h_out, uint16_t* y) {
+  if (!h) return FM_EINVAL;
+  if (H <= 0 || H % 8 || T < 0 || !(eps >= 0.f)) return set_err(h, FM_EINVAL, "bad sizes (H % 8 == 0) or eps");
+  if (T == 0) return FM_OK;
+  if (T > 0x7fffffffLL) return set_err(h, FM_EUNSUPPORTED, "too many rows");
+  if (!x || !weight || !y) return set_err(h, FM_EINVAL, "null pointer");
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (residual && !aligned16(residual)) ||
+      (h_out && !aligned16(h_out)))
+    return set_err(h, FM_EINVAL, "rows must be 16-byte aligned");
+  if (y == x || y == residual) return set_err(h, FM_EINVAL, "y may not alias x or residual");
+  prof_begin(h, "rms_norm");
+  const cudaError_t e = fm::launch_rms_norm(x, residual, weight, T, H, eps, h_out, y, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "rms_norm launch");
+}
+
+int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uint16_t* k, const uint16_t* v,
+                 const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, uint16_t* cache_k,
+                 uint16_t* cache_v, int B, int L, int offset, uint16_t* out) {
+  if (!h) return FM_EINVAL;
+  if (!cfg) return set_err(h, FM_EINVAL, "null config");
+  const int nh = cfg->n_heads, nkv = cfg->n_kv_heads, d = cfg->head_dim;
+  if (nh <= 0 || nkv <= 0 || nh % nkv || cfg->max_len <= 0 || !(cfg->rope_theta > 0.f))
+    return set_err(h, FM_EINVAL, "bad attention config");
+  if (d != 64 && d != 128) return set_err(h, FM_EUNSUPPORTED, "head_dim must be 64 or 128");
+  if (B < 0 || L < 0 || offset < 0) return set_err(h, FM_EINVAL, "negative B, L or offset");
+  if (B == 0 || L == 0) return FM_OK;
+  if (static_cast<int64_t>(offset) + L > cfg->max_len) return set_err(h, FM_EINVAL, "offset + L exceeds max_len");
+  if (static_cast<int64_t>(B) * L > 0x7fffffffLL / (nh + 2 * nkv) || nh > 65535 || B > 65535)
+    return set_err(h, FM_EUNSUPPORTED, "too many tokens or heads");
+  if (!q || !k || !v || !cache_k || !cache_v || !out) return set_err(h, FM_EINVAL, "null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(cache_k) || !aligned16(cache_v) ||
+      !aligned16(out))
+    return set_err(h, FM_EINVAL, "q, k, v, caches and out must be 16-byte aligned");
+  if (out == q) return set_err(h, FM_EINVAL, "out may not alias q");
+  fm::AttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.q_bias = q_bias;
+  a.k_bias = k_bias;
+  a.v_bias = v_bias;
+  a.cache_k = cache_k;
+  a.cache_v = cache_v;
+  a.out = out;
+  a.q_ld = static_cast<int64_t>(nh) * d;
+  a.kv_ld = static_cast<int64_t>(nkv) * d;
+  a.out_ld = static_cast<int64_t>(nh) * d;
+  a.B = B;
+  a.L = L;
+  a.offset = offset;
+  a.nh = nh;
+  a.nkv = nkv;
+  a.head_dim = d;
+  a.max_len = cfg->max_len;
+  a.scale = cfg->scale != 0.f ? cfg->scale : 1.0f / std::sqrt(static_cast<float>(d));
+  a.log2_theta = std::log2(static_cast<double>(cfg->rope_theta));
+  prof_begin(h, "attention");
+  const cudaError_t e = fm::launch_attention(a, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "attention launch");
+}
+
+int fm_swiglu(fm_handle* h, const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out) {
+  if (!h) return FM_EINVAL;
+  if (n < 0) return set_err(h, FM_EINVAL, "negative n");
+  if (n == 0) return FM_OK;
+  if (!gate || !up || !out) return set_err(h, FM_EINVAL, "null pointer");
+  prof_begin(h, "swiglu");
+  const cudaError_t e = fm::launch_swiglu(gate, up, n, out, h->num_sms, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "swiglu launch");
+}
+
+int fm_argmax(fm_handle* h, const uint16_t* logits, int64_t T, int64_t V, int32_t* ids) {
+  if (!h) return FM_EINVAL;
+  if (T < 0 || V <= 0 || V > 0x7fffffffLL) return set_err(h, FM_EINVAL, "bad sizes");
+  if (T == 0) return FM_OK;
+  if (T > 0x7fffffffLL) return set_err(h, FM_EUNSUPPORTED, "too many rows");
+  if (!logits || !ids) return set_err(h, FM_EINVAL, "null pointer");
+  prof_begin(h, "argmax");
+  const cudaError_t e = fm::launch_argmax(logits, T, V, ids, h->stream);
+  prof_end(h);
+  return e == cudaSuccess ? FM_OK : cuda_err(h, e, "argmax launch");
 }
 
 }  // extern "C"

@@ -244,6 +244,24 @@ struct EpP2PArgs {
   uint32_t* err;
 };
 
+// The attention step of a decoder layer (decoder.cu): q / k / v projections in, the KV
+// cache updated, the attention rows out.  Activations are token-major [B * L, n * d].
+struct AttnArgs {
+  uint16_t* q;              // [B*L, q_ld] projections; rotated in place
+  const uint16_t* k;        // [B*L, kv_ld]
+  const uint16_t* v;        // [B*L, kv_ld]
+  const uint16_t* q_bias;   // [nh * d] or null
+  const uint16_t* k_bias;   // [nkv * d] or null
+  const uint16_t* v_bias;   // [nkv * d] or null
+  uint16_t* cache_k;        // [B, nkv, max_len, d]
+  uint16_t* cache_v;
+  uint16_t* out;            // [B*L, out_ld]
+  int64_t q_ld, kv_ld, out_ld;
+  int B, L, offset, nh, nkv, head_dim, max_len;
+  float scale;              // softmax scale (1/sqrt(d) by default)
+  double log2_theta;        // log2 of the RoPE base
+};
+
 constexpr int kRouteThreads = 256;  // 8 warps
 constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
 constexpr int kRouterMaxKsplit = 16;  // K slices of the router partial logits

@@ -98,7 +98,15 @@ ModelConfig load_config(const std::string& model_dir) {
   if (!c.is_object()) throw err(model_dir + "/config.json: not a JSON object");
   ModelConfig m;
   m.hidden_size = to_int(c.number_or("hidden_size", 4096), "hidden_size");
+  m.intermediate_size = to_int(c.number_or("intermediate_size", 14336), "intermediate_size");
   m.num_hidden_layers = to_int(c.number_or("num_hidden_layers", 32), "num_hidden_layers");
+  m.num_attention_heads = to_int(c.number_or("num_attention_heads", 32), "num_attention_heads");
+  m.num_key_value_heads = to_int(c.number_or("num_key_value_heads", 8), "num_key_value_heads");
+  m.head_dim = to_int(c.number_or("head_dim", 0), "head_dim");
+  m.vocab_size = to_int(c.number_or("vocab_size", 128256), "vocab_size");
+  m.rms_norm_eps = static_cast<float>(c.number_or("rms_norm_eps", 1e-5));
+  m.rope_theta = static_cast<float>(c.number_or("rope_theta", 10000.0));
+  m.tie_word_embeddings = c.bool_or("tie_word_embeddings", true);
   m.num_experts = to_int(c.number_or("num_experts", 0), "num_experts");
   m.n_routed_experts = to_int(c.number_or("n_routed_experts", 0), "n_routed_experts");
   m.num_experts_per_tok = to_int(c.number_or("num_experts_per_tok", 0), "num_experts_per_tok");

@@ -30,10 +30,19 @@
 
 namespace flashmoe {
 
-// The ModelConfig fields (server/include/flashmlx/model.h) the MoE layers use.
+// The ModelConfig fields (server/include/flashmlx/model.h) the decoder uses, with
+// LlamaModel::load_config's defaults (server/src/model.cpp:105-142).
 struct ModelConfig {
   int hidden_size = 4096;
+  int intermediate_size = 14336;
   int num_hidden_layers = 32;
+  int num_attention_heads = 32;
+  int num_key_value_heads = 8;
+  int head_dim = 0;  // 0: hidden_size / num_attention_heads
+  int vocab_size = 128256;
+  float rms_norm_eps = 1e-5f;
+  float rope_theta = 10000.0f;
+  bool tie_word_embeddings = true;
   int quant_bits = 0;  // 0 = not quantized
   int quant_group_size = 64;
   int num_experts = 0;
@@ -53,6 +62,7 @@ struct ModelConfig {
   // a Nemotron-H model: MoE layers are the 'E' entries of hybrid_override_pattern
   bool sigmoid_routed() const { return hybrid_override_pattern.find('E') != std::string::npos; }
   int experts() const { return num_experts ? num_experts : n_routed_experts; }
+  int attn_head_dim() const { return head_dim > 0 ? head_dim : hidden_size / num_attention_heads; }
   int shared_inter() const {
     if (shared_expert_intermediate_size) return shared_expert_intermediate_size;
     return n_shared_experts ? moe_shared_expert_intermediate_size : 0;

@@ -5,6 +5,11 @@
 //                                        little-endian files OUT/<name>.bin + OUT/manifest.json
 //   fm_host run DIR LAYER X T Y [DEV]    y = moe_block(x, LAYER) on the GPU: X holds T x hidden
 //                                        bf16 (raw), Y receives the same
+//   fm_host check-decoder DIR            the decoder layout of a model directory, checked (JSON)
+//   fm_host generate DIR P B L STEPS OUT [DEV]
+//                                        greedy decoding with the whole model (Decoder): P
+//                                        holds B x L int32 prompt tokens, OUT receives
+//                                        B x STEPS int32 tokens
 //
 // Exit status: 0 ok; 2 usage; 3 a libflashmoe status (the status name and message on
 // stderr, "fm_status <n>" on the first line); 4 any other error.
@@ -20,6 +25,7 @@
 #include <vector>
 
 #include "checkpoint.hpp"
+#include "decoder.hpp"
 #include "moe_model.hpp"
 
 using namespace flashmoe;
@@ -58,7 +64,11 @@ int inspect(const std::string& dir) {
     << ",\"shared_inter\":" << c.shared_inter() << ",\"norm_topk_prob\":" << (c.norm_topk_prob ? "true" : "false")
     << ",\"bits\":" << c.quant_bits << ",\"group_size\":" << c.quant_group_size << ",\"n_group\":" << c.n_group
     << ",\"topk_group\":" << c.topk_group << ",\"routed_scaling_factor\":" << c.routed_scaling_factor
-    << ",\"sigmoid_routed\":" << (c.sigmoid_routed() ? "true" : "false") << ",\"moe_layers\":[";
+    << ",\"sigmoid_routed\":" << (c.sigmoid_routed() ? "true" : "false") << ",\"n_heads\":" << c.num_attention_heads
+    << ",\"n_kv_heads\":" << c.num_key_value_heads << ",\"head_dim\":" << c.attn_head_dim()
+    << ",\"vocab\":" << c.vocab_size << ",\"intermediate\":" << c.intermediate_size
+    << ",\"rms_eps\":" << c.rms_norm_eps << ",\"rope_theta\":" << c.rope_theta
+    << ",\"tie_word_embeddings\":" << (c.tie_word_embeddings ? "true" : "false") << ",\"moe_layers\":[";
   const std::vector<int> layers = ck.moe_layers();
   for (size_t i = 0; i < layers.size(); ++i) o << (i ? "," : "") << layers[i];
   o << "]}";
@@ -155,8 +165,48 @@ int run(const std::string& dir, int layer, const std::string& xpath, int64_t T, 
   return 0;
 }
 
+int generate(const std::string& dir, const std::string& ppath, int B, int L, int steps, const std::string& opath,
+             int dev) {
+  if (B <= 0 || L <= 0 || steps <= 0) throw std::runtime_error("B, L and STEPS must be positive");
+  std::vector<int32_t> prompt(static_cast<size_t>(B) * L);
+  {
+    std::ifstream f(ppath, std::ios::binary);
+    if (!f) throw std::runtime_error(ppath + ": cannot open");
+    f.read(reinterpret_cast<char*>(prompt.data()), static_cast<std::streamsize>(prompt.size() * 4));
+    if (f.gcount() != static_cast<std::streamsize>(prompt.size() * 4))
+      throw std::runtime_error(ppath + ": holds fewer than B x L int32 tokens");
+  }
+  auto dec = Decoder::open(dir, dev, B, L + steps, nullptr);
+  const std::vector<int32_t> out = dec->generate(prompt.data(), B, L, steps);
+  write_raw(opath, out);
+  return 0;
+}
+
+// the decoder layout of a model directory, checked without a device (plan_decoder)
+int check_decoder(const std::string& dir) {
+  Checkpoint ck(dir);
+  const DecoderPlan p = plan_decoder(ck);
+  std::ostringstream o;
+  o << "{\"layers\":" << p.cfg.layers << ",\"moe_layers\":[";
+  bool first = true;
+  for (int i = 0; i < p.cfg.layers; ++i)
+    if (p.layers[i].is_moe) {
+      o << (first ? "" : ",") << i;
+      first = false;
+      (void)ck.moe_layer(i);  // the MoE layer's own checks
+    }
+  bool bias = p.cfg.layers > 0;
+  for (const auto& l : p.layers) bias = bias && l.q_bias && l.k_bias && l.v_bias;
+  o << "],\"attn_bias\":" << (bias ? "true" : "false") << ",\"embed_quantized\":" << (p.embed.w ? "true" : "false")
+    << ",\"tie_word_embeddings\":" << (p.cfg.tie_word_embeddings ? "true" : "false") << ",\"head_dim\":"
+    << p.cfg.head_dim << ",\"vocab\":" << p.cfg.vocab << "}";
+  std::cout << o.str() << std::endl;
+  return 0;
+}
+
 int usage() {
-  std::cerr << "usage: fm_host inspect DIR | dump DIR LAYER OUT | run DIR LAYER X T Y [DEVICE]\n";
+  std::cerr << "usage: fm_host inspect DIR | dump DIR LAYER OUT | run DIR LAYER X T Y [DEVICE] |"
+               " check-decoder DIR | generate DIR PROMPT B L STEPS OUT [DEVICE]\n";
   return 2;
 }
 
@@ -170,6 +220,10 @@ int main(int argc, char** argv) {
     if (cmd == "dump" && argc == 5) return dump(argv[2], std::atoi(argv[3]), argv[4]);
     if (cmd == "run" && (argc == 7 || argc == 8))
       return run(argv[2], std::atoi(argv[3]), argv[4], std::atoll(argv[5]), argv[6], argc == 8 ? std::atoi(argv[7]) : 0);
+    if (cmd == "check-decoder" && argc == 3) return check_decoder(argv[2]);
+    if (cmd == "generate" && (argc == 8 || argc == 9))
+      return generate(argv[2], argv[3], std::atoi(argv[4]), std::atoi(argv[5]), std::atoi(argv[6]), argv[7],
+                      argc == 9 ? std::atoi(argv[8]) : 0);
     return usage();
   } catch (const Error& e) {
     std::cerr << "fm_status " << e.status() << "\n" << e.what() << std::endl;

@@ -1,25 +1,40 @@
-// moe_model.cpp -- see moe_model.hpp.  Device memory comes from the CUDA runtime
-// (cudaMalloc per tensor: 256-byte aligned, as the tcgen05 path's TMA descriptors need).
+// moe_model.cpp -- see moe_model.hpp.
 #include "moe_model.hpp"
-
-#include <cuda_runtime.h>
 
 #include <algorithm>
 #include <stdexcept>
 
 namespace flashmoe {
 
-namespace {
-
-void cuda_check(cudaError_t e, const char* what) {
-  if (e != cudaSuccess) throw Error(FM_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+fm_moe_weights upload_moe_layer(DeviceStore& store, const HostLayer& L, const float** correction_bias) {
+  fm_moe_weights w{};
+  w.router_w = store.u16(L.router_w);
+  if (correction_bias) *correction_bias = nullptr;
+  if (L.sigmoid) {
+    w.up = store.q(L.up);      // fc1
+    w.down = store.q(L.down);  // fc2
+    if (L.has_shared) {
+      w.shared_up = store.q(L.shared_up);
+      w.shared_down = store.q(L.shared_down);
+    }
+    if (!L.correction_bias.empty() && correction_bias) *correction_bias = store.f32(L.correction_bias);
+  } else {
+    w.gate = store.q(L.gate);
+    w.up = store.q(L.up);
+    w.down = store.q(L.down);
+    if (L.has_shared) {
+      w.shared_gate = store.q(L.shared_gate);
+      w.shared_up = store.q(L.shared_up);
+      w.shared_down = store.q(L.shared_down);
+      w.shared_expert_gate_w = store.u16(L.shared_expert_gate_w);
+    }
+  }
+  return w;
 }
-
-}  // namespace
 
 MoEModel::MoEModel(const std::string& model_dir, int device, void* stream, int64_t max_tokens,
                    const std::vector<int>& layers)
-    : device_(device) {
+    : device_(device), store_(device) {
   Checkpoint ck(model_dir);
   config_ = ck.config();
   cfg_ = config_.moe_config();
@@ -33,84 +48,24 @@ MoEModel::MoEModel(const std::string& model_dir, int device, void* stream, int64
   }
   cuda_check(cudaSetDevice(device_), "cudaSetDevice");
   handle_ = Handle(device_, stream);
-  try {
-    for (int i : moe) {
-      const HostLayer L = config_.sigmoid_routed() ? ck.sigmoid_moe_layer(i) : ck.moe_layer(i);
-      DeviceLayer d;
-      d.w.router_w = upload_u16(L.router_w);
-      if (L.sigmoid) {
-        d.w.up = upload_q(L.up);  // fc1
-        d.w.down = upload_q(L.down);  // fc2
-        if (L.has_shared) {
-          d.w.shared_up = upload_q(L.shared_up);
-          d.w.shared_down = upload_q(L.shared_down);
-        }
-        if (!L.correction_bias.empty()) d.correction_bias = upload_f32(L.correction_bias);
-      } else {
-        d.w.gate = upload_q(L.gate);
-        d.w.up = upload_q(L.up);
-        d.w.down = upload_q(L.down);
-        if (L.has_shared) {
-          d.w.shared_gate = upload_q(L.shared_gate);
-          d.w.shared_up = upload_q(L.shared_up);
-          d.w.shared_down = upload_q(L.shared_down);
-          d.w.shared_expert_gate_w = upload_u16(L.shared_expert_gate_w);
-        }
-      }
-      layers_[i] = d;
-    }
-    if (max_tokens > 0 && !layers_.empty()) handle_.reserve(cfg_, max_tokens);
-  } catch (...) {
-    free_all();
-    throw;
+  for (int i : moe) {
+    const HostLayer L = config_.sigmoid_routed() ? ck.sigmoid_moe_layer(i) : ck.moe_layer(i);
+    DeviceLayer d;
+    d.w = upload_moe_layer(store_, L, &d.correction_bias);
+    layers_[i] = d;
   }
+  if (max_tokens > 0 && !layers_.empty()) handle_.reserve(cfg_, max_tokens);
 }
 
-MoEModel::~MoEModel() { free_all(); }
-
-void MoEModel::free_all() noexcept {
-  if (allocations_.empty()) return;
+MoEModel::~MoEModel() {
   // the handle's stream may still read the weights
   if (handle_) fm_sync_status(handle_.get());
-  int cur = 0;
-  cudaGetDevice(&cur);
-  cudaSetDevice(device_);
-  for (void* p : allocations_) cudaFree(p);
-  cudaSetDevice(cur);
-  allocations_.clear();
 }
 
 std::vector<int> MoEModel::moe_layers() const {
   std::vector<int> out;
   for (const auto& kv : layers_) out.push_back(kv.first);
   return out;
-}
-
-void* MoEModel::upload(const void* src, size_t bytes) {
-  if (!bytes) return nullptr;
-  void* p = nullptr;
-  cuda_check(cudaMalloc(&p, bytes), "cudaMalloc");
-  allocations_.push_back(p);
-  cuda_check(cudaMemcpy(p, src, bytes, cudaMemcpyHostToDevice), "cudaMemcpy");
-  return p;
-}
-
-const uint16_t* MoEModel::upload_u16(const std::vector<uint16_t>& v) {
-  return static_cast<const uint16_t*>(upload(v.data(), v.size() * sizeof(uint16_t)));
-}
-const uint32_t* MoEModel::upload_u32(const std::vector<uint32_t>& v) {
-  return static_cast<const uint32_t*>(upload(v.data(), v.size() * sizeof(uint32_t)));
-}
-const float* MoEModel::upload_f32(const std::vector<float>& v) {
-  return static_cast<const float*>(upload(v.data(), v.size() * sizeof(float)));
-}
-
-fm_qweight MoEModel::upload_q(const HostQ& q) {
-  fm_qweight r{};
-  r.w = upload_u32(q.w);
-  r.scales = upload_u16(q.s);
-  r.biases = q.has_biases() ? upload_u16(q.b) : nullptr;
-  return r;
 }
 
 void MoEModel::moe_block(const uint16_t* x, int64_t T, uint16_t* y, int layer) {

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "checkpoint.hpp"
+#include "device_store.hpp"
 #include "flashmoe.hpp"
 
 namespace flashmoe {
@@ -48,19 +49,17 @@ class MoEModel {
     fm_moe_weights w{};
     const float* correction_bias = nullptr;
   };
-  const uint16_t* upload_u16(const std::vector<uint16_t>& v);
-  const uint32_t* upload_u32(const std::vector<uint32_t>& v);
-  const float* upload_f32(const std::vector<float>& v);
-  fm_qweight upload_q(const HostQ& q);
-  void* upload(const void* src, size_t bytes);
-  void free_all() noexcept;
 
   ModelConfig config_;
   fm_moe_config cfg_{};
   int device_ = 0;
   Handle handle_;
   std::map<int, DeviceLayer> layers_;
-  std::vector<void*> allocations_;
+  DeviceStore store_;  // declared after handle_: freed first, after the destructor's sync
 };
+
+// Uploads one MoE layer into `store` and returns its fm_moe_weights (and, for a
+// sigmoid-routed layer, the device correction bias in *correction_bias).
+fm_moe_weights upload_moe_layer(DeviceStore& store, const HostLayer& L, const float** correction_bias);
 
 }  // namespace flashmoe

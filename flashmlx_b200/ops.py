@@ -367,3 +367,110 @@ class MoEBlockVariant:
         return (y, routing) if return_routing else y
 
 
+
+
+# ---------------------------------------------------------------- decoder ops
+# The rest of the reference's decoder layer (model.cpp:486-656, sampling.cpp:5-7) on the
+# same handle and stream as the MoE calls.
+
+def dequantize(w, scales, biases=None, group_size=64, bits=4, handle=None) -> torch.Tensor:
+    """mx::dequantize: [N, K*bits/32] codes -> [N, K] bf16 (bf16(fma(s, q, b)))."""
+    _need(w, "w", _U32, None)
+    dev = w.device
+    _need(scales, "scales", (torch.bfloat16,), dev)
+    if biases is not None:
+        _need(biases, "biases", (torch.bfloat16,), dev)
+    N, K = w.shape[0], w.shape[1] * 32 // bits
+    if scales.shape != (N, K // group_size) or (biases is not None and biases.shape != scales.shape):
+        raise ValueError("scales / biases shape mismatch")
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_dequantize(h.h, _ptr(w), _ptr(scales), _ptr(biases), N, K, group_size, bits, _ptr(out)))
+    return out
+
+
+def embed(table, ids, handle=None) -> torch.Tensor:
+    """mx::take(table, ids, 0): table [V, H] bf16, ids int32 [...] -> [..., H]."""
+    _need(table, "table", (torch.bfloat16,), None)
+    dev = table.device
+    _need(ids, "ids", (torch.int32,), dev)
+    V, H = table.shape
+    out = torch.empty(*ids.shape, H, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_embed(h.h, _ptr(table), V, H, _ptr(ids), ids.numel(), _ptr(out)))
+    return out
+
+
+def rms_norm(x, weight, eps, residual=None, h_out=None, handle=None) -> torch.Tensor:
+    """mx::fast::rms_norm(x + residual, weight, eps) over the last axis; x + residual (bf16)
+    is also written to h_out when given (it may be x)."""
+    _need(x, "x", (torch.bfloat16,), None)
+    dev = x.device
+    _need(weight, "weight", (torch.bfloat16,), dev)
+    H = x.shape[-1]
+    if weight.numel() != H:
+        raise ValueError("weight size differs from the last axis")
+    for t, n in ((residual, "residual"), (h_out, "h_out")):
+        if t is not None:
+            _need(t, n, (torch.bfloat16,), dev)
+            if t.shape != x.shape:
+                raise ValueError(f"{n} shape differs from x")
+    y = torch.empty_like(x)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_rms_norm(h.h, _ptr(x), _ptr(residual), _ptr(weight), x.numel() // H, H, float(eps),
+                              _ptr(h_out), _ptr(y)))
+    return y
+
+
+def attention(q, k, v, cache_k, cache_v, B, L, offset, rope_theta, q_bias=None, k_bias=None, v_bias=None,
+              scale=0.0, handle=None) -> torch.Tensor:
+    """The attention step after the q/k/v projections (model.cpp:560-635): bias adds,
+    RoPE at offset + l, k / v into the caches [B, n_kv, max_len, d] at [offset, offset+L),
+    causal SDPA.  q [B*L, nh*d] is rotated in place; returns [B*L, nh*d] bf16."""
+    _need(q, "q", (torch.bfloat16,), None)
+    dev = q.device
+    for t, n in ((k, "k"), (v, "v"), (cache_k, "cache_k"), (cache_v, "cache_v")):
+        _need(t, n, (torch.bfloat16,), dev)
+    for t, n in ((q_bias, "q_bias"), (k_bias, "k_bias"), (v_bias, "v_bias")):
+        if t is not None:
+            _need(t, n, (torch.bfloat16,), dev)
+    if cache_k.dim() != 4 or cache_v.shape != cache_k.shape or cache_k.shape[0] < B:
+        raise ValueError("caches must be [>= B, n_kv, max_len, d] and alike")
+    _, nkv, max_len, d = cache_k.shape
+    nh = q.shape[-1] // d
+    if q.numel() != B * L * nh * d or k.numel() != B * L * nkv * d or v.numel() != k.numel():
+        raise ValueError("q / k / v sizes do not match B, L and the cache heads")
+    cfg = _lib.AttnConfig(nh, nkv, d, max_len, float(rope_theta), float(scale))
+    out = torch.empty(B * L, nh * d, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_attention(h.h, C.byref(cfg), _ptr(q), _ptr(k), _ptr(v), _ptr(q_bias), _ptr(k_bias),
+                               _ptr(v_bias), _ptr(cache_k), _ptr(cache_v), B, L, offset, _ptr(out)))
+    return out
+
+
+def swiglu(gate, up, handle=None) -> torch.Tensor:
+    """The compiled swiglu of model.cpp:14-25 (silu(g) * u, bf16 after every op)."""
+    _need(gate, "gate", (torch.bfloat16,), None)
+    _need(up, "up", (torch.bfloat16,), gate.device)
+    if up.shape != gate.shape:
+        raise ValueError("gate and up shapes differ")
+    out = torch.empty_like(gate)
+    h = handle or default_handle(gate.device.index)
+    h.bind_stream()
+    h.check(h.lib.fm_swiglu(h.h, _ptr(gate), _ptr(up), gate.numel(), _ptr(out)))
+    return out
+
+
+def argmax(logits, handle=None) -> torch.Tensor:
+    """Greedy sampling: the first index of the largest value along the last axis (int32)."""
+    _need(logits, "logits", (torch.bfloat16,), None)
+    V = logits.shape[-1]
+    out = torch.empty(logits.shape[:-1], dtype=torch.int32, device=logits.device)
+    h = handle or default_handle(logits.device.index)
+    h.bind_stream()
+    h.check(h.lib.fm_argmax(h.h, _ptr(logits), logits.numel() // V, V, _ptr(out)))
+    return out

@@ -230,6 +230,59 @@ FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_wei
 FM_API int fm_moe_block_noalloc(int device, void* stream, const fm_moe_config* cfg, const fm_moe_weights* w,
                                 const uint16_t* x, int64_t T, uint16_t* y);
 
+/* Decoder ops -------------------------------------------------------------------
+ * The rest of the reference's decoder layer (LlamaModel::transformer_block,
+ * model.cpp:813-839, with attention 542-643), so a whole layer runs on this library.
+ * Activations are token-major bf16 rows, 16-byte aligned; T = B * L tokens, token
+ * t = b * L + l.  Same stream ordering and status codes as the operators above. */
+
+/* out[N, K] = dequantize(w, scales, biases) in bf16 (bf16(fma(s, q, b))).  Replaces
+ * mx::dequantize, used at load for the embedding table (model.cpp:216-230). */
+FM_API int fm_dequantize(fm_handle* h, const uint32_t* w, const uint16_t* scales, const uint16_t* biases, int64_t N,
+                         int K, int group_size, int bits, uint16_t* out);
+
+/* y[t] = table[ids[t]] ([V, H] bf16 table).  Replaces mx::take(table, ids, 0)
+ * (model.cpp:490-496).  An id outside [0, V) gives a zero row and FM_EDEVICE at the next
+ * fm_sync_status. */
+FM_API int fm_embed(fm_handle* h, const uint16_t* table, int64_t V, int H, const int32_t* ids, int64_t T,
+                    uint16_t* y);
+
+/* y = rms_norm(h) * weight with h = x + residual (residual NULL: h = x), both [T, H];
+ * h is also written to h_out when it is not NULL (h_out may be x).  Replaces mx::add
+ * (model.cpp:824, 838) followed by mx::fast::rms_norm (486-488): h = bf16(x + r),
+ * n = 1/sqrt(mean_fp32(h^2) + eps), y = bf16(bf16(h * n) * weight).  H % 8 == 0. */
+FM_API int fm_rms_norm(fm_handle* h, const uint16_t* x, const uint16_t* residual, const uint16_t* weight, int64_t T,
+                       int H, float eps, uint16_t* h_out, uint16_t* y);
+
+typedef struct fm_attn_config {
+  int n_heads;       /* num_attention_heads */
+  int n_kv_heads;    /* num_key_value_heads (divides n_heads) */
+  int head_dim;      /* 64 or 128 */
+  int max_len;       /* positions per (sequence, kv head) in the cache */
+  float rope_theta;  /* RoPE base (traditional = false, scale 1) */
+  float scale;       /* softmax scale; 0 = 1/sqrt(head_dim) */
+} fm_attn_config;
+
+/* The attention step of a layer after its q/k/v projections (model.cpp:560-635): bias
+ * adds (biases may be NULL), RoPE at positions offset + l, k / v written into the caches
+ * [B, n_kv_heads, max_len, head_dim] at [offset, offset + L) (mx::slice_update), and
+ * scaled dot-product attention of the L queries over positions [0, offset + l] (causal;
+ * mx::fast::scaled_dot_product_attention) into out [T, n_heads*head_dim].  q [T,
+ * n_heads*head_dim] is overwritten with its rotated rows; k, v are [T,
+ * n_kv_heads*head_dim].  Every sequence of the batch is at the same offset, as in the
+ * reference (model.cpp:594-606). */
+FM_API int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uint16_t* k, const uint16_t* v,
+                        const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, uint16_t* cache_k,
+                        uint16_t* cache_v, int B, int L, int offset, uint16_t* out);
+
+/* out = swiglu(gate, up) elementwise over n values: silu(g) * u with bf16 rounding after
+ * every op, the compiled swiglu of model.cpp:14-25, for dense MLP layers (model.cpp:645-656). */
+FM_API int fm_swiglu(fm_handle* h, const uint16_t* gate, const uint16_t* up, int64_t n, uint16_t* out);
+
+/* ids[t] = argmax over logits[t, 0:V) (bf16), the first index among equal maxima.
+ * Replaces sample_token at temperature 0, mx::argmax(logits, -1) (sampling.cpp:5-7). */
+FM_API int fm_argmax(fm_handle* h, const uint16_t* logits, int64_t T, int64_t V, int32_t* ids);
+
 /* Expert parallelism ------------------------------------------------------------
  * No reference counterpart: the reference runs the whole MoE layer in one process
  * (model.cpp:750-807).  These calls split fm_moe_block into the three stages of an

@@ -69,10 +69,14 @@ def test_llama_checkpoint(tmp_path, fm_host, stacked):
     ck = CK.Checkpoint(str(tmp_path))
     got = _inspect(fm_host, tmp_path)
     c = ck.config
-    assert got == {"hidden": c.hidden, "num_layers": c.num_layers, "num_experts": c.num_experts, "top_k": c.top_k,
-                   "inter": c.inter, "shared_inter": c.shared_inter, "norm_topk_prob": c.norm_topk_prob,
-                   "bits": c.bits, "group_size": c.group_size, "n_group": 1, "topk_group": 1,
-                   "routed_scaling_factor": 1, "sigmoid_routed": False, "moe_layers": ck.moe_layers()}
+    want = {"hidden": c.hidden, "num_layers": c.num_layers, "num_experts": c.num_experts, "top_k": c.top_k,
+            "inter": c.inter, "shared_inter": c.shared_inter, "norm_topk_prob": c.norm_topk_prob,
+            "bits": c.bits, "group_size": c.group_size, "n_group": 1, "topk_group": 1,
+            "routed_scaling_factor": 1, "sigmoid_routed": False, "moe_layers": ck.moe_layers()}
+    assert {k: got[k] for k in want} == want
+    # decoder keys absent from this config take LlamaModel::load_config's defaults
+    assert (got["n_heads"], got["n_kv_heads"], got["vocab"], got["tie_word_embeddings"]) == (32, 8, 128256, True)
+    assert got["head_dim"] == c.hidden // 32 and got["rope_theta"] == 10000 and got["rms_eps"] == pytest.approx(1e-5)
     sig, arrays = _dump(fm_host, tmp_path, 0, tmp_path / "dump")
     assert not sig
     ref = ck.moe_layer(0)
@@ -211,3 +215,39 @@ def test_run_without_a_device_fails_loudly(tmp_path, fm_host):
     assert r.returncode == 3, (r.returncode, r.stderr)
     assert r.stderr.startswith("fm_status 3"), r.stderr
     assert not os.path.exists(tmp_path / "y.bin")
+
+
+# ---------------------------------------------------------------- the decoder's loader
+from tests.decoder_util import write_decoder_checkpoint  # noqa: E402
+
+DEC = S.DecoderShape("dec_ckpt", 256, 2, 4, 2, 64, 320, 1e6, 1e-6, S.MoEShape("dec_moe", 256, 128, 4, 2, 0, False, 256))
+
+
+def test_decoder_checkpoint_layout(tmp_path, fm_host):
+    w = S.make_decoder(DEC, 51)
+    write_decoder_checkpoint(str(tmp_path), DEC, w)
+    got = json.loads(_run(fm_host, "check-decoder", tmp_path).stdout)
+    assert got == {"layers": 2, "moe_layers": [0, 1], "attn_bias": True, "embed_quantized": True,
+                   "tie_word_embeddings": False, "head_dim": 64, "vocab": 320}
+    info = _inspect(fm_host, tmp_path)
+    assert (info["n_heads"], info["n_kv_heads"], info["rope_theta"]) == (4, 2, 1e6)
+
+
+def test_decoder_checkpoint_rejects_misshapen(tmp_path, fm_host):
+    w = S.make_decoder(DEC, 52)
+    write_decoder_checkpoint(str(tmp_path), DEC, w)
+    with open(tmp_path / "config.json") as f:
+        c = json.load(f)
+    c["num_key_value_heads"] = 4  # k/v projections were written for 2 heads
+    with open(tmp_path / "config.json", "w") as f:
+        json.dump(c, f)
+    _expect_error(fm_host, tmp_path, "check-decoder", match="self_attn.k_proj: shape differs")
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device error path")
+def test_generate_without_a_device_fails_loudly(tmp_path, fm_host):
+    w = S.make_decoder(DEC, 53)
+    write_decoder_checkpoint(str(tmp_path), DEC, w)
+    np.zeros((1, 4), np.int32).tofile(tmp_path / "p.bin")
+    r = _run(fm_host, "generate", tmp_path, tmp_path / "p.bin", 1, 4, 3, tmp_path / "o.bin", check=False)
+    assert r.returncode == 3 and r.stderr.startswith("fm_status 3"), (r.returncode, r.stderr)
