@@ -21,6 +21,11 @@ N > 1  = expert parallelism (flashmlx_b200.ep): each rank holds the router, the 
          staged calls (--ep-impl nccl); --replicas runs N independent single-GPU layers
 --impl reference: the CPU restatement of the reference's MLX path (the reference
 needs MLX + Metal, which this box cannot run) timed on the host cores, rank 0 only.
+
+--config qwen15_decoder: the whole 24-layer decoder through the C++ host
+layer (host/decoder.cpp): a step is one greedy decode forward of --batch sequences
+(1, 4 or 32) after a 512-token prompt; value = decode tokens/s, e2e = generate() of
+prompt + steps from host memory to host tokens.  N > 1 runs independent replicas.
 """
 from __future__ import annotations
 
@@ -47,7 +52,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default=DEFAULT_CONFIG, choices=sorted(S.CONFIGS) + sorted(S.VARIANT_CONFIGS))
+    ap.add_argument("--config", default=DEFAULT_CONFIG,
+                    choices=sorted(S.CONFIGS) + sorted(S.VARIANT_CONFIGS) + sorted(S.DECODER_CONFIGS))
+    ap.add_argument("--batch", type=int, default=32, help="decoder configs: sequences per step (1, 4, 32)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -453,9 +460,191 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+# ----------------------------------------------------------------------------- decoder
+PROMPT_LEN, DECODE_STEPS = 512, 256  # configs[2]: 512-token prompts, 256 greedy steps
+
+
+def decoder_step_bytes(shape, B: int, pos: int) -> float:
+    """Algorithmic HBM bytes of one decode forward of B sequences at cache position pos:
+    every weight a step reads once (attention projections, the expected active experts of
+    each MoE layer for B*k routed pairs, the shared expert and router, lm_head), the KV
+    cache rows read and written, the embedding rows."""
+    m = shape.moe
+    qb = 0.5 + 2 * 2 / shape.group_size  # bytes per 4-bit weight with bf16 scale + bias
+    H, d, nh, nkv = shape.hidden, shape.head_dim, shape.n_heads, shape.n_kv_heads
+    attn_w = H * (nh + 2 * nkv) * d * qb + nh * d * H * qb
+    active = m.num_experts * (1 - (1 - m.top_k / m.num_experts) ** B)
+    moe_w = active * 3 * H * m.inter * qb + 3 * H * m.shared_inter * qb + m.num_experts * H * 2 + H * 2
+    kv = B * nkv * d * 2 * 2 * (pos + 2)  # K and V rows read (pos + 1) and the new row written
+    per_layer = attn_w + moe_w + kv + 4 * B * H * 2
+    return shape.layers * per_layer + shape.vocab * H * qb + B * H * 2
+
+
+def run_decoder(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    from flashmlx_b200 import decoder as DEC
+    shape = S.DECODER_CONFIGS[args.config]
+    B = args.batch
+    if args.warmup + args.steps > DECODE_STEPS:
+        raise SystemExit(f"--warmup + --steps must be at most {DECODE_STEPS}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=300))
+    weights = DEC.device_decoder_weights(shape, args.seed + rank, dev)
+    dec = DEC.Decoder.from_weights(shape, weights, dev, B, PROMPT_LEN + DECODE_STEPS)
+    h = dec.handle()
+    rng = np.random.default_rng(args.seed + 1000 + rank)
+    prompt_np = rng.integers(0, shape.vocab, (B, PROMPT_LEN)).astype(np.int32)
+    prompt = torch.from_numpy(prompt_np).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # prefill (timed on its own), then the warm-up decode steps
+    torch.cuda.synchronize()
+    e0.record(stream)
+    tok = dec.forward(prompt)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    for _ in range(args.warmup):
+        tok = dec.forward(tok[:, None].contiguous())
+    dec.sync()
+    pos0 = dec.offset
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    h.profile(True)
+    h.profile_report(reset=True)
+    ids = [tok[:, None].contiguous(), torch.empty(B, 1, dtype=torch.int32, device=dev)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for i in range(args.steps):
+        dec.forward(ids[i & 1], out=ids[(i + 1) & 1].view(B))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dec.sync()
+    dev_ms = e0.elapsed_time(e1) / args.steps
+    prof = {k: v for k, v in h.profile_report(reset=True).items() if "." not in k}
+    h.profile(False)
+    # end to end: generate() from a host prompt to host tokens (prefill + steps forwards)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    dec.generate(prompt_np, args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if world > 1:
+        t = torch.tensor([dev_ms, e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, e2e_ms = t.tolist()
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        nbytes = decoder_step_bytes(shape, B, pos0 + args.steps // 2)
+        achieved = nbytes / (dev_ms * 1e-3) / 1e9
+        launches = sum(n for n, _ in prof.values())
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            v, info = cpu_decoder_throughput(shape, args.seed)
+            cpu = {"value": v, "unit": "tokens/s", **info}
+        line = {
+            "metric": "decode_tokens_per_s", "value": world * B / (dev_ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dev_ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+u4",
+            "data": "synthetic (random-init weights generated on the device, random prompt tokens)",
+            "config": {"workload": shape.name, "batch": B, "prompt_len": PROMPT_LEN, "layers": shape.layers,
+                       "position_at_timing": pos0, "prefill_ms": prefill_ms,
+                       "prefill_tokens_per_s": B * PROMPT_LEN / (prefill_ms * 1e-3),
+                       "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "l2": "weights exceed L2 (no flush between steps)"},
+            "e2e": {"value": world * B * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(B * PROMPT_LEN * 4 / args.steps),
+                    "d2h_bytes_per_step": int(B * 4),
+                    "note": "generate(): prompt prefill included, tokens copied back once"},
+            "gpu_launches": launches,
+            "kernels": {k: {"launches": n, "avg_ms": ms / max(1, n)} for k, (n, ms) in prof.items()},
+            "roofline": {"bound": "hbm", "unit": "GB/s", "achieved": achieved, "peak": peaks["hbm_gbs"],
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": None, "kernel": "decode step (all kernels)",
+                         "kernel_ms": dev_ms, "peak_source": peak_src, "algorithmic": nbytes,
+                         "note": "expected active experts per MoE layer for B*k routed pairs"},
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    dec.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+CPU_DECODER_LAYERS = 2  # layers of the bounded CPU sample
+
+
+def cpu_decoder_throughput(shape, seed: int):
+    """The oracle decoder (oracle/decoder.py) on the host cores: one decode step at batch 1
+    over CPU_DECODER_LAYERS of the layers (after a 16-token prompt), its per-layer time
+    scaled to the full depth, plus the lm_head; tokens/s at batch 1."""
+    import dataclasses
+
+    import numpy as np
+
+    from oracle import decoder as D
+    from oracle import oracle as O
+    small = dataclasses.replace(shape, layers=CPU_DECODER_LAYERS)
+    w = S.make_decoder(small, seed)
+    dec = D.Decoder(small, w, 1, 64)
+    dec.forward(np.zeros((1, 16), np.int64))
+    t0 = time.perf_counter()
+    n = 0
+    while n < 3 or time.perf_counter() - t0 < 10.0:
+        if dec.offset == 64:
+            dec.offset = 16  # reuse cache positions 16..63
+        dec.forward(np.array([[n % shape.vocab]]))
+        n += 1
+    step = (time.perf_counter() - t0) / n
+    # split the step: lm_head alone, the rest scaled by depth
+    x = D.rms_norm(dec.embed([0]), w["norm"], shape.rms_eps)
+    t1 = time.perf_counter()
+    head = w["embed"] if shape.tie_word_embeddings else w["lm_head"]
+    O.quantized_matmul(x, *head)
+    head_s = time.perf_counter() - t1
+    full = (step - head_s) * shape.layers / CPU_DECODER_LAYERS + head_s
+    return 1.0 / full, {"cores": O.NTHREADS, "kind": "port",
+                        "sample": f"{n} batch-1 decode steps over {CPU_DECODER_LAYERS} of {shape.layers} layers "
+                                  f"(per-layer time scaled to the full depth, lm_head timed whole)"}
+
+
+def run_decoder_reference(args, rank):
+    if rank != 0:
+        return
+    shape = S.DECODER_CONFIGS[args.config]
+    v, info = cpu_decoder_throughput(shape, args.seed)
+    line = {
+        "metric": "decode_tokens_per_s", "value": v, "unit": "tokens/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+u4", "data": "synthetic",
+        "config": {"workload": shape.name, "batch": 1},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", **info},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference path needs MLX + Apple Metal (not installable here); CPU restatement of its "
+                "MLX semantics (oracle/decoder.py) timed instead",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local_rank = rank_info()
+    if args.config in S.DECODER_CONFIGS:
+        if args.impl == "reference":
+            run_decoder_reference(args, rank)
+        else:
+            run_decoder(args, rank, world, local_rank)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -134,6 +134,13 @@ void Decoder::forward(const int32_t* ids, int B, int L, int32_t* next_ids) {
   offset_ += L;
 }
 
+void Decoder::copy_logits(uint16_t* dst, int B) const {
+  if (B > max_batch_) throw Error(FM_EINVAL, "B exceeds max_batch");
+  cuda_check(cudaMemcpyAsync(dst, logits_, sizeof(uint16_t) * static_cast<size_t>(B) * cfg_.vocab,
+                             cudaMemcpyDeviceToDevice, stream_),
+             "cudaMemcpyAsync logits");
+}
+
 std::vector<int32_t> Decoder::generate(const int32_t* prompt, int B, int L, int steps) {
   if (steps <= 0) return {};
   if (static_cast<int64_t>(L) + steps - 1 > max_len_) throw Error(FM_EINVAL, "prompt + steps exceed max_len");
@@ -354,6 +361,11 @@ int fmh_decoder_forward(fmh_decoder* d, const int32_t* ids, int B, int L, int32_
 
 const uint16_t* fmh_decoder_logits(const fmh_decoder* d) { return d && d->d ? d->d->logits() : nullptr; }
 
+int fmh_decoder_copy_logits(fmh_decoder* d, uint16_t* dst, int B) {
+  if (!d || !d->d || !dst || B < 0) return FM_EINVAL;
+  return guarded(d, [&] { d->d->copy_logits(dst, B); });
+}
+
 int fmh_decoder_offset(const fmh_decoder* d) { return d && d->d ? d->d->offset() : -1; }
 
 int fmh_decoder_reset(fmh_decoder* d) {
@@ -366,6 +378,8 @@ int fmh_decoder_sync(fmh_decoder* d) {
   if (!d || !d->d) return FM_EINVAL;
   return guarded(d, [&] { d->d->sync(); });
 }
+
+fm_handle* fmh_decoder_handle(fmh_decoder* d) { return d && d->d ? d->d->handle().get() : nullptr; }
 
 int fmh_decoder_generate(fmh_decoder* d, const int32_t* prompt, int B, int L, int steps, int32_t* out) {
   if (!d || !d->d || !prompt || !out) return FM_EINVAL;

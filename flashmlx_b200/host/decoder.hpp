@@ -75,6 +75,7 @@ class Decoder {
   // ids [B, L] device int32 -> next_ids [B] device int32; advances the offset by L
   void forward(const int32_t* ids, int B, int L, int32_t* next_ids);
   const uint16_t* logits() const { return logits_; }
+  void copy_logits(uint16_t* dst, int B) const;
   int offset() const { return offset_; }
   void reset() { offset_ = 0; }
   void sync() const { handle_.sync(); }

@@ -70,11 +70,15 @@ const char* fmh_last_error(const fmh_decoder* d);
 int fmh_decoder_forward(fmh_decoder* d, const int32_t* ids, int B, int L, int32_t* next_ids);
 /* logits [B, vocab] bf16 (device) of the last forward's final positions */
 const uint16_t* fmh_decoder_logits(const fmh_decoder* d);
+/* copies the first B rows of those logits to dst (device), ordered on the decoder's stream */
+int fmh_decoder_copy_logits(fmh_decoder* d, uint16_t* dst, int B);
 int fmh_decoder_offset(const fmh_decoder* d);
 /* starts new sequences (offset 0) */
 int fmh_decoder_reset(fmh_decoder* d);
 /* waits for the stream; FM_EDEVICE etc. as fm_sync_status */
 int fmh_decoder_sync(fmh_decoder* d);
+/* the libflashmoe handle the decoder's calls run on (fm_profile_enable / _report) */
+fm_handle* fmh_decoder_handle(fmh_decoder* d);
 /* Greedy generation from host buffers: prompt [B, L] -> out [B, steps] (the first token
  * from the prompt's forward, then steps - 1 single-token forwards).  Resets first. */
 int fmh_decoder_generate(fmh_decoder* d, const int32_t* prompt, int B, int L, int steps, int32_t* out);

@@ -50,9 +50,9 @@ class Handle:
         self.h = h
 
     def close(self):
-        if self.h:
+        if self.h and not getattr(self, "_borrowed", False):  # a borrowed view never destroys
             self.lib.fm_destroy(self.h)
-            self.h = None
+        self.h = None
 
     def __del__(self):
         try:

@@ -129,12 +129,19 @@ class Decoder:
 
     def __init__(self, cfg, weights: dict, max_batch: int, max_len: int):
         self.cfg, self.w = cfg, weights
-        self.table = dequantize(*weights["embed"], cfg.group_size, cfg.bits)
         self.moe = [O.Layer(cfg.moe, lw["moe"]) for lw in weights["layers"]]
         shape = (max_batch, cfg.n_kv_heads, max_len, cfg.head_dim)
         self.cache_k = [np.zeros(shape, np.uint16) for _ in range(cfg.layers)]
         self.cache_v = [np.zeros(shape, np.uint16) for _ in range(cfg.layers)]
         self.offset = 0
+
+    def embed(self, ids) -> np.ndarray:
+        """Rows of the dequantized embedding table for ids (only those rows are dequantized)."""
+        ids = np.asarray(ids, np.int64).reshape(-1)
+        w, s, b = self.w["embed"]
+        uniq, inv = np.unique(ids, return_inverse=True)
+        rows = dequantize(w[uniq], s[uniq], None if b is None else b[uniq], self.cfg.group_size, self.cfg.bits)
+        return rows[inv]
 
     def _qmm(self, x, q):
         w, s, b = q
@@ -164,7 +171,9 @@ class Decoder:
         c = self.cfg
         ids = np.asarray(ids, np.int64)
         B, L = ids.shape
-        x = self.table[ids.reshape(-1)]
+        if self.offset + L > self.cache_k[0].shape[2] or B > self.cache_k[0].shape[0]:
+            raise ValueError("offset + L exceeds max_len, or B exceeds max_batch")
+        x = self.embed(ids)
         for li, lw in enumerate(self.w["layers"]):
             h = add(x, self.attention(rms_norm(x, lw["in_norm"], c.rms_eps), li, B, L))
             m = self.moe[li].moe_block(rms_norm(h, lw["post_norm"], c.rms_eps))[0]

@@ -1,0 +1,199 @@
+"""The decoder's device ops (fm_dequantize, fm_embed, fm_rms_norm, fm_attention,
+fm_swiglu, fm_argmax) and the C++ Decoder (host/decoder.cpp, through fmh.h) against the
+CPU restatement of the reference's forward (oracle/decoder.py: model.cpp:486-660,
+813-839, sampling.cpp:5-7).
+
+Integer and copy ops are bit-exact.  Floating-point ops are held to the north-star
+tolerances (tests/_parity.py); attention rounds its softmax probabilities to bf16 for
+the tensor-core product, so its outputs are compared normwise.  The whole-model logits
+carry two layers of such differences plus the two 4-bit GEMM forms, and are compared
+with the EXACT_FLOOR bound; greedy tokens must agree wherever the oracle's top two
+logits are more than a few ulps apart.
+
+These tests have not yet run on a B200: they run when FM_DECODER_GPU_TESTS=1."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from flashmlx_b200 import synthetic as S
+from oracle import decoder as D
+from tests._parity import EXACT_FLOOR, TIGHT, assert_close
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(os.environ.get("FM_DECODER_GPU_TESTS") != "1",
+                                 reason="decoder kernels not yet run on a B200 (FM_DECODER_GPU_TESTS=1 runs them)")]
+
+
+def _dev(a):
+    from flashmlx_b200 import ops
+    return ops.bf16_from_numpy(a, "cuda")
+
+
+def _host(t):
+    from flashmlx_b200 import ops
+    torch.cuda.synchronize()
+    return ops.bf16_to_numpy(t)
+
+
+def _rnd(rng, shape, std=1.0):
+    return D.bf16(rng.standard_normal(shape).astype(np.float32) * std)
+
+
+def test_dequantize_bit_exact():
+    from flashmlx_b200 import ops
+    w, s, b = S.make_qmatrix(61, "deq", (), 320, 512, 64, 4, scale_std=0.1)
+    got = ops.dequantize(ops.u32_from_numpy(w, "cuda"), _dev(s), _dev(b))
+    np.testing.assert_array_equal(_host(got), D.dequantize(w, s, b))
+
+
+def test_embed_rows_and_bad_ids():
+    from flashmlx_b200 import _lib, ops
+    rng = np.random.default_rng(62)
+    table = _rnd(rng, (50, 256))
+    ids = np.array([[0, 49, 7], [7, 3, 0]], np.int32)
+    got = ops.embed(_dev(table), torch.from_numpy(ids).cuda())
+    np.testing.assert_array_equal(_host(got), table[ids])
+    h = ops.default_handle(torch.cuda.current_device())
+    h.sync()
+    bad = torch.tensor([1, 50], dtype=torch.int32, device="cuda")
+    y = ops.embed(_dev(table), bad)
+    with pytest.raises(_lib.FlashMoEError) as e:
+        h.sync()  # the out-of-range id is a device-side bounds failure
+    assert e.value.status == _lib.FM_EDEVICE
+    np.testing.assert_array_equal(_host(y)[1], np.zeros(256, np.uint16))
+
+
+@pytest.mark.parametrize("residual", [False, True])
+@pytest.mark.parametrize("H", [256, 2048, 2056])
+def test_rms_norm(residual, H):
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(63)
+    x = _rnd(rng, (37, H), 2.0)
+    r = _rnd(rng, (37, H)) if residual else None
+    w = D.bf16(1 + 0.1 * rng.standard_normal(H).astype(np.float32))
+    xt = _dev(x)
+    h_out = xt if residual else None  # in place: x becomes x + r
+    y = ops.rms_norm(xt, _dev(w), 1e-6, residual=_dev(r) if residual else None, h_out=h_out)
+    h = D.add(x, r) if residual else x
+    if residual:
+        np.testing.assert_array_equal(_host(xt), h)
+    assert_close(_host(y), D.rms_norm(h, w, 1e-6), f"rms_norm H={H} residual={residual}", **TIGHT)
+
+
+@pytest.mark.parametrize("B,L,offset,nh,nkv,d", [
+    (1, 1, 0, 4, 4, 128),      # the first decode position
+    (2, 9, 0, 4, 2, 64),       # prefill, GQA
+    (1, 70, 0, 2, 2, 128),     # two query tiles
+    (3, 1, 77, 4, 4, 128),     # decode across a key-block boundary
+    (2, 66, 60, 2, 1, 128),    # a prefill continuing a cache
+])
+def test_attention_against_oracle(B, L, offset, nh, nkv, d):
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(64 + L + offset)
+    max_len = offset + L + 5
+    theta = 1e6
+    # caches hold positions [0, offset) from an earlier call (random), the rest is garbage
+    ck = np.full((B, nkv, max_len, d), 0x7FC0, np.uint16)  # NaN: must never be read
+    cv = ck.copy()
+    ck[:, :, :offset] = _rnd(rng, (B, nkv, offset, d))
+    cv[:, :, :offset] = _rnd(rng, (B, nkv, offset, d))
+    q, k, v = _rnd(rng, (B * L, nh * d)), _rnd(rng, (B * L, nkv * d)), _rnd(rng, (B * L, nkv * d))
+    bq, bk, bv = _rnd(rng, nh * d, 0.02), _rnd(rng, nkv * d, 0.02), _rnd(rng, nkv * d, 0.02)
+    qt, ckt, cvt = _dev(q), _dev(ck), _dev(cv)
+    out = ops.attention(qt, _dev(k), _dev(v), ckt, cvt, B, L, offset, theta, q_bias=_dev(bq), k_bias=_dev(bk),
+                        v_bias=_dev(bv))
+    pos = offset + np.tile(np.arange(L), B)
+    q_ref = D.rope(D.add(q, bq[None]), pos, nh, d, theta)
+    k_ref = D.rope(D.add(k, bk[None]), pos, nkv, d, theta)
+    v_ref = D.add(v, bv[None])
+    ck_ref, cv_ref = ck.copy(), cv.copy()
+    ck_ref[:, :, offset:offset + L] = k_ref.reshape(B, L, nkv, d).transpose(0, 2, 1, 3)
+    cv_ref[:, :, offset:offset + L] = v_ref.reshape(B, L, nkv, d).transpose(0, 2, 1, 3)
+    # rotated q and the cache rows: RoPE's cos / sin may differ by an fp32 ulp from numpy's
+    assert_close(_host(qt), q_ref, "rope q", max_rel=1e-2, mae_rel=1e-4)
+    got_ck, got_cv = _host(ckt), _host(cvt)
+    np.testing.assert_array_equal(got_cv[:, :, :offset + L], cv_ref[:, :, :offset + L])
+    np.testing.assert_array_equal(got_ck[:, :, :offset], ck_ref[:, :, :offset])
+    assert_close(got_ck[:, :, offset:offset + L], ck_ref[:, :, offset:offset + L], "rope k", max_rel=1e-2, mae_rel=1e-4)
+    ref = D.sdpa(q_ref, ck_ref, cv_ref, B, L, offset, nh, nkv, d)
+    assert_close(_host(out), ref, f"sdpa B={B} L={L} offset={offset}", max_rel=2e-2, mae_rel=5e-3)
+
+
+def test_swiglu():
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(65)
+    g, u = _rnd(rng, (7, 1408), 3.0), _rnd(rng, (7, 1408))
+    gf, uf = D.f32(g), D.f32(u)
+    ref = D.bf16(D.f32(D.bf16(gf * D.f32(D.bf16(1 / (1 + np.exp(-gf)))))) * uf)
+    assert_close(_host(ops.swiglu(_dev(g), _dev(u))), ref, "swiglu", max_rel=1e-2, mae_rel=1e-4)
+
+
+def test_argmax_first_of_ties():
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(66)
+    lg = _rnd(rng, (6, 151936))
+    lg[1, [5, 100000]] = D.bf16(np.float32(50.0))   # a tie: the lower index wins
+    lg[2, :] = D.bf16(np.float32(-3.0))             # all equal
+    lg[3, 151935] = D.bf16(np.float32(99.0))        # the last element
+    got = ops.argmax(_dev(lg))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), D.argmax(lg))
+
+
+# ---------------------------------------------------------------- the whole decoder
+MOE = S.MoEShape("dec_moe", 256, 128, 4, 2, 0, False, 256)
+SMALL = S.DecoderShape("dec_small", 256, 2, 4, 2, 64, 320, 1e6, 1e-6, MOE)
+
+
+def _clear_tokens(logits_bits, ulps=4):
+    """Rows whose top two logits are more than `ulps` bf16 ulps apart (at their scale)."""
+    f = np.sort(D.f32(logits_bits), axis=-1)
+    gap = f[:, -1] - f[:, -2]
+    return gap > ulps * np.abs(f[:, -1]) * 2.0 ** -8
+
+
+def test_decoder_against_oracle():
+    from flashmlx_b200 import decoder as DEC
+    w = S.make_decoder(SMALL, 71)
+    B, L = 2, 9
+    prompt = np.random.default_rng(71).integers(0, SMALL.vocab, (B, L)).astype(np.int32)
+    dec = DEC.Decoder.from_weights(SMALL, DEC.upload_weights(w, "cuda"), "cuda", B, 16)
+    ora = D.Decoder(SMALL, w, B, 16)
+    nxt = dec.forward(torch.from_numpy(prompt).cuda())
+    ref = ora.forward(prompt)
+    assert_close(_host(dec.logits(B, SMALL.vocab, "cuda")), ref, "prefill logits", **EXACT_FLOOR)
+    clear = _clear_tokens(ref)
+    np.testing.assert_array_equal(nxt.cpu().numpy()[clear], D.argmax(ref)[clear])
+    # teacher-forced decode steps: both sides take the oracle's tokens
+    tok = D.argmax(ref)
+    for step in range(3):
+        dec.forward(torch.from_numpy(tok[:, None].copy()).cuda())
+        ref = ora.forward(tok[:, None])
+        assert_close(_host(dec.logits(B, SMALL.vocab, "cuda")), ref, f"decode step {step} logits", **EXACT_FLOOR)
+        tok = D.argmax(ref)
+    assert dec.offset == L + 3
+
+
+def test_decoder_from_checkpoint_and_generate(tmp_path):
+    """fmh_decoder_open over a written checkpoint equals the decoder over the same weights
+    uploaded directly (same kernels, bit for bit); generate() equals manual stepping."""
+    from flashmlx_b200 import decoder as DEC
+    from tests.decoder_util import write_decoder_checkpoint
+    w = S.make_decoder(SMALL, 72)
+    write_decoder_checkpoint(str(tmp_path), SMALL, w)
+    B, L, steps = 2, 6, 5
+    prompt = np.random.default_rng(72).integers(0, SMALL.vocab, (B, L)).astype(np.int32)
+    a = DEC.Decoder.open(str(tmp_path), "cuda", B, L + steps)
+    b = DEC.Decoder.from_weights(SMALL, DEC.upload_weights(w, "cuda"), "cuda", B, L + steps)
+    ta = a.generate(prompt, steps)
+    tb = b.generate(prompt, steps)
+    np.testing.assert_array_equal(ta, tb)
+    b.reset()
+    seq = [b.forward(torch.from_numpy(prompt).cuda())]
+    for _ in range(steps - 1):
+        seq.append(b.forward(seq[-1][:, None].contiguous()))
+    np.testing.assert_array_equal(torch.stack(seq, 1).cpu().numpy(), tb)

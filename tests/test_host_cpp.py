@@ -251,3 +251,16 @@ def test_generate_without_a_device_fails_loudly(tmp_path, fm_host):
     np.zeros((1, 4), np.int32).tofile(tmp_path / "p.bin")
     r = _run(fm_host, "generate", tmp_path, tmp_path / "p.bin", 1, 4, 3, tmp_path / "o.bin", check=False)
     assert r.returncode == 3 and r.stderr.startswith("fm_status 3"), (r.returncode, r.stderr)
+
+
+def test_fmh_binding_matches_header_and_exports(fm_host):
+    """Every function fmh.h declares is exported by libflashmoe_host.so and bound by
+    flashmlx_b200.decoder (and nothing else is)."""
+    import re
+    from flashmlx_b200 import decoder as DEC
+    hdr = open(os.path.join(os.path.dirname(DEC.__file__), "host", "fmh.h")).read()
+    declared = set(re.findall(r"\b(fmh_\w+)\s*\(", hdr))
+    assert declared == set(DEC.SIGNATURES), declared ^ set(DEC.SIGNATURES)
+    lib = DEC.load()
+    for name in declared:
+        assert hasattr(lib, name), name
