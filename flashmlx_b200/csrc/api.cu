@@ -70,6 +70,7 @@ struct fm_handle {
   int gemv_blocks_per_sm = 0;
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
+  bool attn_ready = false;  // attention kernels' shared-memory opt-in done (first fm_attention)
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
   bool borrowed_ws = false;  // ws is fixed scratch the handle must never grow or free
@@ -705,7 +706,6 @@ int fm_create(fm_handle** out, int device, void* stream) {
   if (e == cudaSuccess) e = fm::tc::init();
   if (e == cudaSuccess) e = fm::tc::max_pairs(&h->tc_pairs);
   if (e == cudaSuccess && h->tc_pairs < 1) e = cudaErrorInvalidConfiguration;
-  if (e == cudaSuccess) e = fm::attn_init();
   if (e != cudaSuccess) {
     cudaGetLastError();
     delete h;
@@ -1695,6 +1695,11 @@ int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uin
       !aligned16(out))
     return set_err(h, FM_EINVAL, "q, k, v, caches and out must be 16-byte aligned");
   if (out == q) return set_err(h, FM_EINVAL, "out may not alias q");
+  if (!h->attn_ready) {
+    const cudaError_t ie = fm::attn_init();
+    if (ie != cudaSuccess) return cuda_err(h, ie, "attention kernel set-up");
+    h->attn_ready = true;
+  }
   fm::AttnArgs a;
   std::memset(&a, 0, sizeof(a));
   a.q = q;
