@@ -264,3 +264,15 @@ def test_fmh_binding_matches_header_and_exports(fm_host):
     lib = DEC.load()
     for name in declared:
         assert hasattr(lib, name), name
+
+
+def test_json_reader(tmp_path):
+    """The C++ JSON reader's own unit tests (tests/cpp/test_json.cpp), built with g++."""
+    import shutil
+    here = os.path.dirname(os.path.abspath(__file__))
+    exe = str(tmp_path / "test_json")
+    subprocess.check_call([shutil.which("g++") or "g++", "-std=c++17", "-O1", "-Wall", "-Wextra", "-Werror",
+                           "-I", os.path.join(os.path.dirname(here), "flashmlx_b200", "host"),
+                           os.path.join(here, "cpp", "test_json.cpp"), "-o", exe])
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
