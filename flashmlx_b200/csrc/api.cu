@@ -28,6 +28,8 @@ __global__ void finalize_kernel(const float* y_acc, const float* ysh, const floa
                                 uint16_t* y);
 __global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
                                       const float* gate_sig, int64_t T, int H, uint16_t* y);
+__global__ void finalize_pairs_f32_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, const float* score, int k,
+                                          const uint16_t* ysh16, const float* gate_sig, int64_t T, int H, uint16_t* y);
 __global__ void ep_plan_kernel(const EpPlanArgs a);
 __global__ void ep_gather_kernel(const uint16_t* x_perm, const int32_t* sorted_token, int64_t P, int H, uint16_t* send);
 __global__ void finalize_ep_kernel(const uint16_t* ret, const int32_t* pair_pos, const float* score, int k,
@@ -303,9 +305,9 @@ bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols) {
 template <int MODE>
 int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps* maps = nullptr) {
   static const char* names[2][5] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain", "qgemv_relu2", "qgemv_down"},
-                                    {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain", "", ""}};
+                                    {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain", "qgemm_tc_relu2", ""}};
   if (tcgen05 && !maps) return set_err(h, FM_EINVAL, "tcgen05 launch without tensor maps");
-  if (tcgen05 && MODE > fm::MODE_PLAIN) return set_err(h, FM_EUNSUPPORTED, "variant modes run on the GEMV path");
+  if (tcgen05 && MODE == fm::MODE_DOWN_F32) return set_err(h, FM_EUNSUPPORTED, "fp32-score down runs on the GEMV path");
   prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
   const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->tc_pairs, h->stream, ga, *maps)
                                 : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
@@ -1059,7 +1061,12 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   const bool shared = Is > 0;
   const int epad = (E + 1 + 7) / 8 * 8;
   const int ksplit = router_ksplit(h, T, H);
-  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, Is, shared, true, false);
+  // The tcgen05 expert path (relu^2 epilogue, bf16(d) per pair, combine with the scores
+  // in fp32 for sigmoid routing) runs when the handle's path is FM_PATH_TCGEN05; the
+  // automatic choice keeps the GEMV path for the variants.
+  const bool tcp = h->path == FM_PATH_TCGEN05 && I % 128 == 0 && Is % 128 == 0;
+  const int64_t P = T * k;
+  Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, Is, shared, true, tcp);
   int rc = ensure_ws(h, p.total);
   if (rc) return rc;
 
@@ -1080,10 +1087,11 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   ra.partial = at<float>(h, p.partial);
   ra.x_perm = at<uint16_t>(h, p.x_perm);
   ra.x_rows = T;
-  ra.zero0 = at<float>(h, p.y_acc);
-  ra.zero0_n = T * H;
-  ra.zero1 = shared ? at<float>(h, p.ysh) : nullptr;
-  ra.zero1_n = shared ? T * H : 0;
+  ra.zero0 = tcp ? nullptr : at<float>(h, p.y_acc);
+  ra.zero0_n = tcp ? 0 : T * H;
+  ra.zero1 = (shared && !tcp) ? at<float>(h, p.ysh) : nullptr;
+  ra.zero1_n = (shared && !tcp) ? T * H : 0;
+  ra.pair_pos = tcp ? at<int32_t>(h, p.pair_pos) : nullptr;
   ra.topk_ids = at<int32_t>(h, p.topk_ids);
   ra.topk_score = at<float>(h, p.topk_score);
   ra.gate_sig = at<float>(h, p.gate_sig);
@@ -1097,14 +1105,16 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   ra.sorted_flat = at<int32_t>(h, p.sorted_flat);
   ra.tab_a = at<TileTable>(h, p.tab_a);
   ra.tab_b = at<TileTable>(h, p.tab_b);
-  ra.a_rows_per_block = relu2 ? 128 : 64;  // relu^2: one matrix, 4 warps x 32 rows
+  // GEMV: relu^2 is one matrix of 4 warps x 32 rows, gate/up 64 rows of each; tcgen05:
+  // 256 rows of one matrix per CTA pair, or 128 of gate and up each
+  ra.a_rows_per_block = tcp ? (relu2 ? 256 : 128) : (relu2 ? 128 : 64);
   ra.a_n = I;
   ra.a_n_shared = Is;
   ra.b_n = H;
-  ra.b_rows_per_block = 128;
-  ra.chunk_max = 8;
-  ra.chunk_align = 8;
-  ra.b_ksplit_shared = ksplit_sh;
+  ra.b_rows_per_block = tcp ? 256 : 128;
+  ra.chunk_max = tcp ? fm::tc::max_rows() : 8;
+  ra.chunk_align = tcp ? 16 : 8;
+  ra.b_ksplit_shared = tcp ? 1 : ksplit_sh;
   ra.has_shared = shared ? 1 : 0;
   if (outs) {
     ra.out_topk_ids = outs->topk_ids;
@@ -1157,7 +1167,25 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   ga.out_shared = shared ? at<uint16_t>(h, p.a_shared) : nullptr;
   ga.out_shared_ld = Is;
   ga.tab = ra.tab_a;
-  rc = relu2 ? launch_gemm<fm::MODE_RELU2>(h, ga, false) : launch_gemm<fm::MODE_GATEUP>(h, ga, false);
+  fm::TcMaps maps_a, maps_dn;
+  if (tcp) {
+    // relu^2: one 128-row code box of fc1 per CTA; gate/up: 64 rows of each
+    const int box = relu2 ? 128 : 64;
+    bool ok = encode_codes(&maps_a.code[0], relu2 ? w->up.w : w->gate.w, static_cast<int64_t>(E) * I, H, box) &&
+              encode_codes(&maps_a.code[1], relu2 ? nullptr : w->up.w, relu2 ? 0 : static_cast<int64_t>(E) * I, H, box) &&
+              encode_codes(&maps_a.code[2], shared ? (relu2 ? w->shared_up.w : w->shared_gate.w) : nullptr, Is, H, box) &&
+              encode_codes(&maps_a.code[3], (shared && !relu2) ? w->shared_up.w : nullptr, Is, H, box) &&
+              encode_act(&maps_a.act[0], ra.x_perm, T, H) &&
+              encode_act(&maps_a.act[1], shared ? ra.x_perm : nullptr, T, H) &&
+              encode_codes(&maps_dn.code[0], w->down.w, static_cast<int64_t>(E) * H, I, 128) &&
+              encode_codes(&maps_dn.code[1], nullptr, 0, I, 128) &&
+              encode_codes(&maps_dn.code[2], shared ? w->shared_down.w : nullptr, H, shared ? Is : I, 128) &&
+              encode_codes(&maps_dn.code[3], nullptr, 0, I, 128) &&
+              encode_act(&maps_dn.act[0], at<uint16_t>(h, p.a_sorted), P, I) &&
+              encode_act(&maps_dn.act[1], shared ? at<uint16_t>(h, p.a_shared) : nullptr, T, Is);
+    if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
+  }
+  rc = relu2 ? launch_gemm<fm::MODE_RELU2>(h, ga, tcp, &maps_a) : launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_a);
   if (rc) return rc;
   GemmArgs gd = ga;
   gd.K = I;
@@ -1176,16 +1204,32 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   gd.act_shared_ld = Is;
   gd.out = nullptr;
   gd.out_shared = nullptr;
-  gd.y_acc = at<float>(h, p.y_acc);
-  gd.ysh = shared ? at<float>(h, p.ysh) : nullptr;
+  gd.y_acc = tcp ? nullptr : at<float>(h, p.y_acc);
+  gd.ysh = (shared && !tcp) ? at<float>(h, p.ysh) : nullptr;
+  gd.y_pairs = tcp ? at<uint16_t>(h, p.y_pairs) : nullptr;
+  gd.ysh16 = (shared && tcp) ? at<uint16_t>(h, p.ysh16) : nullptr;
+  gd.unit_score = (tcp && sig) ? 1 : 0;  // tcgen05 + sigmoid scores: bf16(d) per pair, scaled in the combine
   gd.y_ld = H;
   gd.tab = ra.tab_b;
-  rc = sig ? launch_gemm<fm::MODE_DOWN_F32>(h, gd, false) : launch_gemm<fm::MODE_DOWN>(h, gd, false);
+  if (tcp)
+    rc = launch_gemm<fm::MODE_DOWN>(h, gd, true, &maps_dn);
+  else
+    rc = sig ? launch_gemm<fm::MODE_DOWN_F32>(h, gd, false) : launch_gemm<fm::MODE_DOWN>(h, gd, false);
   if (rc) return rc;
   prof_begin(h, "finalize");
-  const int64_t n4 = T * H / 4;
-  const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
-  fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
+  if (tcp) {
+    const int64_t n8 = T * H / 8;
+    const int fb = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+    if (sig)
+      fm::finalize_pairs_f32_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, ra.topk_score, k, gd.ysh16,
+                                                               ra.gate_sig, T, H, y);
+    else
+      fm::finalize_pairs_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
+  } else {
+    const int64_t n4 = T * H / 4;
+    const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
+    fm::finalize_kernel<<<fb, 256, 0, h->stream>>>(gd.y_acc, gd.ysh, ra.gate_sig, T, H, y);
+  }
   prof_end(h);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_err(h, e, "finalize launch");

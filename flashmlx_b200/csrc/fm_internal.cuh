@@ -78,8 +78,9 @@ FM_DEV TileInfo decode_tile(const TileTable* tab, const int* tile_begin, int ngr
 }
 
 // MODE_RELU2: one ungated matrix (fc1) per expert with relu^2, written like gate/up's
-// activation rows for the down matrix; MODE_DOWN_F32: down with fp32 routing scores, the
-// product d * score kept in fp32 (the sigmoid-routed variant's combine).  GEMV only.
+// activation rows for the down matrix (GEMV and tcgen05); MODE_DOWN_F32: down with fp32
+// routing scores, the product d * score kept in fp32 (the sigmoid-routed variant's
+// combine; GEMV only: the tcgen05 path stores bf16(d) per pair and combines separately).
 enum GemmMode : int { MODE_GATEUP = 0, MODE_DOWN = 1, MODE_PLAIN = 2, MODE_RELU2 = 3, MODE_DOWN_F32 = 4 };
 
 // Arguments of the expert-product kernels (GEMV and tcgen05 paths).
@@ -89,7 +90,7 @@ struct GemmArgs {
   int N;          // output rows of a routed matrix (I for gate/up, H for down)
   int N_shared;   // output rows of a shared matrix
   int gs;         // quantization group size
-  int pad0;
+  int unit_score; // tcgen05 down: store bf16(d) per routed pair (the scores are applied by the combine)
   // routed matrices, stacked [E, N, K/8]; gate/up mode: 0 = gate, 1 = up
   const uint32_t* w0; const uint16_t* s0; const uint16_t* b0;
   const uint32_t* w1; const uint16_t* s1; const uint16_t* b1;

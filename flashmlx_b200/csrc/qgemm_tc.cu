@@ -19,6 +19,9 @@
 //                 per routed pair (expert-major rows; the combine kernel sums the k
 //                 pairs of a token in a fixed order) or bf16(d) per shared row.
 //   plain mode:   quantized_matmul / gather_qmm output rows, bf16.
+//   relu2 mode:   A = 128 rows of one ungated matrix (fc1) per CTA; the epilogue stores
+//                 bf16(relu(bf16(acc))^2) as pair-permuted activation rows for down (the
+//                 sigmoid-routed variant, nemotron_h.cpp:53-58).
 //
 // Data movement: packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows) per
 // load, 128B-swizzled, into a 3-deep ring per CTA.  Contiguous activation rows arrive
@@ -723,6 +726,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           store_staged(stg, 64, col0, N - col0,
                        [&](int i) -> uint16_t* { return i < c_lim ? outb + static_cast<int64_t>(prow + i) * ld : nullptr; },
                        et);
+        } else if (MODE == MODE_RELU2) {
+          // staging row = token column c, this CTA's 128 outputs at their pair-permuted
+          // slots (n -> perm8(n)); outputs n and n + 4 (lanes L and L ^ 4) share one word
+          const int pn = perm8(row_in);
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float r = fmaxf(rbf(v[c]), 0.f);
+            const uint32_t mine = f2bf(r * r);
+            const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 4);
+            if ((row_in & 4) == 0) *reinterpret_cast<uint32_t*>(stg + c * 256 + pn * 2) = mine | (other << 16);
+          }
+          named_bar_sync(1, 128);
+          uint16_t* outb = sh ? a.out_shared : a.out;
+          const int64_t ld = sh ? a.out_shared_ld : a.out_ld;
+          const int col0 = ti.rb * 256 + rank * 128;
+          store_staged(stg, 128, col0, N - col0,
+                       [&](int i) -> uint16_t* { return i < c_lim ? outb + static_cast<int64_t>(prow + i) * ld : nullptr; },
+                       et);
         } else {
           // staging row = token column c, 128 outputs; lanes (2m, 2m+1) hold rows
           // (n, n+1): the even lane stores even columns, the odd lane odd columns
@@ -731,7 +752,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           // routing scores are bf16 values, so bf16(bf16(d) * score) per MLX op is one
           // bf16x2 product per column pair; lane c (even) holds the scores of columns c, c+1
           uint32_t s_pair = 0x3F803F80u;  // (1, 1)
-          if (MODE == MODE_DOWN && !sh) {
+          if (MODE == MODE_DOWN && !sh && !a.unit_score) {
             const float my_score = a.sorted_score[pc];
             s_pair = pack_bf16x2(my_score, __shfl_down_sync(0xffffffffu, my_score, 1));
           }
@@ -739,7 +760,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int c = 0; c < 32; c += 2) {
             uint32_t r2 = pack_bf16x2(v[c], v[c + 1]);  // this row, columns c and c+1
-            if (MODE == MODE_DOWN && !sh) r2 = bmul2(r2, __shfl_sync(0xffffffffu, s_pair, c));
+            if (MODE == MODE_DOWN && !sh && !a.unit_score) r2 = bmul2(r2, __shfl_sync(0xffffffffu, s_pair, c));
             // lanes (2m, 2m+1) hold rows (n0, n0+1): the even lane stores column c, the
             // odd lane column c+1, each word holding both rows
             const uint32_t other = __shfl_xor_sync(0xffffffffu, r2, 1);
@@ -815,6 +836,14 @@ cudaError_t launch(int mode, int pairs, cudaStream_t stream, const GemmArgs& a, 
   switch (mode) {
     case MODE_GATEUP: qgemm_tc_kernel<MODE_GATEUP><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
     case MODE_DOWN: qgemm_tc_kernel<MODE_DOWN><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
+    case MODE_RELU2: {
+      // its shared-memory limit is set here, on first use, not with the others at fm_create
+      const cudaError_t e =
+          cudaFuncSetAttribute(qgemm_tc_kernel<MODE_RELU2>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+      if (e != cudaSuccess) return e;
+      qgemm_tc_kernel<MODE_RELU2><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps);
+      break;
+    }
     default: qgemm_tc_kernel<MODE_PLAIN><<<grid, THREADS, SMEM_BYTES, stream>>>(a, maps); break;
   }
   return cudaGetLastError();

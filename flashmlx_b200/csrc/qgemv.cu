@@ -445,6 +445,55 @@ __global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, cons
   }
 }
 
+// The sigmoid-routed variant's combine on the tcgen05 path, y = bf16( bf16(sum_j
+// bf16(d_j) * score_j) + bf16(gate * ysh16[t]) ): y_pairs holds bf16(d) per routed pair,
+// the scores are the fp32 routing scores as applied (nemotron_h.cpp:1094-1100: the
+// products and their sum over j = 0..k-1 stay in fp32), gate_sig is 1 for an ungated
+// shared expert.  One thread per 8 outputs.
+__global__ void finalize_pairs_f32_kernel(const uint16_t* __restrict__ y_pairs, const int32_t* __restrict__ pair_pos,
+                                          const float* __restrict__ score, int k, const uint16_t* __restrict__ ysh16,
+                                          const float* __restrict__ gate_sig, int64_t T, int H,
+                                          uint16_t* __restrict__ y) {
+  const int segs = H / 8;
+  const int64_t n = T * segs;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t t = i / segs;
+    const int col = static_cast<int>(i - t * segs) * 8;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int pos = pair_pos[t * k + j];
+      if (pos < 0) continue;
+      const float sc = score[t * k + j];
+      const uint4 v = *reinterpret_cast<const uint4*>(y_pairs + static_cast<int64_t>(pos) * H + col);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = fmaf(bf2f(static_cast<uint16_t>(w[q] & 0xffffu)), sc, acc[2 * q]);
+        acc[2 * q + 1] = fmaf(bf2f(static_cast<uint16_t>(w[q] >> 16)), sc, acc[2 * q + 1]);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc[q] = rbf(acc[q]);
+    if (ysh16) {
+      const float gsv = gate_sig[t];
+      const uint4 s = *reinterpret_cast<const uint4*>(ysh16 + t * H + col);
+      const uint32_t w[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        acc[2 * q] = rbf(acc[2 * q] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] & 0xffffu))));
+        acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(gsv * bf2f(static_cast<uint16_t>(w[q] >> 16))));
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(y + t * H + col) = o;
+  }
+}
+
 // Expert-parallel send buffer: row p = x_perm[sorted_token[p]] (the routed pairs in
 // expert-major order, so the rows bound for each owner rank are contiguous).
 __global__ void ep_gather_kernel(const uint16_t* __restrict__ x_perm, const int32_t* __restrict__ sorted_token,

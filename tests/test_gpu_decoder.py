@@ -10,7 +10,7 @@ carry two layers of such differences plus the two 4-bit GEMM forms, and are comp
 with the EXACT_FLOOR bound; greedy tokens must agree wherever the oracle's top two
 logits are more than a few ulps apart.
 
-These tests have not yet run on a B200: they run when FM_DECODER_GPU_TESTS=1."""
+These tests have not yet run on a B200: they run when FM_NEW_GPU_TESTS=1."""
 from __future__ import annotations
 
 import os
@@ -24,8 +24,8 @@ from oracle import decoder as D
 from tests._parity import EXACT_FLOOR, TIGHT, assert_close
 
 pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FM_DECODER_GPU_TESTS") != "1",
-                                 reason="decoder kernels not yet run on a B200 (FM_DECODER_GPU_TESTS=1 runs them)")]
+              pytest.mark.skipif(os.environ.get("FM_NEW_GPU_TESTS") != "1",
+                                 reason="decoder kernels not yet run on a B200 (FM_NEW_GPU_TESTS=1 runs them)")]
 
 
 def _dev(a):

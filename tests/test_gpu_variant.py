@@ -5,6 +5,8 @@ oracle's restatement: the routing against the oracle's own routing where no near
 decides a pick, the block against the oracle under the device's routing."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -81,3 +83,29 @@ def test_variant_rejects_bad_arguments():
     blk.block.W.router_bias = blk.block.weights.router_w.data_ptr()  # a softmax-only logit bias
     with pytest.raises(FlashMoEError):
         blk(x)
+
+
+@pytest.mark.skipif(os.environ.get("FM_NEW_GPU_TESTS") != "1",
+                    reason="the variant's tcgen05 path has not run on a B200 yet (FM_NEW_GPU_TESTS=1 runs it)")
+@pytest.mark.parametrize("tokens", [48, 700])
+@pytest.mark.parametrize("shared", [0, 256])
+def test_sigmoid_block_tcgen05_path(tokens, shared):
+    """The variant on the tcgen05 expert path (FM_PATH_TCGEN05): the relu^2 epilogue of
+    the 2-CTA GEMM, bf16(d) per routed pair, the fp32-score combine."""
+    from flashmlx_b200 import _lib, ops
+    shape = _shape(tokens, shared)
+    layer = S.make_sigmoid_layer(shape, 24)
+    x_np = S.make_x(shape, 24)
+    routing = {"n_group": 4, "topk_group": 2, "routed_scaling_factor": 2.5}
+    blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", **routing)
+    h = blk.block._h(torch.device("cuda"))
+    h.set_path(_lib.FM_PATH_TCGEN05)
+    try:
+        y, r = blk(ops.bf16_from_numpy(x_np, "cuda"), return_routing=True)
+        torch.cuda.synchronize()
+    finally:
+        h.set_path(_lib.FM_PATH_AUTO)
+    L = O.SigmoidLayer(shape, layer, routing)
+    ids, sc = r["topk_ids"].cpu().numpy(), r["topk_scores_f32"].cpu().numpy()
+    check_vs_oracle(host_bf16(y), lambda: L.moe_block(x_np, forced_ids=ids, forced_scores=sc),
+                    f"sigmoid block tcgen05 T={tokens} shared={shared}")
