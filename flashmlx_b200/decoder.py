@@ -72,6 +72,10 @@ def load() -> C.CDLL:
     return lib
 
 
+def _index(dev: torch.device) -> int:
+    return dev.index if dev.index is not None else torch.cuda.current_device()
+
+
 def _q(t):
     return _lib.QWeight(*(x.data_ptr() if x is not None else None for x in t)) if t is not None else _lib.QWeight()
 
@@ -206,7 +210,7 @@ class Decoder:
         stream = torch.cuda.current_stream(dev)
         out = C.c_void_p()
         torch.cuda.synchronize(dev)  # the dequantized table is ready before another stream may read it
-        rc = lib.fmh_decoder_create(C.byref(cfg), C.byref(wt), dev.index or 0, max_batch, max_len,
+        rc = lib.fmh_decoder_create(C.byref(cfg), C.byref(wt), _index(dev), max_batch, max_len,
                                     C.c_void_p(stream.cuda_stream), C.byref(out))
         if rc != 0:
             raise _lib.FlashMoEError(rc, f"fmh_decoder_create: status {rc}")
@@ -218,7 +222,7 @@ class Decoder:
         dev = torch.device(device)
         stream = torch.cuda.current_stream(dev)
         out = C.c_void_p()
-        rc = lib.fmh_decoder_open(model_dir.encode(), dev.index or 0, max_batch, max_len,
+        rc = lib.fmh_decoder_open(model_dir.encode(), _index(dev), max_batch, max_len,
                                   C.c_void_p(stream.cuda_stream), C.byref(out))
         if rc != 0:
             raise _lib.FlashMoEError(rc, f"fmh_decoder_open: status {rc}")
