@@ -71,6 +71,7 @@ SIGNATURES = {
     "fm_sync_status": (_i, [_p]),
     "fm_reserve": (_i, [_p, C.POINTER(MoEConfig), _i64]),
     "fm_workspace_bytes": (_sz, [_p]),
+    "fm_workspace_size": (_sz, [C.POINTER(MoEConfig), _i64]),
     "fm_set_path": (_i, [_p, _i]),
     "fm_profile_enable": (_i, [_p, _i]),
     "fm_profile_report": (_i, [_p, C.POINTER(KernelTime), _i, C.POINTER(C.c_int), _i]),

@@ -184,6 +184,21 @@ Plan make_plan(int64_t T, int64_t x_rows, int H, int E, int k, int epad, int ksp
   return p;
 }
 
+// the allocation ensure_ws makes for a request of `bytes` (1/8 slack, whole MiB)
+size_t ws_alloc_bytes(size_t bytes) { return align_up(bytes + bytes / 8, 1 << 20); }
+
+// workspace of the largest MoE-block call of max_tokens tokens on either expert path
+// (the router's K split at its maximum)
+size_t reserve_need(const fm_moe_config* c, int64_t max_tokens) {
+  const int epad = (c->num_experts + 1 + 7) / 8 * 8;
+  size_t need = 0;
+  for (bool tcp : {false, true})
+    need = std::max(need, make_plan(max_tokens, max_tokens, c->hidden, c->num_experts, c->top_k, epad,
+                                    fm::kRouterMaxKsplit, c->inter, c->shared_inter, c->shared_inter > 0, true, tcp)
+                              .total);
+  return need;
+}
+
 int ensure_ws(fm_handle* h, size_t bytes) {
   if (bytes <= h->ws_bytes) return FM_OK;
   if (h->borrowed_ws) return set_err(h, FM_ETOOLARGE, "request exceeds the fixed scratch");
@@ -192,7 +207,7 @@ int ensure_ws(fm_handle* h, size_t bytes) {
   if (h->ws) cudaFree(h->ws);
   h->ws = nullptr;
   h->ws_bytes = 0;
-  const size_t want = align_up(bytes + bytes / 8, 1 << 20);
+  const size_t want = ws_alloc_bytes(bytes);
   e = cudaMalloc(&h->ws, want);
   if (e != cudaSuccess) {
     cudaGetLastError();
@@ -822,15 +837,14 @@ int fm_sync_status(fm_handle* h) {
 
 int fm_reserve(fm_handle* h, const fm_moe_config* c, int64_t max_tokens) {
   if (!h || !c || max_tokens < 0) return FM_EINVAL;
-  const int epad = (c->num_experts + 1 + 7) / 8 * 8;
-  const int ksplit = router_ksplit(h, max_tokens, c->hidden);
-  (void)ksplit;
-  size_t need = 0;
-  for (bool tcp : {false, true})
-    need = std::max(need, make_plan(max_tokens, max_tokens, c->hidden, c->num_experts, c->top_k, epad, 16, c->inter,
-                                    c->shared_inter, c->shared_inter > 0, true, tcp)
-                              .total);
-  return ensure_ws(h, need);
+  return ensure_ws(h, reserve_need(c, max_tokens));
+}
+
+size_t fm_workspace_size(const fm_moe_config* c, int64_t max_tokens) {
+  if (!c || max_tokens < 0 || c->hidden <= 0 || c->num_experts <= 0 || c->top_k <= 0 || c->inter <= 0 ||
+      c->shared_inter < 0)
+    return 0;
+  return ws_alloc_bytes(reserve_need(c, max_tokens));
 }
 
 int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, const uint16_t* x, int64_t T,

@@ -153,6 +153,10 @@ FM_API int fm_sync_status(fm_handle* h);
 /* Pre-sizes the workspace for fm_moe_block calls of up to max_tokens tokens. */
 FM_API int fm_reserve(fm_handle* h, const fm_moe_config* cfg, int64_t max_tokens);
 FM_API size_t fm_workspace_bytes(const fm_handle* h);
+/* The device workspace fm_reserve(h, cfg, max_tokens) makes a handle hold, computed on
+ * the host without a handle or a device (for a caller budgeting device memory before
+ * creating handles); 0 for an invalid config or max_tokens < 0. */
+FM_API size_t fm_workspace_size(const fm_moe_config* cfg, int64_t max_tokens);
 
 /* Path selection for the expert products.  FM_PATH_AUTO picks the small-batch
  * dequant-GEMV for few tokens per expert and the tcgen05 grouped GEMM otherwise. */

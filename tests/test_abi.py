@@ -85,3 +85,20 @@ def test_oracle_structs_mirror_the_abi():
     from oracle import oracle as O
     assert [f[0] for f in O.MoEConfig._fields_] == [f[0] for f in _lib.MoEConfig._fields_]
     assert C.sizeof(O.MoEWeights) == C.sizeof(_lib.MoEWeights)
+
+
+def test_workspace_size_is_a_host_query():
+    """fm_workspace_size needs no device: it grows with the batch, covers both expert
+    paths, and rejects invalid configs with 0."""
+    import ctypes as C
+    from flashmlx_b200 import _lib
+    lib = _lib.load()
+    cfg = _lib.MoEConfig(2048, 1408, 60, 4, 64, 4, 0, 5632, 0, 0)
+    sizes = [lib.fm_workspace_size(C.byref(cfg), t) for t in (0, 1, 32, 4096, 16384)]
+    assert all(s > 0 for s in sizes) and sizes == sorted(sizes) and sizes[-1] > sizes[0]
+    assert all(s % (1 << 20) == 0 for s in sizes)  # whole MiB, as the handle allocates
+    # 4096 tokens: at least the bf16 activations of every pair (y_pairs, P x H) are held
+    assert sizes[3] >= 4096 * 4 * 2048 * 2
+    bad = _lib.MoEConfig(0, 1408, 60, 4, 64, 4, 0, 5632, 0, 0)
+    assert lib.fm_workspace_size(C.byref(bad), 32) == 0
+    assert lib.fm_workspace_size(C.byref(cfg), -1) == 0
