@@ -76,6 +76,7 @@ SIGNATURES = {
     "fm_profile_enable": (_i, [_p, _i]),
     "fm_profile_report": (_i, [_p, C.POINTER(KernelTime), _i, C.POINTER(C.c_int), _i]),
     "fm_quantized_matmul": (_i, [_p, _p, _i64, _i, _p, _p, _p, _i, _i, _i, _i, _p]),
+    "fm_linear": (_i, [_p, _p, _i64, _i, _p, _p, _p, _i, _i, _i, _p]),
     "fm_gather_qmm": (_i, [_p, _p, _i64, _i, _i, _p, _p, _p, _i, _i, _p, _p, _i64, _i, _i, _i, _i, _p]),
     "fm_moe_block": (_i, [_p, C.POINTER(MoEConfig), C.POINTER(MoEWeights), _p, _i64, _p,
                           C.POINTER(MoEOutputs)]),

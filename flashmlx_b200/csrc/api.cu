@@ -24,6 +24,7 @@
 namespace fm {
 __global__ void route_kernel(const RouteArgs a);
 __global__ void route_kernel_sigmoid(const RouteArgs a);
+__global__ void dense_prep_kernel(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
 __global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
@@ -1250,11 +1251,16 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   return FM_OK;
 }
 
-int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int K, const uint32_t* w,
-                  const uint16_t* scales, const uint16_t* biases, int E, int N, const uint32_t* lhs_indices,
-                  const uint32_t* rhs_indices, int64_t B, int transpose, int group_size, int bits,
-                  int sorted_indices, uint16_t* out) {
-  (void)sorted_indices;  // a hint in MLX; the expert-major order is rebuilt either way
+}  // extern "C"
+
+namespace {
+
+// gather_qmm / quantized_matmul.  direct: one matrix, rows in order (fm_linear) -- the
+// row layout and tile table come from dense_prep_kernel instead of the routing kernel.
+int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int K, const uint32_t* w,
+                    const uint16_t* scales, const uint16_t* biases, int E, int N, const uint32_t* lhs_indices,
+                    const uint32_t* rhs_indices, int64_t B, int transpose, int group_size, int bits, uint16_t* out,
+                    bool direct) {
   if (!h) return FM_EINVAL;
   if (!transpose) return set_err(h, FM_EUNSUPPORTED, "transpose=false is not implemented");
   if (!quant_ok(K, group_size, bits)) return set_err(h, FM_EUNSUPPORTED, "only 4-bit affine, group 32/64/128");
@@ -1311,9 +1317,20 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
   ra.b_ksplit_shared = 1;
   ra.gsync = grid_sync(h);
   ra.err = err_word(h);
-  const int64_t items = (ra.x_rows * (K / 8) + 255) / 256 * 8;
-  rc = launch_route(h, ra, items);
-  if (rc) return rc;
+  if (direct) {
+    const int64_t n = ra.x_rows * (K / 8);
+    const int grid = static_cast<int>(std::max<int64_t>(
+        1, std::min<int64_t>((std::max<int64_t>(n, rows) + 255) / 256, static_cast<int64_t>(h->num_sms) * 8)));
+    prof_begin(h, "dense_prep");
+    fm::dense_prep_kernel<<<grid, 256, 0, h->stream>>>(ra);
+    prof_end(h);
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) return cuda_err(h, le, "dense_prep launch");
+  } else {
+    const int64_t items = (ra.x_rows * (K / 8) + 255) / 256 * 8;
+    rc = launch_route(h, ra, items);
+    if (rc) return rc;
+  }
 
   GemmArgs ga;
   std::memset(&ga, 0, sizeof(ga));
@@ -1342,6 +1359,29 @@ int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
   return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps);
+}
+
+}  // namespace
+
+extern "C" {
+
+int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, int K, const uint32_t* w,
+                  const uint16_t* scales, const uint16_t* biases, int E, int N, const uint32_t* lhs_indices,
+                  const uint32_t* rhs_indices, int64_t B, int transpose, int group_size, int bits,
+                  int sorted_indices, uint16_t* out) {
+  (void)sorted_indices;  // a hint in MLX; the expert-major order is rebuilt either way
+  return gather_qmm_impl(h, x, x_batches, M, K, w, scales, biases, E, N, lhs_indices, rhs_indices, B, transpose,
+                         group_size, bits, out, false);
+}
+
+int fm_linear(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w, const uint16_t* scales,
+              const uint16_t* biases, int N, int group_size, int bits, uint16_t* out) {
+  if (!h) return FM_EINVAL;
+  if (M < 0) return set_err(h, FM_EINVAL, "negative M");
+  if (M == 0) return FM_OK;
+  if (M > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
+  return gather_qmm_impl(h, x, 1, static_cast<int>(M), K, w, scales, biases, 1, N, nullptr, nullptr, 1, 1,
+                         group_size, bits, out, true);
 }
 
 

@@ -560,6 +560,34 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
 
 }  // namespace
 
+// Dense rows in order (fm_linear: one matrix, no indices): the pair-permuted copy of x,
+// identity row maps and a one-group tile table -- what the routing kernel's given-ids path
+// writes in that case -- from one plain launch, without its grid barriers.
+__global__ void __launch_bounds__(256) dense_prep_kernel(const RouteArgs a) {
+  phase_permute_x(a);
+  const int64_t T = a.T;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; r < T;
+       r += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    a.sorted_token[r] = static_cast<int32_t>(r);
+    a.sorted_flat[r] = static_cast<int32_t>(r);
+    a.sorted_score[r] = 1.f;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    TileGroup G;
+    G.expert = 0;
+    G.row_begin = 0;
+    G.rows = static_cast<int32_t>(T);
+    G.ksplit = 1;
+    plan_one(G, a.a_n, a.a_rows_per_block, a.chunk_max, a.chunk_align);
+    G.tile_begin = 0;
+    a.tab_a->g[0] = G;
+    a.tab_a->num_groups = 1;
+    a.tab_a->num_tiles = G.nblocks * G.chunks;
+    a.offsets[0] = 0;
+    a.offsets[1] = static_cast<int32_t>(T);
+  }
+}
+
 FM_DEV unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

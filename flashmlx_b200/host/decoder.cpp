@@ -86,9 +86,9 @@ void Decoder::validate() const {
   }
 }
 
+// the dense projections (q, k, v, o, dense MLP, lm_head): LlamaModel::linear_fast
 void Decoder::qmm(const uint16_t* x, int64_t M, int K, const fm_qweight& w, int N, uint16_t* out) {
-  handle_.check(fm_quantized_matmul(handle_.get(), x, M, K, w.w, w.scales, w.biases, N, 1, cfg_.group_size,
-                                    cfg_.bits, out));
+  handle_.check(fm_linear(handle_.get(), x, M, K, w.w, w.scales, w.biases, N, cfg_.group_size, cfg_.bits, out));
 }
 
 void Decoder::forward(const int32_t* ids, int B, int L, int32_t* next_ids) {

@@ -163,6 +163,29 @@ def quantized_matmul(x, w, scales, biases=None, transpose=True, group_size=64, b
     return out
 
 
+def linear(x, w, scales, biases=None, group_size=64, bits=4, handle=None):
+    """fm_linear: the quantized_matmul of a dense layer (LlamaModel::linear_fast), without
+    the routing kernel; x [..., K] bf16 -> [..., N] bf16."""
+    _need(x, "x", (torch.bfloat16,), None)
+    dev = x.device
+    _need(w, "w", _U32, dev)
+    _need(scales, "scales", (torch.bfloat16,), dev)
+    if biases is not None:
+        _need(biases, "biases", (torch.bfloat16,), dev)
+    K = x.shape[-1]
+    if w.dim() != 2 or w.shape[1] * 32 // bits != K:
+        raise ValueError(f"w of shape {tuple(w.shape)} does not match K={K} at {bits} bits")
+    N = w.shape[0]
+    if scales.shape != (N, K // group_size) or (biases is not None and biases.shape != scales.shape):
+        raise ValueError("scales / biases shape mismatch")
+    out = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    h.check(h.lib.fm_linear(h.h, _ptr(x), x.numel() // K, K, _ptr(w), _ptr(scales), _ptr(biases), N, group_size,
+                            bits, _ptr(out)))
+    return out
+
+
 def gather_qmm(x, w, scales, biases=None, lhs_indices=None, rhs_indices=None, transpose=True, group_size=64,
                bits=4, sorted_indices=False, handle=None):
     """mx::gather_qmm: out[i] = x[lhs(i)] @ dequant(w[rhs[i]])^T, shape batch(idx) + [M, N]."""

@@ -200,6 +200,13 @@ FM_API int fm_gather_qmm(fm_handle* h, const uint16_t* x, int64_t x_batches, int
                   const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t B, int transpose,
                   int group_size, int bits, int sorted_indices, uint16_t* out);
 
+/* out[M, N] = x[M, K] @ w_hat^T for a dense layer (the quantized_matmul of
+ * LlamaModel::linear_fast, model.cpp:476-480, with transpose=true): the same result as
+ * fm_quantized_matmul, but the rows are laid out and tiled by one plain kernel instead of
+ * the routing kernel (no grid barriers; one launch fewer per call on the decode path). */
+FM_API int fm_linear(fm_handle* h, const uint16_t* x, int64_t M, int K, const uint32_t* w, const uint16_t* scales,
+                     const uint16_t* biases, int N, int group_size, int bits, uint16_t* out);
+
 /* y[T, H] = moe_block(x[T, H]).  Replaces LlamaModel::moe_block (model.cpp:750-807):
  * router logits (bf16), softmax (fp32 inside, bf16 out), top-k, optional renorm,
  * gate/up/down expert products with silu(g)*u, bf16(d*score) summed over k, plus

@@ -123,6 +123,22 @@ def test_attention_against_oracle(B, L, offset, nh, nkv, d):
     assert_close(_host(out), ref, f"sdpa B={B} L={L} offset={offset}", max_rel=2e-2, mae_rel=5e-3)
 
 
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 2048), (32, 2048, 512), (100, 1408, 2048), (600, 2048, 1024),
+                                   (3, 2112, 256)])
+def test_linear_equals_quantized_matmul(M, K, N):
+    """fm_linear (rows laid out by dense_prep_kernel) gives fm_quantized_matmul's output bit
+    for bit: the same GEMM kernels on either expert path (GEMV for few rows, tcgen05 for
+    many; K % 128 == 64 always tcgen05)."""
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(M + K + N)
+    w, s, b = S.make_qmatrix(67, "lin", (), N, K, 64, 4)
+    x = _rnd(rng, (M, K))
+    wt, st, bt, xt = ops.u32_from_numpy(w, "cuda"), _dev(s), _dev(b), _dev(x)
+    a = ops.linear(xt, wt, st, bt)
+    ref = ops.quantized_matmul(xt, wt, st, bt)
+    np.testing.assert_array_equal(_host(a), _host(ref))
+
+
 def test_swiglu():
     from flashmlx_b200 import ops
     rng = np.random.default_rng(65)
