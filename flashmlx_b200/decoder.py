@@ -87,7 +87,8 @@ def _moe_config(m) -> _lib.MoEConfig:
 
 def config_of(shape) -> DecoderConfig:
     """The C description of a synthetic.DecoderShape."""
-    return DecoderConfig(shape.hidden, shape.layers, shape.n_heads, shape.n_kv_heads, shape.head_dim, shape.vocab, 0,
+    return DecoderConfig(shape.hidden, shape.layers, shape.n_heads, shape.n_kv_heads, shape.head_dim, shape.vocab,
+                         shape.intermediate,
                          float(shape.rope_theta), float(shape.rms_eps), shape.group_size, shape.bits,
                          int(shape.tie_word_embeddings), _moe_config(shape.moe))
 
@@ -117,7 +118,10 @@ def upload_weights(w: dict, device) -> dict:
         for k in ("q_bias", "k_bias", "v_bias"):
             if lw.get(k) is not None:
                 d[k] = ops.bf16_from_numpy(lw[k], device)
-        d["moe"] = moe(lw["moe"])
+        if "moe" in lw:
+            d["moe"] = moe(lw["moe"])
+        else:
+            d["mlp"] = {k: q(lw["mlp"][k]) for k in ("gate", "up", "down")}
         out["layers"].append(d)
     return out
 
@@ -144,11 +148,16 @@ def device_decoder_weights(shape, seed: int, device) -> dict:
     out = {"embed": qm(shape.vocab, H, 0.1), "norm": vec(H, 1.0, 0.1), "layers": []}
     if not shape.tie_word_embeddings:
         out["lm_head"] = qm(shape.vocab, H)
-    for _ in range(shape.layers):
+    for li in range(shape.layers):
         lw = {"in_norm": vec(H, 1.0, 0.1), "post_norm": vec(H, 1.0, 0.1), "q": qm(nh * d, H), "k": qm(nkv * d, H),
               "v": qm(nkv * d, H), "o": qm(H, nh * d)}
         if shape.attn_bias:
             lw["q_bias"], lw["k_bias"], lw["v_bias"] = vec(nh * d, 0, 0.02), vec(nkv * d, 0, 0.02), vec(nkv * d, 0, 0.02)
+        if li in shape.dense_layers:
+            I = shape.intermediate
+            lw["mlp"] = {"gate": qm(I, H), "up": qm(I, H), "down": qm(H, I)}
+            out["layers"].append(lw)
+            continue
         E, I = m.num_experts, m.inter
         mo = {"router_w": vec(E * H, 0, 0.02).view(E, H)}
         gw, gsc, gb = qm(E * I, H)
@@ -188,6 +197,10 @@ class Decoder:
             L.q, L.k, L.v, L.o = _q(lw["q"]), _q(lw["k"]), _q(lw["v"]), _q(lw["o"])
             for k in ("q_bias", "k_bias", "v_bias"):
                 setattr(L, k, lw[k].data_ptr() if lw.get(k) is not None else None)
+            if "mlp" in lw:  # a dense SwiGLU layer
+                L.is_moe = 0
+                L.gate, L.up, L.down = _q(lw["mlp"]["gate"]), _q(lw["mlp"]["up"]), _q(lw["mlp"]["down"])
+                continue
             L.is_moe = 1
             mo = lw["moe"]
             W = _lib.MoEWeights()

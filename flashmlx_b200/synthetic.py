@@ -133,6 +133,8 @@ class DecoderShape:
     tie_word_embeddings: bool = False
     group_size: int = 64
     bits: int = 4
+    dense_layers: tuple = ()          # layers with a dense SwiGLU MLP instead of an MoE block
+    intermediate: int = 0             # their intermediate_size
 
 
 # the 24-layer Qwen1.5-MoE-A2.7B-shaped decoder, every MoE block as configs[0]
@@ -145,8 +147,9 @@ DECODER_CONFIGS = {
 def make_decoder(shape: DecoderShape, seed: int) -> dict:
     """Random-init weights of a decoder (numpy, bf16 as uint16): the 4-bit embedding
     `embed` (w, s, b) [V, H]; per layer `in_norm`, `post_norm` [H], 4-bit `q`, `k`, `v`, `o`,
-    bf16 `q_bias`, `k_bias`, `v_bias`, and the MoE layer `moe` (make_layer); `norm` [H] and
-    the 4-bit `lm_head` [V, H] unless the embeddings are tied."""
+    bf16 `q_bias`, `k_bias`, `v_bias`, and the MoE layer `moe` (make_layer) or, for the
+    shape's dense layers, the 4-bit SwiGLU MLP `mlp` {gate, up, down}; `norm` [H] and the
+    4-bit `lm_head` [V, H] unless the embeddings are tied."""
     H, nh, nkv, d = shape.hidden, shape.n_heads, shape.n_kv_heads, shape.head_dim
     gs, bits = shape.group_size, shape.bits
 
@@ -166,8 +169,14 @@ def make_decoder(shape: DecoderShape, seed: int) -> dict:
               "q": make_qmatrix(seed, p + "q", (), nh * d, H, gs, bits),
               "k": make_qmatrix(seed, p + "k", (), nkv * d, H, gs, bits),
               "v": make_qmatrix(seed, p + "v", (), nkv * d, H, gs, bits),
-              "o": make_qmatrix(seed, p + "o", (), H, nh * d, gs, bits),
-              "moe": make_layer(shape.moe, seed * 1000 + li)}
+              "o": make_qmatrix(seed, p + "o", (), H, nh * d, gs, bits)}
+        if li in shape.dense_layers:
+            I = shape.intermediate
+            lw["mlp"] = {"gate": make_qmatrix(seed, p + "mlp.gate", (), I, H, gs, bits),
+                         "up": make_qmatrix(seed, p + "mlp.up", (), I, H, gs, bits),
+                         "down": make_qmatrix(seed, p + "mlp.down", (), H, I, gs, bits)}
+        else:
+            lw["moe"] = make_layer(shape.moe, seed * 1000 + li)
         if shape.attn_bias:
             lw["q_bias"], lw["k_bias"], lw["v_bias"] = bias(p + "qb", nh * d), bias(p + "kb", nkv * d), bias(
                 p + "vb", nkv * d)

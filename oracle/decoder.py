@@ -21,6 +21,8 @@ boundary as the reference's op sequence does:
   attention      model.cpp:542-643: q/k/v quantized_matmul, bf16 bias adds, rope,
                  slice_update of the bf16 cache at the batch's (uniform) offset, sdpa, o_proj
   block          model.cpp:813-839: x + attention(rms_norm(x)), then + moe_block / mlp
+  mlp            model.cpp:645-656: down(swiglu(gate(x), up(x))), the swiglu of 14-25 with
+                 bf16 rounding after every op
   embed          model.cpp:216-230, 490-496: the embedding table dequantized once to bf16
                  (bf16(fma(s, q, b))), rows taken by token id
   lm_head        model.cpp:499-520: quantized_matmul with lm_head.* (or the quantized
@@ -114,6 +116,14 @@ def dequantize(w, s, b, group_size: int = 64, bits: int = 4) -> np.ndarray:
     return bf16((sf.astype(np.float64) * q + bfv).astype(np.float32))  # one rounding of the exact s*q + b
 
 
+def swiglu(g, u) -> np.ndarray:
+    """silu(g) * u with bf16 rounding after every op (model.cpp:14-25): bf16(sigmoid(g)),
+    bf16(g * that), bf16(that * u); sigmoid in fp32."""
+    gf = f32(g)
+    sg = f32(bf16(np.float32(1.0) / (np.float32(1.0) + np.exp(-gf))))
+    return bf16(f32(bf16(gf * sg)) * f32(u))
+
+
 def argmax(logits) -> np.ndarray:
     """First index of the maximum along the last axis (bf16 bits compared as values)."""
     return np.argmax(f32(logits), axis=-1).astype(np.int32)
@@ -129,7 +139,7 @@ class Decoder:
 
     def __init__(self, cfg, weights: dict, max_batch: int, max_len: int):
         self.cfg, self.w = cfg, weights
-        self.moe = [O.Layer(cfg.moe, lw["moe"]) for lw in weights["layers"]]
+        self.moe = [O.Layer(cfg.moe, lw["moe"]) if "moe" in lw else None for lw in weights["layers"]]
         shape = (max_batch, cfg.n_kv_heads, max_len, cfg.head_dim)
         self.cache_k = [np.zeros(shape, np.uint16) for _ in range(cfg.layers)]
         self.cache_v = [np.zeros(shape, np.uint16) for _ in range(cfg.layers)]
@@ -146,6 +156,10 @@ class Decoder:
     def _qmm(self, x, q):
         w, s, b = q
         return O.quantized_matmul(x, w, s, b, self.cfg.group_size, self.cfg.bits)
+
+    def mlp(self, x, m):
+        g, u = self._qmm(x, m["gate"]), self._qmm(x, m["up"])
+        return self._qmm(swiglu(g, u), m["down"])
 
     def attention(self, x, li: int, B: int, L: int):
         c, lw = self.cfg, self.w["layers"][li]
@@ -176,7 +190,8 @@ class Decoder:
         x = self.embed(ids)
         for li, lw in enumerate(self.w["layers"]):
             h = add(x, self.attention(rms_norm(x, lw["in_norm"], c.rms_eps), li, B, L))
-            m = self.moe[li].moe_block(rms_norm(h, lw["post_norm"], c.rms_eps))[0]
+            n2 = rms_norm(h, lw["post_norm"], c.rms_eps)
+            m = self.moe[li].moe_block(n2)[0] if self.moe[li] is not None else self.mlp(n2, lw["mlp"])
             x = add(h, m)
             if trace is not None:
                 trace.append(x)

@@ -18,7 +18,8 @@ def write_decoder_checkpoint(path, shape, w, shards: int = 2) -> None:
            "tie_word_embeddings": shape.tie_word_embeddings, "num_experts": m.num_experts,
            "num_experts_per_tok": m.top_k, "moe_intermediate_size": m.inter,
            "shared_expert_intermediate_size": m.shared_inter, "norm_topk_prob": m.norm_topk_prob,
-           "quantization": {"group_size": shape.group_size, "bits": shape.bits}}
+           "quantization": {"group_size": shape.group_size, "bits": shape.bits},
+           "intermediate_size": shape.intermediate or 14336}
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(cfg, f)
     t = {}
@@ -39,7 +40,11 @@ def write_decoder_checkpoint(path, shape, w, shards: int = 2) -> None:
         for proj in ("q", "k", "v"):
             if lw.get(proj + "_bias") is not None:
                 t[f"{p}.self_attn.{proj}_proj.bias"] = lw[proj + "_bias"]
-        t.update(_layer_tensors(lw["moe"], li, stacked=True))
+        if "moe" in lw:
+            t.update(_layer_tensors(lw["moe"], li, stacked=True))
+        else:
+            for proj in ("gate", "up", "down"):
+                q(f"{p}.mlp.{proj}_proj", lw["mlp"][proj])
     names = sorted(t)
     per = (len(names) + shards - 1) // shards
     for i in range(shards):

@@ -213,3 +213,16 @@ def test_decoder_from_checkpoint_and_generate(tmp_path):
     for _ in range(steps - 1):
         seq.append(b.forward(seq[-1][:, None].contiguous()))
     np.testing.assert_array_equal(torch.stack(seq, 1).cpu().numpy(), tb)
+
+
+def test_mixed_decoder_with_a_dense_layer():
+    """A dense SwiGLU layer (fm_linear, fm_swiglu, fm_linear) followed by MoE layers."""
+    from flashmlx_b200 import decoder as DEC
+    mixed = S.DecoderShape("dec_mixed", 256, 3, 4, 2, 64, 320, 1e6, 1e-6, MOE, dense_layers=(0,), intermediate=384)
+    w = S.make_decoder(mixed, 73)
+    B, L = 2, 7
+    prompt = np.random.default_rng(73).integers(0, mixed.vocab, (B, L)).astype(np.int32)
+    dec = DEC.Decoder.from_weights(mixed, DEC.upload_weights(w, "cuda"), "cuda", B, 12)
+    dec.forward(torch.from_numpy(prompt).cuda())
+    ref = D.Decoder(mixed, w, B, 12).forward(prompt)
+    assert_close(_host(dec.logits(B, mixed.vocab, "cuda")), ref, "mixed decoder logits", **EXACT_FLOOR)

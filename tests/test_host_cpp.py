@@ -276,3 +276,12 @@ def test_json_reader(tmp_path):
                            os.path.join(here, "cpp", "test_json.cpp"), "-o", exe])
     r = subprocess.run([exe], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0 and r.stdout.strip() == "ok", r.stdout + r.stderr
+
+
+def test_decoder_checkpoint_with_a_dense_layer(tmp_path, fm_host):
+    shape = S.DecoderShape("dec_mixed", 256, 3, 4, 2, 64, 320, 1e6, 1e-6,
+                           S.MoEShape("dec_moe", 256, 128, 4, 2, 0, False, 256), dense_layers=(0,), intermediate=384)
+    write_decoder_checkpoint(str(tmp_path), shape, S.make_decoder(shape, 54))
+    got = json.loads(_run(fm_host, "check-decoder", tmp_path).stdout)
+    assert got["moe_layers"] == [1, 2] and got["layers"] == 3
+    assert _inspect(fm_host, tmp_path)["intermediate"] == 384

@@ -143,3 +143,30 @@ def test_decoder_configs_are_consistent(name):
     sh = S.DECODER_CONFIGS[name]
     assert sh.n_heads * sh.head_dim == sh.hidden and sh.n_heads % sh.n_kv_heads == 0
     assert sh.moe.hidden == sh.hidden
+
+
+MIXED = S.DecoderShape("dec_mixed", 256, 3, 4, 2, 64, 320, 1e6, 1e-6, MOE, dense_layers=(0,), intermediate=384)
+
+
+def test_dense_layer_mlp():
+    """A dense layer's MLP: down(swiglu(gate(x), up(x))) with the compiled swiglu's bf16
+    rounding after every op (model.cpp:14-25, 645-656), against a float64 restatement of
+    the same rounding chain."""
+    w = S.make_decoder(MIXED, 8)
+    assert "mlp" in w["layers"][0] and "moe" in w["layers"][1]
+    dec = D.Decoder(MIXED, w, 1, 8)
+    x = _bf16(np.random.default_rng(8).standard_normal((5, 256)))
+    m = w["layers"][0]["mlp"]
+    g, u = O.quantized_matmul(x, *m["gate"]), O.quantized_matmul(x, *m["up"])
+    gf = D.f32(g).astype(np.float64)
+    sg = D.f32(_bf16(1.0 / (1.0 + np.exp(-gf))))
+    act = _bf16(D.f32(_bf16(gf * sg)) * D.f32(u))
+    np.testing.assert_array_equal(dec.mlp(x, m), O.quantized_matmul(act, *m["down"]))
+
+
+def test_mixed_decoder_cache_pass_equals_full_pass():
+    w = S.make_decoder(MIXED, 9)
+    ids = np.random.default_rng(9).integers(0, MIXED.vocab, (2, 6))
+    a = D.Decoder(MIXED, w, 2, 8)
+    a.forward(ids[:, :5])
+    np.testing.assert_array_equal(a.forward(ids[:, 5:6]), D.Decoder(MIXED, w, 2, 8).forward(ids))
