@@ -55,7 +55,7 @@ FM_ACT_SWIGLU, FM_ACT_RELU2 = 0, 1
 
 class AttnConfig(C.Structure):
     _fields_ = [("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("max_len", C.c_int),
-                ("rope_theta", C.c_float), ("scale", C.c_float)]
+                ("rope_theta", C.c_float), ("scale", C.c_float), ("norm_eps", C.c_float)]
 
 
 class KernelTime(C.Structure):
@@ -96,7 +96,7 @@ SIGNATURES = {
     "fm_dequantize": (_i, [_p, _p, _p, _p, _i64, _i, _i, _i, _p]),
     "fm_embed": (_i, [_p, _p, _i64, _i, _p, _i64, _p]),
     "fm_rms_norm": (_i, [_p, _p, _p, _p, _i64, _i, C.c_float, _p, _p]),
-    "fm_attention": (_i, [_p, C.POINTER(AttnConfig), _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p]),
+    "fm_attention": (_i, [_p, C.POINTER(AttnConfig), _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p]),
     "fm_swiglu": (_i, [_p, _p, _p, _i64, _p]),
     "fm_argmax": (_i, [_p, _p, _i64, _i64, _p]),
 }

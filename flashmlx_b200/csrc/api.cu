@@ -1775,14 +1775,16 @@ int fm_rms_norm(fm_handle* h, const uint16_t* x, const uint16_t* residual, const
 }
 
 int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uint16_t* k, const uint16_t* v,
-                 const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, uint16_t* cache_k,
-                 uint16_t* cache_v, int B, int L, int offset, uint16_t* out) {
+                 const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, const uint16_t* q_norm,
+                 const uint16_t* k_norm, uint16_t* cache_k, uint16_t* cache_v, int B, int L, int offset,
+                 uint16_t* out) {
   if (!h) return FM_EINVAL;
   if (!cfg) return set_err(h, FM_EINVAL, "null config");
   const int nh = cfg->n_heads, nkv = cfg->n_kv_heads, d = cfg->head_dim;
   if (nh <= 0 || nkv <= 0 || nh % nkv || cfg->max_len <= 0 || !(cfg->rope_theta > 0.f))
     return set_err(h, FM_EINVAL, "bad attention config");
   if (d != 64 && d != 128) return set_err(h, FM_EUNSUPPORTED, "head_dim must be 64 or 128");
+  if ((q_norm || k_norm) && !(cfg->norm_eps >= 0.f)) return set_err(h, FM_EINVAL, "bad QK-norm eps");
   if (B < 0 || L < 0 || offset < 0) return set_err(h, FM_EINVAL, "negative B, L or offset");
   if (B == 0 || L == 0) return FM_OK;
   if (static_cast<int64_t>(offset) + L > cfg->max_len) return set_err(h, FM_EINVAL, "offset + L exceeds max_len");
@@ -1806,6 +1808,9 @@ int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uin
   a.q_bias = q_bias;
   a.k_bias = k_bias;
   a.v_bias = v_bias;
+  a.q_norm = q_norm;
+  a.k_norm = k_norm;
+  a.norm_eps = cfg->norm_eps;
   a.cache_k = cache_k;
   a.cache_v = cache_v;
   a.out = out;

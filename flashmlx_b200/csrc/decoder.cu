@@ -8,7 +8,8 @@
 //   embed_kernel        mx::take(table, ids, 0) (490-496): row copies
 //   add_rms_norm_kernel mx::add (824, 838) + mx::fast::rms_norm (486-488): h = bf16(x + r),
 //                       n = 1 / sqrt(mean_fp32(h^2) + eps), y = bf16(bf16(h * n) * w)
-//   qkv_rope_kernel     bias adds (560-566), mx::fast::rope(traditional=false, base, scale 1,
+//   qkv_rope_kernel     bias adds (560-566), the optional QK-norm (mx::fast::rms_norm of each
+//                       q / k head, 573-581), mx::fast::rope(traditional=false, base, scale 1,
 //                       offset) (588-589), mx::slice_update of the cache (608-617): pairs
 //                       (i, i + d/2) rotated in fp32 by theta = fp32(pos) * inv_freq_i,
 //                       inv_freq_i = base^(-2i/d) evaluated in fp64 and rounded once
@@ -170,7 +171,9 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(const uint16
 // ------------------------------------------------------------------ q/k/v bias + rope + cache
 // One warp per (token, head slot): slots [0, nh) rotate q in place, [nh, nh + nkv) rotate
 // k into cache_k, [nh + nkv, nh + 2 nkv) copy v into cache_v; the bias is added first
-// (bf16 add, model.cpp:560-566).  Lanes take pair indices i, i + 32, ... < d / 2.
+// (bf16 add, model.cpp:560-566), then the head's RMSNorm when a QK-norm weight is given
+// (fp32 sum of squares over the head, bf16(bf16(x * n) * w)).  Lane l holds the pairs
+// (i, i + d/2) for i = l and l + 32 (d <= 128).
 __global__ void qkv_rope_kernel(const AttnArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int slots = a.nh + 2 * a.nkv;
@@ -183,16 +186,19 @@ __global__ void qkv_rope_kernel(const AttnArgs a) {
   const int d = a.head_dim, half = d / 2;
   const uint16_t* src;
   const uint16_t* bias;
+  const uint16_t* norm = nullptr;
   uint16_t* dst;
   bool rot = true;
   if (slot < a.nh) {
     src = a.q + t * a.q_ld + slot * d;
     bias = a.q_bias ? a.q_bias + slot * d : nullptr;
+    norm = a.q_norm;
     dst = a.q + t * a.q_ld + slot * d;
   } else if (slot < a.nh + a.nkv) {
     const int kh = slot - a.nh;
     src = a.k + t * a.kv_ld + kh * d;
     bias = a.k_bias ? a.k_bias + kh * d : nullptr;
+    norm = a.k_norm;
     dst = a.cache_k + ((static_cast<int64_t>(b) * a.nkv + kh) * a.max_len + pos) * d;
   } else {
     const int vh = slot - a.nh - a.nkv;
@@ -201,22 +207,49 @@ __global__ void qkv_rope_kernel(const AttnArgs a) {
     dst = a.cache_v + ((static_cast<int64_t>(b) * a.nkv + vh) * a.max_len + pos) * d;
     rot = false;
   }
-  for (int i = lane; i < half; i += 32) {
-    float x1 = bf2f(src[i]), x2 = bf2f(src[i + half]);
-    if (bias) {
-      x1 = rbf(x1 + bf2f(bias[i]));
-      x2 = rbf(x2 + bf2f(bias[i + half]));
+  // the lane's pairs (i, i + d/2), i = lane + 32 j < d/2, bias added
+  float x1[2] = {0.f, 0.f}, x2[2] = {0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = lane + 32 * j;
+    if (i < half) {
+      x1[j] = bf2f(src[i]);
+      x2[j] = bf2f(src[i + half]);
+      if (bias) {
+        x1[j] = rbf(x1[j] + bf2f(bias[i]));
+        x2[j] = rbf(x2[j] + bf2f(bias[i + half]));
+      }
     }
+  }
+  if (norm) {  // QK-norm over the head's d values (lanes past d/2 hold zeros); norm is warp-uniform
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) ss = fmaf(x1[j], x1[j], fmaf(x2[j], x2[j], ss));
+    ss = warp_sum(ss);
+    const float n = 1.0f / sqrtf(ss / static_cast<float>(d) + a.norm_eps);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int i = lane + 32 * j;
+      if (i < half) {
+        x1[j] = rbf(rbf(x1[j] * n) * bf2f(norm[i]));
+        x2[j] = rbf(rbf(x2[j] * n) * bf2f(norm[i + half]));
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int i = lane + 32 * j;
+    if (i >= half) continue;
+    float o1 = x1[j], o2 = x2[j];
     if (rot) {
       const float inv = static_cast<float>(exp2(-(2.0 * i / d) * a.log2_theta));
       const float ang = static_cast<float>(pos) * inv;
       const float cs = cosf(ang), sn = sinf(ang);
-      const float o1 = x1 * cs - x2 * sn, o2 = x1 * sn + x2 * cs;
-      x1 = o1;
-      x2 = o2;
+      o1 = x1[j] * cs - x2[j] * sn;
+      o2 = x1[j] * sn + x2[j] * cs;
     }
-    dst[i] = f2bf(x1);
-    dst[i + half] = f2bf(x2);
+    dst[i] = f2bf(o1);
+    dst[i + half] = f2bf(o2);
   }
 }
 

@@ -254,12 +254,15 @@ struct AttnArgs {
   const uint16_t* q_bias;   // [nh * d] or null
   const uint16_t* k_bias;   // [nkv * d] or null
   const uint16_t* v_bias;   // [nkv * d] or null
+  const uint16_t* q_norm;   // [d] per-head RMSNorm weight of q (QK-norm) or null
+  const uint16_t* k_norm;   // [d] the same for k
   uint16_t* cache_k;        // [B, nkv, max_len, d]
   uint16_t* cache_v;
   uint16_t* out;            // [B*L, out_ld]
   int64_t q_ld, kv_ld, out_ld;
   int B, L, offset, nh, nkv, head_dim, max_len;
   float scale;              // softmax scale (1/sqrt(d) by default)
+  float norm_eps;           // QK-norm eps
   double log2_theta;        // log2 of the RoPE base
 };
 

@@ -29,7 +29,8 @@ class DecoderConfig(C.Structure):
 class Layer(C.Structure):
     _fields_ = [("in_norm", C.c_void_p), ("post_norm", C.c_void_p), ("q", _lib.QWeight), ("k", _lib.QWeight),
                 ("v", _lib.QWeight), ("o", _lib.QWeight), ("q_bias", C.c_void_p), ("k_bias", C.c_void_p),
-                ("v_bias", C.c_void_p), ("is_moe", C.c_int), ("moe", _lib.MoEWeights), ("gate", _lib.QWeight),
+                ("v_bias", C.c_void_p), ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("is_moe", C.c_int),
+                ("moe", _lib.MoEWeights), ("gate", _lib.QWeight),
                 ("up", _lib.QWeight), ("down", _lib.QWeight)]
 
 
@@ -115,7 +116,7 @@ def upload_weights(w: dict, device) -> dict:
         d = {k: ops.bf16_from_numpy(lw[k], device) for k in ("in_norm", "post_norm")}
         for k in ("q", "k", "v", "o"):
             d[k] = q(lw[k])
-        for k in ("q_bias", "k_bias", "v_bias"):
+        for k in ("q_bias", "k_bias", "v_bias", "q_norm", "k_norm"):
             if lw.get(k) is not None:
                 d[k] = ops.bf16_from_numpy(lw[k], device)
         if "moe" in lw:
@@ -153,6 +154,8 @@ def device_decoder_weights(shape, seed: int, device) -> dict:
               "v": qm(nkv * d, H), "o": qm(H, nh * d)}
         if shape.attn_bias:
             lw["q_bias"], lw["k_bias"], lw["v_bias"] = vec(nh * d, 0, 0.02), vec(nkv * d, 0, 0.02), vec(nkv * d, 0, 0.02)
+        if shape.qk_norm:
+            lw["q_norm"], lw["k_norm"] = vec(d, 1.0, 0.1), vec(d, 1.0, 0.1)
         if li in shape.dense_layers:
             I = shape.intermediate
             lw["mlp"] = {"gate": qm(I, H), "up": qm(I, H), "down": qm(H, I)}
@@ -195,7 +198,7 @@ class Decoder:
             L = layers[i]
             L.in_norm, L.post_norm = lw["in_norm"].data_ptr(), lw["post_norm"].data_ptr()
             L.q, L.k, L.v, L.o = _q(lw["q"]), _q(lw["k"]), _q(lw["v"]), _q(lw["o"])
-            for k in ("q_bias", "k_bias", "v_bias"):
+            for k in ("q_bias", "k_bias", "v_bias", "q_norm", "k_norm"):
                 setattr(L, k, lw[k].data_ptr() if lw.get(k) is not None else None)
             if "mlp" in lw:  # a dense SwiGLU layer
                 L.is_moe = 0

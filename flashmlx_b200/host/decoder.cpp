@@ -31,6 +31,7 @@ Decoder::Decoder(const fmh_decoder_config& cfg, const fmh_weights& w, int device
   attn_.max_len = max_len_;
   attn_.rope_theta = cfg_.rope_theta;
   attn_.scale = 0.f;
+  attn_.norm_eps = cfg_.rms_eps;  // QK-norm uses the model's rms_norm_eps (model.cpp:486-488)
   const int64_t tokens = static_cast<int64_t>(max_batch_) * max_len_;
   const int64_t H = cfg_.hidden, QD = static_cast<int64_t>(cfg_.n_heads) * cfg_.head_dim,
                 KVD = static_cast<int64_t>(cfg_.n_kv_heads) * cfg_.head_dim;
@@ -106,8 +107,8 @@ void Decoder::forward(const int32_t* ids, int B, int L, int32_t* next_ids) {
     qmm(normed_, T, H, l.q, QD, q_);
     qmm(normed_, T, H, l.k, KVD, k_);
     qmm(normed_, T, H, l.v, KVD, v_);
-    handle_.check(fm_attention(h, &attn_, q_, k_, v_, l.q_bias, l.k_bias, l.v_bias, cache_k_[li], cache_v_[li], B, L,
-                               offset_, attn_out_));
+    handle_.check(fm_attention(h, &attn_, q_, k_, v_, l.q_bias, l.k_bias, l.v_bias, l.q_norm, l.k_norm, cache_k_[li],
+                               cache_v_[li], B, L, offset_, attn_out_));
     qmm(attn_out_, T, QD, l.o, H, o_);
     // h = x + attention; normed = rms_norm(h, post_attention_layernorm)
     handle_.check(fm_rms_norm(h, x_, o_, l.post_norm, T, H, eps, x_, normed_));
@@ -234,6 +235,8 @@ DecoderPlan plan_decoder(const Checkpoint& ck) {
     l.q_bias = vview_opt(pre + ".self_attn.q_proj.bias", QD);
     l.k_bias = vview_opt(pre + ".self_attn.k_proj.bias", KVD);
     l.v_bias = vview_opt(pre + ".self_attn.v_proj.bias", KVD);
+    l.q_norm = vview_opt(pre + ".self_attn.q_norm.weight", cfg.head_dim);
+    l.k_norm = vview_opt(pre + ".self_attn.k_norm.weight", cfg.head_dim);
     l.is_moe = ck.has(pre + ".mlp.gate.weight");
     if (!l.is_moe) {
       l.gate = qview(pre + ".mlp.gate_proj", cfg.intermediate, H);
@@ -286,6 +289,8 @@ std::unique_ptr<Decoder> Decoder::open(const std::string& model_dir, int device,
     l.q_bias = static_cast<const uint16_t*>(up(lp.q_bias));
     l.k_bias = static_cast<const uint16_t*>(up(lp.k_bias));
     l.v_bias = static_cast<const uint16_t*>(up(lp.v_bias));
+    l.q_norm = static_cast<const uint16_t*>(up(lp.q_norm));
+    l.k_norm = static_cast<const uint16_t*>(up(lp.k_norm));
     l.is_moe = lp.is_moe ? 1 : 0;
     if (lp.is_moe) {
       l.moe = upload_moe_layer(*store, ck.moe_layer(i), nullptr);

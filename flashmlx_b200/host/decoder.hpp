@@ -46,6 +46,8 @@ struct LayerPlan {
   const TensorView* q_bias = nullptr;
   const TensorView* k_bias = nullptr;
   const TensorView* v_bias = nullptr;
+  const TensorView* q_norm = nullptr;
+  const TensorView* k_norm = nullptr;
   bool is_moe = false;
   QView gate, up, down;
 };

@@ -195,9 +195,13 @@ int check_decoder(const std::string& dir) {
       first = false;
       (void)ck.moe_layer(i);  // the MoE layer's own checks
     }
-  bool bias = p.cfg.layers > 0;
-  for (const auto& l : p.layers) bias = bias && l.q_bias && l.k_bias && l.v_bias;
-  o << "],\"attn_bias\":" << (bias ? "true" : "false") << ",\"embed_quantized\":" << (p.embed.w ? "true" : "false")
+  bool bias = p.cfg.layers > 0, qk_norm = p.cfg.layers > 0;
+  for (const auto& l : p.layers) {
+    bias = bias && l.q_bias && l.k_bias && l.v_bias;
+    qk_norm = qk_norm && l.q_norm && l.k_norm;
+  }
+  o << "],\"attn_bias\":" << (bias ? "true" : "false") << ",\"qk_norm\":" << (qk_norm ? "true" : "false")
+    << ",\"embed_quantized\":" << (p.embed.w ? "true" : "false")
     << ",\"tie_word_embeddings\":" << (p.cfg.tie_word_embeddings ? "true" : "false") << ",\"head_dim\":"
     << p.cfg.head_dim << ",\"vocab\":" << p.cfg.vocab << "}";
   std::cout << o.str() << std::endl;

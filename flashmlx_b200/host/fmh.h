@@ -42,6 +42,8 @@ typedef struct fmh_layer {
   const uint16_t* q_bias;     /* self_attn.{q,k,v}_proj.bias, NULL if absent */
   const uint16_t* k_bias;
   const uint16_t* v_bias;
+  const uint16_t* q_norm;     /* self_attn.{q,k}_norm.weight [head_dim] (QK-norm), NULL if absent */
+  const uint16_t* k_norm;
   int is_moe;                 /* layer_is_moe_ (model.cpp:253-266) */
   fm_moe_weights moe;         /* the stacked MoE weights when is_moe */
   fm_qweight gate, up, down;  /* the dense MLP otherwise */

@@ -449,15 +449,16 @@ def rms_norm(x, weight, eps, residual=None, h_out=None, handle=None) -> torch.Te
 
 
 def attention(q, k, v, cache_k, cache_v, B, L, offset, rope_theta, q_bias=None, k_bias=None, v_bias=None,
-              scale=0.0, handle=None) -> torch.Tensor:
-    """The attention step after the q/k/v projections (model.cpp:560-635): bias adds,
-    RoPE at offset + l, k / v into the caches [B, n_kv, max_len, d] at [offset, offset+L),
-    causal SDPA.  q [B*L, nh*d] is rotated in place; returns [B*L, nh*d] bf16."""
+              scale=0.0, q_norm=None, k_norm=None, norm_eps=1e-6, handle=None) -> torch.Tensor:
+    """The attention step after the q/k/v projections (model.cpp:560-635): bias adds, the
+    optional per-head q / k RMSNorm (QK-norm weights [d]), RoPE at offset + l, k / v into
+    the caches [B, n_kv, max_len, d] at [offset, offset+L), causal SDPA.  q [B*L, nh*d] is
+    rotated in place; returns [B*L, nh*d] bf16."""
     _need(q, "q", (torch.bfloat16,), None)
     dev = q.device
     for t, n in ((k, "k"), (v, "v"), (cache_k, "cache_k"), (cache_v, "cache_v")):
         _need(t, n, (torch.bfloat16,), dev)
-    for t, n in ((q_bias, "q_bias"), (k_bias, "k_bias"), (v_bias, "v_bias")):
+    for t, n in ((q_bias, "q_bias"), (k_bias, "k_bias"), (v_bias, "v_bias"), (q_norm, "q_norm"), (k_norm, "k_norm")):
         if t is not None:
             _need(t, n, (torch.bfloat16,), dev)
     if cache_k.dim() != 4 or cache_v.shape != cache_k.shape or cache_k.shape[0] < B:
@@ -466,12 +467,13 @@ def attention(q, k, v, cache_k, cache_v, B, L, offset, rope_theta, q_bias=None, 
     nh = q.shape[-1] // d
     if q.numel() != B * L * nh * d or k.numel() != B * L * nkv * d or v.numel() != k.numel():
         raise ValueError("q / k / v sizes do not match B, L and the cache heads")
-    cfg = _lib.AttnConfig(nh, nkv, d, max_len, float(rope_theta), float(scale))
+    cfg = _lib.AttnConfig(nh, nkv, d, max_len, float(rope_theta), float(scale), float(norm_eps))
     out = torch.empty(B * L, nh * d, dtype=torch.bfloat16, device=dev)
     h = handle or default_handle(dev.index)
     h.bind_stream()
     h.check(h.lib.fm_attention(h.h, C.byref(cfg), _ptr(q), _ptr(k), _ptr(v), _ptr(q_bias), _ptr(k_bias),
-                               _ptr(v_bias), _ptr(cache_k), _ptr(cache_v), B, L, offset, _ptr(out)))
+                               _ptr(v_bias), _ptr(q_norm), _ptr(k_norm), _ptr(cache_k), _ptr(cache_v), B, L, offset,
+                               _ptr(out)))
     return out
 
 

@@ -135,6 +135,7 @@ class DecoderShape:
     bits: int = 4
     dense_layers: tuple = ()          # layers with a dense SwiGLU MLP instead of an MoE block
     intermediate: int = 0             # their intermediate_size
+    qk_norm: bool = False             # per-head q / k RMSNorm (Qwen3), model.cpp:573-581
 
 
 # the 24-layer Qwen1.5-MoE-A2.7B-shaped decoder, every MoE block as configs[0]
@@ -180,6 +181,9 @@ def make_decoder(shape: DecoderShape, seed: int) -> dict:
         if shape.attn_bias:
             lw["q_bias"], lw["k_bias"], lw["v_bias"] = bias(p + "qb", nh * d), bias(p + "kb", nkv * d), bias(
                 p + "vb", nkv * d)
+        if shape.qk_norm:
+            lw["q_norm"] = f32_to_bf16(1.0 + 0.1 * _rng(seed, p + "qn").standard_normal(d, dtype=np.float32))
+            lw["k_norm"] = f32_to_bf16(1.0 + 0.1 * _rng(seed, p + "kn").standard_normal(d, dtype=np.float32))
         w["layers"].append(lw)
     return w
 

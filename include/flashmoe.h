@@ -272,10 +272,13 @@ typedef struct fm_attn_config {
   int max_len;       /* positions per (sequence, kv head) in the cache */
   float rope_theta;  /* RoPE base (traditional = false, scale 1) */
   float scale;       /* softmax scale; 0 = 1/sqrt(head_dim) */
+  float norm_eps;    /* eps of the per-head q / k RMSNorm (QK-norm), when its weights are given */
 } fm_attn_config;
 
 /* The attention step of a layer after its q/k/v projections (model.cpp:560-635): bias
- * adds (biases may be NULL), RoPE at positions offset + l, k / v written into the caches
+ * adds (biases may be NULL), the per-head RMSNorm of q and k over head_dim when q_norm /
+ * k_norm [head_dim] are given (QK-norm, model.cpp:573-581), RoPE at positions offset + l,
+ * k / v written into the caches
  * [B, n_kv_heads, max_len, head_dim] at [offset, offset + L) (mx::slice_update), and
  * scaled dot-product attention of the L queries over positions [0, offset + l] (causal;
  * mx::fast::scaled_dot_product_attention) into out [T, n_heads*head_dim].  q [T,
@@ -283,8 +286,9 @@ typedef struct fm_attn_config {
  * n_kv_heads*head_dim].  Every sequence of the batch is at the same offset, as in the
  * reference (model.cpp:594-606). */
 FM_API int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uint16_t* k, const uint16_t* v,
-                        const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, uint16_t* cache_k,
-                        uint16_t* cache_v, int B, int L, int offset, uint16_t* out);
+                        const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, const uint16_t* q_norm,
+                        const uint16_t* k_norm, uint16_t* cache_k, uint16_t* cache_v, int B, int L, int offset,
+                        uint16_t* out);
 
 /* out = swiglu(gate, up) elementwise over n values: silu(g) * u with bf16 rounding after
  * every op, the compiled swiglu of model.cpp:14-25, for dense MLP layers (model.cpp:645-656). */

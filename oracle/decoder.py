@@ -18,7 +18,8 @@ boundary as the reference's op sequence does:
                  in float64, rounded to fp32), theta = fp32(pos) * inv_freq_i, rotation in fp32
   sdpa           model.cpp:630-635 -> mx::fast::scaled_dot_product_attention with scale
                  1/sqrt(d), causal for L > 1: fp32 scores, fp32 softmax, fp32 weighted sum
-  attention      model.cpp:542-643: q/k/v quantized_matmul, bf16 bias adds, rope,
+  attention      model.cpp:542-643: q/k/v quantized_matmul, bf16 bias adds, the optional
+                 per-head RMSNorm of q and k (QK-norm, 573-581), rope,
                  slice_update of the bf16 cache at the batch's (uniform) offset, sdpa, o_proj
   block          model.cpp:813-839: x + attention(rms_norm(x)), then + moe_block / mlp
   mlp            model.cpp:645-656: down(swiglu(gate(x), up(x))), the swiglu of 14-25 with
@@ -170,6 +171,11 @@ class Decoder:
             k = add(k, lw["k_bias"][None, :])
         if lw.get("v_bias") is not None:
             v = add(v, lw["v_bias"][None, :])
+        T = q.shape[0]
+        if lw.get("q_norm") is not None:
+            q = rms_norm(q.reshape(T, c.n_heads, c.head_dim), lw["q_norm"], c.rms_eps).reshape(T, -1)
+        if lw.get("k_norm") is not None:
+            k = rms_norm(k.reshape(T, c.n_kv_heads, c.head_dim), lw["k_norm"], c.rms_eps).reshape(T, -1)
         pos = self.offset + np.tile(np.arange(L), B)
         q = rope(q, pos, c.n_heads, c.head_dim, c.rope_theta)
         k = rope(k, pos, c.n_kv_heads, c.head_dim, c.rope_theta)

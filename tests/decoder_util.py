@@ -40,6 +40,9 @@ def write_decoder_checkpoint(path, shape, w, shards: int = 2) -> None:
         for proj in ("q", "k", "v"):
             if lw.get(proj + "_bias") is not None:
                 t[f"{p}.self_attn.{proj}_proj.bias"] = lw[proj + "_bias"]
+        for proj in ("q", "k"):
+            if lw.get(proj + "_norm") is not None:
+                t[f"{p}.self_attn.{proj}_norm.weight"] = lw[proj + "_norm"]
         if "moe" in lw:
             t.update(_layer_tensors(lw["moe"], li, stacked=True))
         else:

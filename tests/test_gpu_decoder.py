@@ -123,6 +123,35 @@ def test_attention_against_oracle(B, L, offset, nh, nkv, d):
     assert_close(_host(out), ref, f"sdpa B={B} L={L} offset={offset}", max_rel=2e-2, mae_rel=5e-3)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_attention_with_qk_norm(d):
+    """QK-norm inside fm_attention: each q / k head RMS-normalised (after the bias, before
+    RoPE), against the oracle's rms_norm of the reshaped heads."""
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(68 + d)
+    B, L, nh, nkv, max_len, theta, eps = 2, 5, 4, 2, 8, 1e6, 1e-6
+    ck = np.zeros((B, nkv, max_len, d), np.uint16)
+    cv = ck.copy()
+    q, k, v = _rnd(rng, (B * L, nh * d), 3.0), _rnd(rng, (B * L, nkv * d), 3.0), _rnd(rng, (B * L, nkv * d))
+    qn, kn = D.bf16(1 + 0.1 * rng.standard_normal(d).astype(np.float32)), D.bf16(
+        1 + 0.1 * rng.standard_normal(d).astype(np.float32))
+    qt, ckt, cvt = _dev(q), _dev(ck), _dev(cv)
+    out = ops.attention(qt, _dev(k), _dev(v), ckt, cvt, B, L, 0, theta, q_norm=_dev(qn), k_norm=_dev(kn),
+                        norm_eps=eps)
+    T = B * L
+    pos = np.tile(np.arange(L), B)
+    q_ref = D.rope(D.rms_norm(q.reshape(T, nh, d), qn, eps).reshape(T, -1), pos, nh, d, theta)
+    k_ref = D.rope(D.rms_norm(k.reshape(T, nkv, d), kn, eps).reshape(T, -1), pos, nkv, d, theta)
+    assert_close(_host(qt), q_ref, "qk-norm q", max_rel=1e-2, mae_rel=1e-4)
+    ck_ref = ck.copy()
+    ck_ref[:, :, :L] = k_ref.reshape(B, L, nkv, d).transpose(0, 2, 1, 3)
+    assert_close(_host(ckt), ck_ref, "qk-norm k cache", max_rel=1e-2, mae_rel=1e-4)
+    cv_ref = cv.copy()
+    cv_ref[:, :, :L] = v.reshape(B, L, nkv, d).transpose(0, 2, 1, 3)
+    ref = D.sdpa(q_ref, ck_ref, cv_ref, B, L, 0, nh, nkv, d)
+    assert_close(_host(out), ref, "qk-norm sdpa", max_rel=2e-2, mae_rel=5e-3)
+
+
 @pytest.mark.parametrize("M,K,N", [(1, 2048, 2048), (32, 2048, 512), (100, 1408, 2048), (600, 2048, 1024),
                                    (3, 2112, 256)])
 def test_linear_equals_quantized_matmul(M, K, N):
@@ -226,3 +255,15 @@ def test_mixed_decoder_with_a_dense_layer():
     dec.forward(torch.from_numpy(prompt).cuda())
     ref = D.Decoder(mixed, w, B, 12).forward(prompt)
     assert_close(_host(dec.logits(B, mixed.vocab, "cuda")), ref, "mixed decoder logits", **EXACT_FLOOR)
+
+
+def test_qk_norm_decoder_against_oracle():
+    from flashmlx_b200 import decoder as DEC
+    qkn = S.DecoderShape("dec_qkn", 256, 2, 4, 2, 64, 320, 1e6, 1e-6, MOE, attn_bias=False, qk_norm=True)
+    w = S.make_decoder(qkn, 74)
+    B, L = 2, 7
+    prompt = np.random.default_rng(74).integers(0, qkn.vocab, (B, L)).astype(np.int32)
+    dec = DEC.Decoder.from_weights(qkn, DEC.upload_weights(w, "cuda"), "cuda", B, 12)
+    dec.forward(torch.from_numpy(prompt).cuda())
+    ref = D.Decoder(qkn, w, B, 12).forward(prompt)
+    assert_close(_host(dec.logits(B, qkn.vocab, "cuda")), ref, "qk-norm decoder logits", **EXACT_FLOOR)

@@ -227,7 +227,7 @@ def test_decoder_checkpoint_layout(tmp_path, fm_host):
     w = S.make_decoder(DEC, 51)
     write_decoder_checkpoint(str(tmp_path), DEC, w)
     got = json.loads(_run(fm_host, "check-decoder", tmp_path).stdout)
-    assert got == {"layers": 2, "moe_layers": [0, 1], "attn_bias": True, "embed_quantized": True,
+    assert got == {"layers": 2, "moe_layers": [0, 1], "attn_bias": True, "qk_norm": False, "embed_quantized": True,
                    "tie_word_embeddings": False, "head_dim": 64, "vocab": 320}
     info = _inspect(fm_host, tmp_path)
     assert (info["n_heads"], info["n_kv_heads"], info["rope_theta"]) == (4, 2, 1e6)
@@ -285,3 +285,11 @@ def test_decoder_checkpoint_with_a_dense_layer(tmp_path, fm_host):
     got = json.loads(_run(fm_host, "check-decoder", tmp_path).stdout)
     assert got["moe_layers"] == [1, 2] and got["layers"] == 3
     assert _inspect(fm_host, tmp_path)["intermediate"] == 384
+
+
+def test_decoder_checkpoint_with_qk_norm(tmp_path, fm_host):
+    shape = S.DecoderShape("dec_qkn", 256, 2, 4, 2, 64, 320, 1e6, 1e-6,
+                           S.MoEShape("dec_moe", 256, 128, 4, 2, 0, False, 256), attn_bias=False, qk_norm=True)
+    write_decoder_checkpoint(str(tmp_path), shape, S.make_decoder(shape, 55))
+    got = json.loads(_run(fm_host, "check-decoder", tmp_path).stdout)
+    assert got["qk_norm"] and not got["attn_bias"]

@@ -170,3 +170,20 @@ def test_mixed_decoder_cache_pass_equals_full_pass():
     a = D.Decoder(MIXED, w, 2, 8)
     a.forward(ids[:, :5])
     np.testing.assert_array_equal(a.forward(ids[:, 5:6]), D.Decoder(MIXED, w, 2, 8).forward(ids))
+
+
+QKN = S.DecoderShape("dec_qkn", 256, 2, 4, 2, 64, 320, 1e6, 1e-6, MOE, attn_bias=False, qk_norm=True)
+
+
+def test_qk_norm_decoder():
+    """Qwen3-style QK-norm (model.cpp:573-581): the per-head RMSNorm of q and k changes the
+    logits, and the cached pass still equals the full pass."""
+    w = S.make_decoder(QKN, 10)
+    assert "q_norm" in w["layers"][0] and "q_bias" not in w["layers"][0]
+    ids = np.random.default_rng(10).integers(0, QKN.vocab, (2, 6))
+    a = D.Decoder(QKN, w, 2, 8)
+    a.forward(ids[:, :5])
+    step = a.forward(ids[:, 5:6])
+    np.testing.assert_array_equal(step, D.Decoder(QKN, w, 2, 8).forward(ids))
+    plain = {**w, "layers": [{k: v for k, v in lw.items() if k not in ("q_norm", "k_norm")} for lw in w["layers"]]}
+    assert not np.array_equal(D.Decoder(QKN, plain, 2, 8).forward(ids), D.Decoder(QKN, w, 2, 8).forward(ids))
