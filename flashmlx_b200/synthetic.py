@@ -138,10 +138,15 @@ class DecoderShape:
     qk_norm: bool = False             # per-head q / k RMSNorm (Qwen3), model.cpp:573-581
 
 
-# the 24-layer Qwen1.5-MoE-A2.7B-shaped decoder, every MoE block as configs[0]
+# the 24-layer Qwen1.5-MoE-A2.7B-shaped decoder, every MoE block as configs[0];
+# and a Qwen3-30B-A3B-shaped decoder (48 layers, 32 query / 4 KV heads of 128, QK-norm, no
+# attention biases, every MoE block as configs[3]) -- not a BASELINE config
 DECODER_CONFIGS = {
     "qwen15_decoder": DecoderShape("qwen15_decoder", 2048, 24, 16, 16, 128, 151936, 1e6, 1e-6,
                                    MoEShape("qwen15_moe", 2048, 1408, 60, 4, 0, False, 5632)),
+    "qwen3_decoder": DecoderShape("qwen3_decoder", 2048, 48, 32, 4, 128, 151936, 1e6, 1e-6,
+                                  MoEShape("qwen3_moe", 2048, 768, 128, 8, 0, True, 0),
+                                  attn_bias=False, qk_norm=True),
 }
 
 

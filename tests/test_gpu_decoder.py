@@ -267,3 +267,17 @@ def test_qk_norm_decoder_against_oracle():
     dec.forward(torch.from_numpy(prompt).cuda())
     ref = D.Decoder(qkn, w, B, 12).forward(prompt)
     assert_close(_host(dec.logits(B, qkn.vocab, "cuda")), ref, "qk-norm decoder logits", **EXACT_FLOOR)
+
+
+def test_wide_query_gqa_decoder_against_oracle():
+    """Query width twice the hidden size (8 heads of 64 over hidden 256), 2 KV heads, QK-norm:
+    the Qwen3-30B-A3B layout in small."""
+    from flashmlx_b200 import decoder as DEC
+    sh = S.DecoderShape("dec_wide", 256, 2, 8, 2, 64, 320, 1e6, 1e-6, MOE, attn_bias=False, qk_norm=True)
+    w = S.make_decoder(sh, 75)
+    B, L = 2, 6
+    prompt = np.random.default_rng(75).integers(0, sh.vocab, (B, L)).astype(np.int32)
+    dec = DEC.Decoder.from_weights(sh, DEC.upload_weights(w, "cuda"), "cuda", B, 10)
+    dec.forward(torch.from_numpy(prompt).cuda())
+    ref = D.Decoder(sh, w, B, 10).forward(prompt)
+    assert_close(_host(dec.logits(B, sh.vocab, "cuda")), ref, "wide-query decoder logits", **EXACT_FLOOR)

@@ -141,7 +141,7 @@ def test_tied_embeddings_use_the_quantized_embedding():
 @pytest.mark.parametrize("name", list(S.DECODER_CONFIGS))
 def test_decoder_configs_are_consistent(name):
     sh = S.DECODER_CONFIGS[name]
-    assert sh.n_heads * sh.head_dim == sh.hidden and sh.n_heads % sh.n_kv_heads == 0
+    assert sh.n_heads % sh.n_kv_heads == 0 and sh.head_dim in (64, 128)
     assert sh.moe.hidden == sh.hidden
 
 
@@ -187,3 +187,15 @@ def test_qk_norm_decoder():
     np.testing.assert_array_equal(step, D.Decoder(QKN, w, 2, 8).forward(ids))
     plain = {**w, "layers": [{k: v for k, v in lw.items() if k not in ("q_norm", "k_norm")} for lw in w["layers"]]}
     assert not np.array_equal(D.Decoder(QKN, plain, 2, 8).forward(ids), D.Decoder(QKN, w, 2, 8).forward(ids))
+
+
+def test_query_width_differs_from_hidden():
+    """Qwen3-style attention whose query width (heads x head_dim) is twice the hidden size,
+    with GQA and QK-norm: the cached pass still equals the full pass."""
+    sh = S.DecoderShape("dec_wide", 256, 2, 8, 2, 64, 320, 1e6, 1e-6, MOE, attn_bias=False, qk_norm=True)
+    w = S.make_decoder(sh, 11)
+    assert w["layers"][0]["q"][0].shape == (512, 256 // 8) and w["layers"][0]["o"][0].shape == (256, 512 // 8)
+    ids = np.random.default_rng(11).integers(0, sh.vocab, (2, 5))
+    a = D.Decoder(sh, w, 2, 8)
+    a.forward(ids[:, :4])
+    np.testing.assert_array_equal(a.forward(ids[:, 4:5]), D.Decoder(sh, w, 2, 8).forward(ids))
