@@ -1,0 +1,47 @@
+"""The algorithmic work bench.py divides by a kernel's time for its roofline fraction,
+against the figures derived independently for the BASELINE configs: configs[1] (the
+4096-token Qwen1.5-MoE prefill layer) is 567,959,093,248 FLOP per layer call (routed
+gate/up/down 283.47 G, shared expert 283.47 G, router and shared-expert gate 1.02 G), and a
+Qwen1.5-MoE expert is 3 x 2048 x 1408 4-bit weights with bf16 scale and bias per 64 =
+4,866,048 bytes."""
+from __future__ import annotations
+
+import numpy as np
+
+import bench
+from flashmlx_b200 import synthetic as S
+
+
+def test_prefill_flops_match_the_layer_total():
+    shape = S.CONFIGS["qwen15_prefill"]
+    T = shape.tokens
+    counts = np.full(shape.num_experts, T * shape.top_k // shape.num_experts)
+    work, active = bench.kernel_work(shape, T, counts)
+    assert active == shape.num_experts
+    total = work["qgemm_tc_gateup"][0] + work["qgemm_tc_down"][0] + work["route"][0]
+    assert total == 567_959_093_248
+    assert work["qgemm_tc_gateup"][0] == 2 * work["qgemm_tc_down"][0]  # two matrices against one
+
+
+def test_decode_bytes_count_the_active_experts_once():
+    shape = S.CONFIGS["qwen15_decode"]
+    T, H, I, Is = shape.tokens, shape.hidden, shape.inter, shape.shared_inter
+    per_expert = 3 * H * I * (0.5 + 2 * 2 / 64)
+    assert per_expert == 4_866_048
+    for active in (1, 31, 53, 60):
+        counts = np.zeros(shape.num_experts, int)
+        counts[:active] = 1
+        work, got = bench.kernel_work(shape, T, counts)
+        assert got == active
+        weights = work["qgemv_gateup"][1] + work["qgemv_down"][1]
+        acts = (T * H * 2 + T * shape.top_k * I * 2 + T * Is * 2) + (T * shape.top_k * I * 2 + T * Is * 2 + T * H * 8)
+        assert weights - acts == active * per_expert + 3 * H * Is * (0.5 + 2 * 2 / 64)
+
+
+def test_decoder_step_bytes_grow_with_batch_and_position():
+    shape = S.DECODER_CONFIGS["qwen15_decoder"]
+    b1, b32 = bench.decoder_step_bytes(shape, 1, 600), bench.decoder_step_bytes(shape, 32, 600)
+    assert b1 < b32 and bench.decoder_step_bytes(shape, 32, 100) < b32
+    # batch 1 reads the attention projections, ~4 experts + the shared expert and router of
+    # every layer, and the lm_head: between 1.3 and 1.6 GB
+    assert 1.3e9 < b1 < 1.6e9
