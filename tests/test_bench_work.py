@@ -45,3 +45,28 @@ def test_decoder_step_bytes_grow_with_batch_and_position():
     # batch 1 reads the attention projections, ~4 experts + the shared expert and router of
     # every layer, and the lm_head: between 1.3 and 1.6 GB
     assert 1.3e9 < b1 < 1.6e9
+
+
+def test_expert_parallel_work_splits_the_layer():
+    """Summed over ranks, the owner-side expert work of an expert-parallel step is the
+    single-GPU layer's routed work plus one shared expert per rank (each rank runs it
+    over its own tokens)."""
+    shape = S.CONFIGS["qwen15_prefill"]
+    T, k, E, world = shape.tokens, shape.top_k, shape.num_experts, 4
+    per_rank_experts = E // world
+    routed_rows = T * k  # every rank routes T tokens; rows spread evenly over the owners
+    f_gu = f_dn = 0.0
+    for _ in range(world):
+        counts = np.full(world * per_rank_experts, routed_rows // (world * per_rank_experts))
+        counts[: routed_rows - int(counts.sum())] += 1  # every owner receives T * k rows
+        counts = counts.reshape(world, per_rank_experts)
+        work, active = bench.ep_kernel_work(shape, T, int(counts.sum()), counts.ravel(), per_rank_experts)
+        assert active == per_rank_experts
+        f_gu += work["qgemm_tc_gateup"][0]
+        f_dn += work["qgemm_tc_down"][0]
+    single, _ = bench.kernel_work(shape, T, np.full(E, routed_rows // E))
+    H, I, Is = shape.hidden, shape.inter, shape.shared_inter
+    # world ranks x T tokens each: world x the single-GPU routed rows and shared expert
+    assert f_gu == world * single["qgemm_tc_gateup"][0]
+    assert f_dn == world * single["qgemm_tc_down"][0]
+    assert single["qgemm_tc_down"][0] == 2.0 * T * k * I * H + 2.0 * T * Is * H
