@@ -468,6 +468,9 @@ def run_ours(args, rank, world, local_rank):
             "config": {"workload": shape.name, "tokens_per_rank": T, "hidden": shape.hidden,
                        "inter": shape.inter, "experts": shape.num_experts, "top_k": shape.top_k,
                        "shared_inter": shape.shared_inter, "active_experts": active,
+                       # routed pairs per expert this batch (one GPU): the hottest expert bounds a skewed layer
+                       "expert_load": None if counts is None else {
+                           "max_pairs": int(np.max(counts)), "mean_pairs": float(np.mean(counts))},
                        "parallelism": ((f"ep{world}-{args.ep_impl}" if ep else f"replicas{world}")
                                        if world > 1 else "single"),
                        "l2": l2_note},
