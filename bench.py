@@ -61,6 +61,8 @@ def parse():
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent replicas instead of expert parallelism")
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-all between staged calls")
+    ap.add_argument("--route-mode", default="grid", choices=["grid", "last-block"],
+                    help="MoE workloads: routing kernel form (fm_set_route_mode)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -245,7 +247,7 @@ def run_ours(args, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=__import__("datetime").timedelta(seconds=120))
-    from flashmlx_b200 import ops
+    from flashmlx_b200 import _lib, ops
 
     shape, layer_np = workload(args.config, args.seed)
     variant = args.config in S.VARIANT_CONFIGS
@@ -255,6 +257,8 @@ def run_ours(args, rank, world, local_rank):
         raise SystemExit("variant workloads run on one GPU or as --replicas")
     x_np = S.make_x(shape, args.seed + rank)  # each rank routes its own batch
     h = ops.default_handle(local_rank)
+    route_mode = {"grid": _lib.FM_ROUTE_GRID, "last-block": _lib.FM_ROUTE_LAST_BLOCK}[args.route_mode]
+    h.set_route_mode(route_mode)
     x = ops.bf16_from_numpy(x_np, dev)
     y = torch.empty_like(x)
     hp = h  # the handle whose launches are timed
@@ -278,6 +282,7 @@ def run_ours(args, rank, world, local_rank):
         if args.ep_impl == "peer":
             peer_block = MoEBlockEPPeer(shape, W, max_tokens=T)
             hp = peer_block.h
+            hp.set_route_mode(route_mode)
 
             def step(xin, out):
                 peer_block(xin, out=out)
@@ -473,7 +478,7 @@ def run_ours(args, rank, world, local_rank):
                            "max_pairs": int(np.max(counts)), "mean_pairs": float(np.mean(counts))},
                        "parallelism": ((f"ep{world}-{args.ep_impl}" if ep else f"replicas{world}")
                                        if world > 1 else "single"),
-                       "l2": l2_note},
+                       "route_mode": args.route_mode, "l2": l2_note},
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(x.numel() * 2), "d2h_bytes_per_step": int(y.numel() * 2)},
             "gpu_launches": ours_launches,

@@ -24,6 +24,8 @@
 namespace fm {
 __global__ void route_kernel(const RouteArgs a);
 __global__ void route_kernel_sigmoid(const RouteArgs a);
+__global__ void route_last_kernel(const RouteArgs a);
+__global__ void route_last_kernel_sigmoid(const RouteArgs a);
 __global__ void dense_prep_kernel(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
@@ -73,6 +75,7 @@ struct fm_handle {
   int gemv_blocks_per_sm = 0;
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
+  int route_mode = FM_ROUTE_AUTO;
   bool attn_ready = false;  // attention kernels' shared-memory opt-in done (first fm_attention)
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
@@ -249,6 +252,7 @@ void prof_end(fm_handle* h) {
 
 uint32_t* err_word(fm_handle* h) { return reinterpret_cast<uint32_t*>(h->ws); }
 fm::GridSync* grid_sync(fm_handle* h) { return reinterpret_cast<fm::GridSync*>(h->ws + 64); }
+unsigned int* arrive_count(fm_handle* h) { return reinterpret_cast<unsigned int*>(h->ws + 72); }
 // routing-kernel phase timers: 4 x u64 ns + a launch count, accumulated on the device
 unsigned long long* phase_ns(fm_handle* h) { return reinterpret_cast<unsigned long long*>(h->ws + 128); }
 
@@ -264,6 +268,18 @@ bool quant_ok(int K, int gs, int bits) {
 int launch_route(fm_handle* h, RouteArgs& ra, int64_t items, bool sigmoid = false) {
   const int max_blocks = (sigmoid ? h->route_sig_blocks_per_sm : h->route_blocks_per_sm) * h->num_sms;
   const int64_t nchunks = (ra.T + fm::kRouteChunk - 1) / fm::kRouteChunk;
+  ra.arrive = arrive_count(h);
+  if (h->route_mode == FM_ROUTE_LAST_BLOCK && nchunks <= fm::kRouteLastMaxChunks) {
+    // one warp per phase-1 item; no co-residency needed (nothing waits on another block)
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, max_blocks)));
+    prof_begin(h, ra.do_router ? "route" : "route_given");
+    if (sigmoid) fm::route_last_kernel_sigmoid<<<grid, fm::kRouteThreads, 0, h->stream>>>(ra);
+    else fm::route_last_kernel<<<grid, fm::kRouteThreads, 0, h->stream>>>(ra);
+    prof_end(h);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_err(h, e, "route_last_kernel launch");
+    return FM_OK;
+  }
   int64_t want = std::max<int64_t>((items + 7) / 8, nchunks);
   want = std::max<int64_t>(want, std::min<int64_t>(ra.E, h->num_sms));
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks)));
@@ -767,6 +783,14 @@ int fm_set_path(fm_handle* h, int path) {
   if (path != FM_PATH_AUTO && path != FM_PATH_GEMV && path != FM_PATH_TCGEN05)
     return set_err(h, FM_EINVAL, "unknown path");
   h->path = path;
+  return FM_OK;
+}
+
+int fm_set_route_mode(fm_handle* h, int mode) {
+  if (!h) return FM_EINVAL;
+  if (mode != FM_ROUTE_AUTO && mode != FM_ROUTE_GRID && mode != FM_ROUTE_LAST_BLOCK)
+    return set_err(h, FM_EINVAL, "unknown route mode");
+  h->route_mode = mode;
   return FM_OK;
 }
 

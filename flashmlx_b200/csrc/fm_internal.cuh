@@ -200,6 +200,7 @@ struct RouteArgs {
   float* out_scores_f32;        // [T, k] fp32 scores as used (nullable, either routing)
   int shared_ungated;           // the shared expert is added without a gate (gate_sig = 1)
   GridSync* gsync;
+  unsigned int* arrive;  // arrival counter of the last-block routing kernel (0 between launches)
   uint32_t* err;
   unsigned long long* phase_ns;  // [4] accumulated per-phase time of block 0 (profiling)
 };
@@ -269,5 +270,6 @@ struct AttnArgs {
 constexpr int kRouteThreads = 256;  // 8 warps
 constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
 constexpr int kRouterMaxKsplit = 16;  // K slices of the router partial logits
+constexpr int kRouteLastMaxChunks = 8;  // batches the last-block routing kernel takes (<= 128 tokens)
 
 }  // namespace fm

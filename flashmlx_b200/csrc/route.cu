@@ -419,12 +419,14 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) 
   atomicOr(&sm.mask[e], 1u << tl);
 }
 
+// bid / nb: this block's place among the blocks that share the phase (the whole grid in
+// the cooperative kernel, block 0 of 1 in the last-block tail)
 template <bool SIGMOID>
-__device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm) {
+__device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
   const int warp = threadIdx.x >> 5;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
   const int k = a.do_router ? a.k : 1;
-  for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+  for (int ch = bid; ch < nchunks; ch += nb) {
     for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e] = 0u;
     __syncthreads();
     for (int i = 0; i < kRouteChunk / 8; ++i) {
@@ -469,6 +471,25 @@ __device__ void phase_column_scan(const RouteArgs& a, RouteSmem& sm) {
       __syncthreads();
     }
     if (threadIdx.x == 0) a.totals[e] = carry;
+  }
+}
+
+// Phase 3 for one block and at most kRouteLastMaxChunks chunks: each thread scans its
+// experts' chunk counts in registers (same exclusive scan and totals as above).
+__device__ void phase_column_scan_one_block(const RouteArgs& a) {
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) {
+    int c[kRouteLastMaxChunks];
+#pragma unroll
+    for (int i = 0; i < kRouteLastMaxChunks; ++i)
+      c[i] = i < nchunks ? a.chunk_counts[static_cast<int64_t>(i) * a.E + e] : 0;
+    int run = 0;
+#pragma unroll
+    for (int i = 0; i < kRouteLastMaxChunks; ++i) {
+      if (i < nchunks) a.chunk_counts[static_cast<int64_t>(i) * a.E + e] = run;
+      run += c[i];
+    }
+    a.totals[e] = run;
   }
 }
 
@@ -520,13 +541,13 @@ __device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, i
   finish_table(tab, ng, cnt, sm.tmp);
 }
 
-__device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
+__device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.offs[e] = a.totals[e];
   __syncthreads();
   const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
   if (threadIdx.x == 0) sm.offs[a.E] = P;
   __syncthreads();
-  if (blockIdx.x == 0) {
+  if (bid == 0) {
     for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
       a.offsets[e] = sm.offs[e];
       if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
@@ -537,7 +558,7 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm) {
   }
   const int k = a.do_router ? a.k : 1;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
-  for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+  for (int ch = bid; ch < nchunks; ch += nb) {
     const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
     const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
     for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
@@ -716,7 +737,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 0, t);
   // phase 2
-  phase_topk_count<SIGMOID>(a, sm);
+  phase_topk_count<SIGMOID>(a, sm, blockIdx.x, nb);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 1, t);
   // phase 3
@@ -724,8 +745,43 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 2, t);
   // phase 4
-  phase_scatter(a, sm);
+  phase_scatter(a, sm, blockIdx.x, nb);
   phase_mark(a, 3, t);
+}
+
+// Small batches (at most kRouteLastMaxChunks chunks): phase 1 over the whole grid, then
+// the block that arrives last runs phases 2-4 alone with block barriers.  There is no
+// grid barrier and nothing waits: each block makes its phase-1 stores visible
+// (__threadfence) before it counts itself in, the last arrival fences again before it
+// reads them, and atomicInc wraps the counter back to 0 on that arrival.
+template <bool SIGMOID>
+__device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& sm) {
+  if (a.do_router) phase_router(a);
+  else phase_permute_x(a);
+  phase_zero(a.zero0, a.zero0_n);
+  phase_zero(a.zero1, a.zero1_n);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int arrived = atomicInc(a.arrive, gridDim.x - 1);
+    __threadfence();
+    sm.flag = arrived == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!sm.flag) return;
+  phase_topk_count<SIGMOID>(a, sm, 0, 1);
+  phase_column_scan_one_block(a);
+  __syncthreads();
+  phase_scatter(a, sm, 0, 1);
+}
+
+__global__ void __launch_bounds__(kRouteThreads) route_last_kernel(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_last_body<false>(a, sm);
+}
+__global__ void __launch_bounds__(kRouteThreads) route_last_kernel_sigmoid(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_last_body<true>(a, sm);
 }
 
 // softmax routing (the reference's LlamaModel block) and sigmoid routing (the

@@ -71,6 +71,12 @@ class Handle:
     def set_path(self, path: int):
         self.check(self.lib.fm_set_path(self.h, path))
 
+    def set_route_mode(self, mode: int):
+        """FM_ROUTE_GRID (cooperative, grid barriers) or FM_ROUTE_LAST_BLOCK (batches of
+        at most 128 tokens: top-k, sort and planning in the block that finishes the router
+        GEMV last); FM_ROUTE_AUTO is the grid form."""
+        self.check(self.lib.fm_set_route_mode(self.h, mode))
+
     def sync(self):
         self.check(self.lib.fm_sync_status(self.h))
 

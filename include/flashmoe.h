@@ -163,6 +163,16 @@ FM_API size_t fm_workspace_size(const fm_moe_config* cfg, int64_t max_tokens);
 enum { FM_PATH_AUTO = 0, FM_PATH_GEMV = 1, FM_PATH_TCGEN05 = 2 };
 FM_API int fm_set_path(fm_handle* h, int path);
 
+/* Form of the routing kernel (router, top-k, sort and tile plan; the reference's
+ * op chain of model.cpp:757-775 and 682-700).  FM_ROUTE_GRID: one cooperative kernel
+ * whose four phases are separated by grid barriers.  FM_ROUTE_LAST_BLOCK: for batches
+ * of at most 128 tokens (rows, for fm_gather_qmm), the router GEMV over the whole grid
+ * and top-k, sort and planning in the one block that finishes it last, with no grid
+ * barrier; larger batches take the grid form.  FM_ROUTE_AUTO is FM_ROUTE_GRID.  Both
+ * forms give identical results. */
+enum { FM_ROUTE_AUTO = 0, FM_ROUTE_GRID = 1, FM_ROUTE_LAST_BLOCK = 2 };
+FM_API int fm_set_route_mode(fm_handle* h, int mode);
+
 /* Kernel timing ------------------------------------------------------------------
  * With profiling on, every kernel the handle launches is bracketed by CUDA events on
  * the handle's stream; fm_profile_report() synchronizes and returns, per kernel
