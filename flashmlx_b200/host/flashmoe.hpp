@@ -79,6 +79,9 @@ class Handle {
   // sizes the workspace for up to max_tokens tokens of cfg, so later calls do not allocate
   void reserve(const fm_moe_config& cfg, int64_t max_tokens) { check(fm_reserve(h_, &cfg, max_tokens)); }
   void set_stream(void* stream) { check(fm_set_stream(h_, stream)); }
+  // expert-product path (FM_PATH_*) and routing-kernel form (FM_ROUTE_*) of later calls
+  void set_path(int path) { check(fm_set_path(h_, path)); }
+  void set_route_mode(int mode) { check(fm_set_route_mode(h_, mode)); }
   // waits for the handle's stream; a device-side failure (bounded wait, bounds check) throws
   void sync() const { check(fm_sync_status(h_)); }
 
