@@ -42,6 +42,19 @@ def test_library_exports_every_declared_symbol(lib):
     assert exported == set(header_functions()), exported - set(header_functions())
 
 
+def test_enum_constants_match_the_header():
+    """The Python constants of the header's enums (status codes, paths, routing forms)."""
+    txt = open(HEADER).read()
+    consts = dict((k, int(v)) for k, v in re.findall(r"\b(FM_[A-Z0-9_]+)\s*=\s*(\d+)", txt))
+    for name in ("FM_PATH_AUTO", "FM_PATH_GEMV", "FM_PATH_TCGEN05", "FM_ROUTE_AUTO", "FM_ROUTE_GRID",
+                 "FM_ROUTE_LAST_BLOCK", "FM_OK", "FM_EINVAL"):
+        assert consts[name] == getattr(_lib, name), name
+
+
+def test_route_mode_is_checked_without_a_gpu(lib):
+    assert lib.fm_set_route_mode(None, _lib.FM_ROUTE_LAST_BLOCK) == _lib.FM_EINVAL
+
+
 def test_status_strings(lib):
     assert lib.fm_status_string(0) == b"ok"
     assert lib.fm_status_string(5) == b"device wait timed out"
