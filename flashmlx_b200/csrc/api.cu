@@ -270,8 +270,12 @@ int launch_route(fm_handle* h, RouteArgs& ra, int64_t items, bool sigmoid = fals
   const int64_t nchunks = (ra.T + fm::kRouteChunk - 1) / fm::kRouteChunk;
   ra.arrive = arrive_count(h);
   if (h->route_mode == FM_ROUTE_LAST_BLOCK && nchunks <= fm::kRouteLastMaxChunks) {
-    // one warp per phase-1 item; no co-residency needed (nothing waits on another block)
-    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, max_blocks)));
+    // one warp per phase-1 item, and enough blocks that zeroing the fp32 accumulators
+    // takes at most 8 float4 stores per thread; no co-residency needed (nothing waits on
+    // another block)
+    const int64_t zero_blocks = (ra.zero0_n + ra.zero1_n + 8191) / 8192;
+    const int64_t want = std::max<int64_t>((items + 7) / 8, zero_blocks);
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks)));
     prof_begin(h, ra.do_router ? "route" : "route_given");
     if (sigmoid) fm::route_last_kernel_sigmoid<<<grid, fm::kRouteThreads, 0, h->stream>>>(ra);
     else fm::route_last_kernel<<<grid, fm::kRouteThreads, 0, h->stream>>>(ra);
