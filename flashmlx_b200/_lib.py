@@ -56,7 +56,7 @@ FM_ACT_SWIGLU, FM_ACT_RELU2 = 0, 1
 
 class AttnConfig(C.Structure):
     _fields_ = [("n_heads", C.c_int), ("n_kv_heads", C.c_int), ("head_dim", C.c_int), ("max_len", C.c_int),
-                ("rope_theta", C.c_float), ("scale", C.c_float), ("norm_eps", C.c_float)]
+                ("rope_theta", C.c_float), ("scale", C.c_float), ("norm_eps", C.c_float), ("qkv_ld", C.c_int)]
 
 
 class KernelTime(C.Structure):

@@ -1813,6 +1813,8 @@ int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uin
     return set_err(h, FM_EINVAL, "bad attention config");
   if (d != 64 && d != 128) return set_err(h, FM_EUNSUPPORTED, "head_dim must be 64 or 128");
   if ((q_norm || k_norm) && !(cfg->norm_eps >= 0.f)) return set_err(h, FM_EINVAL, "bad QK-norm eps");
+  if (cfg->qkv_ld < 0 || cfg->qkv_ld % 8 || (cfg->qkv_ld > 0 && cfg->qkv_ld < nh * d))
+    return set_err(h, FM_EINVAL, "qkv_ld must be 0 or a multiple of 8 of at least n_heads * head_dim");
   if (B < 0 || L < 0 || offset < 0) return set_err(h, FM_EINVAL, "negative B, L or offset");
   if (B == 0 || L == 0) return FM_OK;
   if (static_cast<int64_t>(offset) + L > cfg->max_len) return set_err(h, FM_EINVAL, "offset + L exceeds max_len");
@@ -1842,8 +1844,8 @@ int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uin
   a.cache_k = cache_k;
   a.cache_v = cache_v;
   a.out = out;
-  a.q_ld = static_cast<int64_t>(nh) * d;
-  a.kv_ld = static_cast<int64_t>(nkv) * d;
+  a.q_ld = cfg->qkv_ld > 0 ? cfg->qkv_ld : static_cast<int64_t>(nh) * d;
+  a.kv_ld = cfg->qkv_ld > 0 ? cfg->qkv_ld : static_cast<int64_t>(nkv) * d;
   a.out_ld = static_cast<int64_t>(nh) * d;
   a.B = B;
   a.L = L;

@@ -36,14 +36,54 @@ Decoder::Decoder(const fmh_decoder_config& cfg, const fmh_weights& w, int device
   const int64_t H = cfg_.hidden, QD = static_cast<int64_t>(cfg_.n_heads) * cfg_.head_dim,
                 KVD = static_cast<int64_t>(cfg_.n_kv_heads) * cfg_.head_dim;
   auto bf = [&](int64_t n) { return static_cast<uint16_t*>(bufs_.alloc(static_cast<size_t>(n) * 2)); };
+  // Each layer's q, k and v projections as one [QD + 2 KVD, H] matrix (their rows, scales
+  // and biases concatenated): one fm_linear per layer instead of three, q, k and v side by
+  // side in each output row.  The rows of a quantized linear do not interact and the
+  // direct path never splits K, so the fused output equals the three projections' bit
+  // for bit.  A layer whose three matrices disagree on having biases stays separate.
+  const int64_t W = QD + 2 * KVD, kw = H / 8, gpr = H / cfg_.group_size;
+  const bool fusable = cfg_.group_size > 0 && H % cfg_.group_size == 0 && H % 8 == 0;
+  bool any_fused = false, any_split = false;
+  qkv_.assign(cfg_.layers, fm_qweight{nullptr, nullptr, nullptr});
+  for (int li = 0; li < cfg_.layers; ++li) {
+    const fmh_layer& l = layers_[li];
+    const bool nb = !l.q.biases;
+    if (!fusable || !l.q.scales || !l.k.scales || !l.v.scales || !l.k.biases != nb || !l.v.biases != nb) {
+      any_split = true;
+      continue;
+    }
+    auto* w = static_cast<uint32_t*>(bufs_.alloc(static_cast<size_t>(W * kw) * 4));
+    uint16_t* sc = bf(W * gpr);
+    uint16_t* bi = nb ? nullptr : bf(W * gpr);
+    const fm_qweight* parts[3] = {&l.q, &l.k, &l.v};
+    const int64_t rows[3] = {QD, KVD, KVD};
+    int64_t r0 = 0;
+    for (int i = 0; i < 3; ++i) {
+      cuda_check(cudaMemcpyAsync(w + r0 * kw, parts[i]->w, static_cast<size_t>(rows[i] * kw) * 4,
+                                 cudaMemcpyDeviceToDevice, stream_), "cudaMemcpyAsync qkv codes");
+      cuda_check(cudaMemcpyAsync(sc + r0 * gpr, parts[i]->scales, static_cast<size_t>(rows[i] * gpr) * 2,
+                                 cudaMemcpyDeviceToDevice, stream_), "cudaMemcpyAsync qkv scales");
+      if (bi)
+        cuda_check(cudaMemcpyAsync(bi + r0 * gpr, parts[i]->biases, static_cast<size_t>(rows[i] * gpr) * 2,
+                                   cudaMemcpyDeviceToDevice, stream_), "cudaMemcpyAsync qkv biases");
+      r0 += rows[i];
+    }
+    qkv_[li] = fm_qweight{w, sc, bi};
+    any_fused = true;
+  }
+  attn_qkv_ = attn_;
+  attn_qkv_.qkv_ld = static_cast<int>(W);
   x_ = bf(tokens * H);
   normed_ = bf(tokens * H);
   o_ = bf(tokens * H);
   mlp_ = bf(tokens * H);
-  q_ = bf(tokens * QD);
   attn_out_ = bf(tokens * QD);
-  k_ = bf(tokens * KVD);
-  v_ = bf(tokens * KVD);
+  if (any_fused) qkv_out_ = bf(tokens * W);
+  if (any_split) {
+    q_ = bf(tokens * QD);
+    k_ = bf(tokens * KVD);
+    v_ = bf(tokens * KVD);
+  }
   bool dense = false, moe = false;
   for (const auto& l : layers_) (l.is_moe ? moe : dense) = true;
   if (dense) {
@@ -104,11 +144,17 @@ void Decoder::forward(const int32_t* ids, int B, int L, int32_t* next_ids) {
   handle_.check(fm_rms_norm(h, x_, nullptr, layers_[0].in_norm, T, H, eps, nullptr, normed_));
   for (int li = 0; li < cfg_.layers; ++li) {
     const fmh_layer& l = layers_[li];
-    qmm(normed_, T, H, l.q, QD, q_);
-    qmm(normed_, T, H, l.k, KVD, k_);
-    qmm(normed_, T, H, l.v, KVD, v_);
-    handle_.check(fm_attention(h, &attn_, q_, k_, v_, l.q_bias, l.k_bias, l.v_bias, l.q_norm, l.k_norm, cache_k_[li],
-                               cache_v_[li], B, L, offset_, attn_out_));
+    if (qkv_[li].w) {
+      qmm(normed_, T, H, qkv_[li], QD + 2 * KVD, qkv_out_);
+      handle_.check(fm_attention(h, &attn_qkv_, qkv_out_, qkv_out_ + QD, qkv_out_ + QD + KVD, l.q_bias, l.k_bias,
+                                 l.v_bias, l.q_norm, l.k_norm, cache_k_[li], cache_v_[li], B, L, offset_, attn_out_));
+    } else {
+      qmm(normed_, T, H, l.q, QD, q_);
+      qmm(normed_, T, H, l.k, KVD, k_);
+      qmm(normed_, T, H, l.v, KVD, v_);
+      handle_.check(fm_attention(h, &attn_, q_, k_, v_, l.q_bias, l.k_bias, l.v_bias, l.q_norm, l.k_norm,
+                                 cache_k_[li], cache_v_[li], B, L, offset_, attn_out_));
+    }
     qmm(attn_out_, T, QD, l.o, H, o_);
     // h = x + attention; normed = rms_norm(h, post_attention_layernorm)
     handle_.check(fm_rms_norm(h, x_, o_, l.post_norm, T, H, eps, x_, normed_));

@@ -63,7 +63,8 @@ DecoderPlan plan_decoder(const Checkpoint& ck);
 
 class Decoder {
  public:
-  // caller-owned device weights (the tables are copied, the weights are not)
+  // caller-owned device weights (the tables are copied and each layer's q, k and v
+  // matrices into one fused matrix; the other weights are read in place)
   Decoder(const fmh_decoder_config& cfg, const fmh_weights& w, int device, int max_batch, int max_len,
           void* stream = nullptr);
   // an MLX-format model directory, loaded, uploaded and owned by the decoder
@@ -96,11 +97,14 @@ class Decoder {
   int offset_ = 0;
   cudaStream_t stream_ = nullptr;
   fm_attn_config attn_{};
+  fm_attn_config attn_qkv_{};            // attn_ on the fused projection's rows (qkv_ld set)
+  std::vector<fm_qweight> qkv_;          // per layer: q|k|v rows in one matrix (w == nullptr: separate)
   Handle handle_;
   DeviceStore bufs_;                     // activations, caches, token buffers
   std::unique_ptr<DeviceStore> owned_;   // weights loaded by open()
   uint16_t *x_ = nullptr, *normed_ = nullptr, *q_ = nullptr, *k_ = nullptr, *v_ = nullptr, *attn_out_ = nullptr,
-           *o_ = nullptr, *mlp_ = nullptr, *gate_ = nullptr, *up_ = nullptr, *last_ = nullptr, *logits_ = nullptr;
+           *o_ = nullptr, *mlp_ = nullptr, *gate_ = nullptr, *up_ = nullptr, *last_ = nullptr, *logits_ = nullptr,
+           *qkv_out_ = nullptr;
   int32_t* tok_ = nullptr;               // [2][max_batch * max_len] generate()'s token ping-pong
   int32_t* gen_ = nullptr;               // [steps, max_batch] generate()'s output, grown on demand
   int64_t gen_cap_ = 0;

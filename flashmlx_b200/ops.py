@@ -483,6 +483,36 @@ def attention(q, k, v, cache_k, cache_v, B, L, offset, rope_theta, q_bias=None, 
     return out
 
 
+def attention_qkv(qkv, cache_k, cache_v, B, L, offset, rope_theta, q_bias=None, k_bias=None, v_bias=None,
+                  scale=0.0, q_norm=None, k_norm=None, norm_eps=1e-6, handle=None) -> torch.Tensor:
+    """attention() on the output of a fused q|k|v projection: qkv [B*L, (nh + 2 n_kv) * d]
+    holds q, k and v side by side in each row (fm_attn_config.qkv_ld); its q columns are
+    rotated in place.  Returns [B*L, nh*d] bf16."""
+    _need(qkv, "qkv", (torch.bfloat16,), None)
+    dev = qkv.device
+    for t, n in ((cache_k, "cache_k"), (cache_v, "cache_v")):
+        _need(t, n, (torch.bfloat16,), dev)
+    for t, n in ((q_bias, "q_bias"), (k_bias, "k_bias"), (v_bias, "v_bias"), (q_norm, "q_norm"), (k_norm, "k_norm")):
+        if t is not None:
+            _need(t, n, (torch.bfloat16,), dev)
+    if cache_k.dim() != 4 or cache_v.shape != cache_k.shape or cache_k.shape[0] < B:
+        raise ValueError("caches must be [>= B, n_kv, max_len, d] and alike")
+    _, nkv, max_len, d = cache_k.shape
+    W = qkv.shape[-1]
+    nh = W // d - 2 * nkv
+    if qkv.numel() != B * L * W or W % d or nh <= 0:
+        raise ValueError("qkv must be [B*L, (n_heads + 2 n_kv) * d]")
+    cfg = _lib.AttnConfig(nh, nkv, d, max_len, float(rope_theta), float(scale), float(norm_eps), W)
+    out = torch.empty(B * L, nh * d, dtype=torch.bfloat16, device=dev)
+    h = handle or default_handle(dev.index)
+    h.bind_stream()
+    base = qkv.data_ptr()
+    h.check(h.lib.fm_attention(h.h, C.byref(cfg), C.c_void_p(base), C.c_void_p(base + 2 * nh * d),
+                               C.c_void_p(base + 2 * (nh + nkv) * d), _ptr(q_bias), _ptr(k_bias), _ptr(v_bias),
+                               _ptr(q_norm), _ptr(k_norm), _ptr(cache_k), _ptr(cache_v), B, L, offset, _ptr(out)))
+    return out
+
+
 def swiglu(gate, up, handle=None) -> torch.Tensor:
     """The compiled swiglu of model.cpp:14-25 (silu(g) * u, bf16 after every op)."""
     _need(gate, "gate", (torch.bfloat16,), None)

@@ -283,6 +283,9 @@ typedef struct fm_attn_config {
   float rope_theta;  /* RoPE base (traditional = false, scale 1) */
   float scale;       /* softmax scale; 0 = 1/sqrt(head_dim) */
   float norm_eps;    /* eps of the per-head q / k RMSNorm (QK-norm), when its weights are given */
+  int qkv_ld;        /* elements from one token's row of q, k and v to the next when the three
+                        share one buffer (the output of a fused q|k|v projection; a multiple
+                        of 8); 0 = separate packed buffers */
 } fm_attn_config;
 
 /* The attention step of a layer after its q/k/v projections (model.cpp:560-635): bias
@@ -293,7 +296,8 @@ typedef struct fm_attn_config {
  * scaled dot-product attention of the L queries over positions [0, offset + l] (causal;
  * mx::fast::scaled_dot_product_attention) into out [T, n_heads*head_dim].  q [T,
  * n_heads*head_dim] is overwritten with its rotated rows; k, v are [T,
- * n_kv_heads*head_dim].  Every sequence of the batch is at the same offset, as in the
+ * n_kv_heads*head_dim] (with qkv_ld > 0: rows qkv_ld apart, e.g. q, k, v at columns 0,
+ * n_heads*head_dim and (n_heads + n_kv_heads)*head_dim of one [T, qkv_ld] buffer).  Every sequence of the batch is at the same offset, as in the
  * reference (model.cpp:594-606). */
 FM_API int fm_attention(fm_handle* h, const fm_attn_config* cfg, uint16_t* q, const uint16_t* k, const uint16_t* v,
                         const uint16_t* q_bias, const uint16_t* k_bias, const uint16_t* v_bias, const uint16_t* q_norm,

@@ -78,6 +78,7 @@ int main(void) {
   printf("%zu %zu %zu %zu\n", offsetof(fm_moe_weights, gate), offsetof(fm_moe_weights, shared_down),
          offsetof(fm_moe_weights, shared_expert_gate_w), offsetof(fm_moe_weights, router_bias));
   printf("%zu %zu\n", offsetof(fm_moe_config, shared_inter), offsetof(fm_moe_outputs, expert_offsets));
+  printf("%zu %zu\n", sizeof(fm_attn_config), offsetof(fm_attn_config, qkv_ld));
   return 0;
 }
 """
@@ -90,7 +91,8 @@ int main(void) {
     want = [C.sizeof(_lib.QWeight), C.sizeof(_lib.MoEConfig), C.sizeof(_lib.MoEWeights), C.sizeof(_lib.MoEOutputs),
             _lib.MoEWeights.gate.offset, _lib.MoEWeights.shared_down.offset,
             _lib.MoEWeights.shared_expert_gate_w.offset, _lib.MoEWeights.router_bias.offset,
-            _lib.MoEConfig.shared_inter.offset, _lib.MoEOutputs.expert_offsets.offset]
+            _lib.MoEConfig.shared_inter.offset, _lib.MoEOutputs.expert_offsets.offset,
+            C.sizeof(_lib.AttnConfig), _lib.AttnConfig.qkv_ld.offset]
     assert got == want
 
 

@@ -124,6 +124,34 @@ def test_attention_against_oracle(B, L, offset, nh, nkv, d):
 
 
 @pytest.mark.parametrize("d", [64, 128])
+def test_attention_on_fused_qkv_rows(d):
+    """fm_attention with qkv_ld (q, k, v side by side in one [T, (nh + 2 n_kv) d] buffer,
+    the fused projection's output) gives the separate-buffer call's output, rotated q and
+    caches bit for bit."""
+    from flashmlx_b200 import ops
+    rng = np.random.default_rng(70 + d)
+    B, L, offset, nh, nkv, max_len, theta = 2, 7, 3, 4, 2, 16, 1e6
+    ck = np.zeros((B, nkv, max_len, d), np.uint16)
+    ck[:, :, :offset] = _rnd(rng, (B, nkv, offset, d))
+    cv = ck.copy()
+    q, k, v = _rnd(rng, (B * L, nh * d)), _rnd(rng, (B * L, nkv * d)), _rnd(rng, (B * L, nkv * d))
+    bq, bk, bv = _rnd(rng, nh * d, 0.02), _rnd(rng, nkv * d, 0.02), _rnd(rng, nkv * d, 0.02)
+    qn, kn = _rnd(rng, d, 0.1), _rnd(rng, d, 0.1)
+    extra = dict(q_bias=_dev(bq), k_bias=_dev(bk), v_bias=_dev(bv), q_norm=_dev(qn), k_norm=_dev(kn))
+    qt, ck1, cv1 = _dev(q), _dev(ck), _dev(cv)
+    out1 = ops.attention(qt, _dev(k), _dev(v), ck1, cv1, B, L, offset, theta, **extra)
+    qkv = _dev(np.concatenate([q, k, v], axis=1))
+    ck2, cv2 = _dev(ck), _dev(cv)
+    out2 = ops.attention_qkv(qkv, ck2, cv2, B, L, offset, theta, **extra)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(_host(out2), _host(out1))
+    np.testing.assert_array_equal(_host(qkv)[:, :nh * d], _host(qt))
+    np.testing.assert_array_equal(_host(qkv)[:, nh * d:], np.concatenate([k, v], axis=1))  # k, v read only
+    np.testing.assert_array_equal(_host(ck2), _host(ck1))
+    np.testing.assert_array_equal(_host(cv2), _host(cv1))
+
+
+@pytest.mark.parametrize("d", [64, 128])
 def test_attention_with_qk_norm(d):
     """QK-norm inside fm_attention: each q / k head RMS-normalised (after the bias, before
     RoPE), against the oracle's rms_norm of the reshaped heads."""
