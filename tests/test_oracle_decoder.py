@@ -199,3 +199,16 @@ def test_query_width_differs_from_hidden():
     a = D.Decoder(sh, w, 2, 8)
     a.forward(ids[:, :4])
     np.testing.assert_array_equal(a.forward(ids[:, 4:5]), D.Decoder(sh, w, 2, 8).forward(ids))
+
+
+def test_fused_qkv_rows_equal_separate_projections():
+    """The decoder's fused q|k|v matrix (the three matrices' rows, scales and biases
+    concatenated) gives the three projections side by side, bit for bit: the rows of a
+    quantized linear do not interact (model.cpp:476-480 per projection)."""
+    rng = np.random.default_rng(12)
+    H, QD, KVD = 256, 512, 128
+    mats = [S.make_qmatrix(20 + i, f"p{i}", (), n, H, 64, 4, scale_std=0.05) for i, n in enumerate((QD, KVD, KVD))]
+    fused = tuple(np.concatenate([m[j] for m in mats], axis=0) for j in range(3))
+    x = _bf16(rng.standard_normal((7, H)))
+    sep = np.concatenate([O.quantized_matmul(x, *m) for m in mats], axis=1)
+    np.testing.assert_array_equal(O.quantized_matmul(x, *fused), sep)
