@@ -62,7 +62,7 @@ def parse():
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-all between staged calls")
     ap.add_argument("--route-mode", default="grid", choices=["grid", "last-block"],
-                    help="MoE workloads: routing kernel form (fm_set_route_mode)")
+                    help="routing kernel form of the MoE layers (fm_set_route_mode)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
     return a
@@ -535,6 +535,8 @@ def run_decoder(args, rank, world, local_rank):
     weights = DEC.device_decoder_weights(shape, args.seed + rank, dev)
     dec = DEC.Decoder.from_weights(shape, weights, dev, B, PROMPT_LEN + DECODE_STEPS)
     h = dec.handle()
+    from flashmlx_b200 import _lib as L
+    h.set_route_mode({"grid": L.FM_ROUTE_GRID, "last-block": L.FM_ROUTE_LAST_BLOCK}[args.route_mode])
     rng = np.random.default_rng(args.seed + 1000 + rank)
     prompt_np = rng.integers(0, shape.vocab, (B, PROMPT_LEN)).astype(np.int32)
     prompt = torch.from_numpy(prompt_np).to(dev)
@@ -598,6 +600,7 @@ def run_decoder(args, rank, world, local_rank):
                        "position_at_timing": pos0, "prefill_ms": prefill_ms,
                        "prefill_tokens_per_s": B * PROMPT_LEN / (prefill_ms * 1e-3),
                        "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "route_mode": args.route_mode, "qkv": "fused q|k|v projection",
                        "l2": "weights exceed L2 (no flush between steps)"},
             "e2e": {"value": world * B * args.steps / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(B * PROMPT_LEN * 4 / args.steps),
