@@ -469,8 +469,11 @@ __global__ void finalize_pairs_f32_kernel(const uint16_t* __restrict__ y_pairs, 
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        acc[2 * q] = fmaf(bf2f(static_cast<uint16_t>(w[q] & 0xffffu)), sc, acc[2 * q]);
-        acc[2 * q + 1] = fmaf(bf2f(static_cast<uint16_t>(w[q] >> 16)), sc, acc[2 * q + 1]);
+        // d * score rounded to fp32, then added (no fused multiply-add): the per-op
+        // rounding of the reference's multiply then sum, and of the GEMV path's
+        // red.add of the rounded product
+        acc[2 * q] = __fadd_rn(acc[2 * q], __fmul_rn(bf2f(static_cast<uint16_t>(w[q] & 0xffffu)), sc));
+        acc[2 * q + 1] = __fadd_rn(acc[2 * q + 1], __fmul_rn(bf2f(static_cast<uint16_t>(w[q] >> 16)), sc));
       }
     }
 #pragma unroll
