@@ -46,9 +46,33 @@ class Mem:
         self.a[idx] = v
 
 
-def qkv_rope(q, k, v, bias, cache_k, cache_v, B, L, offset, nh, nkv, d, max_len, q_ld, kv_ld, theta):
+def _fma(a, b, c):
+    return (np.float64(a) * np.float64(b) + np.float64(c)).astype(np.float32)
+
+
+def _head_norm(x1, x2, w, d, eps):
+    """The QK-norm of one head in qkv_rope_kernel: lane l's fp32 sum of squares over its
+    pairs i = l, l + 32 (fmaf chain, zeros past d/2), the xor-butterfly warp sum, then
+    bf16(bf16(x * n) * w)."""
+    half = d // 2
+    X1, X2 = np.zeros(64, np.float32), np.zeros(64, np.float32)
+    X1[:half], X2[:half] = x1, x2
+    lane = np.arange(32)
+    ss = np.zeros(32, np.float32)
+    for j in range(2):
+        ss = _fma(X1[lane + 32 * j], X1[lane + 32 * j], _fma(X2[lane + 32 * j], X2[lane + 32 * j], ss))
+    for off in (16, 8, 4, 2, 1):
+        ss = (ss + ss[lane ^ off]).astype(np.float32)
+    assert (ss == ss[0]).all()
+    n = np.float32(1) / np.sqrt(np.float32(ss[0] / np.float32(d) + np.float32(eps)))
+    i = np.arange(half)
+    return (f32(bf(f32(bf(x1 * n)) * f32(w[i]))), f32(bf(f32(bf(x2 * n)) * f32(w[i + half]))))
+
+
+def qkv_rope(q, k, v, bias, cache_k, cache_v, B, L, offset, nh, nkv, d, max_len, q_ld, kv_ld, theta,
+             norms=(None, None), eps=1e-6):
     """qkv_rope_kernel: one warp per (token, head slot), lane l holding pairs (i, i + d/2)
-    for i = l, l + 32 (no QK-norm here)."""
+    for i = l, l + 32; bias, then the optional QK-norm (norms = (q_norm, k_norm)), then RoPE."""
     half = d // 2
     log2_theta = math.log2(theta)
     for t in range(B * L):
@@ -71,6 +95,9 @@ def qkv_rope(q, k, v, bias, cache_k, cache_v, B, L, offset, nh, nkv, d, max_len,
             x2 = f32(src[0].get(src[1] + i + half))
             x1 = f32(bf(x1 + f32(bias_v[i])))
             x2 = f32(bf(x2 + f32(bias_v[i + half])))
+            norm = norms[0] if slot < nh else (norms[1] if slot < nh + nkv else None)
+            if norm is not None:
+                x1, x2 = _head_norm(x1, x2, norm, d, eps)
             if rot:
                 inv = np.exp2(-(2.0 * i / d) * log2_theta).astype(np.float32)
                 ang = np.float32(pos) * inv
@@ -273,3 +300,47 @@ def test_attention_kernels_against_oracle(B, L, offset, nh, nkv, d, fused):
         np.testing.assert_array_equal(q.a.reshape(T, -1)[:, QD:], np.concatenate([kn, vn], axis=1))
     ref = D.sdpa(q_ref, ck_ref, cv_ref, B, L, offset, nh, nkv, d)
     assert_close(out.a.reshape(T, QD), ref, f"sdpa B={B} L={L} offset={offset}", max_rel=2e-2, mae_rel=5e-3)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("fused", [False, True])
+def test_qk_norm_lanes_against_oracle(d, fused):
+    """Qwen3's QK-norm inside qkv_rope_kernel (model.cpp:573-581), lane by lane, against
+    the oracle's rms_norm of each q / k head followed by RoPE."""
+    rng = np.random.default_rng(90 + d)
+    B, L, offset, nh, nkv, theta, eps = 2, 3, 4, 4, 2, 1e6, 1e-6
+    max_len, T, QD, KVD = offset + L, B * L, nh * d, nkv * d
+    qn = bf(3 * rng.standard_normal((T, QD)))
+    kn, vn = bf(3 * rng.standard_normal((T, KVD))), bf(rng.standard_normal((T, KVD)))
+    wq, wk = bf(1 + 0.1 * rng.standard_normal(d)), bf(1 + 0.1 * rng.standard_normal(d))
+    zero = [np.zeros(n, np.uint16) for n in (QD, KVD, KVD)]
+    ck = np.zeros((B, nkv, max_len, d), np.uint16)
+    cv = ck.copy()
+    if fused:
+        buf = Mem(np.concatenate([qn, kn, vn], axis=1))
+        views, q_ld, kv_ld = ((buf, 0), (buf, QD), (buf, QD + KVD)), QD + 2 * KVD, QD + 2 * KVD
+    else:
+        views, q_ld, kv_ld = ((Mem(qn), 0), (Mem(kn), 0), (Mem(vn), 0)), QD, KVD
+
+    class At:
+        def __init__(self, mem, base):
+            self.mem, self.base = mem, base
+
+        def get(self, idx):
+            return self.mem.get(np.asarray(idx) + self.base)
+
+        def put(self, idx, val):
+            self.mem.put(np.asarray(idx) + self.base, val)
+    cache_k, cache_v = Mem(ck), Mem(cv)
+    qv = At(*views[0])
+    qkv_rope(qv, At(*views[1]), At(*views[2]), zero, cache_k, cache_v, B, L, offset, nh, nkv, d, max_len, q_ld,
+             kv_ld, theta, norms=(wq, wk), eps=eps)
+    pos = offset + np.tile(np.arange(L), B)
+    q_ref = D.rope(D.rms_norm(qn.reshape(T, nh, d), wq, eps).reshape(T, -1), pos, nh, d, theta)
+    k_ref = D.rope(D.rms_norm(kn.reshape(T, nkv, d), wk, eps).reshape(T, -1), pos, nkv, d, theta)
+    q_got = views[0][0].a.reshape(T, -1)[:, :QD]
+    assert_close(q_got, q_ref, "qk-norm q", max_rel=1e-2, mae_rel=1e-4)
+    got_k = cache_k.a.reshape(ck.shape)[:, :, offset:].transpose(0, 2, 1, 3).reshape(T, KVD)
+    assert_close(got_k, k_ref, "qk-norm k", max_rel=1e-2, mae_rel=1e-4)
+    got_v = cache_v.a.reshape(cv.shape)[:, :, offset:].transpose(0, 2, 1, 3).reshape(T, KVD)
+    np.testing.assert_array_equal(got_v, vn)  # v: no norm, no rotation
