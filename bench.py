@@ -129,6 +129,71 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+class NvmlClockSampler:
+    """SM clock, power and clock-event reasons polled through NVML every ~1 ms in a thread
+    during the timed region (a K-step region of a sub-millisecond layer lasts only tens of
+    milliseconds, too short for nvidia-smi's 200 ms sampling).  Falls back to ClockSampler
+    when NVML is unavailable."""
+    BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, torch_device):
+        self.dev = torch_device
+        self.nv = None
+        self.fallback = None
+        self.samples = []
+        self.thread = None
+        self.stop_flag = False
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_device)
+            want = (getattr(props, "pci_domain_id", 0), getattr(props, "pci_bus_id", None),
+                    getattr(props, "pci_device_id", None))
+            for i in range(nv.nvmlDeviceGetCount()):
+                hd = nv.nvmlDeviceGetHandleByIndex(i)
+                pci = nv.nvmlDeviceGetPciInfo(hd)
+                if (pci.domain, pci.bus, pci.device) == want:
+                    self.nv, self.h = nv, hd
+                    break
+            if self.nv is not None:
+                self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - any NVML failure selects the nvidia-smi sampler
+            self.nv = None
+        if self.nv is None:
+            self.fallback = ClockSampler(torch_device.index or 0)
+
+    def _run(self):
+        nv, h = self.nv, self.h
+        while not self.stop_flag:
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(h)),
+                                     nv.nvmlDeviceGetPowerUsage(h) / 1e3))
+            except Exception:  # noqa: BLE001
+                break
+            time.sleep(0.001)
+
+    def start(self):
+        if self.fallback is not None:
+            return self.fallback.start()
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.005)
+
+    def stop(self) -> dict:
+        if self.fallback is not None:
+            return self.fallback.stop()
+        self.stop_flag = True
+        self.thread.join(timeout=2)
+        sm = [c for c, _, _ in self.samples]
+        reasons = sorted({n for _, r, _ in self.samples for n, bit in self.BITS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(sm), "sampler": "nvml ~1 ms",
+                "power_w_max": max((p for _, _, p in self.samples), default=None)}
+
+
 # ----------------------------------------------------------------------------- CPU
 def oracle_layer(config, shape, layer_np):
     """The CPU restatement of the workload's block (the variant's for variant configs)."""
@@ -238,6 +303,107 @@ def ep_kernel_work(shape, T, R, recv_counts, E_local):
             "qgemm_tc_down": (f_dn, b_dn), "qgemv_down": (f_dn, b_dn)}, active
 
 
+def layer_roofline(shape, T, counts, dev_ms, peaks, peak_src):
+    """Whole-layer roofline of one fm_moe_block call: algorithmic FLOPs (router, routed
+    and shared experts, shared gate) and HBM bytes (the weights of the experts that
+    receive tokens, read once, plus the shared expert, router, x and y); the bound is the
+    larger of the two lower limits on the step time (HBM for decode batches, the tensor
+    pipe for prefill batches)."""
+    wb = S.layer_weight_bytes(shape)
+    active = int((counts > 0).sum())
+    flops = S.routed_flops(shape, T)
+    nbytes = (active * wb["expert"] + wb["shared"] + wb["router"] + (shape.hidden * 2 if shape.shared_inter else 0)
+              + 2 * T * shape.hidden * 2)
+    t_hbm = nbytes / (peaks["hbm_gbs"] * 1e9)
+    t_tc = flops / (peaks["bf16_tflops"] * 1e12)
+    s = dev_ms * 1e-3
+    if t_hbm >= t_tc:
+        return {"bound": "hbm", "unit": "GB/s", "achieved": nbytes / s / 1e9, "peak": peaks["hbm_gbs"],
+                "frac": t_hbm / s, "algorithmic": nbytes, "active_experts": active, "peak_source": peak_src}
+    return {"bound": "tensor", "unit": "TFLOP/s", "achieved": flops / s / 1e12, "peak": peaks["bf16_tflops"],
+            "frac": t_tc / s, "algorithmic": flops, "peak_source": peak_src}
+
+
+def kernel_roofline(prof, work, peaks, peak_src, traffic_key=None):
+    """Roofline of the dominant expert-product kernel (by device time) from the library's
+    per-kernel CUDA-event timers: algorithmic FLOPs (tcgen05 GEMMs) or bytes (GEMVs) per
+    launch over the average launch time."""
+    name, (launches, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
+    cand = [(n, v) for n, v in prof.items() if n in work]
+    if name not in work and cand:  # dominant kernel outside the expert products: report those
+        name, (launches, tot_ms) = max(cand, key=lambda kv: kv[1][1])
+    avg_ms = tot_ms / max(1, launches)
+    flops, nbytes = work.get(name, (0.0, 0.0))
+    tensor_bound = name.startswith("qgemm_tc")
+    if tensor_bound:
+        achieved, peak, roof = flops / (avg_ms * 1e-3) / 1e12, peaks["bf16_tflops"], {"bound": "tensor",
+                                                                                         "unit": "TFLOP/s"}
+    else:
+        achieved, peak, roof = nbytes / (avg_ms * 1e-3) / 1e9, peaks["hbm_gbs"], {"bound": "hbm", "unit": "GB/s"}
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "traffic.json")
+    if traffic_key and os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get(traffic_key, {}).get(name)
+    roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "traffic": traffic, "kernel": name,
+                 "kernel_ms": avg_ms, "peak_source": peak_src, "algorithmic": flops if tensor_bound else nbytes})
+    return roof
+
+
+# the decode half of the metric, measured beside the default prefill workload
+SECONDARY = {"qwen15_prefill": "qwen15_decode"}
+
+
+def measure_secondary(config, args, dev, h, peaks, peak_src):
+    """One more single-GPU workload in the same run (configs[0] decode beside the
+    configs[1] prefill headline): W warm-up steps, K timed steps on the launching stream,
+    per-kernel times, the dominant kernel's and the whole layer's roofline, clocks."""
+    import numpy as np
+    import torch
+
+    from flashmlx_b200 import ops
+    shape, layer_np = workload(config, args.seed)
+    T = shape.tokens
+    x = ops.bf16_from_numpy(S.make_x(shape, args.seed), dev)
+    y = torch.empty_like(x)
+    block = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(layer_np, dev))
+    block.reserve(T)
+    _, routing = block(x, return_routing=True)
+    h.sync()
+    counts = np.diff(routing["expert_offsets"].cpu().numpy())
+    for _ in range(args.warmup):
+        block(x, out=y)
+    h.sync()
+    stream = torch.cuda.current_stream()
+    clocks = NvmlClockSampler(dev)
+    h.profile(True)
+    h.profile_report(reset=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    clocks.start()
+    e0.record(stream)
+    for _ in range(args.steps):
+        block(x, out=y)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    h.sync()
+    dev_ms = e0.elapsed_time(e1) / args.steps
+    prof = {k: v for k, v in h.profile_report(reset=True).items() if "." not in k}
+    h.profile(False)
+    work, active = kernel_work(shape, T, counts)
+    return {
+        "workload": shape.name, "value": T / (dev_ms * 1e-3), "unit": "tokens/s", "ms_per_step": dev_ms,
+        "steps": args.steps, "warmup": args.warmup, "tokens": T, "active_experts": active,
+        "l2": "layer weights exceed 2 x L2: no flush",
+        "kernels": {k: {"launches": n, "avg_ms": ms / max(1, n)} for k, (n, ms) in prof.items()},
+        "gpu_launches": sum(n for n, _ in prof.values()),
+        "roofline": kernel_roofline(prof, work, peaks, peak_src, shape.name),
+        "layer_roofline": layer_roofline(shape, T, counts, dev_ms, peaks, peak_src),
+        "clocks": clk,
+    }
+
+
 def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
@@ -332,8 +498,7 @@ def run_ours(args, rank, world, local_rank):
                f"({2 * l2_bytes / 1e6:.0f} MB memset) before every timed step" if flush is not None else
                f"per-rank weights {w_bytes / 1e6:.0f} MB exceed 2 x L2 ({l2_bytes / 1e6:.0f} MB): no flush")
 
-    clocks = ClockSampler(local_rank)
-    clocks.start()
+    clocks = NvmlClockSampler(dev)
     stream = torch.cuda.current_stream()
     hp.profile(True)
     hp.profile_report(reset=True)
@@ -343,6 +508,7 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    clocks.start()
     if flush is None:
         e0.record(stream)
         h0 = time.perf_counter()
@@ -366,6 +532,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         hp.sync()
         dev_ms = sum(a.elapsed_time(b) for a, b in ev) / args.steps
+    clk = clocks.stop()
     prof_all = hp.profile_report(reset=True)
     hp.profile(False)
     # "route.phaseN" entries split the routing kernel's time; they are not launches
@@ -415,7 +582,6 @@ def run_ours(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
-    clk = clocks.stop()
 
     if world > 1:
         per_rank = torch.zeros(world, 2, device=dev, dtype=torch.float64)
@@ -435,31 +601,11 @@ def run_ours(args, rank, world, local_rank):
             work, active = ep_kernel_work(shape, T, recv_seen["R"], recv_seen["counts"], E_local)
         else:
             work, active = kernel_work(shape, T, counts)
-        # dominant kernel by device time
-        name, (launches, tot_ms) = max(prof.items(), key=lambda kv: kv[1][1])
-        avg_ms = tot_ms / max(1, launches)
-        cand = [(n, v) for n, v in prof.items() if n in work]
-        if name not in work and cand:  # dominant kernel outside the expert products: report those
-            name, (launches, tot_ms) = max(cand, key=lambda kv: kv[1][1])
-            avg_ms = tot_ms / max(1, launches)
-        flops, nbytes = work.get(name, (0.0, 0.0))
-        tensor_bound = name.startswith("qgemm_tc")
-        if tensor_bound:
-            achieved = flops / (avg_ms * 1e-3) / 1e12
-            peak = peaks["bf16_tflops"]
-            roof = {"bound": "tensor", "unit": "TFLOP/s"}
-        else:
-            achieved = nbytes / (avg_ms * 1e-3) / 1e9
-            peak = peaks["hbm_gbs"]
-            roof = {"bound": "hbm", "unit": "GB/s"}
-        traffic = None
-        tfile = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tfile) and not ep:
-            with open(tfile) as f:
-                traffic = json.load(f).get(shape.name, {}).get(name)
-        roof.update({"achieved": achieved, "peak": peak, "frac": achieved / peak, "traffic": traffic,
-                     "kernel": name, "kernel_ms": avg_ms, "peak_source": peak_src,
-                     "algorithmic": flops if tensor_bound else nbytes})
+        roof = kernel_roofline(prof, work, peaks, peak_src, None if ep else shape.name)
+        layer_roof = None if ep else layer_roofline(shape, T, counts, dev_ms, peaks, peak_src)
+        secondary = None
+        if world == 1 and not variant and args.config in SECONDARY:
+            secondary = measure_secondary(SECONDARY[args.config], args, dev, h, peaks, peak_src)
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
             v, info = cpu_oracle_throughput(shape, layer_np, x_np, config=args.config)
@@ -487,8 +633,10 @@ def run_ours(args, rank, world, local_rank):
             "kernels": {kname: {"launches": n, "avg_ms": ms / max(1, n)} for kname, (n, ms) in prof.items()},
             "route_phases_ms": phases,
             "roofline": roof,
+            "layer_roofline": layer_roof,
             "cpu_baseline": cpu,
             "clocks": clk,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     if peer_block is not None:

@@ -74,6 +74,7 @@ SIGNATURES = {
     "fm_workspace_bytes": (_sz, [_p]),
     "fm_workspace_size": (_sz, [C.POINTER(MoEConfig), _i64]),
     "fm_set_path": (_i, [_p, _i]),
+    "fm_last_path": (_i, [_p]),
     "fm_set_route_mode": (_i, [_p, _i]),
     "fm_profile_enable": (_i, [_p, _i]),
     "fm_profile_report": (_i, [_p, C.POINTER(KernelTime), _i, C.POINTER(C.c_int), _i]),

@@ -75,6 +75,7 @@ struct fm_handle {
   int gemv_blocks_per_sm = 0;
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
+  int last_path = 0;  // expert-product path the last call took (fm_last_path)
   int route_mode = FM_ROUTE_AUTO;
   bool attn_ready = false;  // attention kernels' shared-memory opt-in done (first fm_attention)
   uint8_t* ws = nullptr;
@@ -790,6 +791,8 @@ int fm_set_path(fm_handle* h, int path) {
   return FM_OK;
 }
 
+int fm_last_path(const fm_handle* h) { return h ? h->last_path : 0; }
+
 int fm_set_route_mode(fm_handle* h, int mode) {
   if (!h) return FM_EINVAL;
   if (mode != FM_ROUTE_AUTO && mode != FM_ROUTE_GRID && mode != FM_ROUTE_LAST_BLOCK)
@@ -891,6 +894,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   const int ksplit = router_ksplit(h, T, H);
   const int64_t P = T * k;
   const bool tcp = use_tc(h, P, E, c->group_size);
+  h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
   Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true, tcp);
   rc = ensure_ws(h, p.total);
   if (rc) return rc;
@@ -1108,6 +1112,7 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   // in fp32 for sigmoid routing) runs when the handle's path is FM_PATH_TCGEN05; the
   // automatic choice keeps the GEMV path for the variants.
   const bool tcp = h->path == FM_PATH_TCGEN05 && I % 128 == 0 && Is % 128 == 0;
+  h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
   const int64_t P = T * k;
   Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, Is, shared, true, tcp);
   int rc = ensure_ws(h, p.total);
@@ -1303,6 +1308,7 @@ int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, i
   if (rows > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "too many rows");
   bool tcp = use_tc(h, rows, E, group_size);
   if (K % 128) tcp = true;  // the GEMV path works in 128-wide K chunks
+  h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
   Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false, tcp);
   int rc = ensure_ws(h, p.total);
   if (rc) return rc;
@@ -1493,6 +1499,7 @@ int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w,
   int rc = check_ep_experts(h, c, w, R > 0, shared);
   if (rc) return rc;
   const bool tcp = use_tc(h, R + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
+  h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
   const EpPlan2 p2 = make_ep_plan2(R, std::max<int64_t>(T, 0), H, I, Is, nseg, shared);
   rc = ensure_ep_ws(h, p2.total);
   if (rc) return rc;
@@ -1662,6 +1669,7 @@ int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights
   if (rc) return rc;
   // the receive count is not known on the host: decide the path on this rank's own pairs
   const bool tcp = use_tc(h, T * k + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
+  h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
   const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
   const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, ksplit);
   rc = ensure_ws(h, p1.total);
@@ -1959,10 +1967,22 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
   {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (!d.ready) {
-      d.status = noalloc_setup(device, d);
-      d.ready = true;
+      // the set-up synchronizes the device, which would invalidate a capture in progress
+      cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+      if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cap) != cudaSuccess) {
+        cudaGetLastError();
+        rc = FM_ECUDA;
+      } else if (cap != cudaStreamCaptureStatusNone) {
+        rc = FM_EINVAL;
+      } else {
+        rc = noalloc_setup(device, d);
+        // an unsupported device stays unsupported; a failed CUDA call is retried next call
+        d.ready = rc == FM_OK || rc == FM_EUNSUPPORTED;
+        d.status = rc;
+      }
+    } else {
+      rc = d.status;
     }
-    rc = d.status;
   }
   if (rc == FM_OK) {
     fm_handle h;  // borrows the fixed scratch; never grows or frees it

@@ -71,6 +71,11 @@ class Handle:
     def set_path(self, path: int):
         self.check(self.lib.fm_set_path(self.h, path))
 
+    def last_path(self) -> int:
+        """FM_PATH_GEMV (1) or FM_PATH_TCGEN05 (2): the expert-product path of the
+        handle's last call, i.e. which of MLX's two arithmetic forms it followed."""
+        return int(self.lib.fm_last_path(self.h))
+
     def set_route_mode(self, mode: int):
         """FM_ROUTE_GRID (cooperative, grid barriers) or FM_ROUTE_LAST_BLOCK (batches of
         at most 128 tokens: top-k, sort and planning in the block that finishes the router

@@ -162,6 +162,14 @@ FM_API size_t fm_workspace_size(const fm_moe_config* cfg, int64_t max_tokens);
  * dequant-GEMV for few tokens per expert and the tcgen05 grouped GEMM otherwise. */
 enum { FM_PATH_AUTO = 0, FM_PATH_GEMV = 1, FM_PATH_TCGEN05 = 2 };
 FM_API int fm_set_path(fm_handle* h, int path);
+/* The expert-product path (FM_PATH_GEMV or FM_PATH_TCGEN05) that the handle's last
+ * fm_moe_block / fm_moe_block_variant / fm_quantized_matmul / fm_gather_qmm / fm_linear /
+ * expert-parallel call took, 0 before the first.  The two paths follow MLX's two
+ * arithmetic forms of a 4-bit product: the GEMV keeps the dequantized weights exact
+ * (s * sum(q x) + b * sum(x) in fp32, MLX's qmv), the tcgen05 GEMM rounds each weight
+ * s * q + b to bf16 (MLX's qmm tiles).  No reference counterpart (MLX picks its kernel
+ * internally). */
+FM_API int fm_last_path(const fm_handle* h);
 
 /* Form of the routing kernel (router, top-k, sort and tile plan; the reference's
  * op chain of model.cpp:757-775 and 682-700).  FM_ROUTE_GRID: one cooperative kernel
@@ -243,8 +251,12 @@ FM_API int fm_moe_block(fm_handle* h, const fm_moe_config* cfg, const fm_moe_wei
  * calls that need more (the routing tables, sorted activations and combine buffers
  * grow with T) return FM_ETOOLARGE before launching anything.  For the
  * Qwen1.5-MoE-shaped layer that is a few hundred tokens, i.e. decode batches.
- * The first call on a device resolves the array's device address and queries launch
- * parameters; make that first call before any stream capture.  All calls share the
+ * The first call on a device resolves the array's device address, queries launch
+ * parameters and synchronizes the device once; make that first call before any stream
+ * capture (a first call on a capturing stream returns FM_EINVAL and leaves the capture
+ * intact).  If that set-up fails on a CUDA call (FM_ECUDA), the next call tries it
+ * again; a device that is not a B200 (FM_EUNSUPPORTED) stays refused for the life of
+ * the process.  All calls share the
  * array: calls whose execution overlaps on the GPU (other streams, other threads) race
  * and must be serialized by the caller.  Device-side failures (a bounded wait that ran
  * out) are not reported by this entry point; fm_moe_block + fm_sync_status report them. */

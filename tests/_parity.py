@@ -29,14 +29,19 @@ from flashmlx_b200.synthetic import bf16_to_f32
 
 MAX_REL = 1e-2
 MAE_REL = 1e-3
-# bf16 keeps 8 significant bits: 1e-2 of the largest element is only 1.3-2.6 ulps there,
-# and the double roundings of the MLX op chain (g, u, silu, d, d*score, sum, shared)
-# give two valid evaluation orders up to ~2 ulps at the top of a tensor (measured 1.1%
-# on the Mixtral-shaped layer).  The tight bound therefore allows 2e-2 normwise.
-TIGHT = {"max_rel": 2e-2, "mae_rel": MAE_REL}
-# exact-dequantization oracle: measured mae_rel 4.0-4.5e-3 for the whole MoE block,
-# 1.4e-3 for one 4-bit GEMM (the bf16 rounding of the dequantized weights)
+# The tight bound is the north-star's: max_rel 1e-2 (normwise) and mae_rel 1e-3, against
+# the oracle evaluated in the arithmetic form the device path follows (exact weights for
+# the GEMV, bf16-rounded weights for tcgen05).  bf16 keeps 8 significant bits, so 1e-2 of
+# the largest element is 1.3-2.6 ulps there.
+TIGHT = {"max_rel": MAX_REL, "mae_rel": MAE_REL}
+# Against the other form: measured mae_rel 4.0-4.5e-3 for the whole MoE block, 1.4e-3 for
+# one 4-bit GEMM (the bf16 rounding of the dequantized weights)
 EXACT_FLOOR = {"max_rel": 2e-2, "mae_rel": 6e-3}
+# Whole-decoder logits (a chain of attention, 4-bit products and MoE layers, then the
+# lm_head): the oracle's two valid forms (exact vs bf16-rounded weights) differ there by
+# up to max_rel 1.06e-2 and mae_rel 6.8e-3 on the small test decoder's prefill and
+# teacher-forced decode steps; the device must stay within a margin of that gap.
+DECODER_LOGITS = {"max_rel": 2e-2, "mae_rel": 1e-2}
 
 
 def metrics(a_bits: np.ndarray, b_bits: np.ndarray) -> dict:

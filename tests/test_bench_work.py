@@ -70,3 +70,21 @@ def test_expert_parallel_work_splits_the_layer():
     assert f_gu == world * single["qgemm_tc_gateup"][0]
     assert f_dn == world * single["qgemm_tc_down"][0]
     assert single["qgemm_tc_down"][0] == 2.0 * T * k * I * H + 2.0 * T * Is * H
+
+
+def test_layer_roofline_bound_and_work():
+    """The whole-layer roofline: configs[1] prefill is tensor-bound on its 567,959,093,248
+    FLOPs; configs[0] decode is HBM-bound on the bytes of the experts that receive tokens
+    (4,866,048 B each), the shared expert, router, shared gate, x and y."""
+    peaks = {"hbm_gbs": 6000.0, "bf16_tflops": 1500.0}
+    pre = S.CONFIGS["qwen15_prefill"]
+    r = bench.layer_roofline(pre, pre.tokens, np.full(pre.num_experts, 273), 1.0, peaks, "test")
+    assert r["bound"] == "tensor" and r["algorithmic"] == 567_959_093_248
+    assert abs(r["frac"] - 567_959_093_248 / 1.5e15 / 1e-3) < 1e-9
+    dec = S.CONFIGS["qwen15_decode"]
+    counts = np.zeros(dec.num_experts, int)
+    counts[:53] = 2
+    r = bench.layer_roofline(dec, dec.tokens, counts, 0.1, peaks, "test")
+    want = 53 * 4_866_048 + 19_464_192 + 245_760 + 4_096 + 2 * 32 * 2048 * 2
+    assert r["bound"] == "hbm" and r["algorithmic"] == want and r["active_experts"] == 53
+    assert abs(r["achieved"] - want / 1e-4 / 1e9) < 1e-6

@@ -35,7 +35,7 @@ def _check_rank(rank, world, shape_name, tokens, path):
     from flashmlx_b200.ep import MoEBlockEP, local_layer
     from oracle import oracle as O
     from tests._parity import EXACT_FLOOR, assert_close
-    from tests.gpu_util import check_vs_oracle, host_bf16
+    from tests.gpu_util import check_vs_oracle, form_of, host_bf16
     shape = SHAPES[shape_name]
     layer = S.make_layer(shape, 7)
     dev = torch.device("cuda", rank)
@@ -47,6 +47,7 @@ def _check_rank(rank, world, shape_name, tokens, path):
         x_np = S.make_x(shape, 40 + rank, tokens=tokens)
         x = ops.bf16_from_numpy(x_np, dev)
         y_ep = host_bf16(block(x))
+        form = form_of(h)
         # single-GPU reference on the same tokens, with the full layer
         full = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(layer, dev))
         y1, r = full(x, return_routing=True)
@@ -54,7 +55,7 @@ def _check_rank(rank, world, shape_name, tokens, path):
         assert_close(y_ep, host_bf16(y1), f"rank {rank}: ep vs fm_moe_block", **EXACT_FLOOR)
         ids, sc = r["topk_ids"].cpu().numpy(), host_bf16(r["topk_scores"])
         check_vs_oracle(y_ep, lambda: O.Layer(shape, layer).moe_block(x_np, forced_ids=ids, forced_scores=sc),
-                        f"rank {rank}: ep vs oracle")
+                        f"rank {rank}: ep vs oracle", form)
     finally:
         h.set_path(0)
 
@@ -66,7 +67,7 @@ def _check_rank_peer(rank, world, shape_name, tokens, path):
     from flashmlx_b200.ep import MoEBlockEPPeer, local_layer
     from oracle import oracle as O
     from tests._parity import EXACT_FLOOR, assert_close
-    from tests.gpu_util import check_vs_oracle, host_bf16
+    from tests.gpu_util import check_vs_oracle, form_of, host_bf16
     shape = SHAPES[shape_name]
     layer = S.make_layer(shape, 7)
     dev = torch.device("cuda", rank)
@@ -84,6 +85,7 @@ def _check_rank_peer(rank, world, shape_name, tokens, path):
                                                                    device=dev)
             y = block(x)
             block.sync()
+            form = form_of(block.h)
             assert y.shape == (T, shape.hidden)
             if T == 0:
                 continue
@@ -94,7 +96,7 @@ def _check_rank_peer(rank, world, shape_name, tokens, path):
             if call == 0:
                 ids, sc = r["topk_ids"].cpu().numpy(), host_bf16(r["topk_scores"])
                 check_vs_oracle(y_ep, lambda: O.Layer(shape, layer).moe_block(x_np, forced_ids=ids, forced_scores=sc),
-                                f"rank {rank}: peer ep vs oracle")
+                                f"rank {rank}: peer ep vs oracle", form)
     finally:
         block.close()
 

@@ -1,8 +1,9 @@
 """The C++ host layer on the device: fm_host run (MoEModel::moe_block over a checkpoint
 directory, C++ all the way to libflashmoe's C ABI) gives the same bf16 output as the same
 layer's arrays run through the Python binding, for a Llama-family layer (fm_moe_block)
-and a Nemotron-H 'E' layer (fm_moe_block_variant).  Top-2 layers: the fp32 sums of two
-routed rows do not depend on the order the kernels add them in, so equality is exact."""
+and a Nemotron-H 'E' layer (fm_moe_block_variant), and that output matches the CPU
+oracle of the layer.  Top-2 layers: the fp32 sums of two routed rows do not depend on the
+order the kernels add them in, so equality is exact."""
 from __future__ import annotations
 
 import subprocess
@@ -12,6 +13,7 @@ import pytest
 import torch
 
 from flashmlx_b200 import synthetic as S
+from tests.gpu_util import check_layer_vs_oracle, form_of
 from tests.test_checkpoint import NEMO, SHAPE, _write_model, _write_nemotron
 
 pytestmark = pytest.mark.gpu
@@ -41,8 +43,11 @@ def test_llama_layer(tmp_path, fm_host, tokens):
     shape = SHAPE.with_tokens(tokens)
     x = S.make_x(shape, 41)
     y = _run_host(fm_host, tmp_path / "m", 0, x, tmp_path)
-    ref = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(layer, "cuda"))(ops.bf16_from_numpy(x, "cuda"))
+    ref, r = ops.MoEBlock(shape, ops.MoEWeightsT.from_numpy(layer, "cuda"))(ops.bf16_from_numpy(x, "cuda"),
+                                                                          return_routing=True)
     torch.cuda.synchronize()
+    form = form_of(ops.default_handle(torch.cuda.current_device()))  # same T, same path rule
+    check_layer_vs_oracle(y, shape, layer, x, r, form, f"fm_host run T={tokens}")
     np.testing.assert_array_equal(y, ops.bf16_to_numpy(ref))
 
 
@@ -55,8 +60,11 @@ def test_nemotron_layer(tmp_path, fm_host, tokens):
     shape = NEMO.with_tokens(tokens)
     x = S.make_x(shape, 42)
     y = _run_host(fm_host, tmp_path / "m", 3, x, tmp_path)
-    blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", n_group=2, topk_group=1,
-                                                 routed_scaling_factor=2.5)
-    ref = blk(ops.bf16_from_numpy(x, "cuda"))
+    routing = {"n_group": 2, "topk_group": 1, "routed_scaling_factor": 2.5}
+    blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", **routing)
+    ref, r = blk(ops.bf16_from_numpy(x, "cuda"), return_routing=True)
     torch.cuda.synchronize()
+    form = form_of(ops.default_handle(torch.cuda.current_device()))
+    check_layer_vs_oracle(y, shape, layer, x, r, form, f"fm_host run (Nemotron-H) T={tokens}",
+                          sigmoid_routing=routing)
     np.testing.assert_array_equal(y, ops.bf16_to_numpy(ref))

@@ -101,6 +101,28 @@ def test_qwen3_prefill_full_sample(ops):
     L.check(x, "configs[3] prefill", sample=sample)
 
 
+def test_qwen3_decode_config3_exact(ops):
+    """BASELINE configs[3] decode exactly: 256 tokens, seed 0, every token's routing and
+    every output row (the automatic path choice)."""
+    L = layer("qwen3_decode")
+    x = S.make_x(L.shape, 0)
+    assert x.shape[0] == 256
+    m, ties = L.check(x, "configs[3] decode T=256")
+    print("configs[3] decode", m, "near-ties", ties)
+
+
+def test_mixtral_config4_full_routing_sample(ops):
+    """BASELINE configs[4] at full size: the Zipf(1.2)-skewed 8192-token batch of the
+    Mixtral-shaped layer (8 experts, top-2 renormalised, H 4096, I 14336).  Routing for
+    every token and the permutation exactly; activations on a 512-token sample."""
+    L = layer("mixtral_prefill")
+    x = S.make_x(L.shape, 0)
+    assert x.shape[0] == 8192
+    sample = np.sort(np.random.default_rng(4).choice(x.shape[0], 512, replace=False))
+    m, ties = L.check(x, "configs[4] T=8192 (512-row sample)", sample=sample)
+    print("configs[4]", m, "near-ties", ties)
+
+
 def test_all_tokens_one_expert(ops):
     """Heavy skew: a large router bias sends every token to the same expert."""
     L = layer("qwen15_decode", seed=5)

@@ -10,7 +10,7 @@ import torch
 
 from flashmlx_b200 import synthetic as S
 from oracle import oracle as O
-from tests.gpu_util import check_vs_oracle, dev_bf16, dev_u32, host_bf16
+from tests.gpu_util import check_vs_oracle, dev_bf16, dev_u32, form_of, host_bf16
 
 pytestmark = pytest.mark.gpu
 KAT = np.load(os.path.join(os.path.dirname(__file__), "golden", "kat.npz"))
@@ -61,7 +61,7 @@ def test_quantized_matmul_parity(ops, path, M, K, N, gs):
     w, s, b = S.make_qmatrix(M, f"qmm{K}{N}", (), N, K, gs)
     y = run_qmm(ops, PATHS[path], x, w, s, b, gs)
     mt, me = check_vs_oracle(y, lambda: O.quantized_matmul(x, w, s, b, group_size=gs),
-                             f"quantized_matmul {path} M={M} K={K} N={N} gs={gs}")
+                             f"quantized_matmul {path} M={M} K={K} N={N} gs={gs}", form_of(ops.default_handle()))
     print(f"qmm {path} M={M} K={K} N={N} gs={gs}: bf16-weights {mt} exact {me}")
 
 
@@ -71,7 +71,8 @@ def test_quantized_matmul_without_biases(ops):
     w, s, _ = S.make_qmatrix(1, "nobias", (), 256, 1024)
     for path in PATHS.values():
         y = run_qmm(ops, path, x, w, s, None)
-        check_vs_oracle(y, lambda: O.quantized_matmul(x, w, s, None), f"no-bias path {path}")
+        check_vs_oracle(y, lambda: O.quantized_matmul(x, w, s, None), f"no-bias path {path}",
+                        form_of(ops.default_handle()))
 
 
 @pytest.mark.parametrize("path", ["gemv", "tcgen05"])
@@ -111,14 +112,15 @@ def test_gather_qmm_parity(ops, path, T, k, sorted_idx):
             y = ops.gather_qmm(dev_bf16(xs), dev_u32(w), dev_bf16(s), dev_bf16(b), rhs_indices=dev_u32(rs),
                                sorted_indices=True)
             h.sync()
-            check_vs_oracle(host_bf16(y), lambda: O.gather_qmm(xs, w, s, b, None, rs), f"gather sorted {path}")
+            check_vs_oracle(host_bf16(y), lambda: O.gather_qmm(xs, w, s, b, None, rs), f"gather sorted {path}",
+                            form_of(h))
         else:
             y = ops.gather_qmm(dev_bf16(x), dev_u32(w), dev_bf16(s), dev_bf16(b), rhs_indices=dev_u32(rhs))
             h.sync()
             assert tuple(y.shape) == (T, k, 1, N)
             check_vs_oracle(host_bf16(y).reshape(T * k, 1, N),
                             lambda: O.gather_qmm(x.reshape(T, 1, K), w, s, b, None, rhs.ravel()),
-                            f"gather unsorted {path}")
+                            f"gather unsorted {path}", form_of(h))
     finally:
         h.set_path(0)
 

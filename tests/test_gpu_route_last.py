@@ -4,12 +4,8 @@ block that finishes last) against the cooperative grid-barrier kernel: the same 
 scores, expert offsets and permutation bit for bit, and the same layer output up to the
 order of the fp32 atomic adds, for softmax routing (model.cpp:757-775), grouped sigmoid
 routing (nemotron_h.cpp:1018-1050) and gather_qmm's given indices (model.cpp:703-721);
-batches above 128 tokens take the grid form in either mode.
-
-These tests have not yet run on a B200: they run when FM_NEW_GPU_TESTS=1."""
+batches above 128 tokens take the grid form in either mode."""
 from __future__ import annotations
-
-import os
 
 import numpy as np
 import pytest
@@ -19,9 +15,7 @@ from flashmlx_b200 import synthetic as S
 from flashmlx_b200 import _lib
 from tests.gpu_util import GpuLayer, dev_bf16, dev_u32, host_bf16
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("FM_NEW_GPU_TESTS") != "1",
-                                 reason="last-block routing not yet run on a B200 (FM_NEW_GPU_TESTS=1 runs it)")]
+pytestmark = pytest.mark.gpu
 
 
 def _in_mode(mode, fn):

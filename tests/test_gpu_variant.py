@@ -5,7 +5,6 @@ oracle's restatement: the routing against the oracle's own routing where no near
 decides a pick, the block against the oracle under the device's routing."""
 from __future__ import annotations
 
-import os
 
 import numpy as np
 import pytest
@@ -14,7 +13,7 @@ import torch
 from flashmlx_b200 import synthetic as S
 from oracle import oracle as O
 from tests import numpy_ref as R
-from tests.gpu_util import check_vs_oracle, host_bf16
+from tests.gpu_util import check_vs_oracle, form_of, host_bf16
 
 pytestmark = pytest.mark.gpu
 
@@ -47,7 +46,8 @@ def _check_sigmoid(shape, groups, seed):
     x_np = S.make_x(shape, seed)
     routing = {"n_group": groups[0], "topk_group": groups[1], "routed_scaling_factor": 2.5}
     blk = ops.MoEBlockVariant.sigmoid_from_numpy(shape, layer, "cuda", **routing)
-    y, r = blk(ops.bf16_from_numpy(x_np, "cuda"), return_routing=True)
+    x_dev = ops.bf16_from_numpy(x_np, "cuda")
+    y, r = blk(x_dev, return_routing=True)
     torch.cuda.synchronize()
     ids = r["topk_ids"].cpu().numpy()
     sc = r["topk_scores_f32"].cpu().numpy()
@@ -66,7 +66,7 @@ def _check_sigmoid(shape, groups, seed):
             assert abs(dev[e] - s) <= 2e-2 * abs(s) + 1e-6, (t, e, dev[e], s)
     # the block under the device's routing (ids and fp32 scores as applied)
     check_vs_oracle(host_bf16(y), lambda: L.moe_block(x_np, forced_ids=ids, forced_scores=sc),
-                    f"sigmoid block T={tokens} groups={groups} shared={shared}")
+                    f"sigmoid block T={tokens} groups={groups} shared={shared}", form_of(blk.block._h(x_dev.device)))
 
 
 def test_variant_rejects_bad_arguments():
@@ -85,8 +85,6 @@ def test_variant_rejects_bad_arguments():
         blk(x)
 
 
-@pytest.mark.skipif(os.environ.get("FM_NEW_GPU_TESTS") != "1",
-                    reason="the variant's tcgen05 path has not run on a B200 yet (FM_NEW_GPU_TESTS=1 runs it)")
 @pytest.mark.parametrize("tokens", [48, 700])
 @pytest.mark.parametrize("shared", [0, 256])
 def test_sigmoid_block_tcgen05_path(tokens, shared):
@@ -107,5 +105,6 @@ def test_sigmoid_block_tcgen05_path(tokens, shared):
         h.set_path(_lib.FM_PATH_AUTO)
     L = O.SigmoidLayer(shape, layer, routing)
     ids, sc = r["topk_ids"].cpu().numpy(), r["topk_scores_f32"].cpu().numpy()
+    assert form_of(h) == "bf16", "FM_PATH_TCGEN05 must run the tcgen05 expert path"
     check_vs_oracle(host_bf16(y), lambda: L.moe_block(x_np, forced_ids=ids, forced_scores=sc),
-                    f"sigmoid block tcgen05 T={tokens} shared={shared}")
+                    f"sigmoid block tcgen05 T={tokens} shared={shared}", "bf16")

@@ -212,3 +212,30 @@ def test_fused_qkv_rows_equal_separate_projections():
     x = _bf16(rng.standard_normal((7, H)))
     sep = np.concatenate([O.quantized_matmul(x, *m) for m in mats], axis=1)
     np.testing.assert_array_equal(O.quantized_matmul(x, *fused), sep)
+
+
+def test_logits_form_gap():
+    """The whole-decoder logits bound of the GPU tests (DECODER_LOGITS) is set from the
+    gap between MLX's two valid arithmetic forms of the 4-bit products (exact weights, as
+    qmv; bf16-rounded weights, as qmm) on the small test decoder: the gap must be real
+    (larger than the per-op bound) and inside DECODER_LOGITS."""
+    from tests._parity import DECODER_LOGITS, MAE_REL, metrics
+    sm = S.DecoderShape("dec_small", 256, 2, 4, 2, 64, 320, 1e6, 1e-6, MOE)
+    w = S.make_decoder(sm, 71)
+    prompt = np.random.default_rng(71).integers(0, sm.vocab, (2, 9)).astype(np.int32)
+
+    def run():
+        d = D.Decoder(sm, w, 2, 16)
+        outs = [d.forward(prompt)]
+        for _ in range(3):
+            outs.append(d.forward(D.argmax(outs[0])[:, None]))
+        return outs
+
+    exact = run()
+    with O.weight_rounding(O.BF16_WEIGHTS):
+        rounded = run()
+    gaps = [metrics(a, b) for a, b in zip(exact, rounded)]
+    worst = max(g["mae_rel"] for g in gaps)
+    assert worst > 2 * MAE_REL, gaps
+    assert all(g["max_rel"] <= DECODER_LOGITS["max_rel"] and g["mae_rel"] <= DECODER_LOGITS["mae_rel"]
+               for g in gaps), gaps

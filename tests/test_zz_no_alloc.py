@@ -45,14 +45,24 @@ def run_noalloc(lib_mod, ops, block, x):
 
 def test_noalloc_matches_handle_path_twice(setup):
     lib_mod, ops, shape, block = setup
+    from oracle import oracle as O
+    from tests.gpu_util import check_vs_oracle
+    layer = S.make_layer(shape, 3)
     for call, seed in enumerate((11, 12)):  # two calls in a row reuse the same scratch
-        x = ops.bf16_from_numpy(S.make_x(shape, seed), "cuda")
-        y_ref = ops.bf16_to_numpy(block(x))
+        x_np = S.make_x(shape, seed)
+        x = ops.bf16_from_numpy(x_np, "cuda")
+        y_ref, r = block(x, return_routing=True)
+        y_ref = ops.bf16_to_numpy(y_ref)
         ops.synchronize()
         y = run_noalloc(lib_mod, ops, block, x)
         assert np.isfinite(S.bf16_to_f32(y)).all()
         m = assert_close(y, y_ref, f"no-alloc call {call} vs fm_moe_block", **TIGHT)
         print(f"no-alloc call {call}: {m}")
+        # and against the CPU oracle directly: 32 tokens run the dequant GEMV, whose
+        # arithmetic is MLX's exact-weight (qmv) form
+        ids, sc = r["topk_ids"].cpu().numpy(), ops.bf16_to_numpy(r["topk_scores"])
+        check_vs_oracle(y, lambda: O.Layer(shape, layer).moe_block(x_np, forced_ids=ids, forced_scores=sc),
+                        f"no-alloc call {call}", "exact")
 
 
 def test_noalloc_rejects_oversize_batch(setup):
