@@ -37,6 +37,12 @@ TIGHT = {"max_rel": MAX_REL, "mae_rel": MAE_REL}
 # Against the other form: measured mae_rel 4.0-4.5e-3 for the whole MoE block, 1.4e-3 for
 # one 4-bit GEMM (the bf16 rounding of the dequantized weights)
 EXACT_FLOOR = {"max_rel": 2e-2, "mae_rel": 6e-3}
+# The one layer shape where 1e-2 does not hold: the Mixtral-shaped layer (H 4096,
+# I 14336) on the tcgen05 path at T = 48 measured max_rel 1.124e-2 against the bf16-weight
+# oracle (mae_rel 1.9e-4): outputs there reach ~1e3 and differ by one or two bf16 ulps at
+# the largest element, where the oracle's two forms also differ by 1.124e-2.  Its full
+# 8192-token configs[4] batch measured 4.7e-3 on a 512-row sample.
+MIXTRAL_TC = {"max_rel": 1.5e-2, "mae_rel": MAE_REL}
 # Whole-decoder logits (a chain of attention, 4-bit products and MoE layers, then the
 # lm_head): the oracle's two valid forms (exact vs bf16-rounded weights) differ there by
 # up to max_rel 1.06e-2 and mae_rel 6.8e-3 on the small test decoder's prefill and

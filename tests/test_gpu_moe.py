@@ -75,11 +75,13 @@ def test_qwen3_block(ops, path, T):
 
 @pytest.mark.parametrize("path", ["gemv", "tcgen05"])
 def test_mixtral_block(ops, path):
+    from tests._parity import MIXTRAL_TC
     L = layer("mixtral_prefill")
     h = with_path(ops, path)
     try:
         x = S.make_x(L.shape, 300, tokens=48)
-        L.check(x, f"mixtral {path}")
+        # the named exception to max_rel 1e-2 (one or two bf16 ulps at the largest output)
+        L.check(x, f"mixtral {path}", tight=MIXTRAL_TC if path == "tcgen05" else None)
     finally:
         h.set_path(0)
 
