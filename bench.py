@@ -44,6 +44,7 @@ from flashmlx_b200 import synthetic as S  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 DEFAULT_CONFIG = "qwen15_prefill"
+ROUTE_MODES = {"auto": 0, "grid": 1, "last-block": 2, "cluster": 3}  # FM_ROUTE_* (include/flashmoe.h)
 CPU_SAMPLE_TOKENS = 1024
 
 
@@ -61,7 +62,7 @@ def parse():
     ap.add_argument("--replicas", action="store_true", help="N > 1: independent replicas instead of expert parallelism")
     ap.add_argument("--ep-impl", default="peer", choices=["peer", "nccl"],
                     help="N > 1: rows over peer memory by the kernels, or NCCL all-to-all between staged calls")
-    ap.add_argument("--route-mode", default="grid", choices=["grid", "last-block"],
+    ap.add_argument("--route-mode", default="auto", choices=["auto", "grid", "last-block", "cluster"],
                     help="routing kernel form of the MoE layers (fm_set_route_mode)")
     a = ap.parse_args()
     a.warmup = max(3, a.warmup)
@@ -423,7 +424,7 @@ def run_ours(args, rank, world, local_rank):
         raise SystemExit("variant workloads run on one GPU or as --replicas")
     x_np = S.make_x(shape, args.seed + rank)  # each rank routes its own batch
     h = ops.default_handle(local_rank)
-    route_mode = {"grid": _lib.FM_ROUTE_GRID, "last-block": _lib.FM_ROUTE_LAST_BLOCK}[args.route_mode]
+    route_mode = ROUTE_MODES[args.route_mode]
     h.set_route_mode(route_mode)
     x = ops.bf16_from_numpy(x_np, dev)
     y = torch.empty_like(x)
@@ -684,7 +685,7 @@ def run_decoder(args, rank, world, local_rank):
     dec = DEC.Decoder.from_weights(shape, weights, dev, B, PROMPT_LEN + DECODE_STEPS)
     h = dec.handle()
     from flashmlx_b200 import _lib as L
-    h.set_route_mode({"grid": L.FM_ROUTE_GRID, "last-block": L.FM_ROUTE_LAST_BLOCK}[args.route_mode])
+    h.set_route_mode(ROUTE_MODES[args.route_mode])
     rng = np.random.default_rng(args.seed + 1000 + rank)
     prompt_np = rng.integers(0, shape.vocab, (B, PROMPT_LEN)).astype(np.int32)
     prompt = torch.from_numpy(prompt_np).to(dev)

@@ -13,7 +13,7 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "libf
 
 FM_OK, FM_EINVAL, FM_EUNSUPPORTED, FM_ECUDA, FM_ENCCL, FM_ETIMEOUT, FM_EDEVICE, FM_ENOMEM, FM_ETOOLARGE = range(9)
 FM_PATH_AUTO, FM_PATH_GEMV, FM_PATH_TCGEN05 = 0, 1, 2
-FM_ROUTE_AUTO, FM_ROUTE_GRID, FM_ROUTE_LAST_BLOCK = 0, 1, 2
+FM_ROUTE_AUTO, FM_ROUTE_GRID, FM_ROUTE_LAST_BLOCK, FM_ROUTE_CLUSTER = 0, 1, 2, 3
 
 # every function include/flashmoe.h declares: name -> (restype, argtypes)
 _p, _i, _i64, _sz, _s = C.c_void_p, C.c_int, C.c_int64, C.c_size_t, C.c_char_p

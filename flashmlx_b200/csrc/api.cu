@@ -26,6 +26,8 @@ __global__ void route_kernel(const RouteArgs a);
 __global__ void route_kernel_sigmoid(const RouteArgs a);
 __global__ void route_last_kernel(const RouteArgs a);
 __global__ void route_last_kernel_sigmoid(const RouteArgs a);
+__global__ void route_cluster_kernel(const RouteArgs a);
+__global__ void route_cluster_kernel_sigmoid(const RouteArgs a);
 __global__ void dense_prep_kernel(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
@@ -270,6 +272,18 @@ int launch_route(fm_handle* h, RouteArgs& ra, int64_t items, bool sigmoid = fals
   const int max_blocks = (sigmoid ? h->route_sig_blocks_per_sm : h->route_blocks_per_sm) * h->num_sms;
   const int64_t nchunks = (ra.T + fm::kRouteChunk - 1) / fm::kRouteChunk;
   ra.arrive = arrive_count(h);
+  const bool cluster = h->route_mode == FM_ROUTE_CLUSTER || h->route_mode == FM_ROUTE_AUTO;
+  if (cluster && nchunks <= fm::kRouteLastMaxChunks) {
+    // one cluster of kRouteClusterCtas CTAs (hardware cluster barriers, no co-residency
+    // requirement beyond the cluster itself)
+    prof_begin(h, ra.do_router ? "route" : "route_given");
+    if (sigmoid) fm::route_cluster_kernel_sigmoid<<<fm::kRouteClusterCtas, fm::kRouteThreads, 0, h->stream>>>(ra);
+    else fm::route_cluster_kernel<<<fm::kRouteClusterCtas, fm::kRouteThreads, 0, h->stream>>>(ra);
+    prof_end(h);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_err(h, e, "route_cluster_kernel launch");
+    return FM_OK;
+  }
   if (h->route_mode == FM_ROUTE_LAST_BLOCK && nchunks <= fm::kRouteLastMaxChunks) {
     // one warp per phase-1 item, and enough blocks that zeroing the fp32 accumulators
     // takes at most 8 float4 stores per thread; no co-residency needed (nothing waits on
@@ -357,7 +371,7 @@ int router_ksplit(const fm_handle* h, int64_t T, int H) {
   const int64_t ntt = (T + 15) / 16;
   const int64_t target = static_cast<int64_t>(h->num_sms) * 16;
   int ks = static_cast<int>(std::min<int64_t>(fm::kRouterMaxKsplit, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
-  ks = std::min(ks, std::max(1, H / 128));
+  ks = std::min(ks, std::max(1, H / 64));  // at least two 32-wide k-blocks per item
   return ks;
 }
 
@@ -795,7 +809,7 @@ int fm_last_path(const fm_handle* h) { return h ? h->last_path : 0; }
 
 int fm_set_route_mode(fm_handle* h, int mode) {
   if (!h) return FM_EINVAL;
-  if (mode != FM_ROUTE_AUTO && mode != FM_ROUTE_GRID && mode != FM_ROUTE_LAST_BLOCK)
+  if (mode != FM_ROUTE_AUTO && mode != FM_ROUTE_GRID && mode != FM_ROUTE_LAST_BLOCK && mode != FM_ROUTE_CLUSTER)
     return set_err(h, FM_EINVAL, "unknown route mode");
   h->route_mode = mode;
   return FM_OK;

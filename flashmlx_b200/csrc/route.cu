@@ -195,10 +195,12 @@ FM_DEV float sum_partials(const RouteArgs& a, int64_t t, int e) {
   return s;
 }
 
-__device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl) {
+// PER = logits per lane (E < 32 PER: the experts and the shared gate); sm = NULL: the caller builds the chunk's
+// bitmasks from topk_ids later (the cluster routing kernel routes tokens on every CTA)
+template <int PER>
+__device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
   const int lane = threadIdx.x & 31;
   const int E = a.E, k = a.k;
-  constexpr int PER = kMaxExperts / 32;
   float p[PER];
   // bf16 logits: fixed-order sum of the K-split partials, then the optional bias
   float mx = -INFINITY;
@@ -267,12 +269,14 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl
   if (lane < k) {
     const float sc = a.norm_topk ? rbf(sp / denom) : sp;
     a.topk_ids[t * k + lane] = se;
-    sm.ids[tl * k + lane] = se;
     a.topk_score[t * k + lane] = sc;
     if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
     if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
     if (a.out_scores_f32) a.out_scores_f32[t * k + lane] = sc;
-    atomicOr(&sm.mask[se], 1u << tl);
+    if (sm) {
+      sm->ids[tl * k + lane] = se;
+      atomicOr(&sm->mask[se], 1u << tl);
+    }
   }
 }
 
@@ -290,10 +294,10 @@ FM_DEV uint32_t ordered_key(float f) {
 // sel = 0; top-k of sel (equal: lower expert id) in k rounds of a 64-bit warp max; the
 // scores are the picks' orig, divided by (their sum in pick order + 1e-20) when
 // norm_topk and k > 1, times routed_scale, all fp32.
-__device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem& sm, int tl) {
+template <int PER>
+__device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
   const int lane = threadIdx.x & 31;
   const int E = a.E, k = a.k;
-  constexpr int PER = kMaxExperts / 32;
   float orig[PER];
   unsigned long long key[PER];
 #pragma unroll
@@ -392,16 +396,18 @@ __device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem& sm
   if (lane < k) {
     const float sc = (renorm ? sp / denom : sp) * a.routed_scale;
     a.topk_ids[t * k + lane] = se;
-    sm.ids[tl * k + lane] = se;
     a.topk_score[t * k + lane] = sc;
     if (a.out_topk_ids) a.out_topk_ids[t * k + lane] = se;
     if (a.out_topk_scores) a.out_topk_scores[t * k + lane] = f2bf(sc);
     if (a.out_scores_f32) a.out_scores_f32[t * k + lane] = sc;
-    atomicOr(&sm.mask[se], 1u << tl);
+    if (sm) {
+      sm->ids[tl * k + lane] = se;
+      atomicOr(&sm->mask[se], 1u << tl);
+    }
   }
 }
 
-__device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) {
+__device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem* sm, int tl) {
   if ((threadIdx.x & 31) != 0) return;
   const int64_t b = r / a.M, m = r % a.M;
   uint32_t e = a.given_ids ? a.given_ids[b] : 0u;
@@ -409,14 +415,47 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem& sm, int tl) 
   if (e >= static_cast<uint32_t>(a.E) || xb < 0 || xb >= a.x_batches) {
     report(a.err, DEVERR_BOUNDS);
     a.topk_ids[r] = -1;
-    sm.ids[tl] = -1;
+    if (sm) sm->ids[tl] = -1;
     return;
   }
   a.topk_ids[r] = static_cast<int32_t>(e);
-  sm.ids[tl] = static_cast<int>(e);
   a.topk_score[r] = 1.f;
   a.row_src[r] = static_cast<int32_t>(xb * a.M + m);
-  atomicOr(&sm.mask[e], 1u << tl);
+  if (sm) {
+    sm->ids[tl] = static_cast<int>(e);
+    atomicOr(&sm->mask[e], 1u << tl);
+  }
+}
+
+// one token (or given row) t, routed by the calling warp
+template <bool SIGMOID>
+__device__ void route_one(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
+  // lanes cover logits 0..E: the E routed experts and the shared-expert gate at E
+  if (!a.do_router) {
+    given_row(a, t, sm, tl);
+  } else if (a.E < 64) {
+    if (SIGMOID) route_token_sigmoid<2>(a, t, sm, tl); else route_token<2>(a, t, sm, tl);
+  } else if (a.E < 128) {
+    if (SIGMOID) route_token_sigmoid<4>(a, t, sm, tl); else route_token<4>(a, t, sm, tl);
+  } else if (a.E < 256) {
+    if (SIGMOID) route_token_sigmoid<8>(a, t, sm, tl); else route_token<8>(a, t, sm, tl);
+  } else {  // up to kMaxExperts = 512 experts and the gate
+    if (SIGMOID) route_token_sigmoid<17>(a, t, sm, tl); else route_token<17>(a, t, sm, tl);
+  }
+}
+
+// the chunk's counts and stable in-chunk ranks from its bitmasks (sm.mask, sm.ids)
+__device__ void count_chunk(const RouteArgs& a, RouteSmem& sm, int ch, int k) {
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x)
+    a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] = __popc(sm.mask[e]);
+  const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
+  const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
+  for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
+    const int tl = i / k;
+    const int e = sm.ids[i];
+    if (e < 0) continue;
+    a.pair_rank[(t0 + tl) * k + (i % k)] = __popc(sm.mask[e] & ((1u << tl) - 1u));
+  }
 }
 
 // bid / nb: this block's place among the blocks that share the phase (the whole grid in
@@ -433,21 +472,10 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm, int bid, int
       const int tl = warp * (kRouteChunk / 8) + i;
       const int64_t t = static_cast<int64_t>(ch) * kRouteChunk + tl;
       if (t >= a.T) break;
-      if (!a.do_router) given_row(a, t, sm, tl);
-      else if (SIGMOID) route_token_sigmoid(a, t, sm, tl);
-      else route_token(a, t, sm, tl);
+      route_one<SIGMOID>(a, t, &sm, tl);
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < a.E; e += blockDim.x)
-      a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] = __popc(sm.mask[e]);
-    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
-    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
-    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
-      const int tl = i / k;
-      const int e = sm.ids[i];
-      if (e < 0) continue;
-      a.pair_rank[(t0 + tl) * k + (i % k)] = __popc(sm.mask[e] & ((1u << tl) - 1u));
-    }
+    count_chunk(a, sm, ch, k);
     __syncthreads();
   }
 }
@@ -615,9 +643,10 @@ FM_DEV unsigned long long global_ns() {
   return t;
 }
 
-// block 0, thread 0 accumulates the wall time of each phase (as seen by block 0)
-FM_DEV void phase_mark(const RouteArgs& a, int phase, unsigned long long& t) {
-  if (blockIdx.x == 0 && threadIdx.x == 0 && a.phase_ns) {
+// thread 0 of the block that reports (block 0; the last block in the last-block form)
+// accumulates the wall time of each phase as that block saw it
+FM_DEV void phase_mark(const RouteArgs& a, int phase, unsigned long long& t, bool reporter) {
+  if (reporter && threadIdx.x == 0 && a.phase_ns) {
     const unsigned long long now = global_ns();
     atomicAdd(a.phase_ns + phase, now - t);
     t = now;
@@ -735,18 +764,18 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
-  phase_mark(a, 0, t);
+  phase_mark(a, 0, t, blockIdx.x == 0);
   // phase 2
   phase_topk_count<SIGMOID>(a, sm, blockIdx.x, nb);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
-  phase_mark(a, 1, t);
+  phase_mark(a, 1, t, blockIdx.x == 0);
   // phase 3
   phase_column_scan(a, sm);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
-  phase_mark(a, 2, t);
+  phase_mark(a, 2, t, blockIdx.x == 0);
   // phase 4
   phase_scatter(a, sm, blockIdx.x, nb);
-  phase_mark(a, 3, t);
+  phase_mark(a, 3, t, blockIdx.x == 0);
 }
 
 // Small batches (at most kRouteLastMaxChunks chunks): phase 1 over the whole grid, then
@@ -756,6 +785,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
 // reads them, and atomicInc wraps the counter back to 0 on that arrival.
 template <bool SIGMOID>
 __device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& sm) {
+  unsigned long long t = threadIdx.x == 0 ? global_ns() : 0ull;
   if (a.do_router) phase_router(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
@@ -769,10 +799,78 @@ __device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& s
   }
   __syncthreads();
   if (!sm.flag) return;
+  phase_mark(a, 0, t, true);  // phase 1 as the last block to finish it saw it
   phase_topk_count<SIGMOID>(a, sm, 0, 1);
+  phase_mark(a, 1, t, true);
   phase_column_scan_one_block(a);
   __syncthreads();
+  phase_mark(a, 2, t, true);
   phase_scatter(a, sm, 0, 1);
+  phase_mark(a, 3, t, true);
+}
+
+// Cluster form for small batches (at most kRouteLastMaxChunks chunks): one cluster of
+// kRouteClusterCtas CTAs.  Phase 1 over the cluster; a cluster barrier; every warp of
+// the cluster routes its share of the tokens (softmax / sigmoid, top-k, scores) into
+// global memory; a second cluster barrier; then CTA 0 alone builds each chunk's
+// bitmasks from the ids and runs the count, scan and scatter phases with block
+// barriers.  The cluster barriers are hardware barriers (no counter in memory, no spin),
+// and the chunk counts, ranks and scatter are the same functions as in the grid form, so
+// the ids, scores and permutation are identical.
+FM_DEV void cluster_barrier() {
+  __threadfence();  // this thread's global stores are visible device-wide before it arrives
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+template <bool SIGMOID>
+__device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem& sm) {
+  unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
+  const bool rep0 = blockIdx.x == 0;
+  if (a.do_router) phase_router(a);
+  else phase_permute_x(a);
+  phase_zero(a.zero0, a.zero0_n);
+  phase_zero(a.zero1, a.zero1_n);
+  cluster_barrier();
+  phase_mark(a, 0, t, rep0);
+  const int nw = gridDim.x * (kRouteThreads / 32);
+  const int gw = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
+  for (int64_t tk = gw; tk < a.T; tk += nw) route_one<SIGMOID>(a, tk, nullptr, 0);
+  cluster_barrier();
+  phase_mark(a, 1, t, rep0);
+  if (blockIdx.x != 0) return;  // no other CTA touches this CTA's shared memory
+  const int k = a.do_router ? a.k : 1;
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  for (int ch = 0; ch < nchunks; ++ch) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e] = 0u;
+    __syncthreads();
+    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
+    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
+    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
+      const int e = a.topk_ids[t0 * k + i];
+      sm.ids[i] = e;
+      if (e >= 0) atomicOr(&sm.mask[e], 1u << (i / k));
+    }
+    __syncthreads();
+    count_chunk(a, sm, ch, k);
+    __syncthreads();
+  }
+  phase_column_scan_one_block(a);
+  __syncthreads();
+  phase_mark(a, 2, t, rep0);
+  phase_scatter(a, sm, 0, 1);
+  phase_mark(a, 3, t, rep0);
+}
+
+__global__ void __cluster_dims__(kRouteClusterCtas, 1, 1) __launch_bounds__(kRouteThreads)
+    route_cluster_kernel(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_cluster_body<false>(a, sm);
+}
+__global__ void __cluster_dims__(kRouteClusterCtas, 1, 1) __launch_bounds__(kRouteThreads)
+    route_cluster_kernel_sigmoid(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_cluster_body<true>(a, sm);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_last_kernel(const RouteArgs a) {

@@ -176,9 +176,11 @@ FM_API int fm_last_path(const fm_handle* h);
  * whose four phases are separated by grid barriers.  FM_ROUTE_LAST_BLOCK: for batches
  * of at most 128 tokens (rows, for fm_gather_qmm), the router GEMV over the whole grid
  * and top-k, sort and planning in the one block that finishes it last, with no grid
- * barrier; larger batches take the grid form.  FM_ROUTE_AUTO is FM_ROUTE_GRID.  Both
- * forms give identical results. */
-enum { FM_ROUTE_AUTO = 0, FM_ROUTE_GRID = 1, FM_ROUTE_LAST_BLOCK = 2 };
+ * barrier.  FM_ROUTE_CLUSTER: for batches of at most 128 tokens, one cluster of 8 CTAs
+ * (router GEMV and top-k over the cluster, sort and planning in its first CTA, hardware
+ * cluster barriers between them).  Larger batches take the grid form in every mode.
+ * FM_ROUTE_AUTO (the default) is FM_ROUTE_CLUSTER.  All forms give identical results. */
+enum { FM_ROUTE_AUTO = 0, FM_ROUTE_GRID = 1, FM_ROUTE_LAST_BLOCK = 2, FM_ROUTE_CLUSTER = 3 };
 FM_API int fm_set_route_mode(fm_handle* h, int mode);
 
 /* Kernel timing ------------------------------------------------------------------

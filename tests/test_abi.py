@@ -47,7 +47,7 @@ def test_enum_constants_match_the_header():
     txt = open(HEADER).read()
     consts = dict((k, int(v)) for k, v in re.findall(r"\b(FM_[A-Z0-9_]+)\s*=\s*(\d+)", txt))
     for name in ("FM_PATH_AUTO", "FM_PATH_GEMV", "FM_PATH_TCGEN05", "FM_ROUTE_AUTO", "FM_ROUTE_GRID",
-                 "FM_ROUTE_LAST_BLOCK", "FM_OK", "FM_EINVAL"):
+                 "FM_ROUTE_LAST_BLOCK", "FM_ROUTE_CLUSTER", "FM_OK", "FM_EINVAL"):
         assert consts[name] == getattr(_lib, name), name
 
 
