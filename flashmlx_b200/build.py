@@ -19,7 +19,7 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB_DIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIB_DIR, "libflashmoe.so")
-SOURCES = ["route.cu", "qgemv.cu", "qgemm_tc.cu", "ep.cu", "decoder.cu", "api.cu"]
+SOURCES = ["route.cu", "qgemv.cu", "qgemv_tma.cu", "qgemm_tc.cu", "ep.cu", "decoder.cu", "api.cu"]
 HEADERS = ["fm_common.cuh", "fm_internal.cuh", "fm_ep.cuh"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -59,6 +59,10 @@ cudaError_t launch_swiglu(const uint16_t* gate, const uint16_t* up, int64_t n, u
                           cudaStream_t st);
 cudaError_t launch_argmax(const uint16_t* logits, int64_t T, int64_t V, int32_t* ids, cudaStream_t st);
 cudaError_t qgemv_blocks_per_sm(int* n);
+bool qgemv_tma_supports(int mode, int K, int K_shared, int gs);
+cudaError_t launch_qgemv_tma(int mode, int grid, cudaStream_t stream, const GemmArgs& a, const TcMaps& maps);
+cudaError_t qgemv_tma_blocks_per_sm(int* n);
+int qgemv_tma_max_rows();
 namespace tc {
 int max_rows();
 cudaError_t init();
@@ -75,6 +79,7 @@ struct fm_handle {
   int route_blocks_per_sm = 0;
   int route_sig_blocks_per_sm = 0;  // route_kernel_sigmoid
   int gemv_blocks_per_sm = 0;
+  int gemv_tma_blocks_per_sm = 0;  // TMA-fed GEMV (qgemv_tma.cu); 0: not available
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
   int path = FM_PATH_AUTO;
   int last_path = 0;  // expert-product path the last call took (fm_last_path)
@@ -353,15 +358,20 @@ bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols) {
   return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, 32);
 }
 
+// tma_gemv: the GEMV path's TMA-fed kernel (qgemv_tma.cu), whose tile table was planned
+// with up to qgemv_tma_max_rows() activation rows per unit; otherwise qgemv.cu (8 rows)
 template <int MODE>
-int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps* maps = nullptr) {
+int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps* maps = nullptr,
+                bool tma_gemv = false) {
   static const char* names[2][5] = {{"qgemv_gateup", "qgemv_down", "qgemv_plain", "qgemv_relu2", "qgemv_down"},
                                     {"qgemm_tc_gateup", "qgemm_tc_down", "qgemm_tc_plain", "qgemm_tc_relu2", ""}};
-  if (tcgen05 && !maps) return set_err(h, FM_EINVAL, "tcgen05 launch without tensor maps");
+  if ((tcgen05 || tma_gemv) && !maps) return set_err(h, FM_EINVAL, "TMA launch without tensor maps");
   if (tcgen05 && MODE == fm::MODE_DOWN_F32) return set_err(h, FM_EUNSUPPORTED, "fp32-score down runs on the GEMV path");
   prof_begin(h, names[tcgen05 ? 1 : 0][MODE]);
-  const cudaError_t e = tcgen05 ? fm::tc::launch(MODE, h->tc_pairs, h->stream, ga, *maps)
-                                : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
+  const cudaError_t e =
+      tcgen05    ? fm::tc::launch(MODE, h->tc_pairs, h->stream, ga, *maps)
+      : tma_gemv ? fm::launch_qgemv_tma(MODE, h->num_sms * h->gemv_tma_blocks_per_sm, h->stream, ga, *maps)
+                 : fm::launch_qgemv(MODE, h->num_sms * std::max(1, h->gemv_blocks_per_sm), h->stream, ga);
   prof_end(h);
   if (e != cudaSuccess) return cuda_err(h, e, tcgen05 ? "qgemm_tc launch" : "qgemv launch");
   return FM_OK;
@@ -756,6 +766,7 @@ int fm_create(fm_handle** out, int device, void* stream) {
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_sig_blocks_per_sm, fm::route_kernel_sigmoid,
                                                       fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&h->gemv_blocks_per_sm);
+  if (e == cudaSuccess) e = fm::qgemv_tma_blocks_per_sm(&h->gemv_tma_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
   if (e == cudaSuccess) e = fm::tc::max_pairs(&h->tc_pairs);
   if (e == cudaSuccess && h->tc_pairs < 1) e = cudaErrorInvalidConfiguration;
@@ -909,6 +920,10 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   const int64_t P = T * k;
   const bool tcp = use_tc(h, P, E, c->group_size);
   h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
+  // the GEMV path's TMA-fed kernel takes every fm_moe_block shape (K multiples of 128)
+  const bool tvp = !tcp && h->gemv_tma_blocks_per_sm > 0 &&
+                   fm::qgemv_tma_supports(fm::MODE_GATEUP, H, H, c->group_size) &&
+                   fm::qgemv_tma_supports(fm::MODE_DOWN, I, shared ? c->shared_inter : I, c->group_size);
   Plan p = make_plan(T, T, H, E, k, epad, ksplit, I, c->shared_inter, shared, true, tcp);
   rc = ensure_ws(h, p.total);
   if (rc) return rc;
@@ -955,7 +970,8 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ra.a_n_shared = c->shared_inter;
   ra.b_n = H;
   ra.b_rows_per_block = tcp ? 256 : 128;
-  ra.chunk_max = tcp ? fm::tc::max_rows() : 8;  // GEMV: one 8-row MMA column tile
+  // GEMV: one 8-row MMA column tile per unit (qgemv.cu), or four (qgemv_tma.cu)
+  ra.chunk_max = tcp ? fm::tc::max_rows() : (tvp ? fm::qgemv_tma_max_rows() : 8);
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = tcp ? 1 : std::max(1, c->shared_inter / std::max(1, I));
   ra.has_shared = shared ? 1 : 0;
@@ -1000,7 +1016,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   ga.out_shared_ld = c->shared_inter;
   ga.tab = ra.tab_a;
   fm::TcMaps maps_gu, maps_dn;
-  if (tcp) {
+  if (tcp || tvp) {
     const int Is = c->shared_inter;
     bool ok = encode_codes(&maps_gu.code[0], w->gate.w, static_cast<int64_t>(E) * I, H, 64) &&
               encode_codes(&maps_gu.code[1], w->up.w, static_cast<int64_t>(E) * I, H, 64) &&
@@ -1016,7 +1032,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
               encode_act(&maps_dn.act[1], shared ? at<uint16_t>(h, p.a_shared) : nullptr, T, Is);
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
-  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu);
+  rc = launch_gemm<fm::MODE_GATEUP>(h, ga, tcp, &maps_gu, tvp);
   if (rc) return rc;
   // down (+ combine)
   GemmArgs gd = ga;
@@ -1042,7 +1058,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   gd.ysh16 = (shared && tcp) ? at<uint16_t>(h, p.ysh16) : nullptr;
   gd.y_ld = H;
   gd.tab = ra.tab_b;
-  rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn);
+  rc = launch_gemm<fm::MODE_DOWN>(h, gd, tcp, &maps_dn, tvp);
   if (rc) return rc;
   // finalize: combine rounding + gated shared expert
   prof_begin(h, "finalize");
@@ -1323,6 +1339,7 @@ int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, i
   bool tcp = use_tc(h, rows, E, group_size);
   if (K % 128) tcp = true;  // the GEMV path works in 128-wide K chunks
   h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
+  const bool tvp = !tcp && h->gemv_tma_blocks_per_sm > 0 && fm::qgemv_tma_supports(fm::MODE_PLAIN, K, K, group_size);
   Plan p = make_plan(rows, x_batches * M, K, E, 1, 8, 1, 0, 0, false, false, tcp);
   int rc = ensure_ws(h, p.total);
   if (rc) return rc;
@@ -1360,7 +1377,7 @@ int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, i
   ra.a_rows_per_block = tcp ? 256 : 128;
   ra.a_n = N;
   ra.a_n_shared = 0;
-  ra.chunk_max = tcp ? fm::tc::max_rows() : 8;  // GEMV: one 8-row MMA column tile
+  ra.chunk_max = tcp ? fm::tc::max_rows() : (tvp ? fm::qgemv_tma_max_rows() : 8);
   ra.chunk_align = tcp ? 16 : 8;
   ra.b_ksplit_shared = 1;
   ra.gsync = grid_sync(h);
@@ -1398,7 +1415,7 @@ int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, i
   ga.tab = ra.tab_a;
   ga.err = err_word(h);
   fm::TcMaps maps;
-  if (tcp) {
+  if (tcp || tvp) {
     const bool ok = encode_codes(&maps.code[0], w, static_cast<int64_t>(E) * N, K, 128) &&
                     encode_codes(&maps.code[1], nullptr, 0, K, 128) && encode_codes(&maps.code[2], nullptr, 0, K, 128) &&
                     encode_codes(&maps.code[3], nullptr, 0, K, 128) &&
@@ -1406,7 +1423,7 @@ int gather_qmm_impl(fm_handle* h, const uint16_t* x, int64_t x_batches, int M, i
                     encode_act(&maps.act[1], nullptr, 0, K);
     if (!ok) return set_err(h, FM_ECUDA, "cuTensorMapEncodeTiled failed (alignment or driver entry point)");
   }
-  return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps);
+  return launch_gemm<fm::MODE_PLAIN>(h, ga, tcp, &maps, tvp);
 }
 
 }  // namespace
@@ -1931,6 +1948,7 @@ struct NoAllocDevice {
   int num_sms = 0;
   int route_blocks_per_sm = 0;
   int gemv_blocks_per_sm = 0;
+  int gemv_tma_blocks_per_sm = 0;  // TMA-fed GEMV (qgemv_tma.cu); 0: not available
   int tc_pairs = 0;
 };
 constexpr int kNoAllocMaxDevices = 64;
@@ -1951,6 +1969,7 @@ int noalloc_setup(int device, NoAllocDevice& d) {
   if (e == cudaSuccess)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&d.gemv_blocks_per_sm);
+  if (e == cudaSuccess) e = fm::qgemv_tma_blocks_per_sm(&d.gemv_tma_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
   if (e == cudaSuccess) e = fm::tc::max_pairs(&d.tc_pairs);
   if (e == cudaSuccess && d.tc_pairs < 1) e = cudaErrorInvalidConfiguration;
@@ -2005,6 +2024,7 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
     h.num_sms = d.num_sms;
     h.route_blocks_per_sm = d.route_blocks_per_sm;
     h.gemv_blocks_per_sm = d.gemv_blocks_per_sm;
+    h.gemv_tma_blocks_per_sm = d.gemv_tma_blocks_per_sm;
     h.tc_pairs = d.tc_pairs;
     h.ws = d.scratch;
     h.ws_bytes = kNoAllocScratchBytes;
