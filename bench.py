@@ -259,7 +259,7 @@ def run_reference(args, rank, world):
         "note": "reference path needs MLX + Apple Metal (not installable here); CPU restatement "
                 "of its MLX semantics (oracle/oracle.cpp) timed instead",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ----------------------------------------------------------------------------- GPU
@@ -639,7 +639,7 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clk,
             "secondary": secondary,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if peer_block is not None:
         peer_block.close()
     if world > 1:
@@ -764,7 +764,7 @@ def run_decoder(args, rank, world, local_rank):
             "cpu_baseline": cpu,
             "clocks": clk,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     dec.close()
     if world > 1:
         dist.barrier()
@@ -823,10 +823,34 @@ def run_decoder_reference(args, rank):
         "note": "reference path needs MLX + Apple Metal (not installable here); CPU restatement of its "
                 "MLX semantics (oracle/decoder.py) timed instead",
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_RESULT_FD = None  # the process's original standard output, kept for the one result line
+
+
+def emit(line: dict) -> None:
+    """Writes the bench's JSON line to the original standard output."""
+    data = (json.dumps(line) + "\n").encode()
+    if _RESULT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_RESULT_FD, data)
+
+
+def quiet_stdout() -> None:
+    """Routes everything else written to standard output (library banners such as
+    NCCL's version line, printed at communicator set-up) to standard error, so that
+    standard output carries only the result line."""
+    global _RESULT_FD
+    sys.stdout.flush()
+    _RESULT_FD = os.dup(1)
+    os.dup2(2, 1)
 
 
 def main():
+    quiet_stdout()
     args = parse()
     rank, world, local_rank = rank_info()
     if args.config in S.DECODER_CONFIGS:
