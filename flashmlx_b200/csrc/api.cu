@@ -377,11 +377,15 @@ int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps
   return FM_OK;
 }
 
-int router_ksplit(const fm_handle* h, int64_t T, int H) {
+// K slices of the router's partial logits: enough items to fill the GPU, at least two
+// 32-wide k-blocks per item, and at most ~1024 partials per token to sum (the top-k
+// phase reads ksplit partials of every logit)
+int router_ksplit(const fm_handle* h, int64_t T, int H, int E) {
   const int64_t ntt = (T + 15) / 16;
   const int64_t target = static_cast<int64_t>(h->num_sms) * 16;
   int ks = static_cast<int>(std::min<int64_t>(fm::kRouterMaxKsplit, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
-  ks = std::min(ks, std::max(1, H / 64));  // at least two 32-wide k-blocks per item
+  ks = std::min(ks, std::max(1, H / 64));
+  ks = std::min(ks, std::max(2, 1024 / (E + 1)));
   return ks;
 }
 
@@ -916,7 +920,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   const int H = c->hidden, I = c->inter, E = c->num_experts, k = c->top_k;
   const bool shared = c->shared_inter > 0;
   const int epad = (E + 1 + 7) / 8 * 8;
-  const int ksplit = router_ksplit(h, T, H);
+  const int ksplit = router_ksplit(h, T, H, E);
   const int64_t P = T * k;
   const bool tcp = use_tc(h, P, E, c->group_size);
   h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
@@ -1137,7 +1141,7 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
   if (T > (1LL << 24)) return set_err(h, FM_EUNSUPPORTED, "T too large");
   const bool shared = Is > 0;
   const int epad = (E + 1 + 7) / 8 * 8;
-  const int ksplit = router_ksplit(h, T, H);
+  const int ksplit = router_ksplit(h, T, H, E);
   // The tcgen05 expert path (relu^2 epilogue, bf16(d) per pair, combine with the scores
   // in fp32 for sigmoid routing) runs when the handle's path is FM_PATH_TCGEN05; the
   // automatic choice keeps the GEMV path for the variants.
@@ -1475,7 +1479,7 @@ int fm_ep_dispatch(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w
   if (rc) return rc;
   const int H = c->hidden, E = c->num_experts, k = c->top_k;
   const int epad = (E + 1 + 7) / 8 * 8;
-  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
+  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H, E);
   const int64_t P = T * k;
   const EpPlan1 p = make_ep_plan1(T, H, E, k, epad, ksplit);
   rc = ensure_ws(h, p.total);
@@ -1535,7 +1539,7 @@ int fm_ep_experts(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w,
   rc = ensure_ep_ws(h, p2.total);
   if (rc) return rc;
   const EpPlan1 p1 = make_ep_plan1(std::max<int64_t>(T, 0), H, E, k, (E + 1 + 7) / 8 * 8,
-                                   router_ksplit(h, std::max<int64_t>(T, 1), H));
+                                   router_ksplit(h, std::max<int64_t>(T, 1), H, E));
   h->ep_ysh_bf16 = tcp;
   h->ep_shared = shared;
   h->ep_R = R;
@@ -1568,7 +1572,7 @@ int fm_ep_combine(fm_handle* h, const fm_moe_config* c, const uint16_t* ret_rows
   if (!y || !ret_rows) return set_err(h, FM_EINVAL, "null rows");
   if (!aligned16(ret_rows) || !aligned16(y)) return set_err(h, FM_EINVAL, "rows must be 16-byte aligned");
   const int H = c->hidden, E = c->num_experts, k = c->top_k;
-  const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, router_ksplit(h, std::max<int64_t>(T, 1), H));
+  const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, router_ksplit(h, std::max<int64_t>(T, 1), H, E));
   const int Is = c->shared_inter, I = c->inter;
   int first = 0, E_local = 0;
   ep_range(E, h->ep_rank, h->ep_world, &first, &E_local);
@@ -1701,7 +1705,7 @@ int fm_ep_p2p_forward(fm_handle* h, const fm_moe_config* c, const fm_moe_weights
   // the receive count is not known on the host: decide the path on this rank's own pairs
   const bool tcp = use_tc(h, T * k + (shared ? T : 0), E_local + (shared ? 1 : 0), c->group_size);
   h->last_path = tcp ? FM_PATH_TCGEN05 : FM_PATH_GEMV;
-  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H);
+  const int ksplit = router_ksplit(h, std::max<int64_t>(T, 1), H, E);
   const EpPlan1 p1 = make_ep_plan1(T, H, E, k, (E + 1 + 7) / 8 * 8, ksplit);
   rc = ensure_ws(h, p1.total);
   if (rc) return rc;
@@ -2030,7 +2034,7 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
     h.ws_bytes = kNoAllocScratchBytes;
     h.borrowed_ws = true;
     const int epad = (c->num_experts + 1 + 7) / 8 * 8;
-    const size_t need = make_plan(T, T, c->hidden, c->num_experts, c->top_k, epad, router_ksplit(&h, T, c->hidden),
+    const size_t need = make_plan(T, T, c->hidden, c->num_experts, c->top_k, epad, router_ksplit(&h, T, c->hidden, c->num_experts),
                                   c->inter, c->shared_inter, c->shared_inter > 0, true,
                                   use_tc(&h, T * c->top_k, c->num_experts, c->group_size))
                             .total;

@@ -270,7 +270,7 @@ struct AttnArgs {
 constexpr int kRouteThreads = 256;  // 8 warps
 constexpr int kRouteChunk = 16;     // tokens per counting chunk (one bitmask word)
 constexpr int kRouterMaxKsplit = 32;  // K slices of the router partial logits
-constexpr int kRouteLastMaxChunks = 8;  // batches the last-block routing kernel takes (<= 128 tokens)
+constexpr int kRouteLastMaxChunks = 8;  // batches the small-batch routing forms take (<= 128 tokens)
 constexpr int kRouteClusterCtas = 8;    // CTAs of the cluster routing kernel (one portable cluster)
 
 }  // namespace fm

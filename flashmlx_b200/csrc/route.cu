@@ -105,8 +105,8 @@ __device__ void phase_router(const RouteArgs& a) {
   const int ntt = static_cast<int>((T + 15) / 16);
   const int kblocks = H / 32;
   const int items = ntt * a.ksplit;
-  const int ngroups = (a.epad + 63) / 64;
-  const int Etot = a.E + (a.shared_gate_w ? 1 : 0);
+  const int Etot = a.E + (a.shared_gate_w ? 1 : 0);  // logits: the experts and the shared gate
+  const int ngroups = (Etot + 63) / 64;               // 64-logit groups (columns past Etot are never read)
   for (int item = gw; item < items; item += nw) {
     const int tt = item / a.ksplit, ks = item % a.ksplit;
     const int64_t t0 = static_cast<int64_t>(tt) * 16;
@@ -124,21 +124,37 @@ __device__ void phase_router(const RouteArgs& a) {
         const int e = eg * 64 + 8 * j + g;
         wr[j] = (e < a.E) ? a.router_w + static_cast<int64_t>(e) * H : (e == a.E ? a.shared_gate_w : nullptr);
       }
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // the loads of k-block kb + 1 are issued before the MMAs of kb (double-buffered
+      // registers), so an item pays the load latency about once, not once per k-block
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      uint4 va, vb, w[8];
+      auto load_kb = [&](int kb, uint4& xa_v, uint4& xb_v, uint4 (&wv)[8]) {
         const int koff = kb * 32 + 8 * c;
-        const uint4 z = make_uint4(0, 0, 0, 0);
-        const uint4 va = xa ? ldg_v4(xa + koff) : z;
-        const uint4 vb = xb ? ldg_v4(xb + koff) : z;
+        xa_v = xa ? ldg_v4(xa + koff) : z;
+        xb_v = xb ? ldg_v4(xb + koff) : z;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) wv[j] = wr[j] ? ldg_v4(wr[j] + koff) : z;
+      };
+      if (kb0 < kb1) load_kb(kb0, va, vb, w);
+      for (int kb = kb0; kb < kb1; ++kb) {
+        uint4 na = z, nb = z, nw[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nw[j] = z;
+        if (kb + 1 < kb1) load_kb(kb + 1, na, nb, nw);
+        const int koff = kb * 32 + 8 * c;
         if (eg == 0) {
           if (xa) *reinterpret_cast<uint4*>(a.x_perm + ta * H + koff) = perm_chunk(va);
           if (xb) *reinterpret_cast<uint4*>(a.x_perm + tb * H + koff) = perm_chunk(vb);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint4 w = wr[j] ? ldg_v4(wr[j] + koff) : z;
-          mma_bf16_16816(acc[j], va.x, vb.x, va.y, vb.y, w.x, w.y);
-          mma_bf16_16816(acc[j], va.z, vb.z, va.w, vb.w, w.z, w.w);
+          mma_bf16_16816(acc[j], va.x, vb.x, va.y, vb.y, w[j].x, w[j].y);
+          mma_bf16_16816(acc[j], va.z, vb.z, va.w, vb.w, w[j].z, w[j].w);
         }
+        va = na;
+        vb = nb;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) w[j] = nw[j];
       }
       float* part = a.partial + static_cast<int64_t>(ks) * T * a.epad;
 #pragma unroll
@@ -151,7 +167,6 @@ __device__ void phase_router(const RouteArgs& a) {
       }
     }
   }
-  (void)Etot;
 }
 
 __device__ void phase_permute_x(const RouteArgs& a) {
@@ -180,25 +195,39 @@ __device__ void phase_zero(float* p, int64_t n) {
 // ------------------------------------------------------------------ phase 2
 static_assert(kRouteChunk <= 32, "one bitmask word per expert and chunk");
 
-// fixed-order sum of the K-split router partials of (token t, logit e); all loads are
-// issued before the first add so their latencies overlap
+// fixed-order sum (ks = 0, 1, ...) of the K-split router partials of (token t, logit e);
+// the loads of four slices are issued together (a runtime loop keeps the code small:
+// the top-k phase runs it for every logit slot of a lane and two tokens at a time)
 FM_DEV float sum_partials(const RouteArgs& a, int64_t t, int e) {
-  float v[kRouterMaxKsplit];
   const float* p = a.partial + t * a.epad + e;
   const int64_t stride = a.T * a.epad;
-#pragma unroll
-  for (int ks = 0; ks < kRouterMaxKsplit; ++ks) v[ks] = ks < a.ksplit ? p[ks * stride] : 0.f;
   float s = 0.f;
-#pragma unroll
-  for (int ks = 0; ks < kRouterMaxKsplit; ++ks)
-    if (ks < a.ksplit) s += v[ks];
+  int ks = 0;
+  for (; ks + 4 <= a.ksplit; ks += 4) {
+    const float v0 = p[ks * stride], v1 = p[(ks + 1) * stride], v2 = p[(ks + 2) * stride], v3 = p[(ks + 3) * stride];
+    s += v0;
+    s += v1;
+    s += v2;
+    s += v3;
+  }
+  for (; ks < a.ksplit; ++ks) s += p[ks * stride];
   return s;
 }
 
-// PER = logits per lane (E < 32 PER: the experts and the shared gate); sm = NULL: the caller builds the chunk's
-// bitmasks from topk_ids later (the cluster routing kernel routes tokens on every CTA)
+// the raw (fp32, summed) logits of token t held by this lane: logit lane + 32 i, for the
+// experts and the shared gate (slot E); issued together so their latencies overlap
 template <int PER>
-__device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
+FM_DEV void load_logits(const RouteArgs& a, int64_t t, float (&raw)[PER]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    raw[i] = (e < a.E || (e == a.E && a.shared_gate_w)) ? sum_partials(a, t, e) : 0.f;
+  }
+}
+
+template <int PER>
+__device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl, const float (&raw)[PER]) {
   const int lane = threadIdx.x & 31;
   const int E = a.E, k = a.k;
   float p[PER];
@@ -209,12 +238,12 @@ __device__ void route_token(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl
     const int e = lane + 32 * i;
     p[i] = -INFINITY;
     if (e < E) {
-      float l = rbf(sum_partials(a, t, e));
+      float l = rbf(raw[i]);
       if (a.router_bias) l = rbf(l + bf2f(a.router_bias[e]));
       p[i] = l;
       mx = fmaxf(mx, l);
     } else if (e == E && a.shared_gate_w) {
-      a.gate_sig[t] = rbf(sigmoid_f(rbf(sum_partials(a, t, e))));
+      a.gate_sig[t] = rbf(sigmoid_f(rbf(raw[i])));
     }
   }
   if (a.shared_ungated && lane == 0) a.gate_sig[t] = 1.0f;
@@ -295,7 +324,7 @@ FM_DEV uint32_t ordered_key(float f) {
 // scores are the picks' orig, divided by (their sum in pick order + 1e-20) when
 // norm_topk and k > 1, times routed_scale, all fp32.
 template <int PER>
-__device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
+__device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl, const float (&raw)[PER]) {
   const int lane = threadIdx.x & 31;
   const int E = a.E, k = a.k;
   float orig[PER];
@@ -306,10 +335,10 @@ __device__ void route_token_sigmoid(const RouteArgs& a, int64_t t, RouteSmem* sm
     orig[i] = 0.f;
     key[i] = 0ull;
     if (e < E) {
-      const float l = rbf(sum_partials(a, t, e));
+      const float l = rbf(raw[i]);
       orig[i] = 1.0f / (1.0f + expf(-l));
     } else if (e == E && a.shared_gate_w) {
-      a.gate_sig[t] = rbf(sigmoid_f(rbf(sum_partials(a, t, e))));
+      a.gate_sig[t] = rbf(sigmoid_f(rbf(raw[i])));
     }
   }
   if (a.shared_ungated && lane == 0) a.gate_sig[t] = 1.0f;
@@ -428,20 +457,21 @@ __device__ void given_row(const RouteArgs& a, int64_t r, RouteSmem* sm, int tl) 
 }
 
 // one token (or given row) t, routed by the calling warp
+template <bool SIGMOID, int PER>
+__device__ void route_one_per(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
+  float raw[PER];
+  load_logits<PER>(a, t, raw);
+  if (SIGMOID) route_token_sigmoid<PER>(a, t, sm, tl, raw); else route_token<PER>(a, t, sm, tl, raw);
+}
+
 template <bool SIGMOID>
 __device__ void route_one(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
   // lanes cover logits 0..E: the E routed experts and the shared-expert gate at E
-  if (!a.do_router) {
-    given_row(a, t, sm, tl);
-  } else if (a.E < 64) {
-    if (SIGMOID) route_token_sigmoid<2>(a, t, sm, tl); else route_token<2>(a, t, sm, tl);
-  } else if (a.E < 128) {
-    if (SIGMOID) route_token_sigmoid<4>(a, t, sm, tl); else route_token<4>(a, t, sm, tl);
-  } else if (a.E < 256) {
-    if (SIGMOID) route_token_sigmoid<8>(a, t, sm, tl); else route_token<8>(a, t, sm, tl);
-  } else {  // up to kMaxExperts = 512 experts and the gate
-    if (SIGMOID) route_token_sigmoid<17>(a, t, sm, tl); else route_token<17>(a, t, sm, tl);
-  }
+  if (!a.do_router) given_row(a, t, sm, tl);
+  else if (a.E < 64) route_one_per<SIGMOID, 2>(a, t, sm, tl);
+  else if (a.E < 128) route_one_per<SIGMOID, 4>(a, t, sm, tl);
+  else if (a.E < 256) route_one_per<SIGMOID, 8>(a, t, sm, tl);
+  else route_one_per<SIGMOID, 17>(a, t, sm, tl);  // up to kMaxExperts = 512 experts and the gate
 }
 
 // the chunk's counts and stable in-chunk ranks from its bitmasks (sm.mask, sm.ids)
@@ -575,15 +605,16 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb
   const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
   if (threadIdx.x == 0) sm.offs[a.E] = P;
   __syncthreads();
+  // the offsets and table a in block 0, table b in block 1 (or block 0 when alone)
   if (bid == 0) {
     for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
       a.offsets[e] = sm.offs[e];
       if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
     }
     if (a.tab_a) plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
-    if (a.tab_b)
-      plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
   }
+  if (bid == (nb > 1 ? 1 : 0) && a.tab_b)
+    plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
   const int k = a.do_router ? a.k : 1;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
   for (int ch = bid; ch < nchunks; ch += nb) {
