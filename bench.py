@@ -723,22 +723,31 @@ def run_decoder(args, rank, world, local_rank):
         tok = dec.forward(tok[:, None].contiguous())
     dec.sync()
     pos0 = dec.offset
-    clocks = ClockSampler(local_rank)
-    clocks.start()
-    h.profile(True)
-    h.profile_report(reset=True)
+    clocks = NvmlClockSampler(dev)
     ids = [tok[:, None].contiguous(), torch.empty(B, 1, dtype=torch.int32, device=dev)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    clocks.start()
     e0.record(stream)
     for i in range(args.steps):
         dec.forward(ids[i & 1], out=ids[(i + 1) & 1].view(B))
     e1.record(stream)
     torch.cuda.synchronize()
+    clk = clocks.stop()
     dec.sync()
     dev_ms = e0.elapsed_time(e1) / args.steps
-    prof = {k: v for k, v in h.profile_report(reset=True).items() if "." not in k}
+    # per-kernel times from a few more decode steps with the kernel timers on (their
+    # events between kernels add host and device time, so the timed region runs without)
+    h.profile(True)
+    h.profile_report(reset=True)
+    prof_steps = min(args.steps, DECODE_STEPS - args.warmup - args.steps)
+    for i in range(prof_steps):
+        dec.forward(ids[(args.steps + i) & 1], out=ids[(args.steps + i + 1) & 1].view(B))
+    torch.cuda.synchronize()
+    dec.sync()
+    prof = {k: (n * args.steps / max(1, prof_steps), ms * args.steps / max(1, prof_steps))
+            for k, (n, ms) in h.profile_report(reset=True).items() if "." not in k}
     h.profile(False)
     # end to end: generate() from a host prompt to host tokens (prefill + steps forwards)
     torch.cuda.synchronize()
@@ -747,7 +756,6 @@ def run_decoder(args, rank, world, local_rank):
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
     if world > 1:
         t = torch.tensor([dev_ms, e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
