@@ -353,9 +353,11 @@ bool encode_codes(CUtensorMap* m, const uint32_t* w, int64_t rows, int K, uint32
   return encode_2d(m, true, w, static_cast<uint64_t>(K / 8), static_cast<uint64_t>(rows), 32, box_rows);
 }
 
-// bf16 activation rows [rows, cols], 128B-swizzled boxes of 64 columns x 32 rows
+// bf16 activation rows [rows, cols], 128B-swizzled boxes of 64 columns: m[0] with 32-row
+// boxes, m[2] (TcMaps::act[i + 2] for m = &act[i]) with kActBigBoxRows-row boxes
 bool encode_act(CUtensorMap* m, const uint16_t* x, int64_t rows, int64_t cols) {
-  return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, 32);
+  return encode_2d(m, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, 32) &&
+         encode_2d(m + 2, false, x, static_cast<uint64_t>(cols), static_cast<uint64_t>(rows), 64, fm::kActBigBoxRows);
 }
 
 // tma_gemv: the GEMV path's TMA-fed kernel (qgemv_tma.cu), whose tile table was planned

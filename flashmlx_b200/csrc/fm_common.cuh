@@ -100,6 +100,14 @@ FM_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, uint3
   }
 }
 
+// The same wait polled by lane 0 alone, the result broadcast to the warp (which must be
+// converged); lane 0 is the lane that then acts for the warp (elect.sync's choice).
+FM_DEV bool mbar_wait_lane0(uint64_t* bar, uint32_t parity, volatile int* abort, uint32_t* err) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort, err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 FM_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
@@ -257,6 +265,22 @@ FM_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+
+// 32 lanes x 32 columns of 32-bit values into TMEM (lane quadrant fixed by the warp
+// id): column c of this thread's lane receives word c % 4 of v[c / 4]
+FM_DEV void tmem_st32(uint32_t taddr, const uint4 (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z), "r"(v[1].w),
+      "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z), "r"(v[3].w),
+      "r"(v[4].x), "r"(v[4].y), "r"(v[4].z), "r"(v[4].w), "r"(v[5].x), "r"(v[5].y), "r"(v[5].z), "r"(v[5].w),
+      "r"(v[6].x), "r"(v[6].y), "r"(v[6].z), "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z), "r"(v[7].w)
+      : "memory");
+}
+// this thread's earlier tcgen05.st are complete
+FM_DEV void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- legacy mma
 // mma.sync m16n8k16, bf16 in, fp32 accumulate (used by the small-token GEMV path,

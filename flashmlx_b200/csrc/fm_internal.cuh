@@ -42,8 +42,8 @@ struct TileInfo {
   int nrows;   // activation rows in the chunk
 };
 
-FM_DEV TileInfo tile_of_group(const TileTable* tab, int lo, int tile) {
-  const TileGroup G = tab->g[lo];
+// tile `tile` of group G (index lo)
+FM_DEV TileInfo tile_in_group(const TileGroup& G, int lo, int tile) {
   int local = tile - G.tile_begin;
   TileInfo t;
   t.group = lo;
@@ -57,6 +57,8 @@ FM_DEV TileInfo tile_of_group(const TileTable* tab, int lo, int tile) {
   t.nrows = min(G.chunk_rows, G.rows - ch * G.chunk_rows);
   return t;
 }
+
+FM_DEV TileInfo tile_of_group(const TileTable* tab, int lo, int tile) { return tile_in_group(tab->g[lo], lo, tile); }
 
 FM_DEV TileInfo decode_tile(const TileTable* tab, int tile) {
   int lo = 0, hi = tab->num_groups - 1;
@@ -131,9 +133,12 @@ struct GemmArgs {
 //               (read by TMA only where the rows are contiguous: down; gate/up and
 //               plain gather their token rows with cp.async)
 //   act[1]:     shared-expert activation rows, box {64, 32}
+//   act[2], act[3]: the same two tensors with boxes of {64, kActBigBoxRows} rows, so
+//               a tile half of more than 64 rows takes one TMA per k-step, not 3-4
+constexpr int kActBigBoxRows = 128;
 struct alignas(64) TcMaps {
   CUtensorMap code[4];
-  CUtensorMap act[2];
+  CUtensorMap act[4];
 };
 
 // Arguments of the routing kernel.

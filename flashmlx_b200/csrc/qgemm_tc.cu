@@ -3,14 +3,17 @@
 //
 // Replaces mx::gather_qmm (sorted, model.cpp:703-721) and mx::quantized_matmul
 // (model.cpp:741-747) for prefill-sized batches.  Each pair walks a device-built tile
-// table (expert / shared-expert group, 256-row weight block, chunk of <= 256
+// table (expert / shared-expert group, 256-row weight block, chunk of <= 192
 // activation rows).  One tile is D[256 x N] = A[256 x K] * B[N x K]^T:
-//   A (dequantized weights): rows 0..127 in CTA 0's shared memory, 128..255 in CTA 1's;
-//   B (activation rows):     rows 0..N/2-1 in CTA 0, N/2..N-1 in CTA 1;
+//   A (dequantized weights): rows 0..127 in CTA 0's tensor memory, 128..255 in CTA 1's;
+//   B (activation rows):     rows 0..N/2-1 in CTA 0's shared memory, N/2..N-1 in CTA 1's;
 //   D (fp32, TMEM):          CTA r holds its 128 A rows x all N columns.
-// Per SM and 64-wide k-step that is 4 KB of codes and <= 16 KB of activations from
-// L2 for 4.2 MFLOP, half the L2 bytes per FLOP of a one-CTA 128 x 192 tile, which
-// the L2 -> SM bandwidth (~11 TB/s on B200) could not feed.
+// Per SM and 64-wide k-step that is 4 KB of codes and <= 12 KB of activations from
+// L2 for <= 3.1 MFLOP, half the L2 bytes per FLOP of a one-CTA tile, which the
+// L2 -> SM bandwidth (~11 TB/s on B200) could not feed.  A lives in TMEM (the MMA's
+// A-from-tensor-memory form) because with A in shared memory the dequantized stores
+// and the MMA's reads of them came on top of the activation and code traffic there.
+// TMEM (512 columns): two accumulator buffers of 192 columns, four A stages of 32.
 //   gate/up mode: CTA r's A rows 0..63 = gate rows f0 + 64r .. +63, rows 64..127 =
 //                 the same up rows (f0 = 128 x block), so one CTA's accumulator holds
 //                 g and u of a row; the epilogue applies silu(g)*u and stores the
@@ -31,16 +34,16 @@
 //
 // Roles (512 threads per CTA):
 //   warps 0-7   dequant producers in two groups of four that take alternate k-steps;
-//               thread t of a group owns A row t.  Per k-step: two 16-byte code reads,
-//               bf16 fma of the exact codes with the group's scale and bias (staged in
-//               shared memory by the code loader), eight 16-byte stores into the
-//               128B-swizzled K-major A stage; one arrival per warp on the leader's
+//               the thread in TMEM lane L owns A row L.  Per k-step: two 16-byte code
+//               reads, bf16 fma of the exact codes with the group's scale and bias
+//               (staged in shared memory by the code loader), one 32-column tcgen05.st
+//               into its lane of the A stage; one arrival per warp on the leader's
 //               stage barrier.
 //   warp 8      code loader (an elected lane issues the TMA of each super-step; all
 //               lanes copy the scales).
 //   warps 9-10  activation loaders (this CTA's half of the tile's rows).
 //   warp 11     TMEM allocation (both CTAs) and, in the leader CTA only, the
-//               tcgen05.mma issuer (M=256, N<=256, K=16 x 4 per stage): the whole warp
+//               tcgen05.mma issuer (M=256, N<=192, K=16 x 4 per stage): the whole warp
 //               walks the k-steps with warp-uniform operands, one elected lane issues;
 //               commits free the stage / publish the accumulator in both CTAs.
 // Single-thread tcgen05 / TMA instructions are issued from a converged warp through
@@ -48,7 +51,7 @@
 // from memory broadcast from lane 0): a thread computing them on its own paid ~90
 // cycles of issue per MMA, more than an N = 128 MMA takes to execute.
 //   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
-//               buffered accumulators (2 x 256 columns) overlap the next mainloop.
+//               buffered accumulators (2 x 192 columns) overlap the next mainloop.
 // Cross-CTA signalling: mbarrier arrivals on the peer's barriers through mapa
 // addresses, tcgen05.commit to each CTA's barrier, and the 2-CTA form of the TMA
 // load whose completion lands on the leader's barrier.  No load is multicast; every
@@ -59,48 +62,52 @@ namespace fm {
 namespace tc {
 
 constexpr int BM = 128;          // A rows per CTA (M = 256 per pair)
-constexpr int BN = 256;          // max activation rows per pair tile (MMA N)
+constexpr int ACC_COLS = 224;    // TMEM columns per accumulator buffer (two buffers)
+constexpr int BN = ACC_COLS;     // max activation rows per pair tile (MMA N)
 constexpr int BNH = BN / 2;      // B rows per CTA
-constexpr int ACC_COLS = 256;    // TMEM columns per accumulator buffer
-constexpr int STAGES = 4;
+constexpr int STAGES = 2;        // A stages (TMEM)
+constexpr int RING = 8;          // k-step ring: B stages (shared memory) and the full / empty barriers
+constexpr int A_COLS = 32;                        // TMEM columns of one A stage: 64 bf16 per lane
+constexpr uint32_t A_TMEM0 = 2u * ACC_COLS;       // first column of the A stages
+static_assert(A_TMEM0 + STAGES * A_COLS <= 512, "accumulators and A stages fit the 512 TMEM columns");
 constexpr int NC = 3;            // code ring depth (super-steps of 4 k-steps)
 constexpr int KS_PER_SS = 4;
-constexpr int A_BYTES = BM * 128;
-constexpr int B_BYTES = BNH * 128;
+constexpr int B_BYTES = ((BNH + 31) / 32 * 32 > kActBigBoxRows ? (BNH + 31) / 32 * 32 : kActBigBoxRows) * 128;  // whole TMA boxes
 constexpr int C_BYTES = BM * 128;  // 128 rows x 32 words
 constexpr int SC_GROUPS = 8;                     // max quant groups per row per super-step (gs 32)
 constexpr int SC_BYTES = 2 * BM * SC_GROUPS * 2; // scales + biases of one code slot
 constexpr int STG_BYTES = 32 * 256;              // 32 rows x 128 bf16 outputs
-constexpr int OFF_A = 0;
-constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-constexpr int OFF_C = OFF_B + STAGES * B_BYTES;
+constexpr int OFF_B = 0;
+constexpr int OFF_C = OFF_B + RING * B_BYTES;
 constexpr int OFF_SC = OFF_C + NC * C_BYTES;
 constexpr int OFF_STG = OFF_SC + NC * SC_BYTES;  // two staging tiles
 constexpr int OFF_TB = OFF_STG + 2 * STG_BYTES;  // tile_begin of every group
 constexpr int OFF_BAR = OFF_TB + ((kMaxGroups * 4 + 255) / 256) * 256;
-constexpr int BAR_BYTES = 256;
+constexpr int BAR_BYTES = 512;
 constexpr int SMEM_BYTES = OFF_BAR + BAR_BYTES + 1024;  // + alignment slack
-constexpr int NA = 256;          // dequant-producer threads: two groups of 128, one A row per thread
 constexpr int DQ_GROUPS = 2;     // group g dequantizes the k-steps with (k-step % 2) == g
-constexpr int CODE_WARP = 8;
-constexpr int ACT_WARP = 9;      // two activation-loader warps: 9 and 10
+constexpr int NA = 128 * DQ_GROUPS;  // dequant-producer threads: groups of 128, one A row per thread
+constexpr int CODE_WARP = NA / 32;
+constexpr int ACT_WARP = CODE_WARP + 1;  // two activation-loader warps
 constexpr int NB = 64;
-constexpr int B_ROWS = BNH / 8;  // rows per activation-loader thread (16)
-constexpr int B_LAG = 2;
-constexpr int MMA_WARP = 11;
-constexpr int EPI_WARP = 12;     // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
+constexpr int B_ROWS = BNH / 8;  // rows per activation-loader thread (12)
+constexpr int B_LAG = 4;
+constexpr int MMA_WARP = ACT_WARP + 2;
+constexpr int EPI_WARP = MMA_WARP + 1;  // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
+static_assert(EPI_WARP % 4 == 0, "epilogue warp q reads TMEM lane quadrant q");
 constexpr int THREADS = (EPI_WARP + 4) * 32;
 constexpr uint32_t TMEM_COLS = 512;
-constexpr int FULL_ARRIVALS = 2 * (NA / 32 / DQ_GROUPS + NB / 32);  // per stage, both CTAs
+constexpr int FULL_ARRIVALS = 2 * (NA / 32 / DQ_GROUPS + NB / 32);  // per k-step: one dequant group and the activation loaders, both CTAs
 constexpr int CFULL_ARRIVALS = 1 + 32;  // code-loader lane 0 (meta + expect_tx) + one per lane's scale copies
 constexpr int ACCE_ARRIVALS = 2 * 4;                     // epilogue warps of both CTAs
 
 static_assert(OFF_B % 1024 == 0 && OFF_C % 1024 == 0 && B_BYTES % 1024 == 0, "1 KB aligned stages");
+static_assert(B_BYTES >= kActBigBoxRows * 128, "a big activation box fits one B stage");
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 
 struct Bars {
-  uint64_t full[STAGES];   // leader: A and B of both CTAs ready
-  uint64_t empty[STAGES];  // each CTA: the MMAs reading the stage are done
+  uint64_t full[RING];   // leader: k-step j % RING's A and B stages of both CTAs ready
+  uint64_t empty[RING];  // each CTA: k-step j % RING's MMAs are done (A stage j % STAGES, B stage j % RING)
   uint64_t cfull[NC];
   uint64_t cempty[NC];
   uint64_t accf[2];        // each CTA: accumulator buffer complete
@@ -110,7 +117,6 @@ struct Bars {
   int abort;
   int epi_ok[2][4];
   int slot_nk[NC];    // k-steps in the code slot's super-step; 0 marks the end of work
-  int slot_vlim[NC];  // A rows of this CTA inside the weight matrix (per 64-row half in gate/up)
 };
 static_assert(sizeof(Bars) <= BAR_BYTES, "barrier block");
 
@@ -184,13 +190,14 @@ FM_DEV void tmem_relinquish2() {
 FM_DEV void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
-// D[tmem, both CTAs] (+)= A[smem, 256 rows over the pair] * B[smem, N rows over the pair]^T
-FM_DEV void umma2_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
+// D[tmem, both CTAs] (+)= A[tmem, lanes 0..127 of each CTA: 256 rows over the pair, 16 K
+// per 8 columns] * B[smem, N rows over the pair]^T
+FM_DEV void umma2_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum)
       : "memory");
 }
 // arrive once on the barrier at caddr (either CTA of the pair) when all previously
@@ -198,6 +205,22 @@ FM_DEV void umma2_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t
 FM_DEV void umma2_commit(uint32_t caddr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(caddr)
                : "memory");
+}
+
+// tile `tile` of group G (index lo) of a tcgen05 tile table, whose groups have no K split
+FM_DEV TileInfo tile_tc(const TileGroup& G, int lo, int tile) {
+  const int local = tile - G.tile_begin;
+  const int rb = local / G.chunks;
+  const int ch = local - rb * G.chunks;
+  TileInfo t;
+  t.group = lo;
+  t.expert = G.expert;
+  t.ksplit = 1;
+  t.ks = 0;
+  t.rb = rb;
+  t.row0 = G.row_begin + ch * G.chunk_rows;
+  t.nrows = min(G.chunk_rows, G.rows - ch * G.chunk_rows);
+  return t;
 }
 
 FM_DEV int tile_ksteps(const GemmArgs& a, const TileInfo& ti, int mode) {
@@ -224,6 +247,15 @@ struct TileDir {
   const int* tb;
   int ng;
   FM_DEV TileInfo get(int tile) const { return decode_tile(tab, tb, ng, tile); }
+  // group index of a tile (shared-memory search only)
+  FM_DEV int find(int tile) const {
+    int lo = 0, hi = ng - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tb[mid] <= tile) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
 };
 
 FM_DEV void siter_load(SIter& it, const GemmArgs& a, const TileDir& dir, int tile, int ntiles, int mode) {
@@ -313,7 +345,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   volatile int* abort_flag = &bars->abort;
 
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < RING; ++s) {
       mbar_init(&bars->full[s], FULL_ARRIVALS);
       mbar_init(&bars->empty[s], 1);
     }
@@ -348,14 +380,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 
   if (warp < NA / 32) {
     // ------------------------------------------------------------ dequant producers
-    const int grp = warp / 4;              // takes the k-steps with (k-step % DQ_GROUPS) == grp
-    const int t = (warp % 4) * 32 + lane;  // code / scale row in the slot
-    // A row (= TMEM lane) it dequantizes into: in gate/up mode code rows 0..63 are gate
-    // rows f and 64..127 the up rows f of the same outputs, and A interleaves them in
-    // blocks of 8 (gate f -> 16 (f / 8) + f % 8, up f -> the same + 8), so an epilogue
-    // warp holds both halves of its SwiGLUs in lanes L and L ^ 8, and the 8 lanes of a
-    // 16-byte store phase still cover all 8 chunk positions of the 128-byte swizzle
-    const int a_row = (MODE == MODE_GATEUP) ? 16 * ((t & 63) >> 3) + 8 * (t >> 6) + (t & 7) : t;
+    const int grp = warp / 4;               // takes the k-steps with (k-step % DQ_GROUPS) == grp
+    const int L = (warp % 4) * 32 + lane;   // A row = TMEM lane it writes (the warp's lane quadrant)
+    // code / scale row of the slot that A row L holds: in gate/up mode code rows 0..63
+    // are gate rows f and 64..127 the up rows f of the same outputs, and A interleaves
+    // them in blocks of 8 (gate f -> 16 (f / 8) + f % 8, up f -> the same + 8), so an
+    // epilogue warp holds both halves of its SwiGLUs in lanes L and L ^ 8
+    const int t = (MODE == MODE_GATEUP) ? 64 * ((L >> 3) & 1) + 8 * (L >> 4) + (L & 7) : L;
+    // this thread's lane of the A stages; column A_TMEM0 + 32 s + c of stage s holds
+    // the bf16 pair (2c, 2c + 1) of the k-step's 64 (pair-permuted) weights
+    const uint32_t a_taddr = tmem_base + (static_cast<uint32_t>((warp % 4) * 32) << 16) + A_TMEM0;
     const int gs_shift = __ffs(a.gs) - 1;  // group sizes are powers of two (32, 64, 128)
     int cs = 0, it0 = 0;                   // super-step, k-steps before it
     bool ok = true;
@@ -367,8 +401,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
       const int nk = bars->slot_nk[slot];
       if (nk == 0) break;  // end of this pair's tiles
-      const int vlim = bars->slot_vlim[slot];
-      const bool valid = ((MODE == MODE_GATEUP) ? (t & 63) : t) < vlim;
       const uint8_t* code = smem + OFF_C + slot * C_BYTES + t * 128;
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + OFF_SC + slot * SC_BYTES) + t * SC_GROUPS;
       const uint16_t* bi = sc + BM * SC_GROUPS;
@@ -378,9 +410,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const int it = it0 + kk;
         const int stage = it % STAGES;
         // the k-step's 64 weights into registers first (codes and scales are in the
-        // code slot already), so the math overlaps the wait for the stage to drain
+        // code slot already), so the math overlaps the wait for the stage to drain.
+        // Rows past the matrix end need no test: the code loader gives them zero scales
+        // and biases, so they dequantize to zeros (and their outputs are never stored)
         uint4 o[8];
-        if (valid) {
+        {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {  // the two 32-element halves of the k-step
             const uint4 w = *reinterpret_cast<const uint4*>(code + (((2 * kk + h) ^ (t & 7)) << 4));
@@ -399,18 +433,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
           }
         }
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
+        const int jr = it - STAGES;  // the k-step whose MMAs read this A stage last
+        if (jr >= 0 && !__all_sync(0xffffffffu, mbar_wait(&bars->empty[jr % RING], (jr / RING) & 1, abort_flag, a.err))) {
           ok = false;
           break;
         }
-        if (valid) {
-          uint8_t* As = smem + OFF_A + stage * A_BYTES;
-#pragma unroll
-          for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(As + sw128_off(a_row, j)) = o[j];
-        }
-        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
+        // the MMAs that read the stage before are complete (commit -> empty): order
+        // the TMEM stores after them, make them complete, and publish
+        tc_fence_after();
+        tmem_st32(a_taddr + static_cast<uint32_t>(stage * A_COLS), o);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(full0 + stage * 8);
+        if (lane == 0) mbar_arrive_cluster(full0 + (it % RING) * 8);
       }
       if (!ok) break;
       __syncwarp();
@@ -421,8 +456,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int it = it0;
     // drain: the last commits of every stage land before this CTA may exit
     if (warp == 0 && ok) {
-      for (int i = it; i < it + STAGES; ++i)
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[i % STAGES], ((i / STAGES) & 1) ^ 1, abort_flag, a.err)))
+      for (int j = max(0, it - RING); j < it; ++j)
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[j % RING], (j / RING) & 1, abort_flag, a.err)))
           break;
     }
   } else if (warp == CODE_WARP) {
@@ -442,7 +477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint16_t* brow[4];
     bool rv[4];
     int gpr = 0, tile_ready = -1;
-    int u_vlim = 0, u_row = 0, u_map0 = 0;
+    int u_row = 0, u_map0 = 0;
     int cs = 0;
     while (true) {
       const int slot = cs % NC;
@@ -474,7 +509,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           brow[i] = B ? B + r * gpr : nullptr;
         }
         const int base = (MODE == MODE_GATEUP) ? ti.rb * 128 + rank * 64 : ti.rb * 256 + rank * 128;
-        u_vlim = __shfl_sync(0xffffffffu, max(0, N - base), 0);
         u_row = __shfl_sync(0xffffffffu, (sh ? 0 : ti.expert * N) + base, 0);
         u_map0 = __shfl_sync(0xffffffffu, sh ? 2 : 0, 0);
       }
@@ -511,7 +545,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int x = ss * (KS_PER_SS * 8);
       if (elect_one()) {
         bars->slot_nk[slot] = nk;
-        bars->slot_vlim[slot] = u_vlim;
         mbar_arrive_expect_tx(&bars->cfull[slot], C_BYTES);  // also publishes the metadata
         tma_load_2d(dst, &maps.code[u_map0], x, u_row, &bars->cfull[slot]);
         if (MODE == MODE_GATEUP) tma_load_2d(dst + 64 * 128, &maps.code[u_map0 + 1], x, u_row, &bars->cfull[slot]);
@@ -548,10 +581,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           srow[i] = (r < rmine) ? static_cast<uint32_t>(a.sorted_token[ti.row0 + rbeg + r]) : 0u;
         }
       }
-      const int nblk = (hrows + 31) >> 5;  // 32-row TMA boxes
+      // TMA boxes per k-step: up to two of 32 rows, or one of kActBigBoxRows rows (whose
+      // rows past the tile are read but never used by the MMA)
+      const bool big_box = hrows > 64;
+      const int nblk = big_box ? 1 : (hrows + 31) >> 5;
+      const uint32_t box_bytes = big_box ? kActBigBoxRows * 128u : 4096u;
       for (int ks = 0; ks < nks; ++ks) {
-        const int stage = it % STAGES;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / STAGES) & 1) ^ 1, abort_flag, a.err))) {
+        const int stage = it % RING;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bars->empty[stage], ((it / RING) & 1) ^ 1, abort_flag, a.err))) {
           ok = false;
           break;
         }
@@ -569,7 +606,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             cp_async_wait<B_LAG>();
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
+            if (lane == 0) mbar_arrive_cluster(full0 + (pend % RING) * 8);
             ++pend;
           }
         } else {
@@ -578,15 +615,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             fence_proxy_async();
             __syncwarp();
             for (; pend < it; ++pend)
-              if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
+              if (lane == 0) mbar_arrive_cluster(full0 + (pend % RING) * 8);
           }
           if (warp == ACT_WARP) {  // the whole warp: operands warp-uniform, one lane issues
             const int row_base = __shfl_sync(0xffffffffu, ti.row0 + rbeg, 0);
             const int nb = __shfl_sync(0xffffffffu, nblk, 0);
-            const CUtensorMap* map = &maps.act[__shfl_sync(0xffffffffu, sh ? 1 : 0, 0)];
+            const uint32_t bb = __shfl_sync(0xffffffffu, box_bytes, 0);
+            const CUtensorMap* map = &maps.act[__shfl_sync(0xffffffffu, (sh ? 1 : 0) + (big_box ? 2 : 0), 0)];
             const uint32_t bs = smem_u32(smem + OFF_B + stage * B_BYTES);
             if (elect_one()) {
-              mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nb) * 4096u);
+              mbar_arrive_expect_tx_cluster(full0 + stage * 8, static_cast<uint32_t>(nb) * bb);
               for (int b = 0; b < nb; ++b)
                 tma_load_2d_pair(bs + b * 4096, map, ks * 64, row_base + b * 32, full0 + stage * 8);
             }
@@ -603,7 +641,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fence_proxy_async();
     __syncwarp();
     for (; pend < it; ++pend)
-      if (lane == 0) mbar_arrive_cluster(full0 + (pend % STAGES) * 8);
+      if (lane == 0) mbar_arrive_cluster(full0 + (pend % RING) * 8);
   } else if (warp == MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer (leader)
     // The whole warp walks the loop with every MMA operand (TMEM address, descriptors,
@@ -616,36 +654,45 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint32_t empty_l = map_to_rank(&bars->empty[0], 0), empty_p = map_to_rank(&bars->empty[0], 1);
       const uint32_t accf_l = map_to_rank(&bars->accf[0], 0), accf_p = map_to_rank(&bars->accf[0], 1);
       const uint32_t tbase = __shfl_sync(0xffffffffu, tmem_base, 0);
-      const uint32_t a_base = smem_u32(smem + OFF_A), b_base = smem_u32(smem + OFF_B);
+      const uint32_t b_base = smem_u32(smem + OFF_B);
       const int ntl = __shfl_sync(0xffffffffu, ntiles, 0);
-      int stage = 0, phase = 0, lt = 0;
+      int kc = 0, lt = 0;  // k-steps issued so far, tiles started
       bool ok = true;
+      // The next tile's group is found (a forward scan from the current group) and its
+      // global-memory record loaded after the current tile's first MMAs are issued; the
+      // tile change then only does one division (a binary search, the record's load
+      // latency and the general decode took ~1300 cycles there with the tensor pipe idle)
+      int g_next = pair < ntl ? dir.find(pair) : 0;
+      TileGroup G_next = a.tab->g[g_next];
       for (int tile = pair; tile < ntl && ok; tile += npairs, ++lt) {
-        const TileInfo ti = dir.get(tile);
+        const TileInfo ti = tile_tc(G_next, g_next, tile);
         const int nks = __shfl_sync(0xffffffffu, tile_ksteps(a, ti, MODE), 0);
         const uint32_t idesc = __shfl_sync(0xffffffffu, idesc_bf16(2 * BM, tile_nmma(ti.nrows)), 0);
         const int buf = lt & 1;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err))) break;
+        if (!mbar_wait_lane0(&bars->acce[buf], ((lt >> 1) & 1) ^ 1, abort_flag, a.err)) break;
         tc_fence_after();
         const uint32_t d = tbase + static_cast<uint32_t>(buf * ACC_COLS);
-        for (int ks = 0; ks < nks; ++ks) {
-          if (!__all_sync(0xffffffffu, mbar_wait(&bars->full[stage], phase, abort_flag, a.err))) {
+        for (int ks = 0; ks < nks; ++ks, ++kc) {
+          const int slot = kc % RING;
+          // one lane polls (the A and B stages of the k-step complete one barrier)
+          if (!mbar_wait_lane0(&bars->full[slot], (kc / RING) & 1, abort_flag, a.err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t ad = sdesc_sw128(a_base + static_cast<uint32_t>(stage * A_BYTES));
-          const uint64_t bd = sdesc_sw128(b_base + static_cast<uint32_t>(stage * B_BYTES));
+          const uint32_t at = tbase + A_TMEM0 + static_cast<uint32_t>((kc % STAGES) * A_COLS);  // lane 0 of both CTAs
+          const uint64_t bd = sdesc_sw128(b_base + static_cast<uint32_t>(slot * B_BYTES));
           if (elect_one()) {
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) umma2_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
-            umma2_commit(empty_l + stage * 8);
-            umma2_commit(empty_p + stage * 8);
+            for (int kk = 0; kk < 4; ++kk) umma2_bf16_ts(d, at + 8 * kk, bd + 2 * kk, idesc, (ks | kk) != 0);
+            umma2_commit(empty_l + slot * 8);
+            umma2_commit(empty_p + slot * 8);
           }
           __syncwarp();
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1;
+          if (ks == 0 && tile + npairs < ntl) {
+            const int nt = tile + npairs;
+            while (g_next + 1 < dir.ng && dir.tb[g_next + 1] <= nt) ++g_next;
+            G_next = a.tab->g[g_next];
           }
         }
         if (ok && elect_one()) {
