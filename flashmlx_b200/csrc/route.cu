@@ -580,6 +580,8 @@ __device__ void finish_table(TileTable* tab, int ng, int* cnt, int* s_tmp) {
   }
 }
 
+// One block plans a table: a group per thread, the tile counts' exclusive scan over the
+// block (the grid form, whose blocks 0 and 1 have nothing else to do meanwhile).
 __device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, int rows_per_block, int n_routed,
                             int n_shared, int ksplit_shared, int* cnt) {
   const int has_sh = (n_shared > 0) ? 1 : 0;
@@ -599,22 +601,74 @@ __device__ void plan_groups(const RouteArgs& a, RouteSmem& sm, TileTable* tab, i
   finish_table(tab, ng, cnt, sm.tmp);
 }
 
+// One warp plans a whole table (the one-CTA tails of the small-batch forms): 32 groups at a time, the tile counts' exclusive scan by
+// shuffles (group order, as the block scan gives), no block barrier -- so the tables and
+// the scatter run on different warps at once.
+__device__ void plan_groups_warp(const RouteArgs& a, const int* offs, TileTable* tab, int rows_per_block,
+                                 int n_routed, int n_shared, int ksplit_shared) {
+  const int lane = threadIdx.x & 31;
+  const int has_sh = (n_shared > 0) ? 1 : 0;
+  const int ng = a.E + has_sh;
+  int running = 0;  // tiles of the groups before this batch of 32
+  for (int base = 0; base < ng; base += 32) {
+    const int gi = base + lane;
+    TileGroup G;
+    int cnt = 0;
+    if (gi < ng) {
+      const bool sh = has_sh && gi == 0;
+      const int e = sh ? -1 : gi - has_sh;
+      G.expert = e;
+      G.row_begin = sh ? 0 : offs[e];
+      G.rows = sh ? static_cast<int>(a.T) : (offs[e + 1] - offs[e]);
+      G.ksplit = sh ? ksplit_shared : 1;
+      plan_one(G, sh ? n_shared : n_routed, rows_per_block, a.chunk_max, a.chunk_align);
+      cnt = G.nblocks * G.chunks * G.ksplit;
+    }
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += u;
+    }
+    if (gi < ng) {
+      G.tile_begin = running + incl - cnt;
+      tab->g[gi] = G;
+    }
+    running += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) {
+    tab->num_groups = ng;
+    tab->num_tiles = running;
+  }
+}
+
 __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.offs[e] = a.totals[e];
   __syncthreads();
   const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
   if (threadIdx.x == 0) sm.offs[a.E] = P;
   __syncthreads();
-  // the offsets and table a in block 0, table b in block 1 (or block 0 when alone)
+  // the offsets and table a in block 0, table b in block 1 -- each planned by the whole
+  // block -- in the grid form; a block alone (the small-batch forms) has its warp 0 plan
+  // table a and its warp 1 table b while the other warps go on to the scatter
+  const int warp = threadIdx.x >> 5;
   if (bid == 0) {
     for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
       a.offsets[e] = sm.offs[e];
       if (a.out_offsets) a.out_offsets[e] = sm.offs[e];
     }
-    if (a.tab_a) plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
   }
-  if (bid == (nb > 1 ? 1 : 0) && a.tab_b)
-    plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
+  if (nb > 1) {
+    if (bid == 0 && a.tab_a)
+      plan_groups(a, sm, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1, sm.cnt_a);
+    if (bid == 1 && a.tab_b)
+      plan_groups(a, sm, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared, sm.cnt_b);
+  } else {
+    if (warp == 0 && a.tab_a)
+      plan_groups_warp(a, sm.offs, a.tab_a, a.a_rows_per_block, a.a_n, a.has_shared ? a.a_n_shared : 0, 1);
+    if (warp == 1 && a.tab_b)
+      plan_groups_warp(a, sm.offs, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared);
+  }
   const int k = a.do_router ? a.k : 1;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
   for (int ch = bid; ch < nchunks; ch += nb) {
