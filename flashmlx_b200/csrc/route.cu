@@ -642,15 +642,11 @@ __device__ void plan_groups_warp(const RouteArgs& a, const int* offs, TileTable*
   }
 }
 
-__device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
-  for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.offs[e] = a.totals[e];
-  __syncthreads();
-  const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
-  if (threadIdx.x == 0) sm.offs[a.E] = P;
-  __syncthreads();
-  // the offsets and table a in block 0, table b in block 1 -- each planned by the whole
-  // block -- in the grid form; a block alone (the small-batch forms) has its warp 0 plan
-  // table a and its warp 1 table b while the other warps go on to the scatter
+// The offsets (block 0) and the two tile tables, once sm.offs[0..E] holds the experts'
+// exclusive row starts: table a in block 0 and table b in block 1 -- each planned by the
+// whole block -- in the grid form; a block alone (the small-batch forms) has its warp 0
+// plan table a and its warp 1 table b while the other warps go on to the scatter.
+__device__ void emit_offsets_tables(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
   const int warp = threadIdx.x >> 5;
   if (bid == 0) {
     for (int e = threadIdx.x; e <= a.E; e += blockDim.x) {
@@ -669,6 +665,25 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb
     if (warp == 1 && a.tab_b)
       plan_groups_warp(a, sm.offs, a.tab_b, a.b_rows_per_block, a.b_n, a.has_shared ? a.b_n : 0, a.b_ksplit_shared);
   }
+}
+
+// the outputs of pair `flat` (expert e) placed at sorted position pos
+__device__ __forceinline__ void emit_pair(const RouteArgs& a, int64_t flat, int k, int pos) {
+  if (a.pair_pos) a.pair_pos[flat] = pos;
+  const int64_t t = flat / k;
+  a.sorted_token[pos] = a.do_router ? static_cast<int32_t>(t) : a.row_src[t];
+  a.sorted_score[pos] = a.topk_score[flat];
+  a.sorted_flat[pos] = static_cast<int32_t>(flat);
+  if (a.out_sorted_token) a.out_sorted_token[pos] = static_cast<int32_t>(t);
+}
+
+__device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
+  for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.offs[e] = a.totals[e];
+  __syncthreads();
+  const int P = block_exclusive_scan(sm.offs, a.E, sm.tmp);
+  if (threadIdx.x == 0) sm.offs[a.E] = P;
+  __syncthreads();
+  emit_offsets_tables(a, sm, bid, nb);
   const int k = a.do_router ? a.k : 1;
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
   for (int ch = bid; ch < nchunks; ch += nb) {
@@ -681,14 +696,61 @@ __device__ void phase_scatter(const RouteArgs& a, RouteSmem& sm, int bid, int nb
         if (a.pair_pos) a.pair_pos[flat] = -1;
         continue;
       }
-      const int pos = sm.offs[e] + a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] + a.pair_rank[flat];
-      if (a.pair_pos) a.pair_pos[flat] = pos;
-      const int64_t t = flat / k;
-      a.sorted_token[pos] = a.do_router ? static_cast<int32_t>(t) : a.row_src[t];
-      a.sorted_score[pos] = a.topk_score[flat];
-      a.sorted_flat[pos] = static_cast<int32_t>(flat);
-      if (a.out_sorted_token) a.out_sorted_token[pos] = static_cast<int32_t>(t);
+      emit_pair(a, flat, k, sm.offs[e] + a.chunk_counts[static_cast<int64_t>(ch) * a.E + e] + a.pair_rank[flat]);
     }
+  }
+}
+
+// Phases 2b-4 of a small batch (T <= kTailTokens) in one block, in shared memory: the
+// ids once from global memory, a token bitmask per expert (atomicOr), the experts'
+// counts and exclusive starts, the tables, and each pair's position = its expert's start
+// + the expert's tokens before it (popc of the mask below the token).  The same stable
+// (expert, token) order as the chunked count / scan / scatter, without their round trips
+// through global memory.
+constexpr int kTailTokens = kRouteLastMaxChunks * kRouteChunk;
+constexpr int kTailWords = kTailTokens / 32;
+struct TailSmem {
+  uint32_t tmask[kMaxExperts * kTailWords];  // [expert][token / 32]
+  int ids[kTailTokens * 16];                 // the pairs' expert ids (k <= 16)
+};
+
+__device__ void tail_fused(const RouteArgs& a, RouteSmem& sm, TailSmem& ts, int k) {
+  const int T = static_cast<int>(a.T), E = a.E, np = T * k;
+  for (int i = threadIdx.x; i < E * kTailWords; i += blockDim.x) ts.tmask[i] = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = a.topk_ids[i];
+    ts.ids[i] = e;
+    if (e >= 0) {
+      const int t = i / k;
+      atomicOr(&ts.tmask[e * kTailWords + (t >> 5)], 1u << (t & 31));
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+#pragma unroll
+    for (int w = 0; w < kTailWords; ++w) c += __popc(ts.tmask[e * kTailWords + w]);
+    sm.offs[e] = c;
+  }
+  __syncthreads();
+  const int P = block_exclusive_scan(sm.offs, E, sm.tmp);
+  if (threadIdx.x == 0) sm.offs[E] = P;
+  __syncthreads();
+  emit_offsets_tables(a, sm, 0, 1);
+  for (int i = threadIdx.x; i < np; i += blockDim.x) {
+    const int e = ts.ids[i];
+    if (e < 0) {
+      if (a.pair_pos) a.pair_pos[i] = -1;
+      continue;
+    }
+    const int t = i / k, wt = t >> 5;
+    const uint32_t* m = ts.tmask + e * kTailWords;
+    int rank = __popc(m[wt] & ((1u << (t & 31)) - 1u));
+#pragma unroll
+    for (int w = 0; w < kTailWords; ++w)
+      if (w < wt) rank += __popc(m[w]);
+    emit_pair(a, i, k, sm.offs[e] + rank);
   }
 }
 
@@ -897,11 +959,11 @@ __device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& s
 // Cluster form for small batches (at most kRouteLastMaxChunks chunks): one cluster of
 // kRouteClusterCtas CTAs.  Phase 1 over the cluster; a cluster barrier; every warp of
 // the cluster routes its share of the tokens (softmax / sigmoid, top-k, scores) into
-// global memory; a second cluster barrier; then CTA 0 alone builds each chunk's
-// bitmasks from the ids and runs the count, scan and scatter phases with block
-// barriers.  The cluster barriers are hardware barriers (no counter in memory, no spin),
-// and the chunk counts, ranks and scatter are the same functions as in the grid form, so
-// the ids, scores and permutation are identical.
+// global memory; a second cluster barrier; then CTA 0 alone counts, scans, plans and
+// scatters in shared memory (tail_fused).  The cluster barriers are hardware barriers
+// (no counter in memory, no spin); the stable (expert, token) order is the one the grid
+// form's chunked count / scan / scatter gives, so the ids, scores and permutation are
+// identical.
 FM_DEV void cluster_barrier() {
   __threadfence();  // this thread's global stores are visible device-wide before it arrives
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -909,7 +971,7 @@ FM_DEV void cluster_barrier() {
 }
 
 template <bool SIGMOID>
-__device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem& sm) {
+__device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem& sm, TailSmem& ts) {
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   const bool rep0 = blockIdx.x == 0;
   if (a.do_router) phase_router(a);
@@ -924,38 +986,21 @@ __device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem
   cluster_barrier();
   phase_mark(a, 1, t, rep0);
   if (blockIdx.x != 0) return;  // no other CTA touches this CTA's shared memory
-  const int k = a.do_router ? a.k : 1;
-  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
-  for (int ch = 0; ch < nchunks; ++ch) {
-    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e] = 0u;
-    __syncthreads();
-    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
-    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
-    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
-      const int e = a.topk_ids[t0 * k + i];
-      sm.ids[i] = e;
-      if (e >= 0) atomicOr(&sm.mask[e], 1u << (i / k));
-    }
-    __syncthreads();
-    count_chunk(a, sm, ch, k);
-    __syncthreads();
-  }
-  phase_column_scan_one_block(a);
-  __syncthreads();
+  tail_fused(a, sm, ts, a.do_router ? a.k : 1);
   phase_mark(a, 2, t, rep0);
-  phase_scatter(a, sm, 0, 1);
-  phase_mark(a, 3, t, rep0);
 }
 
 __global__ void __cluster_dims__(kRouteClusterCtas, 1, 1) __launch_bounds__(kRouteThreads)
     route_cluster_kernel(const RouteArgs a) {
   __shared__ RouteSmem sm;
-  route_cluster_body<false>(a, sm);
+  __shared__ TailSmem ts;
+  route_cluster_body<false>(a, sm, ts);
 }
 __global__ void __cluster_dims__(kRouteClusterCtas, 1, 1) __launch_bounds__(kRouteThreads)
     route_cluster_kernel_sigmoid(const RouteArgs a) {
   __shared__ RouteSmem sm;
-  route_cluster_body<true>(a, sm);
+  __shared__ TailSmem ts;
+  route_cluster_body<true>(a, sm, ts);
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_last_kernel(const RouteArgs a) {
