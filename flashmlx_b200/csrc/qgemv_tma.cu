@@ -32,7 +32,7 @@ namespace fm {
 
 namespace {
 
-constexpr int kTvConsumers = 4;                       // consumer warps
+constexpr int kTvConsumers = 8;                       // consumer warps (one 16-row MMA tile each)
 constexpr int kTvThreads = 32 * (kTvConsumers + 1);   // + the producer warp
 constexpr int kTvStages = 4;
 constexpr int kTvRows = 128;                          // weight rows per unit and stage
@@ -122,32 +122,31 @@ FM_DEV int tv_row(const TvUnit& u, int t) {
   return MODE == MODE_GATEUP ? u.ti.rb * 64 + (t & 63) : u.ti.rb * 128 + t;
 }
 
-// One stage of one consumer warp: NH valid 64-wide halves (4, or 2 at a K tail), NT
-// 8-column MMA tiles of activation rows.  The halves are unrolled without branches, so
-// the compiler overlaps the shared-memory reads, code unpacking, MMAs and group folds of
-// different halves.
-//   cs: this lane's code bytes in the stage (row lr0 + g; tile 1 is tile1 bytes further,
-//       row g + 8 1 KB further), chunk_off: its swizzled 16-byte chunk per half
+// One stage of one consumer warp: its 16-row MMA tile (rows g and g + 8 of the lane
+// group; the second row rstep bytes after the first in the code stage), NH valid
+// 64-wide halves (4, or 2 at a K tail), NT 8-column MMA tiles of activation rows.  The
+// halves are unrolled without branches, so the compiler overlaps the shared-memory
+// reads, code unpacking, MMAs and group folds of different halves.
+//   cs: this lane's code bytes in the stage (row g of the tile), chunk_off: its swizzled
+//       16-byte chunk per half
 //   xs: its activation bytes (row g, K positions 16 c ..), rows of tile n 8 * pitch further
-//   S, B: scales / biases of rows g, g + 8 of both tiles (4 groups each, bf16)
-// Per half: words 8h + 2c, 8h + 2c + 1 of rows g, g + 8; code pair p of a word is
+//   S0 / S1, B0 / B1: scales / biases of the tile's rows g and g + 8 (4 groups each, bf16)
+// Per half: words 8h + 2c, 8h + 2c + 1 of both rows; code pair p of a word is
 // (q_p, q_{p+4}) as bf16x2 (128 + q_p, 128 + q_{p+4}); MMA step ps of a word takes pairs
 // 2 ps, 2 ps + 1 against the activation slots of the same positions, the two steps in
-// separate accumulators (short MMA chains); per group y += s * acc + (b - 128 s) * sum(x).
+// separate accumulators (short MMA chains), sum(x) in one; per group
+// y += s * acc + (b - 128 s) * sum(x).
 template <int GS, int NT, int NH>
-FM_DEV void tv_stage(const uint8_t* cs, uint32_t tile1, const uint32_t (&chunk_off)[4], const uint8_t* xs,
-                     const uint2 (&S)[2][2], const uint2 (&B)[2][2], float (&y)[2][kTvNt][4]) {
+FM_DEV void tv_stage(const uint8_t* cs, uint32_t rstep, const uint32_t (&chunk_off)[4], const uint8_t* xs, uint2 S0,
+                     uint2 S1, uint2 B0, uint2 B1, float (&y)[kTvNt][4]) {
   constexpr uint32_t ONES = 0x3F803F80u;  // bf16x2 (1, 1)
-  float acc[2][NT][2][4], xsum[NT][2][4];
+  float acc[NT][2][4], xsum[NT][4];
 #pragma unroll
   for (int h = 0; h < NH; ++h) {
-    uint2 w[2][2];
+    uint2 w[2];
     uint4 xv[NT][2];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-        w[m][r] = *reinterpret_cast<const uint2*>(cs + chunk_off[h] + (m ? tile1 : 0u) + r * 1024u);
+    for (int r = 0; r < 2; ++r) w[r] = *reinterpret_cast<const uint2*>(cs + chunk_off[h] + r * rstep);
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       xv[n][0] = *reinterpret_cast<const uint4*>(xs + n * 8 * kTvXPitch + 128 * h);
@@ -159,52 +158,43 @@ FM_DEV void tv_stage(const uint8_t* cs, uint32_t tile1, const uint32_t (&chunk_o
 #pragma unroll
         for (int ps = 0; ps < 2; ++ps)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) xsum[n][ps][e] = acc[0][n][ps][e] = acc[1][n][ps][e] = 0.f;
+          for (int e = 0; e < 4; ++e) xsum[n][e] = acc[n][ps][e] = 0.f;
     }
 #pragma unroll
     for (int wi = 0; wi < 2; ++wi) {
-      uint32_t q[2][2][4];  // [m][row g / g + 8][pair]
+      uint32_t q[2][4];  // [row g / g + 8][pair]
 #pragma unroll
-      for (int m = 0; m < 2; ++m)
+      for (int r = 0; r < 2; ++r) {
+        const uint32_t v = wi ? w[r].y : w[r].x;
 #pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const uint32_t v = wi ? w[m][r].y : w[m][r].x;
-#pragma unroll
-          for (int pp = 0; pp < 4; ++pp) q[m][r][pp] = ((v >> (4 * pp)) & 0x000F000Fu) | 0x43004300u;
-        }
+        for (int pp = 0; pp < 4; ++pp) q[r][pp] = ((v >> (4 * pp)) & 0x000F000Fu) | 0x43004300u;
+      }
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         const uint4& x = xv[n][wi];
 #pragma unroll
         for (int ps = 0; ps < 2; ++ps) {
           const uint32_t b0 = ps ? x.z : x.x, b1 = ps ? x.w : x.y;
-          mma_bf16_16816(xsum[n][ps], ONES, ONES, ONES, ONES, b0, b1);
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-            mma_bf16_16816(acc[m][n][ps], q[m][0][2 * ps], q[m][1][2 * ps], q[m][0][2 * ps + 1], q[m][1][2 * ps + 1],
-                           b0, b1);
+          mma_bf16_16816(xsum[n], ONES, ONES, ONES, ONES, b0, b1);
+          mma_bf16_16816(acc[n][ps], q[0][2 * ps], q[1][2 * ps], q[0][2 * ps + 1], q[1][2 * ps + 1], b0, b1);
         }
       }
     }
     if (GS == 64 || (h & 1) == 1 || h + 1 == NH) {  // the group ends with this half
       const int gi = GS == 64 ? h : h >> 1;          // group within the stage
+      const uint32_t sw0 = gi < 2 ? S0.x : S0.y, sw8 = gi < 2 ? S1.x : S1.y;
+      const uint32_t bw0 = gi < 2 ? B0.x : B0.y, bw8 = gi < 2 ? B1.x : B1.y;
+      const float s0 = __uint_as_float((gi & 1) ? (sw0 & 0xFFFF0000u) : (sw0 << 16));
+      const float s8 = __uint_as_float((gi & 1) ? (sw8 & 0xFFFF0000u) : (sw8 << 16));
+      const float c0 = fmaf(-128.f, s0, __uint_as_float((gi & 1) ? (bw0 & 0xFFFF0000u) : (bw0 << 16)));
+      const float c8 = fmaf(-128.f, s8, __uint_as_float((gi & 1) ? (bw8 & 0xFFFF0000u) : (bw8 << 16)));
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const uint32_t sw0 = gi < 2 ? S[m][0].x : S[m][0].y, sw8 = gi < 2 ? S[m][1].x : S[m][1].y;
-        const uint32_t bw0 = gi < 2 ? B[m][0].x : B[m][0].y, bw8 = gi < 2 ? B[m][1].x : B[m][1].y;
-        const float s0 = __uint_as_float((gi & 1) ? (sw0 & 0xFFFF0000u) : (sw0 << 16));
-        const float s8 = __uint_as_float((gi & 1) ? (sw8 & 0xFFFF0000u) : (sw8 << 16));
-        const float c0 = fmaf(-128.f, s0, __uint_as_float((gi & 1) ? (bw0 & 0xFFFF0000u) : (bw0 << 16)));
-        const float c8 = fmaf(-128.f, s8, __uint_as_float((gi & 1) ? (bw8 & 0xFFFF0000u) : (bw8 << 16)));
+      for (int n = 0; n < NT; ++n)
 #pragma unroll
-        for (int n = 0; n < NT; ++n)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float sv = e < 2 ? s0 : s8, cv = e < 2 ? c0 : c8;
-            y[m][n][e] =
-                fmaf(sv, acc[m][n][0][e] + acc[m][n][1][e], fmaf(cv, xsum[n][0][e] + xsum[n][1][e], y[m][n][e]));
-          }
-      }
+        for (int e = 0; e < 4; ++e) {
+          const float sv = e < 2 ? s0 : s8, cv = e < 2 ? c0 : c8;
+          y[n][e] = fmaf(sv, acc[n][0][e] + acc[n][1][e], fmaf(cv, xsum[n][e], y[n][e]));
+        }
     }
   }
 }
@@ -328,11 +318,14 @@ __global__ void __launch_bounds__(kTvThreads, 2) qgemv_tma_kernel(const GemmArgs
   }
 
   // -------------------------------------------------------------------- consumers
+  // Warp w owns one 16-row MMA tile of the unit: in gate/up mode the gate rows of
+  // outputs 8w .. 8w + 7 (MMA rows g) and the up rows of the same outputs (rows g + 8),
+  // so a thread holds both halves of its SwiGLUs; in down / plain mode rows 16w .. 16w + 15.
   const int g = lane >> 2, c = lane & 3;
-  // local rows of this warp's two 16-row MMA tiles (row g; g + 8 is 8 further)
-  const int lr0 = MODE == MODE_GATEUP ? 16 * warp : 32 * warp;
-  const int lr1 = MODE == MODE_GATEUP ? 64 + 16 * warp : 32 * warp + 16;
-  constexpr uint32_t kTile1 = MODE == MODE_GATEUP ? 64u * 128u : 16u * 128u;  // tile 1's rows past tile 0's
+  const int lr0 = MODE == MODE_GATEUP ? 8 * warp : 16 * warp;  // code row of MMA row 0
+  // code-stage bytes from MMA row g to row g + 8: the up half (64 rows on) or 8 rows on
+  constexpr uint32_t kRstep = MODE == MODE_GATEUP ? 64u * 128u : 8u * 128u;
+  const int lr8 = MODE == MODE_GATEUP ? 64 + lr0 : lr0 + 8;    // code row of MMA row 8
   // this lane's bytes in a code stage: row lr0 + g, the 8-byte half c & 1 of its 16-byte
   // chunk, and per 64-wide half h the chunk 2h + c / 2 after the 128B swizzle (row & 7 == g)
   const uint32_t code_lane = static_cast<uint32_t>(lr0 + g) * 128u + 8u * static_cast<uint32_t>(c & 1);
@@ -345,11 +338,9 @@ __global__ void __launch_bounds__(kTvThreads, 2) qgemv_tma_kernel(const GemmArgs
     const TvUnit u = tv_unit<MODE>(a, tab, s_tb, ngroups, tile, GS);
     if (u.ti.nrows > kTvMaxRows) continue;  // reported by the producer
     const int ntn = (u.ti.nrows + 7) >> 3;  // 8-column MMA tiles of activation rows (1 or 2)
-    float y[2][kTvNt][4];
+    float y[kTvNt][4];
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int n = 0; n < kTvNt; ++n) y[m][n][0] = y[m][n][1] = y[m][n][2] = y[m][n][3] = 0.f;
+    for (int n = 0; n < kTvNt; ++n) y[n][0] = y[n][1] = y[n][2] = y[n][3] = 0.f;
     bool ok = true;
     for (int st = u.st0; st < u.st1; ++st, ++it) {
       const int slot = it % kTvStages;
@@ -362,53 +353,55 @@ __global__ void __launch_bounds__(kTvThreads, 2) qgemv_tma_kernel(const GemmArgs
       const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem + kTvOffSb + slot * 2 * kTvSbBytes);
       const uint16_t* bi = sc + kTvRows * 4;
       const int nh = min(4, (u.K - st * kTvStageK) / 64);  // valid 64-wide halves (4, or 2 at a tail: K % 128 == 0)
-      // scales / biases of rows g, g + 8 of both tiles: 4 groups each
-      uint2 S[2][2], B[2][2];
-#pragma unroll
-      for (int m = 0; m < 2; ++m)
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int row = (m ? lr1 : lr0) + g + 8 * r;
-          S[m][r] = *reinterpret_cast<const uint2*>(sc + row * 4);
-          B[m][r] = *reinterpret_cast<const uint2*>(bi + row * 4);
-        }
+      // scales / biases of the tile's rows g and g + 8: 4 groups each
+      const uint2 S0 = *reinterpret_cast<const uint2*>(sc + (lr0 + g) * 4);
+      const uint2 S1 = *reinterpret_cast<const uint2*>(sc + (lr8 + g) * 4);
+      const uint2 B0 = *reinterpret_cast<const uint2*>(bi + (lr0 + g) * 4);
+      const uint2 B1 = *reinterpret_cast<const uint2*>(bi + (lr8 + g) * 4);
       if (nh == 4) {
-        if (ntn == 1) tv_stage<GS, 1, 4>(cs, kTile1, chunk_off, xs, S, B, y);
-        else tv_stage<GS, 2, 4>(cs, kTile1, chunk_off, xs, S, B, y);
+        if (ntn == 1) tv_stage<GS, 1, 4>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
+        else tv_stage<GS, 2, 4>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
       } else {
-        if (ntn == 1) tv_stage<GS, 1, 2>(cs, kTile1, chunk_off, xs, S, B, y);
-        else tv_stage<GS, 2, 2>(cs, kTile1, chunk_off, xs, S, B, y);
+        if (ntn == 1) tv_stage<GS, 1, 2>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
+        else tv_stage<GS, 2, 2>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->empty[slot]);
     }
     if (!ok) break;
 
-    // epilogue: y[m][n][e] is (tile m's row g + 8 (e >> 1), activation row 8n + 2c + (e & 1))
-    const int n0 = MODE == MODE_GATEUP ? u.ti.rb * 64 + lr0 : u.ti.rb * 128 + lr0;
-    const bool mv0 = n0 < u.N, mv1 = (MODE == MODE_GATEUP ? n0 : n0 + 16) < u.N;  // N % 16 == 0
+    // epilogue: y[n][e] is (MMA row g + 8 (e >> 1), activation row 8n + 2c + (e & 1))
+    if (MODE == MODE_GATEUP) {
+      const int nn = u.ti.rb * 64 + lr0 + g;  // output (gate row e < 2, up row e >= 2)
+      if (u.ti.rb * 64 + lr0 < u.N) {         // N % 8 == 0: the warp's 8 outputs are in or out together
 #pragma unroll
-    for (int n = 0; n < kTvNt; ++n) {
-      if (n >= ntn) break;
+        for (int n = 0; n < kTvNt; ++n) {
+          if (n >= ntn) break;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int slot_r = 8 * n + 2 * c + (e & 1);
-        if (slot_r >= u.ti.nrows) continue;
-        const int p = u.ti.row0 + slot_r;
-        const int rr = g + 8 * (e >> 1);
-        if (MODE == MODE_GATEUP) {
-          if (!mv0) continue;
-          const int nn = n0 + rr;
-          const float gv = rbf(y[0][n][e]), uv = rbf(y[1][n][e]);
-          uint16_t* out = u.sh ? a.out_shared + static_cast<int64_t>(p) * a.out_shared_ld
-                               : a.out + static_cast<int64_t>(p) * a.out_ld;
-          out[perm8(nn)] = f2bf(swiglu_1(gv, uv));
-        } else {
+          for (int e = 0; e < 2; ++e) {
+            const int slot_r = 8 * n + 2 * c + e;
+            if (slot_r >= u.ti.nrows) continue;
+            const int p = u.ti.row0 + slot_r;
+            const float gv = rbf(y[n][e]), uv = rbf(y[n][e + 2]);
+            uint16_t* out = u.sh ? a.out_shared + static_cast<int64_t>(p) * a.out_shared_ld
+                                 : a.out + static_cast<int64_t>(p) * a.out_ld;
+            out[perm8(nn)] = f2bf(swiglu_1(gv, uv));
+          }
+        }
+      }
+    } else {
+      const int n0 = u.ti.rb * 128 + lr0;
+      if (n0 < u.N) {  // N % 16 == 0
 #pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            if (!(m ? mv1 : mv0)) continue;
-            const int nn = n0 + 16 * m + rr;
-            const float v = y[m][n][e];
+        for (int n = 0; n < kTvNt; ++n) {
+          if (n >= ntn) break;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int slot_r = 8 * n + 2 * c + (e & 1);
+            if (slot_r >= u.ti.nrows) continue;
+            const int p = u.ti.row0 + slot_r;
+            const int nn = n0 + g + 8 * (e >> 1);
+            const float v = y[n][e];
             if (MODE == MODE_DOWN) {
               if (u.sh) {
                 red_add_f32(a.ysh + static_cast<int64_t>(p) * a.y_ld + nn, v);
