@@ -127,8 +127,8 @@ FM_DEV int tv_row(const TvUnit& u, int t) {
 // 64-wide halves (4, or 2 at a K tail), NT 8-column MMA tiles of activation rows.  The
 // halves are unrolled without branches, so the compiler overlaps the shared-memory
 // reads, code unpacking, MMAs and group folds of different halves.
-//   cs: this lane's code bytes in the stage (row g of the tile), chunk_off: its swizzled
-//       16-byte chunk per half
+//   cs: this lane's code bytes in the stage (row g of the tile); chunk_x: (c / 2) ^ g, so
+//       half h's 16-byte chunk after the 128B swizzle is (2h) ^ chunk_x
 //   xs: its activation bytes (row g, K positions 16 c ..), rows of tile n 8 * pitch further
 //   S0 / S1, B0 / B1: scales / biases of the tile's rows g and g + 8 (4 groups each, bf16)
 // Per half: words 8h + 2c, 8h + 2c + 1 of both rows; code pair p of a word is
@@ -137,7 +137,7 @@ FM_DEV int tv_row(const TvUnit& u, int t) {
 // separate accumulators (short MMA chains), sum(x) in one; per group
 // y += s * acc + (b - 128 s) * sum(x).
 template <int GS, int NT, int NH>
-FM_DEV void tv_stage(const uint8_t* cs, uint32_t rstep, const uint32_t (&chunk_off)[4], const uint8_t* xs, uint2 S0,
+FM_DEV void tv_stage(const uint8_t* cs, uint32_t rstep, uint32_t chunk_x, const uint8_t* xs, uint2 S0,
                      uint2 S1, uint2 B0, uint2 B1, float (&y)[kTvNt][4]) {
   constexpr uint32_t ONES = 0x3F803F80u;  // bf16x2 (1, 1)
   float acc[NT][2][4], xsum[NT][4];
@@ -146,7 +146,7 @@ FM_DEV void tv_stage(const uint8_t* cs, uint32_t rstep, const uint32_t (&chunk_o
     uint2 w[2];
     uint4 xv[NT][2];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) w[r] = *reinterpret_cast<const uint2*>(cs + chunk_off[h] + r * rstep);
+    for (int r = 0; r < 2; ++r) w[r] = *reinterpret_cast<const uint2*>(cs + (((2u * h) ^ chunk_x) << 4) + r * rstep);
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       xv[n][0] = *reinterpret_cast<const uint4*>(xs + n * 8 * kTvXPitch + 128 * h);
@@ -329,9 +329,7 @@ __global__ void __launch_bounds__(kTvThreads, 2) qgemv_tma_kernel(const GemmArgs
   // this lane's bytes in a code stage: row lr0 + g, the 8-byte half c & 1 of its 16-byte
   // chunk, and per 64-wide half h the chunk 2h + c / 2 after the 128B swizzle (row & 7 == g)
   const uint32_t code_lane = static_cast<uint32_t>(lr0 + g) * 128u + 8u * static_cast<uint32_t>(c & 1);
-  uint32_t chunk_off[4];
-#pragma unroll
-  for (int h = 0; h < 4; ++h) chunk_off[h] = (static_cast<uint32_t>(2 * h + (c >> 1)) ^ static_cast<uint32_t>(g)) << 4;
+  const uint32_t chunk_x = static_cast<uint32_t>(c >> 1) ^ static_cast<uint32_t>(g);  // (2h + c/2) ^ g == 2h ^ chunk_x
   const uint32_t x_lane = static_cast<uint32_t>(g) * kTvXPitch + 32u * static_cast<uint32_t>(c);
   int it = 0;
   for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
@@ -359,11 +357,11 @@ __global__ void __launch_bounds__(kTvThreads, 2) qgemv_tma_kernel(const GemmArgs
       const uint2 B0 = *reinterpret_cast<const uint2*>(bi + (lr0 + g) * 4);
       const uint2 B1 = *reinterpret_cast<const uint2*>(bi + (lr8 + g) * 4);
       if (nh == 4) {
-        if (ntn == 1) tv_stage<GS, 1, 4>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
-        else tv_stage<GS, 2, 4>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
+        if (ntn == 1) tv_stage<GS, 1, 4>(cs, kRstep, chunk_x, xs, S0, S1, B0, B1, y);
+        else tv_stage<GS, 2, 4>(cs, kRstep, chunk_x, xs, S0, S1, B0, B1, y);
       } else {
-        if (ntn == 1) tv_stage<GS, 1, 2>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
-        else tv_stage<GS, 2, 2>(cs, kRstep, chunk_off, xs, S0, S1, B0, B1, y);
+        if (ntn == 1) tv_stage<GS, 1, 2>(cs, kRstep, chunk_x, xs, S0, S1, B0, B1, y);
+        else tv_stage<GS, 2, 2>(cs, kRstep, chunk_x, xs, S0, S1, B0, B1, y);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars->empty[slot]);
