@@ -1,8 +1,13 @@
-"""The last-block routing kernel's arrival logic (route.cu, route_last_body), restated on
-the CPU: each block counts itself in with atomicInc(counter, gridDim.x - 1), whose PTX
-semantics are old = *p; *p = (old >= limit) ? 0 : old + 1.  For any arrival order exactly
-one block -- the last to arrive -- sees gridDim.x - 1 and goes on to phases 2-4, and the
-counter is back at 0 for the next launch, whatever that launch's grid size."""
+"""Logic of the small-batch routing forms, restated on the CPU.
+
+The last-block kernel's arrival (route.cu, route_last_body): each block counts itself in
+with atomicInc(counter, gridDim.x - 1), whose PTX semantics are old = *p;
+*p = (old >= limit) ? 0 : old + 1.  For any arrival order exactly one block -- the last to
+arrive -- sees gridDim.x - 1 and goes on to phases 2-4, and the counter is back at 0 for
+the next launch, whatever that launch's grid size.
+
+The cluster kernel's one-CTA tail (route.cu, tail_fused): pair positions from per-expert
+token bitmasks equal the stable sort by expert that the grid form produces."""
 from __future__ import annotations
 
 import numpy as np
@@ -22,3 +27,45 @@ def test_one_last_block_per_launch_and_the_counter_returns_to_zero():
         last = [b for b in order if atomic_inc(counter, grid - 1) == grid - 1]
         assert last == [order[-1]], (grid, last)
         assert counter[0] == 0
+
+
+def _tail_fused_positions(ids: np.ndarray, E: int, T: int, k: int) -> np.ndarray:
+    """The cluster form's one-CTA tail (route.cu, tail_fused), restated: a 128-bit token mask
+    per expert (bit t set when token t routes to it), exclusive starts of the experts'
+    popcounts, and pair (t, j) at start[e] + popc(mask[e] below bit t); -1 for dropped
+    pairs (id < 0)."""
+    words = 4  # kTailTokens / 32
+    mask = np.zeros((E, words), np.uint64)
+    for i, e in enumerate(ids):
+        if e >= 0:
+            t = i // k
+            mask[e, t >> 5] |= np.uint64(1) << np.uint64(t & 31)
+    popc = lambda v: bin(int(v)).count("1")
+    counts = np.array([sum(popc(mask[e, w]) for w in range(words)) for e in range(E)])
+    starts = np.concatenate([[0], np.cumsum(counts)])[:-1]
+    pos = np.full(len(ids), -1, np.int64)
+    for i, e in enumerate(ids):
+        if e < 0:
+            continue
+        t = i // k
+        w, b = t >> 5, t & 31
+        rank = popc(int(mask[e, w]) & ((1 << b) - 1)) + sum(popc(mask[e, ww]) for ww in range(w))
+        pos[i] = starts[e] + rank
+    return pos
+
+
+def test_fused_tail_positions_equal_the_stable_expert_sort():
+    """Positions from the token bitmasks equal a stable sort of the pairs by expert id (the
+    order the grid form's chunked count / column scan / scatter produces), for batches up to
+    128 tokens, top-k up to 16, with dropped pairs."""
+    rng = np.random.default_rng(1)
+    for T, E, k in [(1, 4, 1), (7, 60, 4), (32, 60, 4), (100, 128, 8), (128, 512, 16), (128, 3, 2)]:
+        ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).reshape(-1).astype(np.int64)
+        drop = rng.random(ids.shape) < 0.1
+        ids[drop] = -1
+        pos = _tail_fused_positions(ids, E, T, k)
+        kept = np.flatnonzero(ids >= 0)
+        order = kept[np.argsort(ids[kept], kind="stable")]  # flat pair indices in sorted order
+        expect = np.full(len(ids), -1, np.int64)
+        expect[order] = np.arange(len(order))
+        assert np.array_equal(pos, expect), (T, E, k)
