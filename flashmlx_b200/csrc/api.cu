@@ -24,6 +24,8 @@
 namespace fm {
 __global__ void route_kernel(const RouteArgs a);
 __global__ void route_kernel_sigmoid(const RouteArgs a);
+__global__ void route_kernel_wide(const RouteArgs a);
+__global__ void route_kernel_sigmoid_wide(const RouteArgs a);
 __global__ void route_last_kernel(const RouteArgs a);
 __global__ void route_last_kernel_sigmoid(const RouteArgs a);
 __global__ void route_cluster_kernel(const RouteArgs a);
@@ -31,8 +33,8 @@ __global__ void route_cluster_kernel_sigmoid(const RouteArgs a);
 __global__ void dense_prep_kernel(const RouteArgs a);
 __global__ void finalize_kernel(const float* y_acc, const float* ysh, const float* gate_sig, int64_t T, int H,
                                 uint16_t* y);
-__global__ void finalize_pairs_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, int k, const uint16_t* ysh16,
-                                      const float* gate_sig, int64_t T, int H, uint16_t* y);
+void launch_finalize_pairs(int grid, cudaStream_t stream, const uint16_t* y_pairs, const int32_t* pair_pos, int k,
+                           const uint16_t* ysh16, const float* gate_sig, int64_t T, int H, uint16_t* y);
 __global__ void finalize_pairs_f32_kernel(const uint16_t* y_pairs, const int32_t* pair_pos, const float* score, int k,
                                           const uint16_t* ysh16, const float* gate_sig, int64_t T, int H, uint16_t* y);
 __global__ void ep_plan_kernel(const EpPlanArgs a);
@@ -78,6 +80,8 @@ struct fm_handle {
   int num_sms = 0;
   int route_blocks_per_sm = 0;
   int route_sig_blocks_per_sm = 0;  // route_kernel_sigmoid
+  int route_wide_blocks_per_sm = 0;      // route_kernel_wide
+  int route_sig_wide_blocks_per_sm = 0;  // route_kernel_sigmoid_wide
   int gemv_blocks_per_sm = 0;
   int gemv_tma_blocks_per_sm = 0;  // TMA-fed GEMV (qgemv_tma.cu); 0: not available
   int tc_pairs = 0;  // resident 2-CTA clusters of the tcgen05 kernel
@@ -306,11 +310,16 @@ int launch_route(fm_handle* h, RouteArgs& ra, int64_t items, bool sigmoid = fals
   }
   int64_t want = std::max<int64_t>((items + 7) / 8, nchunks);
   want = std::max<int64_t>(want, std::min<int64_t>(ra.E, h->num_sms));
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, max_blocks)));
+  // the wide instance (two CTAs per SM) when the one-CTA-per-SM grid would cap the blocks
+  const int wide_blocks = (sigmoid ? h->route_sig_wide_blocks_per_sm : h->route_wide_blocks_per_sm) * h->num_sms;
+  const bool wide = want > max_blocks && wide_blocks > max_blocks;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, wide ? wide_blocks : max_blocks)));
   void* args[] = {&ra};
   prof_begin(h, ra.do_router ? "route" : "route_given");
-  const void* fn = sigmoid ? reinterpret_cast<const void*>(&fm::route_kernel_sigmoid)
-                           : reinterpret_cast<const void*>(&fm::route_kernel);
+  const void* fn = sigmoid ? (wide ? reinterpret_cast<const void*>(&fm::route_kernel_sigmoid_wide)
+                                   : reinterpret_cast<const void*>(&fm::route_kernel_sigmoid))
+                           : (wide ? reinterpret_cast<const void*>(&fm::route_kernel_wide)
+                                   : reinterpret_cast<const void*>(&fm::route_kernel));
   cudaError_t e = cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(fm::kRouteThreads), args, 0, h->stream);
   prof_end(h);
   if (e != cudaSuccess) return cuda_err(h, e, "route_kernel launch");
@@ -771,6 +780,12 @@ int fm_create(fm_handle** out, int device, void* stream) {
   if (e == cudaSuccess)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_sig_blocks_per_sm, fm::route_kernel_sigmoid,
                                                       fm::kRouteThreads, 0);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_wide_blocks_per_sm, fm::route_kernel_wide,
+                                                      fm::kRouteThreads, 0);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&h->route_sig_wide_blocks_per_sm, fm::route_kernel_sigmoid_wide,
+                                                      fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&h->gemv_blocks_per_sm);
   if (e == cudaSuccess) e = fm::qgemv_tma_blocks_per_sm(&h->gemv_tma_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
@@ -1071,7 +1086,7 @@ int fm_moe_block(fm_handle* h, const fm_moe_config* c, const fm_moe_weights* w, 
   if (tcp) {
     const int64_t n8 = T * H / 8;
     const int fb = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
-    fm::finalize_pairs_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
+    fm::launch_finalize_pairs(fb, h->stream, gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
   } else {
     const int64_t n4 = T * H / 4;
     const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
@@ -1308,7 +1323,7 @@ int fm_moe_block_variant(fm_handle* h, const fm_moe_config* c, const fm_moe_vari
       fm::finalize_pairs_f32_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, ra.topk_score, k, gd.ysh16,
                                                                ra.gate_sig, T, H, y);
     else
-      fm::finalize_pairs_kernel<<<fb, 256, 0, h->stream>>>(gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
+      fm::launch_finalize_pairs(fb, h->stream, gd.y_pairs, ra.pair_pos, k, gd.ysh16, ra.gate_sig, T, H, y);
   } else {
     const int64_t n4 = T * H / 4;
     const int fb = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, static_cast<int64_t>(h->num_sms) * 8));
@@ -1953,6 +1968,7 @@ struct NoAllocDevice {
   uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
   int num_sms = 0;
   int route_blocks_per_sm = 0;
+  int route_wide_blocks_per_sm = 0;
   int gemv_blocks_per_sm = 0;
   int gemv_tma_blocks_per_sm = 0;  // TMA-fed GEMV (qgemv_tma.cu); 0: not available
   int tc_pairs = 0;
@@ -1974,6 +1990,9 @@ int noalloc_setup(int device, NoAllocDevice& d) {
   if (e == cudaSuccess && !(cc_major == 10 && cc_minor == 0)) return FM_EUNSUPPORTED;
   if (e == cudaSuccess)
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.route_blocks_per_sm, fm::route_kernel, fm::kRouteThreads, 0);
+  if (e == cudaSuccess)
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&d.route_wide_blocks_per_sm, fm::route_kernel_wide,
+                                                      fm::kRouteThreads, 0);
   if (e == cudaSuccess) e = fm::qgemv_blocks_per_sm(&d.gemv_blocks_per_sm);
   if (e == cudaSuccess) e = fm::qgemv_tma_blocks_per_sm(&d.gemv_tma_blocks_per_sm);
   if (e == cudaSuccess) e = fm::tc::init();
@@ -2029,6 +2048,7 @@ extern "C" int fm_moe_block_noalloc(int device, void* stream, const fm_moe_confi
     h.stream = static_cast<cudaStream_t>(stream);
     h.num_sms = d.num_sms;
     h.route_blocks_per_sm = d.route_blocks_per_sm;
+    h.route_wide_blocks_per_sm = d.route_wide_blocks_per_sm;
     h.gemv_blocks_per_sm = d.gemv_blocks_per_sm;
     h.gemv_tma_blocks_per_sm = d.gemv_tma_blocks_per_sm;
     h.tc_pairs = d.tc_pairs;

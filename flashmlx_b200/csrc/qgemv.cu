@@ -403,6 +403,10 @@ __global__ void finalize_kernel(const float* __restrict__ y_acc, const float* __
 // the k routed rows of a token are summed in fp32 in the order j = 0..k-1 (MLX sums
 // the [T, k, H] product over axis -2; model.cpp:780-784), then the gated shared row
 // is added as in model.cpp:800-803.  One thread per 8 outputs (16-byte accesses).
+// KU > 0 (k <= KU): all k rows' loads are issued before the first add (one memory
+// latency per output segment, not k), in an instance whose registers fit KU rows;
+// KU == 0: any k, one row at a time.
+template <int KU>
 __global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, const int32_t* __restrict__ pair_pos,
                                       int k, const uint16_t* __restrict__ ysh16, const float* __restrict__ gate_sig,
                                       int64_t T, int H, uint16_t* __restrict__ y) {
@@ -413,22 +417,39 @@ __global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, cons
     const int64_t t = i / segs;
     const int col = static_cast<int>(i - t * segs) * 8;
     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int j = 0; j < k; ++j) {
-      const int pos = pair_pos[t * k + j];
-      if (pos < 0) continue;
-      const uint4 v = *reinterpret_cast<const uint4*>(y_pairs + static_cast<int64_t>(pos) * H + col);
+    auto add_row = [&](const uint4& v) {
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         acc[2 * q] += bf2f(static_cast<uint16_t>(w[q] & 0xffffu));
         acc[2 * q + 1] += bf2f(static_cast<uint16_t>(w[q] >> 16));
       }
+    };
+    // the shared row's load first; the adds keep the order j = 0..k-1
+    const uint4 shv = ysh16 ? *reinterpret_cast<const uint4*>(ysh16 + t * H + col) : make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (KU > 0) {
+      int pos[KU];
+      uint4 v[KU];
+#pragma unroll
+      for (int j = 0; j < KU; ++j) pos[j] = j < k ? pair_pos[t * k + j] : -1;
+#pragma unroll
+      for (int j = 0; j < KU; ++j)
+        if (pos[j] >= 0) v[j] = *reinterpret_cast<const uint4*>(y_pairs + static_cast<int64_t>(pos[j]) * H + col);
+#pragma unroll
+      for (int j = 0; j < KU; ++j)
+        if (pos[j] >= 0) add_row(v[j]);
+    } else {
+      for (int j = 0; j < k; ++j) {
+        const int pos = pair_pos[t * k + j];
+        if (pos < 0) continue;
+        add_row(*reinterpret_cast<const uint4*>(y_pairs + static_cast<int64_t>(pos) * H + col));
+      }
     }
 #pragma unroll
     for (int q = 0; q < 8; ++q) acc[q] = rbf(acc[q]);
     if (ysh16) {
       const float gsv = gate_sig[t];
-      const uint4 s = *reinterpret_cast<const uint4*>(ysh16 + t * H + col);
+      const uint4 s = shv;
       const uint32_t w[4] = {s.x, s.y, s.z, s.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -443,6 +464,15 @@ __global__ void finalize_pairs_kernel(const uint16_t* __restrict__ y_pairs, cons
     o.w = pack_bf16x2(acc[6], acc[7]);
     *reinterpret_cast<uint4*>(y + t * H + col) = o;
   }
+}
+
+// the combine instance for top-k k: rows' loads batched for k <= 8
+void launch_finalize_pairs(int grid, cudaStream_t stream, const uint16_t* y_pairs, const int32_t* pair_pos, int k,
+                           const uint16_t* ysh16, const float* gate_sig, int64_t T, int H, uint16_t* y) {
+  if (k <= 2) finalize_pairs_kernel<2><<<grid, 256, 0, stream>>>(y_pairs, pair_pos, k, ysh16, gate_sig, T, H, y);
+  else if (k <= 4) finalize_pairs_kernel<4><<<grid, 256, 0, stream>>>(y_pairs, pair_pos, k, ysh16, gate_sig, T, H, y);
+  else if (k <= 8) finalize_pairs_kernel<8><<<grid, 256, 0, stream>>>(y_pairs, pair_pos, k, ysh16, gate_sig, T, H, y);
+  else finalize_pairs_kernel<0><<<grid, 256, 0, stream>>>(y_pairs, pair_pos, k, ysh16, gate_sig, T, H, y);
 }
 
 // The sigmoid-routed variant's combine on the tcgen05 path, y = bf16( bf16(sum_j

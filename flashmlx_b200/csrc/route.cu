@@ -95,6 +95,12 @@ struct RouteSmem {
 };
 
 // ------------------------------------------------------------------ phase 1
+// J: 8-logit MMA tiles per pass over K.  Eight (one pass for <= 64 logits) in the
+// one-cluster / last-block forms and the grid form; four in the grid form's wide instance,
+// which keeps the kernel at <= 128 registers (two CTAs per SM, twice the warps to hide
+// the latency of phase 2's loads; the activations of a token tile are read once per
+// pass, from L2 after the first).
+template <int J>
 __device__ void phase_router(const RouteArgs& a) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -106,7 +112,7 @@ __device__ void phase_router(const RouteArgs& a) {
   const int kblocks = H / 32;
   const int items = ntt * a.ksplit;
   const int Etot = a.E + (a.shared_gate_w ? 1 : 0);  // logits: the experts and the shared gate
-  const int ngroups = (Etot + 63) / 64;               // 64-logit groups (columns past Etot are never read)
+  const int ngroups = (Etot + 8 * J - 1) / (8 * J);  // logit groups (columns past Etot are never read)
   for (int item = gw; item < items; item += nw) {
     const int tt = item / a.ksplit, ks = item % a.ksplit;
     const int64_t t0 = static_cast<int64_t>(tt) * 16;
@@ -115,31 +121,31 @@ __device__ void phase_router(const RouteArgs& a) {
     const uint16_t* xa = (ta < T) ? a.x + ta * H : nullptr;
     const uint16_t* xb = (tb < T) ? a.x + tb * H : nullptr;
     for (int eg = 0; eg < ngroups; ++eg) {
-      float acc[8][4];
+      float acc[J][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-      const uint16_t* wr[8];
+      for (int j = 0; j < J; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+      const uint16_t* wr[J];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int e = eg * 64 + 8 * j + g;
+      for (int j = 0; j < J; ++j) {
+        const int e = eg * 8 * J + 8 * j + g;
         wr[j] = (e < a.E) ? a.router_w + static_cast<int64_t>(e) * H : (e == a.E ? a.shared_gate_w : nullptr);
       }
       // the loads of k-block kb + 1 are issued before the MMAs of kb (double-buffered
       // registers), so an item pays the load latency about once, not once per k-block
       const uint4 z = make_uint4(0, 0, 0, 0);
-      uint4 va, vb, w[8];
-      auto load_kb = [&](int kb, uint4& xa_v, uint4& xb_v, uint4 (&wv)[8]) {
+      uint4 va, vb, w[J];
+      auto load_kb = [&](int kb, uint4& xa_v, uint4& xb_v, uint4 (&wv)[J]) {
         const int koff = kb * 32 + 8 * c;
         xa_v = xa ? ldg_v4(xa + koff) : z;
         xb_v = xb ? ldg_v4(xb + koff) : z;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) wv[j] = wr[j] ? ldg_v4(wr[j] + koff) : z;
+        for (int j = 0; j < J; ++j) wv[j] = wr[j] ? ldg_v4(wr[j] + koff) : z;
       };
       if (kb0 < kb1) load_kb(kb0, va, vb, w);
       for (int kb = kb0; kb < kb1; ++kb) {
-        uint4 na = z, nb = z, nw[8];
+        uint4 na = z, nb = z, nw[J];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) nw[j] = z;
+        for (int j = 0; j < J; ++j) nw[j] = z;
         if (kb + 1 < kb1) load_kb(kb + 1, na, nb, nw);
         const int koff = kb * 32 + 8 * c;
         if (eg == 0) {
@@ -147,19 +153,19 @@ __device__ void phase_router(const RouteArgs& a) {
           if (xb) *reinterpret_cast<uint4*>(a.x_perm + tb * H + koff) = perm_chunk(vb);
         }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < J; ++j) {
           mma_bf16_16816(acc[j], va.x, vb.x, va.y, vb.y, w[j].x, w[j].y);
           mma_bf16_16816(acc[j], va.z, vb.z, va.w, vb.w, w[j].z, w[j].w);
         }
         va = na;
         vb = nb;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) w[j] = nw[j];
+        for (int j = 0; j < J; ++j) w[j] = nw[j];
       }
       float* part = a.partial + static_cast<int64_t>(ks) * T * a.epad;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int e = eg * 64 + 8 * j + 2 * c;
+      for (int j = 0; j < J; ++j) {
+        const int e = eg * 8 * J + 8 * j + 2 * c;
         if (e < a.epad) {
           if (ta < T) *reinterpret_cast<float2*>(part + ta * a.epad + e) = make_float2(acc[j][0], acc[j][1]);
           if (tb < T) *reinterpret_cast<float2*>(part + tb * a.epad + e) = make_float2(acc[j][2], acc[j][3]);
@@ -901,12 +907,12 @@ __global__ void __launch_bounds__(kRouteThreads) ep_p2p_plan_kernel(const EpP2PA
   ep_plan_body(pa);
 }
 
-template <bool SIGMOID>
+template <bool SIGMOID, int J>
 __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   const unsigned nb = gridDim.x;
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   // phase 1
-  if (a.do_router) phase_router(a);
+  if (a.do_router) phase_router<J>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
@@ -933,7 +939,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
 template <bool SIGMOID>
 __device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& sm) {
   unsigned long long t = threadIdx.x == 0 ? global_ns() : 0ull;
-  if (a.do_router) phase_router(a);
+  if (a.do_router) phase_router<8>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
@@ -974,7 +980,7 @@ template <bool SIGMOID>
 __device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem& sm, TailSmem& ts) {
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   const bool rep0 = blockIdx.x == 0;
-  if (a.do_router) phase_router(a);
+  if (a.do_router) phase_router<8>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
@@ -1017,11 +1023,21 @@ __global__ void __launch_bounds__(kRouteThreads) route_last_kernel_sigmoid(const
 // registers and occupancy
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
   __shared__ RouteSmem sm;
-  route_body<false>(a, sm);
+  route_body<false, 8>(a, sm);
 }
 __global__ void __launch_bounds__(kRouteThreads) route_kernel_sigmoid(const RouteArgs a) {
   __shared__ RouteSmem sm;
-  route_body<true>(a, sm);
+  route_body<true, 8>(a, sm);
+}
+// the same with four MMA tiles per router pass, at <= 128 registers: two CTAs per SM, for
+// batches whose grid the one-CTA-per-SM form would cap
+__global__ void __launch_bounds__(kRouteThreads, 2) route_kernel_wide(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_body<false, 4>(a, sm);
+}
+__global__ void __launch_bounds__(kRouteThreads, 2) route_kernel_sigmoid_wide(const RouteArgs a) {
+  __shared__ RouteSmem sm;
+  route_body<true, 4>(a, sm);
 }
 
 }  // namespace fm
