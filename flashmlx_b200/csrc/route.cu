@@ -95,12 +95,14 @@ struct RouteSmem {
 };
 
 // ------------------------------------------------------------------ phase 1
-// J: 8-logit MMA tiles per pass over K.  Eight (one pass for <= 64 logits) in the
-// one-cluster / last-block forms and the grid form; four in the grid form's wide instance,
-// which keeps the kernel at <= 128 registers (two CTAs per SM, twice the warps to hide
-// the latency of phase 2's loads; the activations of a token tile are read once per
-// pass, from L2 after the first).
-template <int J>
+// J: 8-logit MMA tiles per pass over K; TT: 16-token tiles per item (each router-weight
+// fragment a warp loads from L2 feeds TT tiles: the weights are re-read once per item,
+// which bounds phase 1 for long batches).  J = 8, TT = 1 (one pass for <= 64 logits) in
+// the one-cluster / last-block forms and the grid form; J = 4, TT = 2 in the grid form's
+// wide instance, which keeps the kernel at <= 128 registers (two CTAs per SM, twice the
+// warps to hide the latency of phase 2's loads; the activations of a token tile are read
+// once per pass, from L2 after the first).
+template <int J, int TT>
 __device__ void phase_router(const RouteArgs& a) {
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
@@ -109,21 +111,31 @@ __device__ void phase_router(const RouteArgs& a) {
   const int64_t T = a.T;
   const int H = a.H;
   const int ntt = static_cast<int>((T + 15) / 16);
+  const int nti = (ntt + TT - 1) / TT;  // items of TT token tiles
   const int kblocks = H / 32;
-  const int items = ntt * a.ksplit;
+  const int items = nti * a.ksplit;
   const int Etot = a.E + (a.shared_gate_w ? 1 : 0);  // logits: the experts and the shared gate
   const int ngroups = (Etot + 8 * J - 1) / (8 * J);  // logit groups (columns past Etot are never read)
   for (int item = gw; item < items; item += nw) {
-    const int tt = item / a.ksplit, ks = item % a.ksplit;
-    const int64_t t0 = static_cast<int64_t>(tt) * 16;
+    const int ti = item / a.ksplit, ks = item % a.ksplit;
     const int kb0 = kblocks * ks / a.ksplit, kb1 = kblocks * (ks + 1) / a.ksplit;
-    const int64_t ta = t0 + g, tb = t0 + g + 8;
-    const uint16_t* xa = (ta < T) ? a.x + ta * H : nullptr;
-    const uint16_t* xb = (tb < T) ? a.x + tb * H : nullptr;
-    for (int eg = 0; eg < ngroups; ++eg) {
-      float acc[J][4];
+    int64_t ta[TT], tb[TT];
+    const uint16_t* xa[TT];
+    const uint16_t* xb[TT];
 #pragma unroll
-      for (int j = 0; j < J; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    for (int u = 0; u < TT; ++u) {
+      const int64_t t0 = static_cast<int64_t>(ti * TT + u) * 16;
+      ta[u] = t0 + g;
+      tb[u] = t0 + g + 8;
+      xa[u] = (ta[u] < T) ? a.x + ta[u] * H : nullptr;
+      xb[u] = (tb[u] < T) ? a.x + tb[u] * H : nullptr;
+    }
+    for (int eg = 0; eg < ngroups; ++eg) {
+      float acc[TT][J][4];
+#pragma unroll
+      for (int u = 0; u < TT; ++u)
+#pragma unroll
+        for (int j = 0; j < J; ++j) acc[u][j][0] = acc[u][j][1] = acc[u][j][2] = acc[u][j][3] = 0.f;
       const uint16_t* wr[J];
 #pragma unroll
       for (int j = 0; j < J; ++j) {
@@ -133,32 +145,45 @@ __device__ void phase_router(const RouteArgs& a) {
       // the loads of k-block kb + 1 are issued before the MMAs of kb (double-buffered
       // registers), so an item pays the load latency about once, not once per k-block
       const uint4 z = make_uint4(0, 0, 0, 0);
-      uint4 va, vb, w[J];
-      auto load_kb = [&](int kb, uint4& xa_v, uint4& xb_v, uint4 (&wv)[J]) {
+      uint4 va[TT], vb[TT], w[J];
+      auto load_kb = [&](int kb, uint4 (&xa_v)[TT], uint4 (&xb_v)[TT], uint4 (&wv)[J]) {
         const int koff = kb * 32 + 8 * c;
-        xa_v = xa ? ldg_v4(xa + koff) : z;
-        xb_v = xb ? ldg_v4(xb + koff) : z;
+#pragma unroll
+        for (int u = 0; u < TT; ++u) {
+          xa_v[u] = xa[u] ? ldg_v4(xa[u] + koff) : z;
+          xb_v[u] = xb[u] ? ldg_v4(xb[u] + koff) : z;
+        }
 #pragma unroll
         for (int j = 0; j < J; ++j) wv[j] = wr[j] ? ldg_v4(wr[j] + koff) : z;
       };
       if (kb0 < kb1) load_kb(kb0, va, vb, w);
       for (int kb = kb0; kb < kb1; ++kb) {
-        uint4 na = z, nb = z, nw[J];
+        uint4 na[TT], nb[TT], nw[J];
+#pragma unroll
+        for (int u = 0; u < TT; ++u) na[u] = nb[u] = z;
 #pragma unroll
         for (int j = 0; j < J; ++j) nw[j] = z;
         if (kb + 1 < kb1) load_kb(kb + 1, na, nb, nw);
         const int koff = kb * 32 + 8 * c;
         if (eg == 0) {
-          if (xa) *reinterpret_cast<uint4*>(a.x_perm + ta * H + koff) = perm_chunk(va);
-          if (xb) *reinterpret_cast<uint4*>(a.x_perm + tb * H + koff) = perm_chunk(vb);
+#pragma unroll
+          for (int u = 0; u < TT; ++u) {
+            if (xa[u]) *reinterpret_cast<uint4*>(a.x_perm + ta[u] * H + koff) = perm_chunk(va[u]);
+            if (xb[u]) *reinterpret_cast<uint4*>(a.x_perm + tb[u] * H + koff) = perm_chunk(vb[u]);
+          }
         }
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-          mma_bf16_16816(acc[j], va.x, vb.x, va.y, vb.y, w[j].x, w[j].y);
-          mma_bf16_16816(acc[j], va.z, vb.z, va.w, vb.w, w[j].z, w[j].w);
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+          for (int u = 0; u < TT; ++u) {
+            mma_bf16_16816(acc[u][j], va[u].x, vb[u].x, va[u].y, vb[u].y, w[j].x, w[j].y);
+            mma_bf16_16816(acc[u][j], va[u].z, vb[u].z, va[u].w, vb[u].w, w[j].z, w[j].w);
+          }
+#pragma unroll
+        for (int u = 0; u < TT; ++u) {
+          va[u] = na[u];
+          vb[u] = nb[u];
         }
-        va = na;
-        vb = nb;
 #pragma unroll
         for (int j = 0; j < J; ++j) w[j] = nw[j];
       }
@@ -167,8 +192,11 @@ __device__ void phase_router(const RouteArgs& a) {
       for (int j = 0; j < J; ++j) {
         const int e = eg * 8 * J + 8 * j + 2 * c;
         if (e < a.epad) {
-          if (ta < T) *reinterpret_cast<float2*>(part + ta * a.epad + e) = make_float2(acc[j][0], acc[j][1]);
-          if (tb < T) *reinterpret_cast<float2*>(part + tb * a.epad + e) = make_float2(acc[j][2], acc[j][3]);
+#pragma unroll
+          for (int u = 0; u < TT; ++u) {
+            if (ta[u] < T) *reinterpret_cast<float2*>(part + ta[u] * a.epad + e) = make_float2(acc[u][j][0], acc[u][j][1]);
+            if (tb[u] < T) *reinterpret_cast<float2*>(part + tb[u] * a.epad + e) = make_float2(acc[u][j][2], acc[u][j][3]);
+          }
         }
       }
     }
@@ -912,7 +940,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   const unsigned nb = gridDim.x;
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   // phase 1
-  if (a.do_router) phase_router<J>(a);
+  if (a.do_router) phase_router<J, (J == 4 ? 2 : 1)>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
@@ -939,7 +967,7 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
 template <bool SIGMOID>
 __device__ __forceinline__ void route_last_body(const RouteArgs& a, RouteSmem& sm) {
   unsigned long long t = threadIdx.x == 0 ? global_ns() : 0ull;
-  if (a.do_router) phase_router<8>(a);
+  if (a.do_router) phase_router<8, 1>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
@@ -980,7 +1008,7 @@ template <bool SIGMOID>
 __device__ __forceinline__ void route_cluster_body(const RouteArgs& a, RouteSmem& sm, TailSmem& ts) {
   unsigned long long t = (blockIdx.x == 0 && threadIdx.x == 0) ? global_ns() : 0ull;
   const bool rep0 = blockIdx.x == 0;
-  if (a.do_router) phase_router<8>(a);
+  if (a.do_router) phase_router<8, 1>(a);
   else phase_permute_x(a);
   phase_zero(a.zero0, a.zero0_n);
   phase_zero(a.zero1, a.zero1_n);
