@@ -65,6 +65,30 @@ def test_quantized_matmul_parity(ops, path, M, K, N, gs):
     print(f"qmm {path} M={M} K={K} N={N} gs={gs}: bf16-weights {mt} exact {me}")
 
 
+@pytest.mark.parametrize("M,K,N,gs", [
+    (1, 2048, 2048, 64),    # one decode row: 16 output units
+    (4, 2048, 2560, 64),    # q|k|v-shaped
+    (2, 1408, 2048, 128),   # K % 256 == 128: the last stage holds one 128-wide half
+    (32, 2048, 1408, 64),   # 11 units x 2 row chunks
+    (300, 2048, 1408, 64),
+])
+def test_linear_parity(ops, M, K, N, gs):
+    """fm_linear (the decoder's dense projections, without the routing kernel) on the GEMV
+    path against the oracle's quantized_matmul."""
+    rng = np.random.default_rng(M * 7 + K + N + gs)
+    x = S.f32_to_bf16(rng.standard_normal((M, K), dtype=np.float32))
+    w, s, b = S.make_qmatrix(M, f"lin{K}{N}", (), N, K, gs)
+    h = ops.default_handle()
+    h.set_path(PATHS["gemv"])
+    try:
+        y = host_bf16(ops.linear(dev_bf16(x), dev_u32(w), dev_bf16(s), dev_bf16(b), group_size=gs))
+        h.sync()
+        check_vs_oracle(y, lambda: O.quantized_matmul(x, w, s, b, group_size=gs), f"linear M={M} K={K} N={N} gs={gs}",
+                        form_of(h))
+    finally:
+        h.set_path(0)
+
+
 def test_quantized_matmul_without_biases(ops):
     rng = np.random.default_rng(1)
     x = S.f32_to_bf16(rng.standard_normal((40, 1024), dtype=np.float32))
