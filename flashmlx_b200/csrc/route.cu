@@ -544,6 +544,37 @@ __device__ void phase_topk_count(const RouteArgs& a, RouteSmem& sm, int bid, int
   }
 }
 
+// Phase 2 split in two for batches with few chunks (at most half the blocks'): every
+// warp of the grid routes tokens (ids and scores to global memory), then, after a grid
+// barrier, a block per chunk rebuilds the chunk's bitmasks from the ids and counts it --
+// instead of 8 warps per chunk routing 2 tokens each while most blocks idle.  The same
+// route_one and count_chunk, so the same ids, scores, counts and ranks.
+template <bool SIGMOID>
+__device__ void phase_topk_spread(const RouteArgs& a) {
+  const int nw = gridDim.x * (kRouteThreads / 32);
+  const int gw = blockIdx.x * (kRouteThreads / 32) + (threadIdx.x >> 5);
+  for (int64_t tk = gw; tk < a.T; tk += nw) route_one<SIGMOID>(a, tk, nullptr, 0);
+}
+
+__device__ void phase_count_from_ids(const RouteArgs& a, RouteSmem& sm, int bid, int nb) {
+  const int k = a.do_router ? a.k : 1;
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  for (int ch = bid; ch < nchunks; ch += nb) {
+    for (int e = threadIdx.x; e < a.E; e += blockDim.x) sm.mask[e] = 0u;
+    __syncthreads();
+    const int64_t t0 = static_cast<int64_t>(ch) * kRouteChunk;
+    const int ntok = static_cast<int>(a.T - t0 < kRouteChunk ? a.T - t0 : kRouteChunk);
+    for (int i = threadIdx.x; i < ntok * k; i += blockDim.x) {
+      const int e = a.topk_ids[t0 * k + i];
+      sm.ids[i] = e;
+      if (e >= 0) atomicOr(&sm.mask[e], 1u << (i / k));
+    }
+    __syncthreads();
+    count_chunk(a, sm, ch, k);
+    __syncthreads();
+  }
+}
+
 // ------------------------------------------------------------------ phase 3
 __device__ void phase_column_scan(const RouteArgs& a, RouteSmem& sm) {
   const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
@@ -946,8 +977,16 @@ __device__ __forceinline__ void route_body(const RouteArgs& a, RouteSmem& sm) {
   phase_zero(a.zero1, a.zero1_n);
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 0, t, blockIdx.x == 0);
-  // phase 2
-  phase_topk_count<SIGMOID>(a, sm, blockIdx.x, nb);
+  // phase 2 (split for few chunks, in the one-CTA-per-SM instance that medium batches
+  // take; the branch is uniform over the grid)
+  const int nchunks = static_cast<int>((a.T + kRouteChunk - 1) / kRouteChunk);
+  if (J == 8 && 2 * nchunks <= static_cast<int>(nb)) {
+    phase_topk_spread<SIGMOID>(a);
+    if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
+    phase_count_from_ids(a, sm, blockIdx.x, nb);
+  } else {
+    phase_topk_count<SIGMOID>(a, sm, blockIdx.x, nb);
+  }
   if (!grid_sync(a.gsync, nb, a.err, &sm.flag)) return;
   phase_mark(a, 1, t, blockIdx.x == 0);
   // phase 3
