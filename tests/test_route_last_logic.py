@@ -7,7 +7,10 @@ arrive -- sees gridDim.x - 1 and goes on to phases 2-4, and the counter is back 
 the next launch, whatever that launch's grid size.
 
 The cluster kernel's one-CTA tail (route.cu, tail_fused): pair positions from per-expert
-token bitmasks equal the stable sort by expert that the grid form produces."""
+token bitmasks equal the stable sort by expert that the grid form produces.
+
+The last-block tail's column scan (phase_column_scan_one_block) against the grid form's
+(phase_column_scan): the same chunk offsets and totals."""
 from __future__ import annotations
 
 import numpy as np
@@ -69,3 +72,61 @@ def test_fused_tail_positions_equal_the_stable_expert_sort():
         expect = np.full(len(ids), -1, np.int64)
         expect[order] = np.arange(len(order))
         assert np.array_equal(pos, expect), (T, E, k)
+
+
+def _column_scan_grid(counts: np.ndarray, cap: int, nthreads: int = 256):
+    """phase_column_scan restated: per expert, the chunks in passes of `cap`, each pass an
+    exclusive block scan (thread i takes a contiguous range of ceil(n / nthreads) chunks,
+    the per-thread sums scanned across threads) plus the carry of earlier passes."""
+    nch, E = counts.shape
+    out = counts.copy()
+    totals = np.zeros(E, np.int64)
+    for e in range(E):
+        carry = 0
+        for c0 in range(0, nch, cap):
+            n = min(cap, nch - c0)
+            buf = out[c0:c0 + n, e].copy()
+            per = -(-n // nthreads)
+            local = [int(buf[min(n, t * per):min(n, t * per + per)].sum()) for t in range(nthreads)]
+            excl_thread = np.concatenate([[0], np.cumsum(local)])[:-1]
+            for t in range(nthreads):
+                run = int(excl_thread[t])
+                for i in range(min(n, t * per), min(n, t * per + per)):
+                    x = int(buf[i])
+                    buf[i] = run
+                    run += x
+            out[c0:c0 + n, e] = buf + carry
+            carry += sum(local)
+        totals[e] = carry
+    return out, totals
+
+
+def _column_scan_one_block(counts: np.ndarray, max_chunks: int = 8):
+    """phase_column_scan_one_block restated: each thread scans its experts' (at most
+    max_chunks) counts in registers."""
+    nch, E = counts.shape
+    assert nch <= max_chunks
+    out = counts.copy()
+    totals = np.zeros(E, np.int64)
+    for e in range(E):
+        run = 0
+        for i in range(max_chunks):
+            c = int(counts[i, e]) if i < nch else 0
+            if i < nch:
+                out[i, e] = run
+            run += c
+        totals[e] = run
+    return out, totals
+
+
+def test_one_block_column_scan_equals_the_grid_scan():
+    """The last-block form's one-block column scan gives the grid form's chunk offsets and
+    totals (chunk-major counts [chunk][expert]); the grid scan is exercised with passes
+    shorter than the chunk count, so its carry between passes is covered too."""
+    rng = np.random.default_rng(2)
+    for nch, E in [(1, 4), (3, 60), (8, 128), (8, 512), (5, 1)]:
+        counts = rng.integers(0, 17, size=(nch, E)).astype(np.int64)
+        g_out, g_tot = _column_scan_grid(counts, cap=3, nthreads=4)
+        o_out, o_tot = _column_scan_one_block(counts)
+        assert np.array_equal(g_out, o_out) and np.array_equal(g_tot, o_tot), (nch, E)
+        assert np.array_equal(g_out, np.cumsum(counts, axis=0) - counts)
