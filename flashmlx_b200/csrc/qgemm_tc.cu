@@ -3,17 +3,17 @@
 //
 // Replaces mx::gather_qmm (sorted, model.cpp:703-721) and mx::quantized_matmul
 // (model.cpp:741-747) for prefill-sized batches.  Each pair walks a device-built tile
-// table (expert / shared-expert group, 256-row weight block, chunk of <= 192
+// table (expert / shared-expert group, 256-row weight block, chunk of <= 224
 // activation rows).  One tile is D[256 x N] = A[256 x K] * B[N x K]^T:
 //   A (dequantized weights): rows 0..127 in CTA 0's tensor memory, 128..255 in CTA 1's;
 //   B (activation rows):     rows 0..N/2-1 in CTA 0's shared memory, N/2..N-1 in CTA 1's;
 //   D (fp32, TMEM):          CTA r holds its 128 A rows x all N columns.
-// Per SM and 64-wide k-step that is 4 KB of codes and <= 12 KB of activations from
-// L2 for <= 3.1 MFLOP, half the L2 bytes per FLOP of a one-CTA tile, which the
+// Per SM and 64-wide k-step that is 4 KB of codes and <= 14 KB of activations from
+// L2 for <= 3.7 MFLOP, half the L2 bytes per FLOP of a one-CTA tile, which the
 // L2 -> SM bandwidth (~11 TB/s on B200) could not feed.  A lives in TMEM (the MMA's
 // A-from-tensor-memory form) because with A in shared memory the dequantized stores
 // and the MMA's reads of them came on top of the activation and code traffic there.
-// TMEM (512 columns): two accumulator buffers of 192 columns, four A stages of 32.
+// TMEM (512 columns): two accumulator buffers of 224 columns, two A stages of 32.
 //   gate/up mode: CTA r's A rows 0..63 = gate rows f0 + 64r .. +63, rows 64..127 =
 //                 the same up rows (f0 = 128 x block), so one CTA's accumulator holds
 //                 g and u of a row; the epilogue applies silu(g)*u and stores the
@@ -28,7 +28,8 @@
 //
 // Data movement: packed 4-bit codes arrive by TMA, 4 k-steps (128 B x 128 rows) per
 // load, 128B-swizzled, into a 3-deep ring per CTA.  Contiguous activation rows arrive
-// by TMA in 32-row boxes straight into the UMMA B stage, completing on the leader
+// by TMA in 32-row boxes (128-row boxes for halves over 64 rows) straight into the
+// UMMA B stage of an 8-deep ring, completing on the leader
 // CTA's stage barrier; token-gathered rows are copied with cp.async.  Outputs go
 // through a shared-memory staging tile and leave as coalesced 16-byte stores.
 //
@@ -43,7 +44,7 @@
 //               lanes copy the scales).
 //   warps 9-10  activation loaders (this CTA's half of the tile's rows).
 //   warp 11     TMEM allocation (both CTAs) and, in the leader CTA only, the
-//               tcgen05.mma issuer (M=256, N<=192, K=16 x 4 per stage): the whole warp
+//               tcgen05.mma issuer (M=256, N<=224, K=16 x 4 per stage): the whole warp
 //               walks the k-steps with warp-uniform operands, one elected lane issues;
 //               commits free the stage / publish the accumulator in both CTAs.
 // Single-thread tcgen05 / TMA instructions are issued from a converged warp through
@@ -51,7 +52,7 @@
 // from memory broadcast from lane 0): a thread computing them on its own paid ~90
 // cycles of issue per MMA, more than an N = 128 MMA takes to execute.
 //   warps 12-15 epilogue: tcgen05.ld of the four 32-lane TMEM quadrants; double-
-//               buffered accumulators (2 x 192 columns) overlap the next mainloop.
+//               buffered accumulators (2 x 224 columns) overlap the next mainloop.
 // Cross-CTA signalling: mbarrier arrivals on the peer's barriers through mapa
 // addresses, tcgen05.commit to each CTA's barrier, and the 2-CTA form of the TMA
 // load whose completion lands on the leader's barrier.  No load is multicast; every
@@ -90,7 +91,7 @@ constexpr int NA = 128 * DQ_GROUPS;  // dequant-producer threads: groups of 128,
 constexpr int CODE_WARP = NA / 32;
 constexpr int ACT_WARP = CODE_WARP + 1;  // two activation-loader warps
 constexpr int NB = 64;
-constexpr int B_ROWS = BNH / 8;  // rows per activation-loader thread (12)
+constexpr int B_ROWS = BNH / 8;  // rows per activation-loader thread (14)
 constexpr int B_LAG = 4;
 constexpr int MMA_WARP = ACT_WARP + 2;
 constexpr int EPI_WARP = MMA_WARP + 1;  // first of the four epilogue warps (TMEM lane quadrant = warp % 4)
