@@ -52,6 +52,16 @@ Decoder::Decoder(const fmh_decoder_config& cfg, const fmh_weights& w, int device
       any_split = true;
       continue;
     }
+    // q, k and v already side by side (codes, scales and biases each one [QD + 2 KVD]-row
+    // block, as open() uploads them): used in place, no copy
+    const bool adjacent = l.k.w == l.q.w + QD * kw && l.v.w == l.k.w + KVD * kw &&
+                          l.k.scales == l.q.scales + QD * gpr && l.v.scales == l.k.scales + KVD * gpr &&
+                          (nb || (l.k.biases == l.q.biases + QD * gpr && l.v.biases == l.k.biases + KVD * gpr));
+    if (adjacent) {
+      qkv_[li] = fm_qweight{l.q.w, l.q.scales, l.q.biases};
+      any_fused = true;
+      continue;
+    }
     auto* w = static_cast<uint32_t*>(bufs_.alloc(static_cast<size_t>(W * kw) * 4));
     uint16_t* sc = bf(W * gpr);
     uint16_t* bi = nb ? nullptr : bf(W * gpr);
@@ -308,6 +318,40 @@ std::unique_ptr<Decoder> Decoder::open(const std::string& model_dir, int device,
     r.biases = static_cast<const uint16_t*>(up(q.b));
     return r;
   };
+  // q, k and v of a layer in one allocation each for codes, scales and biases (q's rows,
+  // then k's, then v's), which the decoder takes as its fused q|k|v projection without a
+  // second copy; a layer whose three matrices differ in having scales or biases is
+  // uploaded matrix by matrix
+  auto uq3 = [&](const QView& q, const QView& k, const QView& v, fm_qweight& oq, fm_qweight& ok, fm_qweight& ov) {
+    const bool all = q.w && k.w && v.w && q.s && k.s && v.s && !q.b == !k.b && !q.b == !v.b;
+    if (!all) {
+      oq = uq(q);
+      ok = uq(k);
+      ov = uq(v);
+      return;
+    }
+    auto cat = [&](const TensorView* a, const TensorView* b, const TensorView* c, const void* (&out)[3]) {
+      auto* base = static_cast<uint8_t*>(store->alloc(a->nbytes + b->nbytes + c->nbytes));
+      const TensorView* parts[3] = {a, b, c};
+      size_t off = 0;
+      for (int i = 0; i < 3; ++i) {
+        if (parts[i]->nbytes)
+          cuda_check(cudaMemcpy(base + off, parts[i]->data, parts[i]->nbytes, cudaMemcpyHostToDevice), "cudaMemcpy");
+        out[i] = base + off;
+        off += parts[i]->nbytes;
+      }
+    };
+    const void* pw[3];
+    const void* ps[3];
+    const void* pb[3] = {nullptr, nullptr, nullptr};
+    cat(q.w, k.w, v.w, pw);
+    cat(q.s, k.s, v.s, ps);
+    if (q.b) cat(q.b, k.b, v.b, pb);
+    fm_qweight* outs[3] = {&oq, &ok, &ov};
+    for (int i = 0; i < 3; ++i)
+      *outs[i] = fm_qweight{static_cast<const uint32_t*>(pw[i]), static_cast<const uint16_t*>(ps[i]),
+                            static_cast<const uint16_t*>(pb[i])};
+  };
   fmh_weights w{};
   if (p.embed.w) {  // a quantized table is dequantized once on the device (model.cpp:216-230)
     w.embed_q = uq(p.embed);
@@ -328,9 +372,7 @@ std::unique_ptr<Decoder> Decoder::open(const std::string& model_dir, int device,
     fmh_layer& l = layers[i];
     l.in_norm = static_cast<const uint16_t*>(up(lp.in_norm));
     l.post_norm = static_cast<const uint16_t*>(up(lp.post_norm));
-    l.q = uq(lp.q);
-    l.k = uq(lp.k);
-    l.v = uq(lp.v);
+    uq3(lp.q, lp.k, lp.v, l.q, l.k, l.v);
     l.o = uq(lp.o);
     l.q_bias = static_cast<const uint16_t*>(up(lp.q_bias));
     l.k_bias = static_cast<const uint16_t*>(up(lp.k_bias));
