@@ -229,34 +229,36 @@ __device__ void phase_zero(float* p, int64_t n) {
 // ------------------------------------------------------------------ phase 2
 static_assert(kRouteChunk <= 32, "one bitmask word per expert and chunk");
 
-// fixed-order sum (ks = 0, 1, ...) of the K-split router partials of (token t, logit e);
-// the loads of four slices are issued together (a runtime loop keeps the code small:
-// the top-k phase runs it for every logit slot of a lane and two tokens at a time)
-FM_DEV float sum_partials(const RouteArgs& a, int64_t t, int e) {
-  const float* p = a.partial + t * a.epad + e;
-  const int64_t stride = a.T * a.epad;
-  float s = 0.f;
-  int ks = 0;
-  for (; ks + 4 <= a.ksplit; ks += 4) {
-    const float v0 = p[ks * stride], v1 = p[(ks + 1) * stride], v2 = p[(ks + 2) * stride], v3 = p[(ks + 3) * stride];
-    s += v0;
-    s += v1;
-    s += v2;
-    s += v3;
-  }
-  for (; ks < a.ksplit; ++ks) s += p[ks * stride];
-  return s;
-}
-
-// the raw (fp32, summed) logits of token t held by this lane: logit lane + 32 i, for the
-// experts and the shared gate (slot E); issued together so their latencies overlap
+// the raw (fp32) logits of token t held by this lane: logit lane + 32 i, for the experts
+// and the shared gate (slot E), each the fixed-order sum (ks = 0, 1, ...) of its K-split
+// router partials.  The loads of KB slices of all the lane's logits are issued before
+// any is added, so a token waits for ceil(ksplit / KB) L2 round trips, not one per
+// logit and slice group.
 template <int PER>
 FM_DEV void load_logits(const RouteArgs& a, int64_t t, float (&raw)[PER]) {
+  constexpr int KB = PER >= 32 ? 1 : 32 / PER;  // <= 32 loads in flight per lane
   const int lane = threadIdx.x & 31;
+  const float* p = a.partial + t * a.epad + lane;
+  const int64_t stride = a.T * a.epad;
+  bool valid[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
-    raw[i] = (e < a.E || (e == a.E && a.shared_gate_w)) ? sum_partials(a, t, e) : 0.f;
+    valid[i] = e < a.E || (e == a.E && a.shared_gate_w);
+    raw[i] = 0.f;
+  }
+  for (int ks0 = 0; ks0 < a.ksplit; ks0 += KB) {
+    float v[KB][PER];
+#pragma unroll
+    for (int u = 0; u < KB; ++u)
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        v[u][i] = (valid[i] && ks0 + u < a.ksplit) ? p[(ks0 + u) * stride + 32 * i] : 0.f;
+#pragma unroll
+    for (int u = 0; u < KB; ++u)
+#pragma unroll
+      for (int i = 0; i < PER; ++i)
+        if (ks0 + u < a.ksplit) raw[i] += v[u][i];
   }
 }
 
