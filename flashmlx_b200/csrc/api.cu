@@ -396,10 +396,19 @@ int launch_gemm(fm_handle* h, const GemmArgs& ga, bool tcgen05, const fm::TcMaps
 int router_ksplit(const fm_handle* h, int64_t T, int H, int E) {
   const int64_t ntt = (T + 15) / 16;
   const int64_t target = static_cast<int64_t>(h->num_sms) * 16;
-  int ks = static_cast<int>(std::min<int64_t>(fm::kRouterMaxKsplit, std::max<int64_t>(1, (target + ntt - 1) / ntt)));
-  ks = std::min(ks, std::max(1, H / 64));
-  ks = std::min(ks, std::max(2, 4096 / (E + 1)));
-  return ks;
+  const int cap = std::min(std::min(fm::kRouterMaxKsplit, std::max(1, H / 64)), std::max(2, 4096 / (E + 1)));
+  int64_t ks = std::min<int64_t>(cap, std::max<int64_t>(1, (target + ntt - 1) / ntt));
+  // The grid form's wide instance (launch_route takes it when the one-CTA-per-SM grid would
+  // cap the blocks) gives each item of two 16-token tiles to one warp, once: as many slices
+  // as fill its warps, rounded down, so that no warp walks a second item's chain (at
+  // 16384 tokens 4 slices keep 2048 of 2368 warps busy, where 3 kept 1536 and 5 needed
+  // two rounds)
+  const int64_t max_blocks = static_cast<int64_t>(h->route_blocks_per_sm) * h->num_sms;
+  const int64_t wide_warps = static_cast<int64_t>(h->route_wide_blocks_per_sm) * h->num_sms * (fm::kRouteThreads / 32);
+  const int64_t nchunks = (T + fm::kRouteChunk - 1) / fm::kRouteChunk;
+  if (wide_warps > max_blocks * (fm::kRouteThreads / 32) && std::max((ntt * ks + 7) / 8, nchunks) > max_blocks)
+    ks = std::min<int64_t>(cap, std::max<int64_t>(1, wide_warps / ((ntt + 1) / 2)));
+  return static_cast<int>(ks);
 }
 
 // The GEMV path covers group sizes 64 and 128 (each 64-wide half of its 128-wide K
