@@ -10,7 +10,7 @@
 //   1  router partial logits (mma.sync over 16-token x 8-expert tiles, K split across
 //      warps), the pair-permuted copy x_perm of x, zeroing of the fp32 accumulators
 //   2  per token: bf16 logits, softmax, top-k (ties -> lower id), renorm, shared gate;
-//      per 64-token chunk: expert bitmasks -> chunk counts and stable in-chunk ranks
+//      per 16-token chunk: expert bitmasks -> chunk counts and stable in-chunk ranks
 //   3  per expert: exclusive scan of the chunk counts (stable order across chunks)
 //   4  expert offsets, tile tables for the expert-product kernels, scatter of the
 //      pairs into expert-major order
@@ -502,11 +502,13 @@ __device__ void route_one_per(const RouteArgs& a, int64_t t, RouteSmem* sm, int 
 
 template <bool SIGMOID>
 __device__ void route_one(const RouteArgs& a, int64_t t, RouteSmem* sm, int tl) {
-  // lanes cover logits 0..E: the E routed experts and the shared-expert gate at E
+  // lanes cover the logit slots: the E routed experts and, when the block has one, the
+  // shared-expert gate at slot E (128 experts without a gate: four slots a lane)
+  const int slots = a.E + (a.shared_gate_w ? 1 : 0);
   if (!a.do_router) given_row(a, t, sm, tl);
-  else if (a.E < 64) route_one_per<SIGMOID, 2>(a, t, sm, tl);
-  else if (a.E < 128) route_one_per<SIGMOID, 4>(a, t, sm, tl);
-  else if (a.E < 256) route_one_per<SIGMOID, 8>(a, t, sm, tl);
+  else if (slots <= 64) route_one_per<SIGMOID, 2>(a, t, sm, tl);
+  else if (slots <= 128) route_one_per<SIGMOID, 4>(a, t, sm, tl);
+  else if (slots <= 256) route_one_per<SIGMOID, 8>(a, t, sm, tl);
   else route_one_per<SIGMOID, 17>(a, t, sm, tl);  // up to kMaxExperts = 512 experts and the gate
 }
 
